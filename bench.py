@@ -1,0 +1,293 @@
+"""Benchmark of the MoE decode hot path on B200.
+
+Workload (default): Qwen2.5-0.5B-shaped synthetic MoE (dim 896, 24 layers,
+14 heads, vocab 151936, 8 experts top-2, int4 group 32, weights N(0, 0.02)
+seed 1), batch 1, a 512-token uniform-random prompt (numpy default_rng(1))
+prefilled token by token as the reference does, then 512 greedy tokens.
+One step = one such generate call.
+
+  value      decode tok/s: decoded tokens / decode-phase device time (CUDA
+             events on the engine's stream), weights resident in HBM.
+  e2e        decode tok/s through the public API (chalot_generate via
+             Engine.generate) with the prompt in host memory and the tokens
+             copied back: decoded tokens / (wall time of the call - its
+             device prefill time), i.e. every host<->device copy, launch and
+             sync of the call is charged to decoding.
+  roofline   the MoE expert GEMV (gate/up + SwiGLU kernel and down + combine
+             kernel of the top-2 experts), timed with CUDA events over the
+             24 layers' distinct experts: algorithmic bytes = 2 experts x
+             8,171,520 B per layer, against the measured HBM copy bandwidth.
+  cpu_baseline  the CPU restatement of the reference (oracle/), 1 thread +
+             one thread per selected expert as the reference's rayon use,
+             timing decode forwards at positions 512.. (a bounded sample).
+
+Multi-GPU: batch-1 decode does not shard (each forward depends on the last),
+so --gpus N runs N independent replicas, one per rank, and reports the total
+tok/s ("scaling": "weak"). Rank 0 prints one JSON line.
+
+--impl reference times the reference's CPU path (the oracle restatement, all
+host threads) on the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_LEN = 512
+NEW_TOKENS = 512
+KERNELS_PER_LAYER = 7  # qkv, attn scores, attn softmax+PV, o-proj, router, gate/up, down
+
+
+def model_dir() -> str:
+    return os.environ.get("CHALOT_MODEL_DIR", os.path.join(tempfile.gettempdir(), "chalot_models"))
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.p = None
+        self.path = os.path.join(tempfile.gettempdir(), f"chalot_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-i", str(self.index), "-lms", "200"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        if not self.p or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def allmax(ws, v: float) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def prepare_model(ws, rank) -> str:
+    import chalot_c1_b200 as cb
+    path = None
+    if rank == 0:
+        path = cb.ensure_shape(model_dir(), "qwen")
+    barrier(ws)
+    if path is None:
+        path = cb.ensure_shape(model_dir(), "qwen")
+    return path
+
+
+def cpu_sample(path: str, threads: int, n_tokens: int = 4, start: int = 512):
+    """Times `n_tokens` reference-path forwards at positions start.. on the
+    host (KV positions [0, start) filled with seeded values)."""
+    from oracle import oracle as orc
+    e = orc.OracleEngine(path, threads=threads)
+    e.fill_kv_random(start)
+    e.forward(1, start)  # warm the page cache
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        e.forward(100 + i, start + 1 + i)
+    dt = time.perf_counter() - t0
+    e.close()
+    return n_tokens / dt, dt
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    from oracle import oracle as orc
+    orc.build()
+    path = prepare_model(1, 0)
+    threads = orc.hw_threads()
+    for _ in range(args.warmup):
+        cpu_sample(path, threads, n_tokens=1)
+    vals = []
+    for _ in range(args.steps):
+        v, _dt = cpu_sample(path, threads, n_tokens=16)
+        vals.append(v)
+    value = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": "decode tok/s", "value": value, "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 16 / value * 1000, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8/int4 weights, f32 activations", "data": "synthetic",
+        "config": {"workload": "qwen2.5-0.5b-shaped MoE decode, batch 1, 512 prompt + 512 greedy",
+                   "sample": "16 decode forwards per step at positions 513-528"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": "16 decode forwards per step at positions 513-528, KV [0,512) filled"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, ws, rank, local):
+    import numpy as np
+    import torch
+
+    import chalot_c1_b200 as cb
+    from chalot_c1_b200 import build as b
+    b.build()
+    torch.cuda.set_device(local)
+    path = prepare_model(ws, rank)
+    eng = cb.Engine.load(path, device=local)
+    cfg = eng.config
+    prompt = np.random.default_rng(1).integers(0, cfg["vocab_size"], PROMPT_LEN).tolist()
+    for _ in range(args.warmup):
+        eng.generate(prompt, NEW_TOKENS)
+    # dominant kernel: expert GEMV over the layers' experts
+    moe_ms, moe_bytes = eng.bench_moe_layers(reps=10)
+    barrier(ws)
+    torch.cuda.synchronize()
+    dev_decode_ms, dev_prefill_ms, wall, n_dec = 0.0, 0.0, 0.0, 0
+    toks = None
+    with Clocks(local) as clk:
+        t_all = time.perf_counter()
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            toks = eng.generate(prompt, NEW_TOKENS)
+            wall += time.perf_counter() - t0
+            t = eng.last_timing()
+            dev_decode_ms += t["decode_ms"]
+            dev_prefill_ms += t["prefill_ms"]
+            n_dec += t["n_decode"]
+        t_all = time.perf_counter() - t_all
+        moe_ms2, _ = eng.bench_moe_layers(reps=10)
+    torch.cuda.synchronize()
+    barrier(ws)
+    clocks = clk.summary()
+    decode_s = allmax(ws, dev_decode_ms / 1000.0)
+    e2e_s = allmax(ws, wall - dev_prefill_ms / 1000.0)
+    step_s = allmax(ws, t_all / args.steps)
+    moe_ms = min(moe_ms, moe_ms2)
+    if rank != 0:
+        return
+    pk = peaks()
+    achieved = moe_bytes / (moe_ms * 1e-3) / 1e9
+    prof = os.path.join(ROOT, "profiles", "moe_expert_gemv_traffic.json")
+    traffic = json.load(open(prof))["bytes_per_layer"] if os.path.exists(prof) else None
+    cpu_v, cpu_dt = cpu_sample(path, 0, n_tokens=48)
+    from oracle import oracle as orc
+    value = n_dec * ws / decode_s
+    fwd = (PROMPT_LEN + NEW_TOKENS) * args.steps
+    line = {
+        "metric": "decode tok/s", "value": value, "unit": "tok/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000.0,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8/int4 weights (dp4a int32 dots), f32 activations", "data": "synthetic",
+        "config": {"workload": "qwen2.5-0.5b-shaped MoE decode (d896 L24 H14 V151936 E8 top-2 g32), "
+                               "batch 1, 512-token prompt prefilled token by token + 512 greedy tokens",
+                   "replicas": ws, "l2": "inputs larger than L2: 607 MB of weights streamed per token",
+                   "prefill_tok_s": PROMPT_LEN * args.steps * ws / allmax(ws, dev_prefill_ms / 1000.0),
+                   "moe_layer_ms": moe_ms, "tokens_checksum": int(np.asarray(toks, np.uint64).sum())},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                     "kernel": "expert GEMV: k_gateup + k_down, 2 experts x 8,171,520 B per layer",
+                     "peak_source": pk["source"]},
+        "cpu_baseline": {"value": cpu_v, "unit": "tok/s", "cores": 1, "kind": "port",
+                         "sample": f"48 decode forwards at positions 513-560 ({cpu_dt:.2f} s), "
+                                   f"1 thread + 1 thread per selected expert, of "
+                                   f"{orc.hw_threads()} host threads"},
+        "e2e": {"value": n_dec * ws / e2e_s, "unit": "tok/s",
+                "h2d_bytes_per_step": PROMPT_LEN * 4 + 32, "d2h_bytes_per_step": (PROMPT_LEN + NEW_TOKENS) * 4},
+        "gpu_launches": fwd * ws * (1 + cfg["n_layers"] * KERNELS_PER_LAYER + 2),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    eng.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    a = ap.parse_args()
+    ws, rank, local = dist_setup()
+    try:
+        if a.impl == "reference":
+            run_reference(a, ws, rank)
+        else:
+            run_ours(a, ws, rank, local)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,732 @@
+// engine.cu — host engine behind the C ABI: Engine::load / forward / generate /
+// sample_from_logits (src/model/engine.rs:94-569) on one B200.
+//
+// Load parses the .myai header (myai.cpp), copies every tensor the decode path
+// reads into one device allocation at 256-byte aligned offsets, builds the
+// RoPE tables on the host with the same libm calls as InferenceState::new
+// (src/model/state.rs:53-60) and allocates the f32 KV cache
+// [layer][max_seq][dim] (state.rs:45, 73-74).
+//
+// One forward is a fixed sequence of kernels that read the token and position
+// from a device StepState, so it is captured once into a CUDA graph and
+// replayed for every position. Greedy generation without a penalty or stop
+// tokens runs entirely on the device: after each forward the advance kernel
+// stores the argmax and feeds either the next prompt token or the argmax back
+// in, so prefill + decode is one stream of graph launches with no host round
+// trip until the tokens are copied back.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "capi_internal.h"
+#include "kernels.cuh"
+#include "myai.h"
+
+namespace chalot {
+
+struct CudaFail {
+  int code;
+  std::string msg;
+};
+
+#define CK(call)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      throw CudaFail{e_ == cudaErrorMemoryAllocation ? CHALOT_ERR_OOM : CHALOT_ERR_CUDA, \
+                     std::string(#call) + ": " + cudaGetErrorString(e_)};                \
+  } while (0)
+
+class MappedFile {
+ public:
+  ~MappedFile() {
+    if (p_) munmap(p_, n_);
+  }
+  bool open(const char* path, std::string* err) {
+    int fd = ::open(path, O_RDONLY);
+    if (fd < 0) {
+      *err = std::string("open: ") + path;
+      return false;
+    }
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size <= 0) {
+      ::close(fd);
+      *err = std::string("stat: ") + path;
+      return false;
+    }
+    n_ = size_t(st.st_size);
+    p_ = mmap(nullptr, n_, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    if (p_ == MAP_FAILED) {
+      p_ = nullptr;
+      *err = "mmap failed";
+      return false;
+    }
+    return true;
+  }
+  const uint8_t* data() const { return static_cast<const uint8_t*>(p_); }
+  size_t size() const { return n_; }
+
+ private:
+  void* p_ = nullptr;
+  size_t n_ = 0;
+};
+
+}  // namespace chalot
+
+using namespace chalot;
+
+struct chalot_engine {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  ModelConfig cfg;
+  WeightIndex idx;
+  Dims dims{};
+  uint8_t* d_weights = nullptr;
+  size_t weight_bytes = 0;
+  ExpertPtrs* d_experts = nullptr;
+  std::vector<LayerPtrs> layers;
+  std::vector<std::vector<ExpertPtrs>> host_experts;
+  const int8_t* emb = nullptr;
+  const float* emb_s = nullptr;
+  const float* final_norm = nullptr;
+  const int8_t* out_w = nullptr;
+  const float* out_s = nullptr;
+  DecodeBufs b{};
+  std::vector<void*> allocs;
+  StepState* h_state = nullptr;  // pinned staging
+  uint32_t* h_tokens = nullptr;  // pinned, [max_seq]
+  uint32_t* d_hist = nullptr;    // [2*max_seq] token history for the penalty
+  bool use_graph = true;
+  cudaGraphExec_t g_fwd = nullptr;   // embed .. lm_head
+  cudaGraphExec_t g_step = nullptr;  // embed .. lm_head + advance
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  double last_prefill_ms = 0, last_decode_ms = 0;
+  uint32_t last_n_prefill = 0, last_n_decode = 0;
+
+  ~chalot_engine() {
+    if (g_fwd) cudaGraphExecDestroy(g_fwd);
+    if (g_step) cudaGraphExecDestroy(g_step);
+    for (auto& e : ev)
+      if (e) cudaEventDestroy(e);
+    for (void* p : allocs) cudaFree(p);
+    if (d_weights) cudaFree(d_weights);
+    if (h_state) cudaFreeHost(h_state);
+    if (h_tokens) cudaFreeHost(h_tokens);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  template <class T>
+  T* dalloc(size_t n) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16)));
+    CK(cudaMemset(p, 0, std::max<size_t>(n * sizeof(T), 16)));
+    allocs.push_back(p);
+    return static_cast<T*>(p);
+  }
+
+  void record_forward(cudaStream_t s, bool with_advance) {
+    const Dims& d = dims;
+    launch_embed(d, emb, emb_s, b, s);
+    for (int l = 0; l < d.n_layers; ++l) {
+      const LayerPtrs& L = layers[l];
+      launch_qkv(d, L, l, b, s);
+      launch_attention(d, l, b, s);
+      launch_oproj(d, L, b, s);
+      launch_router(d, L, l, b, s);
+      launch_gateup(d, L, b, s);
+      launch_down(d, L, b, s);
+    }
+    launch_lmhead(d, final_norm, out_w, out_s, b, num_sms, s);
+    if (with_advance) launch_advance(d, b, s);
+  }
+
+  cudaGraphExec_t capture(bool with_advance) {
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    record_forward(stream, with_advance);
+    cudaError_t le = cudaGetLastError();
+    CK(cudaStreamEndCapture(stream, &g));
+    CK(le);
+    cudaGraphExec_t ex = nullptr;
+    cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    CK(ie);
+    return ex;
+  }
+
+  void run_forward(bool with_advance) {
+    if (use_graph) {
+      CK(cudaGraphLaunch(with_advance ? g_step : g_fwd, stream));
+    } else {
+      record_forward(stream, with_advance);
+      CK(cudaGetLastError());
+    }
+  }
+
+  void set_state(uint32_t pos, uint32_t token, uint32_t n_prefill, uint32_t step) {
+    h_state->pos = pos;
+    h_state->token = token;
+    h_state->n_prefill = n_prefill;
+    h_state->step = step;
+    h_state->argmax_key = 0ull;
+    CK(cudaMemcpyAsync(b.st, h_state, sizeof(StepState), cudaMemcpyHostToDevice, stream));
+  }
+};
+
+namespace {
+
+int fail(const CudaFail& f) { return set_error(f.code, f.msg); }
+
+bool check_shapes(const ModelConfig& c, std::string* err) {
+  auto bad = [&](const char* m) {
+    *err = std::string("unsupported model shape: ") + m;
+    return false;
+  };
+  if (c.dim == 0 || c.n_heads == 0 || c.n_layers == 0 || c.vocab_size == 0 || c.hidden_dim == 0)
+    return bad("zero dimension");
+  if (c.dim % c.n_heads) return bad("dim is not a multiple of n_heads");
+  if (c.dim % 32) return bad("dim must be a multiple of 32");
+  if (c.hidden_dim % 32) return bad("hidden_dim must be a multiple of 32");
+  if (c.int4_group_size % 32) return bad("int4_group_size must be a multiple of 32");
+  if (c.dim % c.int4_group_size || c.hidden_dim % c.int4_group_size)
+    return bad("dim and hidden_dim must be multiples of int4_group_size");
+  if (c.head_dim % 4 || c.head_dim > 256) return bad("head_dim must be a multiple of 4 and <= 256");
+  if (c.n_experts > 64) return bad("more than 64 experts");
+  if (c.top_k > 8) return bad("top_k above 8");
+  if (c.vocab_size >= (1u << 31)) return bad("vocab too large");
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+__attribute__((visibility("default"))) int chalot_load(const char* path, const chalot_opts* opts,
+                                                       chalot_engine** out) {
+  if (!path || !out) return set_error(CHALOT_ERR_ARG, "null argument");
+  *out = nullptr;
+  MappedFile mf;
+  std::string err;
+  if (!mf.open(path, &err)) return set_error(CHALOT_ERR_IO, err);
+  FileHeader h;
+  if (!parse_header(mf.data(), mf.size(), &h, &err)) return set_error(CHALOT_ERR_FORMAT, err);
+  std::unique_ptr<chalot_engine> e(new chalot_engine());
+  e->cfg = config_from_header(h);
+  e->idx = build_index(e->cfg);
+  const ModelConfig& c = e->cfg;
+  if (!check_shapes(c, &err)) return set_error(CHALOT_ERR_ARG, err);
+  if (mf.size() < e->idx.total_bytes)
+    return set_error(CHALOT_ERR_FORMAT, "file is " + std::to_string(mf.size()) +
+                                            " bytes, its header implies " +
+                                            std::to_string(e->idx.total_bytes));
+  e->device = opts ? opts->device : 0;
+  e->use_graph = opts ? opts->use_cuda_graph != 0 : true;
+  try {
+    CK(cudaSetDevice(e->device));
+    CK(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, e->device));
+    CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+    Dims& d = e->dims;
+    d.dim = int(c.dim);
+    d.hidden = int(c.hidden_dim);
+    d.n_layers = int(c.n_layers);
+    d.n_heads = int(c.n_heads);
+    d.head_dim = int(c.head_dim);
+    d.vocab = int(c.vocab_size);
+    d.max_seq = int(c.max_seq_len);
+    d.n_experts = int(c.n_experts);
+    d.top_k = int(c.top_k);
+    d.group = int(c.int4_group_size);
+
+    // ---- weights: every tensor at a 256-byte aligned device offset ----
+    struct Piece {
+      size_t src, bytes, dst;
+    };
+    std::vector<Piece> pieces;
+    size_t cur = 0;
+    auto place = [&](size_t src, size_t bytes) {
+      pieces.push_back({src, bytes, cur});
+      size_t at = cur;
+      cur = (cur + bytes + 255) & ~size_t(255);
+      return at;
+    };
+    const WeightIndex& ix = e->idx;
+    const size_t dim = c.dim, H = c.hidden_dim, V = c.vocab_size, E = c.n_experts;
+    struct LOff {
+      size_t rms_attn, qkv, qkv_s, o, o_s, rms_ffn, rw, rb;
+      std::vector<std::array<size_t, 4>> ex;
+    };
+    std::vector<LOff> loff(c.n_layers);
+    const size_t emb = place(ix.embed_offset, V * dim), emb_s = place(ix.embed_scales_offset, V * 4);
+    for (size_t l = 0; l < c.n_layers; ++l) {
+      const LayerIndex& L = ix.layers[l];
+      LOff& o = loff[l];
+      o.rms_attn = place(L.rms_attn_offset, dim * 4);
+      o.qkv = place(L.attn_qkv_offset, 3 * dim * dim);
+      o.qkv_s = place(L.attn_qkv_scales_offset, 3 * dim * 4);
+      o.o = place(L.attn_out_offset, dim * dim);
+      o.o_s = place(L.attn_out_scales_offset, dim * 4);
+      o.rms_ffn = place(L.rms_ffn_offset, dim * 4);
+      o.rw = o.rb = 0;
+      if (E >= 2) {
+        o.rw = place(L.router_w_offset, E * dim * 4);
+        o.rb = place(L.router_b_offset, E * 4);
+      }
+      for (size_t x = 0; x < E; ++x) {
+        const ExpertIndex& X = L.experts[x];
+        std::array<size_t, 4> a{place(X.gate_up_offset, X.gate_up_packed_bytes),
+                                place(X.gate_up_scales_offset, X.gate_up_scales_count * 4),
+                                place(X.down_offset, X.down_packed_bytes),
+                                place(X.down_scales_offset, X.down_scales_count * 4)};
+        o.ex.push_back(a);
+      }
+    }
+    const size_t fnorm = place(ix.final_norm_offset, dim * 4);
+    const size_t outw = place(ix.output_proj_offset, V * dim), outs = place(ix.output_proj_scales_offset, V * 4);
+    e->weight_bytes = cur;
+    CK(cudaMalloc(&e->d_weights, cur));
+    {
+      // stage through pinned memory in large chunks
+      const size_t chunk = size_t(64) << 20;
+      uint8_t* stage[2] = {nullptr, nullptr};
+      CK(cudaMallocHost(&stage[0], chunk));
+      CK(cudaMallocHost(&stage[1], chunk));
+      cudaEvent_t done[2];
+      CK(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming));
+      CK(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming));
+      int which = 0;
+      size_t fill = 0;
+      for (const Piece& p : pieces) {
+        size_t done_b = 0;
+        while (done_b < p.bytes) {
+          size_t n = std::min(p.bytes - done_b, chunk - fill);
+          if (fill == 0) CK(cudaEventSynchronize(done[which]));
+          std::memcpy(stage[which] + fill, mf.data() + p.src + done_b, n);
+          CK(cudaMemcpyAsync(e->d_weights + p.dst + done_b, stage[which] + fill, n,
+                             cudaMemcpyHostToDevice, e->stream));
+          fill += n;
+          done_b += n;
+          if (fill == chunk) {
+            CK(cudaEventRecord(done[which], e->stream));
+            which ^= 1;
+            fill = 0;
+          }
+        }
+      }
+      CK(cudaStreamSynchronize(e->stream));
+      cudaEventDestroy(done[0]);
+      cudaEventDestroy(done[1]);
+      cudaFreeHost(stage[0]);
+      cudaFreeHost(stage[1]);
+    }
+    uint8_t* W = e->d_weights;
+    e->emb = reinterpret_cast<const int8_t*>(W + emb);
+    e->emb_s = reinterpret_cast<const float*>(W + emb_s);
+    e->final_norm = reinterpret_cast<const float*>(W + fnorm);
+    e->out_w = reinterpret_cast<const int8_t*>(W + outw);
+    e->out_s = reinterpret_cast<const float*>(W + outs);
+    e->d_experts = e->dalloc<ExpertPtrs>(c.n_layers * E);
+    std::vector<ExpertPtrs> all;
+    for (size_t l = 0; l < c.n_layers; ++l) {
+      const LOff& o = loff[l];
+      LayerPtrs L{};
+      L.rms_attn = reinterpret_cast<const float*>(W + o.rms_attn);
+      L.qkv = reinterpret_cast<const int8_t*>(W + o.qkv);
+      L.qkv_s = reinterpret_cast<const float*>(W + o.qkv_s);
+      L.o = reinterpret_cast<const int8_t*>(W + o.o);
+      L.o_s = reinterpret_cast<const float*>(W + o.o_s);
+      L.rms_ffn = reinterpret_cast<const float*>(W + o.rms_ffn);
+      L.router_w = E >= 2 ? reinterpret_cast<const float*>(W + o.rw) : nullptr;
+      L.router_b = E >= 2 ? reinterpret_cast<const float*>(W + o.rb) : nullptr;
+      L.experts = e->d_experts + l * E;
+      std::vector<ExpertPtrs> exs;
+      for (size_t x = 0; x < E; ++x) {
+        ExpertPtrs p{W + o.ex[x][0], reinterpret_cast<const float*>(W + o.ex[x][1]), W + o.ex[x][2],
+                     reinterpret_cast<const float*>(W + o.ex[x][3])};
+        exs.push_back(p);
+        all.push_back(p);
+      }
+      e->host_experts.push_back(exs);
+      e->layers.push_back(L);
+    }
+    CK(cudaMemcpy(e->d_experts, all.data(), all.size() * sizeof(ExpertPtrs), cudaMemcpyHostToDevice));
+
+    // ---- RoPE tables (state.rs:53-60), computed with glibc powf/cosf/sinf ----
+    const size_t half = c.head_dim / 2;
+    std::vector<float> cosv(c.max_seq_len * half), sinv(c.max_seq_len * half);
+    for (size_t pos = 0; pos < c.max_seq_len; ++pos)
+      for (size_t i = 0; i < half; ++i) {
+        float freq = 1.0f / std::pow(c.rope_theta, float(2 * i) / float(c.head_dim));
+        float th = float(pos) * freq;
+        cosv[pos * half + i] = std::cos(th);
+        sinv[pos * half + i] = std::sin(th);
+      }
+    float* rc = e->dalloc<float>(cosv.size());
+    float* rs = e->dalloc<float>(sinv.size());
+    CK(cudaMemcpy(rc, cosv.data(), cosv.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(rs, sinv.data(), sinv.size() * 4, cudaMemcpyHostToDevice));
+
+    // ---- decode buffers ----
+    DecodeBufs& b = e->b;
+    b.x = e->dalloc<float>(dim);
+    b.q = e->dalloc<float>(dim);
+    b.att_out = e->dalloc<float>(dim);
+    b.scores = e->dalloc<float>(c.n_heads * c.max_seq_len);
+    b.kc = e->dalloc<float>(c.n_layers * c.max_seq_len * dim);
+    b.vc = e->dalloc<float>(c.n_layers * c.max_seq_len * dim);
+    b.rope_cos = rc;
+    b.rope_sin = rs;
+    b.xq_ffn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
+    b.xs_ffn = e->dalloc<float>(1);
+    b.sel = e->dalloc<int32_t>(std::max<size_t>(c.top_k, 1));
+    b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
+    b.h = e->dalloc<float>(std::max<size_t>(c.top_k, 1) * H);
+    b.amax = e->dalloc<unsigned>(std::max<size_t>(c.top_k, 1));
+    b.logits = e->dalloc<float>(V);
+    b.st = e->dalloc<StepState>(1);
+    b.prompt = e->dalloc<uint32_t>(c.max_seq_len);
+    b.out_tokens = e->dalloc<uint32_t>(c.max_seq_len + 1);
+    b.router_trace = nullptr;
+    e->d_hist = e->dalloc<uint32_t>(2 * c.max_seq_len + 64);
+    CK(cudaMallocHost(&e->h_state, sizeof(StepState)));
+    CK(cudaMallocHost(&e->h_tokens, (c.max_seq_len + 1) * sizeof(uint32_t)));
+    for (auto& ev : e->ev) CK(cudaEventCreate(&ev));
+    if (e->use_graph) {
+      e->g_fwd = e->capture(false);
+      e->g_step = e->capture(true);
+    }
+    CK(cudaDeviceSynchronize());
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  *out = e.release();
+  clear_error();
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) void chalot_free(chalot_engine* e) { delete e; }
+
+__attribute__((visibility("default"))) int chalot_get_config(const chalot_engine* e,
+                                                             chalot_model_config* out) {
+  if (!e || !out) return set_error(CHALOT_ERR_ARG, "null argument");
+  const ModelConfig& c = e->cfg;
+  std::memset(out, 0, sizeof *out);
+  out->dim = uint32_t(c.dim);
+  out->hidden_dim = uint32_t(c.hidden_dim);
+  out->n_layers = uint32_t(c.n_layers);
+  out->n_heads = uint32_t(c.n_heads);
+  out->head_dim = uint32_t(c.head_dim);
+  out->vocab_size = uint32_t(c.vocab_size);
+  out->max_seq_len = uint32_t(c.max_seq_len);
+  out->n_experts = uint32_t(c.n_experts);
+  out->top_k = uint32_t(c.top_k);
+  out->int4_group_size = uint32_t(c.int4_group_size);
+  out->depth_router_layer = uint32_t(c.depth_router_layer);
+  out->rope_theta = c.rope_theta;
+  out->total_bytes = e->idx.total_bytes;
+  out->expert_bytes = e->idx.layers.empty() || e->idx.layers[0].experts.empty()
+                          ? 0
+                          : e->idx.layers[0].experts[0].bytes();
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_forward(chalot_engine* e, uint32_t token,
+                                                          uint32_t pos, uint32_t* out_token) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
+  if (token >= e->cfg.vocab_size) return set_error(CHALOT_ERR_ARG, "token id out of range");
+  if (pos >= e->cfg.max_seq_len) return set_error(CHALOT_ERR_ARG, "position out of range");
+  try {
+    CK(cudaSetDevice(e->device));
+    e->set_state(pos, token, 0, 0);
+    e->run_forward(true);
+    CK(cudaMemcpyAsync(e->h_tokens, e->b.out_tokens, sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                       e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    if (out_token) *out_token = e->h_tokens[0];
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  clear_error();
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_get_logits(chalot_engine* e, float* dst, size_t n) {
+  if (!e || !dst) return set_error(CHALOT_ERR_ARG, "null argument");
+  try {
+    CK(cudaSetDevice(e->device));
+    CK(cudaMemcpyAsync(dst, e->b.logits, std::min(n, e->cfg.vocab_size) * 4, cudaMemcpyDeviceToHost,
+                       e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_sample_from_logits(chalot_engine* e,
+                                                                     const chalot_sampling* sp,
+                                                                     const uint32_t* history,
+                                                                     size_t n_history,
+                                                                     uint32_t* out_token) {
+  if (!e || !out_token) return set_error(CHALOT_ERR_ARG, "null argument");
+  if (sp && sp->strategy != CHALOT_GREEDY)
+    return set_error(CHALOT_ERR_ARG, "only the greedy strategy is implemented");
+  try {
+    CK(cudaSetDevice(e->device));
+    const float pen = sp ? sp->repetition_penalty : 1.0f;
+    size_t w = 0;
+    if (pen > 1.0f && n_history > 0 && history) {  // engine.rs:555-560
+      w = std::min<size_t>(n_history, sp->repetition_window);
+      w = std::min<size_t>(w, 2 * e->cfg.max_seq_len + 64);
+      CK(cudaMemcpyAsync(e->d_hist, history + (n_history - w), w * 4, cudaMemcpyHostToDevice,
+                         e->stream));
+    }
+    launch_penalty_argmax(e->dims, e->b, e->d_hist, int(w), w ? pen : 1.0f, e->stream);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(e->h_state, e->b.st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    *out_token = uint32_t(e->h_state->argmax_key & 0xffffffffull);
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, const uint32_t* prompt,
+                                                           size_t n_prompt, size_t max_new,
+                                                           const chalot_sampling* sp, uint32_t* out,
+                                                           size_t* n_out) {
+  if (!e || !n_out || (n_prompt && !prompt) || (max_new && !out))
+    return set_error(CHALOT_ERR_ARG, "null argument");
+  if (sp && sp->strategy != CHALOT_GREEDY)
+    return set_error(CHALOT_ERR_ARG, "only the greedy strategy is implemented");
+  const size_t max_seq = e->cfg.max_seq_len, V = e->cfg.vocab_size;
+  *n_out = 0;
+  // engine.rs:509: n_prefill = min(len, max(max_seq - max_new, 1))
+  const size_t room = max_seq > max_new ? max_seq - max_new : 0;
+  const size_t n_prefill = std::min(n_prompt, std::max<size_t>(room, 1));
+  const size_t n_decode = std::min(max_new, max_seq - std::min(max_seq, n_prefill));
+  const float pen = sp ? sp->repetition_penalty : 1.0f;
+  const bool penalty = pen > 1.0f;
+  const bool stops = sp && sp->n_stop_tokens > 0 && sp->stop_tokens;
+  try {
+    CK(cudaSetDevice(e->device));
+    std::vector<uint32_t> clamped(n_prefill);
+    for (size_t i = 0; i < n_prefill; ++i) clamped[i] = std::min<uint32_t>(prompt[i], uint32_t(V - 1));
+    if (n_prefill)
+      CK(cudaMemcpyAsync(const_cast<uint32_t*>(e->b.prompt), clamped.data(), n_prefill * 4,
+                         cudaMemcpyHostToDevice, e->stream));
+    // the first token processed: prompt[0] or, without a prompt, BOS = 1 (engine.rs:520-524)
+    e->set_state(0, n_prefill ? clamped[0] : 1u, uint32_t(n_prefill), 0);
+    std::vector<uint32_t> hist(prompt, prompt + n_prompt);
+    const size_t total = n_prefill + n_decode;
+    CK(cudaEventRecord(e->ev[0], e->stream));
+    if (!penalty && !stops) {
+      for (size_t f = 0; f < total; ++f) {
+        e->run_forward(true);
+        if (f + 1 == n_prefill) CK(cudaEventRecord(e->ev[1], e->stream));
+      }
+      if (n_prefill == 0) CK(cudaEventRecord(e->ev[1], e->stream));
+      CK(cudaEventRecord(e->ev[2], e->stream));
+      CK(cudaMemcpyAsync(e->h_tokens, e->b.out_tokens, std::max<size_t>(total, 1) * 4,
+                         cudaMemcpyDeviceToHost, e->stream));
+      CK(cudaStreamSynchronize(e->stream));
+      // the token sampled after forward f (f >= n_prefill-1) is output n_prefill-1..
+      size_t cnt = 0;
+      for (size_t s = 0; s < n_decode; ++s)
+        out[cnt++] = (n_prefill == 0 && s == 0) ? 1u : e->h_tokens[n_prefill + s - 1];
+      *n_out = cnt;
+    } else {
+      // host-driven loop: the penalty needs the history, stop tokens end early
+      if (n_prefill == 0) CK(cudaEventRecord(e->ev[1], e->stream));
+      uint32_t next = 1;
+      size_t cnt = 0;
+      auto sample = [&]() -> uint32_t {
+        size_t w = 0;
+        if (penalty && !hist.empty()) {
+          w = std::min<size_t>(hist.size(), sp->repetition_window);
+          w = std::min<size_t>(w, 2 * max_seq + 64);
+          CK(cudaMemcpyAsync(e->d_hist, hist.data() + (hist.size() - w), w * 4,
+                             cudaMemcpyHostToDevice, e->stream));
+        }
+        launch_penalty_argmax(e->dims, e->b, e->d_hist, int(w), w ? pen : 1.0f, e->stream);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(e->h_state, e->b.st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
+        CK(cudaStreamSynchronize(e->stream));
+        return uint32_t(e->h_state->argmax_key & 0xffffffffull);
+      };
+      for (size_t p = 0; p < n_prefill; ++p) {
+        e->set_state(uint32_t(p), clamped[p], 0, 0);
+        e->run_forward(false);
+        if (p + 1 == n_prefill) CK(cudaEventRecord(e->ev[1], e->stream));
+      }
+      if (n_prefill) next = sample();
+      for (size_t s = 0; s < n_decode; ++s) {
+        bool is_stop = false;
+        for (uint32_t i = 0; stops && i < sp->n_stop_tokens; ++i) is_stop |= sp->stop_tokens[i] == next;
+        if (is_stop) break;
+        out[cnt++] = next;
+        hist.push_back(next);
+        e->set_state(uint32_t(n_prefill + s), next, 0, 0);
+        e->run_forward(false);
+        next = sample();
+      }
+      CK(cudaEventRecord(e->ev[2], e->stream));
+      CK(cudaStreamSynchronize(e->stream));
+      *n_out = cnt;
+    }
+    float a = 0, bb = 0;
+    CK(cudaEventElapsedTime(&a, e->ev[0], e->ev[1]));
+    CK(cudaEventElapsedTime(&bb, e->ev[1], e->ev[2]));
+    e->last_prefill_ms = a;
+    e->last_decode_ms = bb;
+    e->last_n_prefill = uint32_t(n_prefill);
+    e->last_n_decode = uint32_t(n_decode);
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  clear_error();
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_last_timing(chalot_engine* e, double* prefill_ms,
+                                                              double* decode_ms, uint32_t* n_prefill,
+                                                              uint32_t* n_decode) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
+  if (prefill_ms) *prefill_ms = e->last_prefill_ms;
+  if (decode_ms) *decode_ms = e->last_decode_ms;
+  if (n_prefill) *n_prefill = e->last_n_prefill;
+  if (n_decode) *n_decode = e->last_n_decode;
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine* e, int reps,
+                                                                   double* ms_per_layer,
+                                                                   double* bytes_per_layer) {
+  if (!e || reps <= 0) return set_error(CHALOT_ERR_ARG, "bad argument");
+  const Dims& d = e->dims;
+  try {
+    CK(cudaSetDevice(e->device));
+    // A fixed selection per layer in device buffers of its own, so the
+    // decode state is untouched.
+    const int K = d.top_k, L = d.n_layers;
+    DecodeBufs b = e->b;
+    int32_t* sel = nullptr;
+    float* selw = nullptr;
+    float* x = nullptr;
+    CK(cudaMalloc(&sel, sizeof(int32_t) * K * L));
+    CK(cudaMalloc(&selw, sizeof(float) * K * L));
+    CK(cudaMalloc(&x, sizeof(float) * d.dim));
+    std::vector<int32_t> hs(K * L);
+    std::vector<float> hw(K * L, 1.0f / K);
+    for (int l = 0; l < L; ++l)
+      for (int k = 0; k < K; ++k) hs[l * K + k] = (l * K + k) % d.n_experts;
+    CK(cudaMemcpy(sel, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(selw, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(x, e->b.x, sizeof(float) * d.dim, cudaMemcpyDeviceToDevice));
+    b.x = x;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ex = nullptr;
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    for (int l = 0; l < L; ++l) {
+      DecodeBufs bl = b;
+      bl.sel = sel + l * K;
+      bl.selw = selw + l * K;
+      CK(cudaMemsetAsync(bl.amax, 0, sizeof(unsigned) * K, e->stream));
+      launch_gateup(d, e->layers[l], bl, e->stream);
+      launch_down(d, e->layers[l], bl, e->stream);
+    }
+    CK(cudaStreamEndCapture(e->stream, &g));
+    CK(cudaGraphInstantiate(&ex, g, 0));
+    cudaGraphDestroy(g);
+    CK(cudaGraphLaunch(ex, e->stream));  // warm-up
+    CK(cudaEventRecord(e->ev[0], e->stream));
+    for (int r = 0; r < reps; ++r) CK(cudaGraphLaunch(ex, e->stream));
+    CK(cudaEventRecord(e->ev[1], e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    float ms = 0;
+    CK(cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]));
+    cudaGraphExecDestroy(ex);
+    cudaFree(sel);
+    cudaFree(selw);
+    cudaFree(x);
+    if (ms_per_layer) *ms_per_layer = double(ms) / (double(reps) * L);
+    if (bytes_per_layer) *bytes_per_layer = double(K) * double(e->idx.layers[0].experts[0].bytes());
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  return CHALOT_OK;
+}
+
+// ---- operators ----------------------------------------------------------------
+
+__attribute__((visibility("default"))) int chalot_matmul_i8(float* out, const int8_t* w,
+                                                            const float* ws, const float* x,
+                                                            size_t out_dim, size_t in_dim,
+                                                            void* stream) {
+  if (!out || !w || !ws || !x) return set_error(CHALOT_ERR_ARG, "null pointer");
+  if (out_dim == 0 || in_dim == 0) return CHALOT_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t r = op_matmul_i8(out, w, ws, x, out_dim, in_dim, sms, static_cast<cudaStream_t>(stream));
+  if (r != cudaSuccess) return set_error(r == cudaErrorInvalidValue ? CHALOT_ERR_ARG : CHALOT_ERR_CUDA,
+                                         std::string("matmul_i8: ") + cudaGetErrorString(r));
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_matmul_i4(float* out, const uint8_t* wp,
+                                                            const float* ws, const float* x,
+                                                            size_t out_dim, size_t in_dim,
+                                                            size_t group, void* stream) {
+  if (!out || !wp || !ws || !x) return set_error(CHALOT_ERR_ARG, "null pointer");
+  if (group == 0) group = kDefaultInt4Group;
+  if (group % 2) return set_error(CHALOT_ERR_ARG, "odd int4 group sizes are not supported");
+  if (out_dim == 0 || in_dim == 0) return CHALOT_OK;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t r = op_matmul_i4(out, wp, ws, x, out_dim, in_dim, group, sms,
+                               static_cast<cudaStream_t>(stream));
+  if (r != cudaSuccess) return set_error(r == cudaErrorInvalidValue ? CHALOT_ERR_ARG : CHALOT_ERR_CUDA,
+                                         std::string("matmul_i4: ") + cudaGetErrorString(r));
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_quantize_i8(int8_t* q, float* scale, const float* x,
+                                                              size_t n_vec, size_t n, void* stream) {
+  if (!q || !scale || !x) return set_error(CHALOT_ERR_ARG, "null pointer");
+  if (n_vec == 0 || n == 0) return CHALOT_OK;
+  cudaError_t r = op_quantize_i8(q, scale, x, n_vec, n, static_cast<cudaStream_t>(stream));
+  if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, cudaGetErrorString(r));
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_router_topk(int32_t* idx, float* weight,
+                                                              const float* x, const float* w,
+                                                              const float* b, size_t n_tok,
+                                                              size_t dim, size_t n_experts,
+                                                              size_t top_k, void* stream) {
+  if (!idx || !weight || !x || !w || !b) return set_error(CHALOT_ERR_ARG, "null pointer");
+  if (n_experts == 0 || top_k == 0 || top_k > n_experts || n_experts > 64)
+    return set_error(CHALOT_ERR_ARG, "need 1 <= top_k <= n_experts <= 64");
+  if (n_tok == 0) return CHALOT_OK;
+  cudaError_t r = op_router_topk(idx, weight, x, w, b, n_tok, dim, n_experts, top_k,
+                                 static_cast<cudaStream_t>(stream));
+  if (r != cudaSuccess) return set_error(r == cudaErrorInvalidValue ? CHALOT_ERR_ARG : CHALOT_ERR_CUDA,
+                                         cudaGetErrorString(r));
+  return CHALOT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,126 @@
+// k_attn.cu — decode attention over the f32 KV cache in the reference's
+// rounding order (src/model/engine.rs:283-309).
+//
+//   k_attn_scores  s[h][t] = 30 * tanh((dot_f32(q_h, K[t]_h) * (1/sqrt(hd))) / 30)
+//                  for t <= pos; one thread per (head, t), the dot in the
+//                  two-accumulator 8-lane order of dot_f32_avx2
+//                  (src/tensor/attention_helpers.rs:41-80) and the cap of
+//                  logit_soft_cap (src/tensor/activations.rs:133-135).
+//   k_attn_pv      softmax_avx2 over s[h][0..pos] (normalization.rs:106-160),
+//                  then out[d] = sum_t p_t * V[t][d] added in t order
+//                  (engine.rs:302-308); one thread per output column.
+// The cache layout is the reference's: [layer][max_seq][dim], head h at
+// columns h*hd .. h*hd+hd-1.
+#include <cuda_runtime.h>
+
+#include "blockops.cuh"
+#include "kernels.cuh"
+
+namespace chalot {
+namespace {
+
+constexpr int kScoreThreads = 128;
+
+__global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer, DecodeBufs b) {
+  __shared__ __align__(16) float qh[256];
+  const int h = blockIdx.y, hd = d.head_dim;
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t pos = b.st->pos;
+  if (blockIdx.x * blockDim.x > pos) return;  // whole CTA beyond the causal range
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = b.q[h * hd + i];
+  __syncthreads();
+  if ((uint32_t)t > pos) return;
+  const float* k = b.kc + ((size_t)layer * d.max_seq + t) * d.dim + (size_t)h * hd;
+  float a0[8], a1[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a0[j] = a1[j] = 0.0f;
+  const int c16 = hd >> 4, rem = c16 * 16;
+  for (int c = 0; c < c16; ++c) {
+    const float4* kv = reinterpret_cast<const float4*>(k + c * 16);
+    const float4 k0 = kv[0], k1 = kv[1], k2 = kv[2], k3 = kv[3];
+    const float kk[16] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w,
+                          k2.x, k2.y, k2.z, k2.w, k3.x, k3.y, k3.z, k3.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[c * 16 + j], kk[j]));
+      a1[j] = __fadd_rn(a1[j], __fmul_rn(qh[c * 16 + 8 + j], kk[8 + j]));
+    }
+  }
+  const bool extra = rem + 8 <= hd;
+  if (extra)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[rem + j], k[rem + j]));
+  float cmb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cmb[j] = __fadd_rn(a0[j], a1[j]);
+  float dot = hsum8(cmb);
+  for (int i = extra ? rem + 8 : rem; i < hd; ++i) dot = __fadd_rn(dot, __fmul_rn(qh[i], k[i]));
+  const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
+  const float x = __fmul_rn(dot, inv_sqrt);
+  b.scores[(size_t)h * d.max_seq + t] = __fmul_rn(30.0f, tanhf(__fdiv_rn(x, 30.0f)));
+}
+
+constexpr int kPvThreads = 32;
+
+__global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, DecodeBufs b) {
+  extern __shared__ __align__(16) float p[];  // [max_seq]
+  __shared__ float lanes[8];
+  __shared__ float inv_s;
+  const int h = blockIdx.x, hd = d.head_dim, col = blockIdx.y * 32 + threadIdx.x;
+  const int n = (int)b.st->pos + 1;
+  const float* s = b.scores + (size_t)h * d.max_seq;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = s[i];
+    p[i] = v;
+    mx = fmaxf(mx, v);
+  }
+  mx = warp_max(mx);
+  const int full = n & ~7;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    p[i] = (i < full) ? fast_exp(__fsub_rn(p[i], mx)) : expf(__fsub_rn(p[i], mx));
+  __syncwarp();
+  if (threadIdx.x < 8) {
+    float acc = 0.0f;
+    for (int c = 0; c < (full >> 3); ++c) acc = __fadd_rn(acc, p[c * 8 + threadIdx.x]);
+    lanes[threadIdx.x] = acc;
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    float l8[8];
+    for (int j = 0; j < 8; ++j) l8[j] = lanes[j];
+    float sum = hsum8(l8);
+    for (int i = full; i < n; ++i) sum = __fadd_rn(sum, p[i]);
+    inv_s = __fdiv_rn(1.0f, sum);
+  }
+  __syncwarp();
+  const float inv = inv_s;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
+  __syncwarp();
+  if (col >= hd) return;
+  const float* v = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + col;
+  float acc = 0.0f;
+  int t = 0;
+  for (; t + 8 <= n; t += 8) {
+    float vv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) vv[u] = v[(size_t)(t + u) * d.dim];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(p[t + u], vv[u]));
+  }
+  for (; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[(size_t)t * d.dim]));
+  b.att_out[h * hd + col] = acc;
+}
+
+}  // namespace
+
+void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s) {
+  dim3 g1((d.max_seq + kScoreThreads - 1) / kScoreThreads, d.n_heads);
+  k_attn_scores<<<g1, kScoreThreads, 0, s>>>(d, layer, b);
+  dim3 g2(d.n_heads, (d.head_dim + 31) / 32);
+  const size_t smem = (size_t)d.max_seq * 4;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  k_attn_pv<<<g2, kPvThreads, smem, s>>>(d, layer, b);
+}
+
+}  // namespace chalot

@@ -1,0 +1,340 @@
+// k_dense.cu — int8 GEMV kernels of the decode step and the int8 operator.
+//
+// matmul_int8 (src/tensor/matmul.rs:47-97, 183-298): the input vector is
+// quantized per call (quantize_f32_to_i8, quantization.rs:56-104), every row
+// dot is an exact int32, and the row result is ((float)dot * w_scale) * x_scale.
+// The decode kernels fuse the producer and consumer of that GEMV:
+//   k_qkv    rmsnorm(x) -> quantize -> Q/K/V rows -> RoPE -> KV-cache write
+//            (engine.rs:235-280)
+//   k_oproj  quantize(att_out) -> O rows -> x += out (engine.rs:312-322)
+//   k_lmhead rmsnorm(x) -> quantize -> vocab rows -> logits + argmax
+//            (engine.rs:470-493, sampling.rs:34-41)
+// Rows are streamed with 16-byte non-allocating loads; each warp owns a few
+// rows and its lanes stride the row in 16-byte chunks (coalesced 512 B per warp
+// instruction), dotting them with dp4a against the quantized vector in shared
+// memory.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "blockops.cuh"
+#include "kernels.cuh"
+
+namespace chalot {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+// R consecutive rows of an int8 matrix dotted with xq (shared, 16-aligned);
+// in_dim % 16 == 0. Every lane returns the full int32 dots.
+template <int R>
+__device__ __forceinline__ void rows_dot_i8(const int8_t* __restrict__ W, int in_dim, int row0,
+                                            int n_rows, const int8_t* xq, int acc[R]) {
+  const int lane = threadIdx.x & 31, chunks = in_dim >> 4;
+  const uint4* xv = reinterpret_cast<const uint4*>(xq);
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = 0;
+#pragma unroll 2
+  for (int c = lane; c < chunks; c += 32) {
+    uint4 w[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i)
+      w[i] = (row0 + i < n_rows) ? ldg_stream(W + (size_t)(row0 + i) * in_dim + (size_t)c * 16)
+                                 : make_uint4(0, 0, 0, 0);
+    const uint4 x = xv[c];
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = dot16_i8(w[i], x, acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = warp_sum_i(acc[i]);
+}
+
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads) k_embed(Dims d, const int8_t* __restrict__ emb,
+                                                    const float* __restrict__ emb_s, DecodeBufs b) {
+  const uint32_t tok = b.st->token;
+  const float s = emb_s[tok];
+  const int8_t* row = emb + (size_t)tok * d.dim;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.dim; i += gridDim.x * blockDim.x)
+    b.x[i] = __fmul_rn((float)row[i], s);  // engine.rs:207-209
+  if (blockIdx.x == 0 && threadIdx.x == 0) b.st->argmax_key = 0ull;
+}
+
+constexpr int kQkvRows = 2;  // rows per warp: one RoPE pair
+
+__global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* xb = reinterpret_cast<float*>(smem);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + d.dim * 4);
+  __shared__ float red[40];
+  rmsnorm_smem(b.x, L.rms_attn, d.dim, xb, red);
+  const float xs = quantize_smem(xb, d.dim, xq, red);
+
+  const int warp = threadIdx.x >> 5;
+  const int r0 = (blockIdx.x * kWarps + warp) * kQkvRows;
+  const int n_rows = 3 * d.dim;
+  if (r0 >= n_rows) return;
+  int acc[kQkvRows];
+  rows_dot_i8<kQkvRows>(L.qkv, d.dim, r0, n_rows, xq, acc);
+  if ((threadIdx.x & 31) != 0) return;
+  float v0 = __fmul_rn(__fmul_rn((float)acc[0], L.qkv_s[r0]), xs);
+  float v1 = __fmul_rn(__fmul_rn((float)acc[1], L.qkv_s[r0 + 1]), xs);
+  const int sec = r0 / d.dim, rr = r0 - sec * d.dim;
+  const uint32_t pos = b.st->pos;
+  if (sec < 2) {  // RoPE on the interleaved pair (engine.rs:252-271)
+    const int half = d.head_dim >> 1;
+    const int i = (rr % d.head_dim) >> 1;
+    const float c = b.rope_cos[pos * half + i], s = b.rope_sin[pos * half + i];
+    const float a = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+    const float e = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
+    v0 = a;
+    v1 = e;
+  }
+  if (sec == 0) {
+    b.q[rr] = v0;
+    b.q[rr + 1] = v1;
+  } else {
+    float* cache = (sec == 1) ? b.kc : b.vc;  // engine.rs:274-280
+    const size_t off = ((size_t)layer * d.max_seq + pos) * d.dim + rr;
+    cache[off] = v0;
+    cache[off + 1] = v1;
+  }
+}
+
+constexpr int kORows = 2;
+
+__global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, DecodeBufs b) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* a = reinterpret_cast<float*>(smem);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + d.dim * 4);
+  __shared__ float red[40];
+  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) a[i] = b.att_out[i];
+  __syncthreads();
+  const float xs = quantize_smem(a, d.dim, xq, red);
+  const int warp = threadIdx.x >> 5;
+  const int r0 = (blockIdx.x * kWarps + warp) * kORows;
+  if (r0 >= d.dim) return;
+  int acc[kORows];
+  rows_dot_i8<kORows>(L.o, d.dim, r0, d.dim, xq, acc);
+  const int lane = threadIdx.x & 31;
+  if (lane < kORows && r0 + lane < d.dim) {
+    const int r = r0 + lane;
+    int dot = acc[0];
+#pragma unroll
+    for (int i = 1; i < kORows; ++i) dot = (lane == i) ? acc[i] : dot;
+    const float v = __fmul_rn(__fmul_rn((float)dot, L.o_s[r]), xs);
+    b.x[r] = __fadd_rn(b.x[r], v);  // residual (engine.rs:320-322)
+  }
+}
+
+constexpr int kLmRows = 4;
+
+__global__ void __launch_bounds__(kThreads) k_lmhead(Dims d, const float* __restrict__ norm_w,
+                                                     const int8_t* __restrict__ W,
+                                                     const float* __restrict__ ws, DecodeBufs b) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* xb = reinterpret_cast<float*>(smem);
+  int8_t* xq = reinterpret_cast<int8_t*>(smem + d.dim * 4);
+  __shared__ float red[40];
+  __shared__ unsigned long long best_w[kWarps];
+  rmsnorm_smem(b.x, norm_w, d.dim, xb, red);
+  const float xs = quantize_smem(xb, d.dim, xq, red);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  unsigned long long best = 0ull;
+  const int step = gridDim.x * kWarps * kLmRows;
+  for (int r0 = (blockIdx.x * kWarps + warp) * kLmRows; r0 < d.vocab; r0 += step) {
+    int acc[kLmRows];
+    rows_dot_i8<kLmRows>(W, d.dim, r0, d.vocab, xq, acc);
+#pragma unroll
+    for (int i = 0; i < kLmRows; ++i) {
+      const int r = r0 + i;
+      if (lane == i && r < d.vocab) {
+        const float v = __fmul_rn(__fmul_rn((float)acc[i], ws[r]), xs);
+        b.logits[r] = v;
+        const unsigned long long key = ((unsigned long long)ordered_key(v) << 32) | (unsigned)r;
+        best = key > best ? key : best;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if (lane == 0) best_w[warp] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long m = 0ull;
+    for (int i = 0; i < kWarps; ++i) m = best_w[i] > m ? best_w[i] : m;
+    atomicMax(&b.st->argmax_key, m);
+  }
+}
+
+// Records the forward's argmax and picks the next token (engine.rs:509-545):
+// during prefill the next prompt token clamped to vocab-1, then the argmax.
+__global__ void k_advance(Dims d, DecodeBufs b) {
+  StepState* st = b.st;
+  const uint32_t idx = (uint32_t)(st->argmax_key & 0xffffffffull);
+  const uint32_t step = st->step;
+  b.out_tokens[step] = idx;
+  const uint32_t next_pos = st->pos + 1;
+  uint32_t next = idx;
+  if (next_pos < st->n_prefill) next = min(b.prompt[next_pos], (uint32_t)(d.vocab - 1));
+  st->pos = next_pos;
+  st->token = next;
+  st->step = step + 1;
+}
+
+// apply_repetition_penalty (src/tensor/sampling.rs:168-178) over hist[0..n),
+// sequentially so that repeated tokens are penalised repeatedly.
+__global__ void k_penalty(Dims d, DecodeBufs b, const uint32_t* __restrict__ hist, int n,
+                          float p) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < n; ++i) {
+      const uint32_t t = hist[i];
+      if (t < (uint32_t)d.vocab) {
+        const float v = b.logits[t];
+        b.logits[t] = (v > 0.0f) ? __fdiv_rn(v, p) : __fmul_rn(v, p);
+      }
+    }
+    b.st->argmax_key = 0ull;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_argmax(const float* __restrict__ v, int n,
+                                                     unsigned long long* key_out) {
+  __shared__ unsigned long long best_w[kWarps];
+  unsigned long long best = 0ull;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const unsigned long long k = ((unsigned long long)ordered_key(v[i]) << 32) | (unsigned)i;
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) best_w[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long m = 0ull;
+    for (int i = 0; i < kWarps; ++i) m = best_w[i] > m ? best_w[i] : m;
+    atomicMax(key_out, m);
+  }
+}
+
+// ---- operator: matmul_int8 over caller-owned device memory ---------------------
+// Each CTA quantizes x into shared memory itself (the quantization depends only
+// on x), then streams rows. Rows with in_dim % 16 != 0 or unaligned weights
+// take a byte-wise path with the same exact int32 result.
+__global__ void __launch_bounds__(kThreads) k_matmul_i8_op(float* __restrict__ out,
+                                                           const int8_t* __restrict__ W,
+                                                           const float* __restrict__ ws,
+                                                           const float* __restrict__ x,
+                                                           int out_dim, int in_dim, int vec) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  int8_t* xq = reinterpret_cast<int8_t*>(smem);
+  __shared__ float red[40];
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < in_dim; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+  m = block_max(m, red);
+  float xs, inv;
+  quant_scale(m, &xs, &inv);
+  for (int i = threadIdx.x; i < in_dim; i += blockDim.x) xq[i] = quant_any(x[i], inv, i, in_dim);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int step = gridDim.x * kWarps * 2;
+  for (int r0 = (blockIdx.x * kWarps + warp) * 2; r0 < out_dim; r0 += step) {
+    int acc[2];
+    if (vec) {
+      rows_dot_i8<2>(W, in_dim, r0, out_dim, xq, acc);
+    } else {
+      for (int i = 0; i < 2; ++i) {
+        int a = 0;
+        if (r0 + i < out_dim)
+          for (int k = lane; k < in_dim; k += 32) a += (int)W[(size_t)(r0 + i) * in_dim + k] * (int)xq[k];
+        acc[i] = warp_sum_i(a);
+      }
+    }
+    if (lane < 2 && r0 + lane < out_dim) {
+      const int r = r0 + lane;
+      out[r] = __fmul_rn(__fmul_rn((float)(lane ? acc[1] : acc[0]), ws[r]), xs);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_quantize_op(int8_t* __restrict__ q, float* scale,
+                                                          const float* __restrict__ x, int n) {
+  __shared__ float red[40];
+  const float* v = x + (size_t)blockIdx.x * n;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(v[i]));
+  m = block_max(m, red);
+  float s, inv;
+  quant_scale(m, &s, &inv);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) q[(size_t)blockIdx.x * n + i] = quant_any(v[i], inv, i, n);
+  if (threadIdx.x == 0) scale[blockIdx.x] = s;
+}
+
+size_t dense_smem(const Dims& d) { return (size_t)d.dim * 4 + (((size_t)d.dim + 15) & ~size_t(15)); }
+
+}  // namespace
+
+void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const DecodeBufs& b,
+                  cudaStream_t s) {
+  k_embed<<<std::max(1, (d.dim + kThreads - 1) / kThreads), kThreads, 0, s>>>(d, emb, emb_s, b);
+}
+
+void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s) {
+  const int rows_per_block = kWarps * kQkvRows;
+  const int grid = (3 * d.dim + rows_per_block - 1) / rows_per_block;
+  k_qkv<<<grid, kThreads, dense_smem(d), s>>>(d, L, layer, b);
+}
+
+void launch_oproj(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s) {
+  const int rows_per_block = kWarps * kORows;
+  k_oproj<<<(d.dim + rows_per_block - 1) / rows_per_block, kThreads, dense_smem(d), s>>>(d, L, b);
+}
+
+void launch_lmhead(const Dims& d, const float* final_norm, const int8_t* w, const float* ws,
+                   const DecodeBufs& b, int num_sms, cudaStream_t s) {
+  const int rows_per_block = kWarps * kLmRows;
+  const int grid = std::min((d.vocab + rows_per_block - 1) / rows_per_block, num_sms * 4);
+  k_lmhead<<<grid, kThreads, dense_smem(d), s>>>(d, final_norm, w, ws, b);
+}
+
+void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s) {
+  k_advance<<<1, 1, 0, s>>>(d, b);
+}
+
+void launch_penalty_argmax(const Dims& d, const DecodeBufs& b, const uint32_t* hist, int n_hist,
+                           float penalty, cudaStream_t s) {
+  k_penalty<<<1, 32, 0, s>>>(d, b, hist, n_hist, penalty);
+  k_argmax<<<std::min(148, (d.vocab + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+      b.logits, d.vocab, &b.st->argmax_key);
+}
+
+cudaError_t op_matmul_i8(float* out, const int8_t* w, const float* ws, const float* x,
+                         size_t out_dim, size_t in_dim, int num_sms, cudaStream_t s) {
+  const int vec = (in_dim % 16 == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);
+  const size_t smem = (in_dim + 15) & ~size_t(15);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(k_matmul_i8_op, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int rows_per_block = kWarps * 2;
+  const int grid = (int)std::min<size_t>((out_dim + rows_per_block - 1) / rows_per_block,
+                                         (size_t)num_sms * 4);
+  k_matmul_i8_op<<<std::max(grid, 1), kThreads, smem, s>>>(out, w, ws, x, (int)out_dim,
+                                                            (int)in_dim, vec);
+  return cudaGetLastError();
+}
+
+cudaError_t op_quantize_i8(int8_t* q, float* scale, const float* x, size_t n_vec, size_t n,
+                           cudaStream_t s) {
+  k_quantize_op<<<(unsigned)n_vec, kThreads, 0, s>>>(q, scale, x, (int)n);
+  return cudaGetLastError();
+}
+
+}  // namespace chalot

@@ -1,0 +1,123 @@
+"""Engine: the reference's inference API over the B200 library.
+
+Mirrors ``Engine`` in src/model/engine.rs: ``Engine.load(path)`` (:94),
+``forward(token, pos) -> int`` (:173), ``generate(tokens, max_new, sampling)``
+(:497), ``sample_from_logits(sampling, history)`` (:551) and the public
+``state.logits`` (state.rs:20), exposed here as ``logits()``. Errors the
+reference reports as ``Err(String)`` or panics on raise ``ChalotError``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from typing import Sequence
+
+import numpy as np
+
+from ._capi import ModelConfig, Opts, Sampling, check, lib
+
+GREEDY, TOP_K, TOP_P, MIN_P = 0, 1, 2, 3
+
+
+@dataclass
+class SamplingConfig:
+    """SamplingConfig (src/model/engine.rs:37-62). Only GREEDY is sampled here;
+    the reference's default (TopP, penalty 1.15) is not, so the default below
+    is greedy without a penalty."""
+    strategy: int = GREEDY
+    temperature: float = 0.7
+    top_k: int = 40
+    top_p: float = 0.9
+    min_p: float = 0.05
+    repetition_penalty: float = 1.0
+    repetition_window: int = 64
+    stop_tokens: Sequence[int] = field(default_factory=list)
+
+    def _c(self):
+        stops = (C.c_uint32 * max(1, len(self.stop_tokens)))(*self.stop_tokens)
+        s = Sampling(self.strategy, self.temperature, self.top_k, self.top_p, self.min_p,
+                     self.repetition_penalty, self.repetition_window,
+                     C.cast(stops, C.POINTER(C.c_uint32)), len(self.stop_tokens))
+        return s, stops
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
+
+
+class Engine:
+    def __init__(self, handle: C.c_void_p):
+        self._h = handle
+        cfg = ModelConfig()
+        check(lib().chalot_get_config(self._h, C.byref(cfg)))
+        self.config = cfg.as_dict()
+
+    @classmethod
+    def load(cls, path: str, device: int = 0, use_cuda_graph: bool = True) -> "Engine":
+        h = C.c_void_p()
+        opts = Opts(device, int(use_cuda_graph))
+        check(lib().chalot_load(path.encode(), C.byref(opts), C.byref(h)))
+        return cls(h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().chalot_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def forward(self, token: int, pos: int) -> int:
+        out = C.c_uint32()
+        check(lib().chalot_forward(self._h, int(token), int(pos), C.byref(out)))
+        return int(out.value)
+
+    def logits(self) -> np.ndarray:
+        v = np.empty(self.config["vocab_size"], np.float32)
+        check(lib().chalot_get_logits(self._h, v.ctypes.data_as(C.c_void_p), v.size))
+        return v
+
+    def generate(self, tokens: Sequence[int], max_new: int,
+                 sampling: SamplingConfig | None = None) -> list[int]:
+        p = _u32(list(tokens) or [0])
+        out = np.zeros(max(1, max_new), np.uint32)
+        n = C.c_size_t()
+        sp = None
+        keep = None
+        if sampling is not None:
+            sp, keep = sampling._c()
+        check(lib().chalot_generate(self._h, p.ctypes.data_as(C.c_void_p), len(tokens), max_new,
+                                    C.byref(sp) if sp is not None else None,
+                                    out.ctypes.data_as(C.c_void_p), C.byref(n)))
+        del keep
+        return out[: n.value].tolist()
+
+    def sample_from_logits(self, sampling: SamplingConfig | None, history: Sequence[int]) -> int:
+        h = _u32(list(history) or [0])
+        tok = C.c_uint32()
+        sp, keep = (sampling or SamplingConfig())._c()
+        check(lib().chalot_sample_from_logits(self._h, C.byref(sp), h.ctypes.data_as(C.c_void_p),
+                                              len(history), C.byref(tok)))
+        del keep
+        return int(tok.value)
+
+    def last_timing(self) -> dict:
+        a, b = C.c_double(), C.c_double()
+        n1, n2 = C.c_uint32(), C.c_uint32()
+        check(lib().chalot_last_timing(self._h, C.byref(a), C.byref(b), C.byref(n1), C.byref(n2)))
+        return {"prefill_ms": a.value, "decode_ms": b.value, "n_prefill": n1.value,
+                "n_decode": n2.value}
+
+    def bench_moe_layers(self, reps: int = 20) -> tuple[float, float]:
+        ms, by = C.c_double(), C.c_double()
+        check(lib().chalot_bench_moe_layers(self._h, reps, C.byref(ms), C.byref(by)))
+        return ms.value, by.value

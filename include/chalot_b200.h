@@ -1,0 +1,174 @@
+/* chalot_b200.h — C ABI of the B200 (sm_100a) implementation of chalot_C1's
+ * sparse-MoE decode hot path.
+ *
+ * Every entry point returns an int status (CHALOT_OK or a negative code); the
+ * message of the last failure on the calling thread is chalot_last_error().
+ * Nothing aborts the process. Engine handles are single-threaded, as the
+ * reference's `&mut self` Engine is.
+ *
+ * Reference interfaces replaced (paths within chalot28/chalot_C1):
+ *   Engine::load             src/model/engine.rs:94
+ *   Engine::forward          src/model/engine.rs:173
+ *   Engine::generate         src/model/engine.rs:497
+ *   Engine::sample_from_logits src/model/engine.rs:551
+ *   InferenceState::logits   src/model/state.rs:20
+ *   matmul_int8              src/tensor/matmul.rs:47
+ *   matmul_int4              src/tensor/matmul.rs:363
+ *   quantize_f32_to_i8       src/tensor/quantization.rs:26
+ *   softmax_top_k (router)   src/tensor/normalization.rs:203, engine.rs:334-344
+ *   PagedKVCache             src/model/memory.rs:100-201
+ */
+#ifndef CHALOT_B200_H
+#define CHALOT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CHALOT_OK 0
+#define CHALOT_ERR_ARG (-1)     /* bad argument or unsupported shape */
+#define CHALOT_ERR_IO (-2)      /* file open/read/write failed */
+#define CHALOT_ERR_FORMAT (-3)  /* bad magic/version/size in a .myai file */
+#define CHALOT_ERR_OOM (-4)     /* device or host allocation failed */
+#define CHALOT_ERR_CUDA (-5)    /* a CUDA runtime call failed */
+#define CHALOT_ERR_NCCL (-6)    /* an NCCL call failed */
+#define CHALOT_ERR_TIMEOUT (-7) /* a bounded wait ran out */
+#define CHALOT_ERR_STATE (-8)   /* call not valid in the handle's state */
+
+/* ---- library ---------------------------------------------------------- */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* chalot_last_error(void);
+/* ABI version: major*10000 + minor*100 + patch. */
+int chalot_abi_version(void);
+
+/* ---- .myai writer (host only) ----------------------------------------- */
+
+/* Shape and seed of a synthetic model. Weights are N(0, weight_std) and are
+ * quantized as the reference's quantizers do (int8 per-tensor absmax for
+ * embeddings/attention/lm_head, int4 per-row-per-group absmax/7 for experts). */
+typedef struct chalot_synth_spec {
+  uint32_t dim, hidden_dim, n_layers, n_heads, vocab_size;
+  uint32_t n_experts, top_k, int4_group_size, max_seq_len;
+  uint32_t rope_theta_x100; /* header field: theta*100, 0 = 10000 */
+  float weight_std;         /* 0 selects 0.02 */
+  uint64_t seed;
+  int n_threads; /* <= 0: all hardware threads; the output does not depend on it */
+} chalot_synth_spec;
+
+/* Writes a .myai v2 file. No counterpart in the reference's Rust API; its
+ * layout is the one src/model/dummy.rs:17 and qwen_to_myai.py write. */
+int chalot_myai_write_synthetic(const char* path, const chalot_synth_spec* spec);
+
+/* Header-derived configuration of a .myai file (src/model/config.rs:40-69). */
+typedef struct chalot_model_config {
+  uint32_t dim, hidden_dim, n_layers, n_heads, head_dim, vocab_size, max_seq_len;
+  uint32_t n_experts, top_k, int4_group_size, depth_router_layer;
+  float rope_theta;
+  uint64_t total_bytes;        /* WeightIndex::total_bytes */
+  uint64_t expert_bytes;       /* bytes of one expert (gate+up+down, with scales) */
+} chalot_model_config;
+
+/* Parses the header of a file and computes its size (host only). */
+int chalot_myai_inspect(const char* path, chalot_model_config* out);
+
+/* ---- engine ----------------------------------------------------------- */
+
+typedef struct chalot_engine chalot_engine;
+
+typedef struct chalot_opts {
+  int device;          /* CUDA device ordinal */
+  int use_cuda_graph;  /* 1: replay one captured graph per forward (default) */
+} chalot_opts;
+
+typedef enum chalot_strategy {
+  CHALOT_GREEDY = 0, /* the only strategy this build samples with */
+  CHALOT_TOP_K = 1,
+  CHALOT_TOP_P = 2,
+  CHALOT_MIN_P = 3
+} chalot_strategy;
+
+/* Mirrors SamplingConfig (src/model/engine.rs:37-62). */
+typedef struct chalot_sampling {
+  int strategy;
+  float temperature;
+  uint32_t top_k;
+  float top_p;
+  float min_p;
+  float repetition_penalty; /* applied when > 1 (engine.rs:555) */
+  uint32_t repetition_window;
+  const uint32_t* stop_tokens;
+  uint32_t n_stop_tokens;
+} chalot_sampling;
+
+/* Engine::load: parse the header, upload the weights to the device, build
+ * the RoPE tables and the KV cache. `opts` may be NULL. */
+int chalot_load(const char* path, const chalot_opts* opts, chalot_engine** out);
+void chalot_free(chalot_engine* e);
+int chalot_get_config(const chalot_engine* e, chalot_model_config* out);
+
+/* Engine::forward: one token at position `pos`; writes the argmax token.
+ * The logits stay on the device until chalot_get_logits. */
+int chalot_forward(chalot_engine* e, uint32_t token, uint32_t pos, uint32_t* out_token);
+
+/* Engine::generate: prefill `prompt` token by token, then decode up to
+ * `max_new` tokens. `out` must hold `max_new` entries; *n_out receives the
+ * count written. `sampling` NULL means greedy with no repetition penalty. */
+int chalot_generate(chalot_engine* e, const uint32_t* prompt, size_t n_prompt,
+                    size_t max_new, const chalot_sampling* sampling,
+                    uint32_t* out, size_t* n_out);
+
+/* Engine::sample_from_logits over the logits of the last forward, with the
+ * repetition penalty applied to `history` (the last repetition_window ids). */
+int chalot_sample_from_logits(chalot_engine* e, const chalot_sampling* sampling,
+                              const uint32_t* history, size_t n_history,
+                              uint32_t* out_token);
+
+/* Copies the logits of the last forward (state.logits) to host memory. */
+int chalot_get_logits(chalot_engine* e, float* dst, size_t n);
+
+/* Device time of the prefill and decode phases of the last chalot_generate,
+ * measured with CUDA events on the engine's stream, and the forward counts. */
+int chalot_last_timing(chalot_engine* e, double* prefill_ms, double* decode_ms,
+                       uint32_t* n_prefill, uint32_t* n_decode);
+
+/* Expert path of every layer at batch 1 (gate/up + down of top_k experts,
+ * expert ids chosen round-robin per layer so successive layers stream
+ * different weights), captured once and replayed `reps` times: mean device
+ * time per layer and the weight bytes one layer streams. */
+int chalot_bench_moe_layers(chalot_engine* e, int reps, double* ms_per_layer,
+                            double* bytes_per_layer);
+
+/* ---- operators (device pointers, caller-owned memory) ------------------- */
+/* `stream` is a cudaStream_t (NULL = the legacy default stream). The input
+ * vector is quantized on the device exactly as quantize_f32_to_i8 does. */
+
+/* matmul_int8: out[r] = ((float)dot_i32(w[r,:], q(x)) * w_scales[r]) * x_scale. */
+int chalot_matmul_i8(float* out, const int8_t* w, const float* w_scales, const float* x,
+                     size_t out_dim, size_t in_dim, void* stream);
+
+/* matmul_int4: per row, t += ((float)gdot_g * s[r,g]) * x_scale in group order;
+ * w_packed is [out_dim][ceil(in_dim/2)] (low nibble = even column, value-8),
+ * w_scales is [out_dim][ceil(in_dim/group)]. group 0 selects 64. */
+int chalot_matmul_i4(float* out, const uint8_t* w_packed, const float* w_scales,
+                     const float* x, size_t out_dim, size_t in_dim, size_t group,
+                     void* stream);
+
+/* quantize_f32_to_i8 for n_vec vectors of length n: q[v,:] and scale[v]. */
+int chalot_quantize_i8(int8_t* q, float* scale, const float* x, size_t n_vec, size_t n,
+                       void* stream);
+
+/* Router of one MoE layer for n_tok tokens (engine.rs:334-344):
+ * logits[t,e] = b[e] + dot_f32(w[e,:], x[t,:]); softmax_top_k(logits[t], k).
+ * Writes idx[t,k] (int32) and weight[t,k] (f32), in descending weight order. */
+int chalot_router_topk(int32_t* idx, float* weight, const float* x, const float* w,
+                       const float* b, size_t n_tok, size_t dim, size_t n_experts,
+                       size_t top_k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CHALOT_B200_H */
