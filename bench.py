@@ -270,13 +270,33 @@ def run_ours(args, ws, rank, local):
     eng.close()
 
 
+def run_profile(args):
+    """A short decode for profilers: 32 prompt tokens + 8 new tokens on the
+    Qwen-shaped model (40 forwards, 171 kernel launches each), run twice; the
+    second run is the one to capture (skip the first 6840 launches)."""
+    import numpy as np
+
+    import chalot_c1_b200 as cb
+    path = prepare_model(1, 0)
+    eng = cb.Engine.load(path)
+    prompt = np.random.default_rng(1).integers(0, eng.config["vocab_size"], 32).tolist()
+    for _ in range(2):
+        toks = eng.generate(prompt, 8)
+    print(json.dumps({"profile_tokens": toks}))
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="bench", choices=["bench", "profile"])
     a = ap.parse_args()
+    if a.mode == "profile":
+        run_profile(a)
+        return
     ws, rank, local = dist_setup()
     try:
         if a.impl == "reference":

@@ -78,7 +78,7 @@ __device__ __forceinline__ void softmax_serial(float* s, int n) {
   }
   float sum = hsum8(lanes);
   for (int i = full; i < n; ++i) {
-    const float e = expf(__fsub_rn(s[i], mx));
+    const float e = expf_cr(__fsub_rn(s[i], mx));
     s[i] = e;
     sum = __fadd_rn(sum, e);
   }

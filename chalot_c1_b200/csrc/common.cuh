@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "libm_f32.h"
+
 namespace chalot {
 
 #define CHALOT_DEV __device__ __forceinline__
@@ -54,11 +56,16 @@ CHALOT_DEV float hsum8(const float s[8]) {
   return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
 }
 
+// libm expf as the reference gets it from glibc: evaluated in double and
+// rounded once, i.e. the correctly rounded value, which glibc's expf returns
+// for all but ~0.07% of arguments (where it is 1 ulp away).
+CHALOT_DEV float expf_cr(float x) { return (float)exp((double)x); }
+
 // SwiGLU of one element at index i of a vector of length n: the first
 // floor(n/8)*8 elements use fast_exp, the tail uses libm exp
 // (src/tensor/activations.rs:59-87).
 CHALOT_DEV float swiglu_elem(float g, float u, size_t i, size_t n) {
-  float e = (i < (n & ~size_t(7))) ? fast_exp(__fsub_rn(0.0f, g)) : expf(-g);
+  float e = (i < (n & ~size_t(7))) ? fast_exp(__fsub_rn(0.0f, g)) : expf_cr(-g);
   float silu = __fdiv_rn(g, __fadd_rn(1.0f, e));
   return __fmul_rn(silu, u);
 }

@@ -202,7 +202,7 @@ bool check_shapes(const ModelConfig& c, std::string* err) {
   if (c.int4_group_size % 32) return bad("int4_group_size must be a multiple of 32");
   if (c.dim % c.int4_group_size || c.hidden_dim % c.int4_group_size)
     return bad("dim and hidden_dim must be multiples of int4_group_size");
-  if (c.head_dim % 4 || c.head_dim > 256) return bad("head_dim must be a multiple of 4 and <= 256");
+  if (c.head_dim % 8 || c.head_dim > 256) return bad("head_dim must be a multiple of 8 and <= 256");
   if (c.n_experts > 64) return bad("more than 64 experts");
   if (c.top_k > 8) return bad("top_k above 8");
   if (c.vocab_size >= (1u << 31)) return bad("vocab too large");

@@ -5,10 +5,15 @@
 //                  for t <= pos; one thread per (head, t), the dot in the
 //                  two-accumulator 8-lane order of dot_f32_avx2
 //                  (src/tensor/attention_helpers.rs:41-80) and the cap of
-//                  logit_soft_cap (src/tensor/activations.rs:133-135).
+//                  logit_soft_cap (src/tensor/activations.rs:133-135) with the
+//                  host libm's tanhf restated in libm_f32.h.
 //   k_attn_pv      softmax_avx2 over s[h][0..pos] (normalization.rs:106-160),
 //                  then out[d] = sum_t p_t * V[t][d] added in t order
-//                  (engine.rs:302-308); one thread per output column.
+//                  (engine.rs:302-308). The add chain of a column is serial by
+//                  definition, so each CTA owns 8 columns of one head: its 256
+//                  threads stage V[0..pos][8 columns] in shared memory with
+//                  wide loads (spreading the KV read over heads*hd/8 CTAs) and
+//                  8 threads then run the chains out of shared memory.
 // The cache layout is the reference's: [layer][max_seq][dim], head h at
 // columns h*hd .. h*hd+hd-1.
 #include <cuda_runtime.h>
@@ -57,59 +62,69 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer
   for (int i = extra ? rem + 8 : rem; i < hd; ++i) dot = __fadd_rn(dot, __fmul_rn(qh[i], k[i]));
   const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   const float x = __fmul_rn(dot, inv_sqrt);
-  b.scores[(size_t)h * d.max_seq + t] = __fmul_rn(30.0f, tanhf(__fdiv_rn(x, 30.0f)));
+  b.scores[(size_t)h * d.max_seq + t] = __fmul_rn(30.0f, libm::tanh_f32(__fdiv_rn(x, 30.0f)));
 }
 
-constexpr int kPvThreads = 32;
+constexpr int kPvThreads = 256;
+constexpr int kPvCols = 8;     // output columns per CTA: V loads spread over heads*hd/8 CTAs
+constexpr int kPvTile = 1024;  // V rows staged in shared memory at a time
 
 __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, DecodeBufs b) {
-  extern __shared__ __align__(16) float p[];  // [max_seq]
-  __shared__ float lanes[8];
+  extern __shared__ __align__(16) float sm[];
+  float* p = sm;                      // [max_seq] probabilities
+  float* vt = sm + ((d.max_seq + 3) & ~3);  // [kPvTile][kPvCols] staged V (16-B aligned)
+  __shared__ float red[40];
   __shared__ float inv_s;
-  const int h = blockIdx.x, hd = d.head_dim, col = blockIdx.y * 32 + threadIdx.x;
+  const int h = blockIdx.x, hd = d.head_dim, c0 = blockIdx.y * kPvCols;
   const int n = (int)b.st->pos + 1;
   const float* s = b.scores + (size_t)h * d.max_seq;
+  // softmax_avx2 over the n scores of this head (normalization.rs:106-160)
   float mx = -INFINITY;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float v = s[i];
     p[i] = v;
     mx = fmaxf(mx, v);
   }
-  mx = warp_max(mx);
+  mx = block_max(mx, red);
   const int full = n & ~7;
   for (int i = threadIdx.x; i < n; i += blockDim.x)
-    p[i] = (i < full) ? fast_exp(__fsub_rn(p[i], mx)) : expf(__fsub_rn(p[i], mx));
-  __syncwarp();
-  if (threadIdx.x < 8) {
+    p[i] = (i < full) ? fast_exp(__fsub_rn(p[i], mx)) : expf_cr(__fsub_rn(p[i], mx));
+  __syncthreads();
+  if (threadIdx.x < 8) {  // lane j sums elements 8c+j in c order
     float acc = 0.0f;
     for (int c = 0; c < (full >> 3); ++c) acc = __fadd_rn(acc, p[c * 8 + threadIdx.x]);
-    lanes[threadIdx.x] = acc;
+    red[threadIdx.x] = acc;
   }
-  __syncwarp();
+  __syncthreads();
   if (threadIdx.x == 0) {
     float l8[8];
-    for (int j = 0; j < 8; ++j) l8[j] = lanes[j];
+    for (int j = 0; j < 8; ++j) l8[j] = red[j];
     float sum = hsum8(l8);
     for (int i = full; i < n; ++i) sum = __fadd_rn(sum, p[i]);
     inv_s = __fdiv_rn(1.0f, sum);
   }
-  __syncwarp();
+  __syncthreads();
   const float inv = inv_s;
   for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
-  __syncwarp();
-  if (col >= hd) return;
-  const float* v = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + col;
+  // out[c] = sum_t p_t * V[t][c], added in t order; V staged tile by tile
+  const float* vbase = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + c0;
   float acc = 0.0f;
-  int t = 0;
-  for (; t + 8 <= n; t += 8) {
-    float vv[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) vv[u] = v[(size_t)(t + u) * d.dim];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(p[t + u], vv[u]));
+  for (int t0 = 0; t0 < n; t0 += kPvTile) {
+    const int rows = min(kPvTile, n - t0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * (kPvCols / 4); i += blockDim.x) {
+      const int r = i / (kPvCols / 4), q = i % (kPvCols / 4);
+      reinterpret_cast<float4*>(vt)[i] =
+          *reinterpret_cast<const float4*>(vbase + (size_t)(t0 + r) * d.dim + q * 4);
+    }
+    __syncthreads();
+    if (threadIdx.x < kPvCols) {
+      const float* pv = p + t0;
+#pragma unroll 8
+      for (int t = 0; t < rows; ++t) acc = __fadd_rn(acc, __fmul_rn(pv[t], vt[t * kPvCols + threadIdx.x]));
+    }
   }
-  for (; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[(size_t)t * d.dim]));
-  b.att_out[h * hd + col] = acc;
+  if (threadIdx.x < kPvCols) b.att_out[h * hd + c0 + threadIdx.x] = acc;
 }
 
 }  // namespace
@@ -117,8 +132,8 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
 void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s) {
   dim3 g1((d.max_seq + kScoreThreads - 1) / kScoreThreads, d.n_heads);
   k_attn_scores<<<g1, kScoreThreads, 0, s>>>(d, layer, b);
-  dim3 g2(d.n_heads, (d.head_dim + 31) / 32);
-  const size_t smem = (size_t)d.max_seq * 4;
+  dim3 g2(d.n_heads, d.head_dim / kPvCols);
+  const size_t smem = ((((size_t)d.max_seq + 3) & ~size_t(3)) + (size_t)kPvTile * kPvCols) * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   k_attn_pv<<<g2, kPvThreads, smem, s>>>(d, layer, b);
 }

@@ -27,61 +27,68 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// Quantizes v[0..n) (n % 32 == 0) into the permuted int4-friendly layout and
-// stores the sum of every 32-column chunk (for the nibble offset of 8).
-__device__ __forceinline__ float quantize_perm(const float* v, int n, int8_t* xp, int* csum,
-                                               float* red, float amax_known, bool have_amax) {
-  float scale, inv;
-  quant_scale(have_amax ? amax_known : absmax_smem(v, n, red), &scale, &inv);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xp[perm32(i)] = quant_any(v[i], inv, i, n);
-  __syncthreads();
-  for (int c = threadIdx.x; c < (n >> 5); c += blockDim.x) {
-    const int8_t* p = xp + c * 32;
-    int s = 0;
-    for (int i = 0; i < 32; ++i) s += p[i];
-    csum[c] = s;
-  }
-  __syncthreads();
-  return scale;
-}
+// One row of a batched int4 GEMV: its packed weights, its group scales and
+// which quantized input vector (index into xp/csum/xs) it is dotted with.
+struct RowJob {
+  const uint8_t* w;
+  const float* s;
+  int x;
+};
 
-// Group products p_g = ((float)gdot_g * s_g) * xs of `nrows` rows into
-// P[row][g] (row stride ps). Rows are [row_ptr(i), scale_ptr(i)] pairs.
-// in_dim % 32 == 0, group % 32 == 0. Warp w handles rows w, w+8, ...
-template <int R>
-__device__ __forceinline__ void group_products(const uint8_t* const* rows, const float* const* scales,
-                                               int nrows, int in_dim, int group, const int8_t* xp,
-                                               const int* csum, float xs, float* P, int ps) {
+// Group products p_g = ((float)gdot_g * s_g) * xs of rows[0..nrows) into
+// P[row][g] (row stride ps); in_dim % 32 == 0, group % 32 == 0. Warp w takes
+// rows w*R.. (R at a time) and loads IT 32-lane strides of each row before
+// computing, so R*IT 16-byte loads per lane are in flight.
+template <int R, int IT>
+__device__ __forceinline__ void group_products(const RowJob* rows, int nrows, int in_dim, int group,
+                                               const int8_t* xp, const int* csum, const float* xs,
+                                               float* P, int ps) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunks = in_dim >> 5, cpg = group >> 5;
-  const uint4* xv = reinterpret_cast<const uint4*>(xp);
   for (int r0 = warp * R; r0 < nrows; r0 += kWarps * R) {
-    for (int c0 = 0; c0 < chunks; c0 += 32) {
-      const int c = c0 + lane;
-      uint4 w[R];
+    for (int cb = 0; cb < chunks; cb += 32 * IT) {
+      uint4 w[R][IT];
 #pragma unroll
       for (int i = 0; i < R; ++i)
-        w[i] = (c < chunks && r0 + i < nrows) ? ldg_stream(rows[r0 + i] + (size_t)c * 16)
-                                              : make_uint4(0, 0, 0, 0);
-      int d[R];
-      const uint4 xe = (c < chunks) ? xv[2 * c] : make_uint4(0, 0, 0, 0);
-      const uint4 xo = (c < chunks) ? xv[2 * c + 1] : make_uint4(0, 0, 0, 0);
-      const int off8 = (c < chunks) ? 8 * csum[c] : 0;
 #pragma unroll
-      for (int i = 0; i < R; ++i) d[i] = dot32_u4(w[i], xe, xo, 0) - off8;
-      // chunks of one group sit in consecutive lanes: reduce them exactly
-      for (int o = 1; o < cpg; o <<= 1)
+        for (int it = 0; it < IT; ++it) {
+          const int c = cb + it * 32 + lane;
+          w[i][it] = (c < chunks && r0 + i < nrows) ? ldg_stream(rows[r0 + i].w + (size_t)c * 16)
+                                                    : make_uint4(0, 0, 0, 0);
+        }
 #pragma unroll
-        for (int i = 0; i < R; ++i) d[i] += __shfl_xor_sync(0xffffffffu, d[i], o);
-      if (c < chunks && (c % cpg) == 0) {
-        const int g = c / cpg;
+      for (int it = 0; it < IT; ++it) {
+        const int c = cb + it * 32 + lane;
+        if (cb + it * 32 >= chunks) break;  // warp-uniform
 #pragma unroll
-        for (int i = 0; i < R; ++i)
-          if (r0 + i < nrows)
-            P[(r0 + i) * ps + g] = __fmul_rn(__fmul_rn((float)d[i], scales[r0 + i][g]), xs);
+        for (int i = 0; i < R; ++i) {
+          const bool live = r0 + i < nrows;
+          const int xsel = live ? rows[r0 + i].x : 0;
+          const uint4* xv = reinterpret_cast<const uint4*>(xp + (size_t)xsel * in_dim);
+          int dv = 0;
+          if (c < chunks) dv = dot32_u4(w[i][it], xv[2 * c], xv[2 * c + 1], 0) - 8 * csum[xsel * chunks + c];
+          // the chunks of one group sit in consecutive lanes: reduce them exactly
+          for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+          if (live && c < chunks && (c % cpg) == 0) {
+            const int g = c / cpg;
+            P[(r0 + i) * ps + g] = __fmul_rn(__fmul_rn((float)dv, rows[r0 + i].s[g]), xs[xsel]);
+          }
+        }
       }
     }
   }
+}
+
+__device__ __forceinline__ void group_products_any(const RowJob* rows, int nrows, int in_dim,
+                                                   int group, const int8_t* xp, const int* csum,
+                                                   const float* xs, float* P, int ps) {
+  const int chunks = in_dim >> 5;
+  if (chunks <= 32)
+    group_products<8, 1>(rows, nrows, in_dim, group, xp, csum, xs, P, ps);
+  else if (chunks <= 64)
+    group_products<4, 2>(rows, nrows, in_dim, group, xp, csum, xs, P, ps);
+  else
+    group_products<1, 8>(rows, nrows, in_dim, group, xp, csum, xs, P, ps);
 }
 
 // Ordered group sum of one row: t = t + p_g for g = 0..ng-1 (matmul.rs:576-577).
@@ -117,7 +124,6 @@ __global__ void __launch_bounds__(kThreads) k_router(Dims d, LayerPtrs L, int la
 }
 
 constexpr int kGuPairs = 32;  // gate/up row pairs per CTA
-constexpr int kGuR = 4;       // rows per warp iteration
 
 __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, DecodeBufs b) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -125,9 +131,9 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, Decode
   int8_t* xp = reinterpret_cast<int8_t*>(smem);
   int* csum = reinterpret_cast<int*>(smem + d.dim);
   float* P = reinterpret_cast<float*>(smem + d.dim + (d.dim >> 5) * 4);
-  __shared__ const uint8_t* rows[2 * kGuPairs];
-  __shared__ const float* scales[2 * kGuPairs];
-  __shared__ float red[40];
+  __shared__ RowJob rows[2 * kGuPairs];
+  __shared__ float xs_s[1];
+  __shared__ float tots[2 * kGuPairs];
 
   const int j = blockIdx.y;
   const ExpertPtrs E = L.experts[b.sel[j]];
@@ -135,14 +141,13 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, Decode
   const int base = blockIdx.x * kGuPairs;
   const int npairs = min(kGuPairs, H - base);
   if (threadIdx.x < 2 * kGuPairs) {
-    const int i = threadIdx.x;
-    const int r = (i < kGuPairs) ? base + i : H + base + (i - kGuPairs);  // gate rows, then up
-    const bool ok = (i < kGuPairs) ? i < npairs : (i - kGuPairs) < npairs;
-    rows[i] = ok ? E.gu + (size_t)r * prow : nullptr;
-    scales[i] = ok ? E.gu_s + (size_t)r * ng : nullptr;
+    const int i = threadIdx.x, k = i % kGuPairs;
+    const int r = (i < kGuPairs ? base : H + base) + min(k, npairs - 1);  // gate rows, then up rows
+    rows[i] = RowJob{E.gu + (size_t)r * prow, E.gu_s + (size_t)r * ng, 0};
   }
   // the quantized FFN input (xb of the router) in permuted order
   for (int i = threadIdx.x; i < d.dim; i += blockDim.x) xp[perm32(i)] = b.xq_ffn[i];
+  if (threadIdx.x == 0) xs_s[0] = *b.xs_ffn;
   __syncthreads();
   for (int c = threadIdx.x; c < (d.dim >> 5); c += blockDim.x) {
     int s = 0;
@@ -150,16 +155,8 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, Decode
     csum[c] = s;
   }
   __syncthreads();
-  const float xs = *b.xs_ffn;
-  // rows with no work are given a valid pointer and discarded
-  if (threadIdx.x < 2 * kGuPairs && rows[threadIdx.x] == nullptr) {
-    rows[threadIdx.x] = E.gu;
-    scales[threadIdx.x] = E.gu_s;
-  }
+  group_products_any(rows, 2 * kGuPairs, d.dim, d.group, xp, csum, xs_s, P, ps);
   __syncthreads();
-  group_products<kGuR>(rows, scales, 2 * kGuPairs, d.dim, d.group, xp, csum, xs, P, ps);
-  __syncthreads();
-  __shared__ float tots[2 * kGuPairs];
   if (threadIdx.x < 2 * kGuPairs) tots[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
   __syncthreads();
   float m = 0.0f;
@@ -181,36 +178,38 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, DecodeBu
   int8_t* xp = reinterpret_cast<int8_t*>(smem);                        // [K][H]
   int* csum = reinterpret_cast<int*>(smem + (size_t)K * H);             // [K][H/32]
   float* P = reinterpret_cast<float*>(smem + (size_t)K * H + (size_t)K * (H >> 5) * 4);
-  float* hbuf = P + (size_t)K * kDnRows * ps;                           // [H] staging
-  __shared__ const uint8_t* rows[kWarps * 4];
-  __shared__ const float* scales[kWarps * 4];
+  __shared__ RowJob rows[8 * kDnRows];
   __shared__ float xs_j[8];
-  __shared__ float y[kWarps * 4];
-  __shared__ float red[40];
+  __shared__ float y[8 * kDnRows];
 
   const int r0 = blockIdx.x * kDnRows;
   const int nr = min(kDnRows, d.dim - r0);
-  for (int j = 0; j < K; ++j) {
-    for (int i = threadIdx.x; i < H; i += blockDim.x) hbuf[i] = b.h[(size_t)j * H + i];
-    __syncthreads();
-    const float s = quantize_perm(hbuf, H, xp + (size_t)j * H, csum + (size_t)j * (H >> 5), red,
-                                  __uint_as_float(b.amax[j]), true);
-    if (threadIdx.x == 0) xs_j[j] = s;
-    __syncthreads();
-  }
   const int prow = H >> 1;
   if (threadIdx.x < K * kDnRows) {
     const int j = threadIdx.x / kDnRows, i = threadIdx.x % kDnRows;
     const ExpertPtrs E = L.experts[b.sel[j]];
     const int r = r0 + min(i, nr - 1);
-    rows[threadIdx.x] = E.dn + (size_t)r * prow;
-    scales[threadIdx.x] = E.dn_s + (size_t)r * ng;
+    rows[threadIdx.x] = RowJob{E.dn + (size_t)r * prow, E.dn_s + (size_t)r * ng, j};
+  }
+  // quantize h of every selected expert with the absmax the gate/up kernel
+  // accumulated (quantize_f32_to_i8 of the down projection's input, engine.rs:383-384)
+  for (int j = 0; j < K; ++j) {
+    float scale, inv;
+    quant_scale(__uint_as_float(b.amax[j]), &scale, &inv);
+    const float* hj = b.h + (size_t)j * H;
+    int8_t* xj = xp + (size_t)j * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xj[perm32(i)] = quant_any(hj[i], inv, i, H);
+    if (threadIdx.x == 0) xs_j[j] = scale;
   }
   __syncthreads();
-  for (int j = 0; j < K; ++j)
-    group_products<1>(rows + j * kDnRows, scales + j * kDnRows, kDnRows, H, d.group,
-                      xp + (size_t)j * H, csum + (size_t)j * (H >> 5), xs_j[j],
-                      P + (size_t)j * kDnRows * ps, ps);
+  for (int c = threadIdx.x; c < K * (H >> 5); c += blockDim.x) {
+    const int8_t* p = xp + (size_t)c * 32;
+    int s = 0;
+    for (int i = 0; i < 32; ++i) s += p[i];
+    csum[c] = s;
+  }
+  __syncthreads();
+  group_products_any(rows, K * kDnRows, H, d.group, xp, csum, xs_j, P, ps);
   __syncthreads();
   if (threadIdx.x < K * kDnRows) y[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
   __syncthreads();
@@ -242,16 +241,16 @@ __global__ void __launch_bounds__(kThreads) k_matmul_i4_op(float* __restrict__ o
   int8_t* xp = reinterpret_cast<int8_t*>(smem);
   int* csum = reinterpret_cast<int*>(smem + in_dim);
   float* P = reinterpret_cast<float*>(smem + in_dim + (in_dim >> 5) * 4);
-  __shared__ const uint8_t* rows[kOpRows];
-  __shared__ const float* scales[kOpRows];
+  __shared__ RowJob rows[kOpRows];
   __shared__ float red[40];
+  __shared__ float xs_s[1];
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < in_dim; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
+  m = block_max(m, red);
   float scale, inv;
-  quant_scale([&] {
-    float m = 0.0f;
-    for (int i = threadIdx.x; i < in_dim; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
-    return block_max(m, red);
-  }(), &scale, &inv);
+  quant_scale(m, &scale, &inv);
   for (int i = threadIdx.x; i < in_dim; i += blockDim.x) xp[perm32(i)] = quant_any(x[i], inv, i, in_dim);
+  if (threadIdx.x == 0) xs_s[0] = scale;
   __syncthreads();
   for (int c = threadIdx.x; c < (in_dim >> 5); c += blockDim.x) {
     int s = 0;
@@ -263,11 +262,10 @@ __global__ void __launch_bounds__(kThreads) k_matmul_i4_op(float* __restrict__ o
   for (int rb = blockIdx.x * kOpRows; rb < out_dim; rb += gridDim.x * kOpRows) {
     if (threadIdx.x < kOpRows) {
       const int r = min(rb + (int)threadIdx.x, out_dim - 1);
-      rows[threadIdx.x] = W + (size_t)r * prow;
-      scales[threadIdx.x] = S + (size_t)r * ng;
+      rows[threadIdx.x] = RowJob{W + (size_t)r * prow, S + (size_t)r * ng, 0};
     }
     __syncthreads();
-    group_products<2>(rows, scales, kOpRows, in_dim, group, xp, csum, scale, P, ps);
+    group_products_any(rows, kOpRows, in_dim, group, xp, csum, xs_s, P, ps);
     __syncthreads();
     if (threadIdx.x < kOpRows && rb + threadIdx.x < out_dim)
       out[rb + threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
@@ -337,7 +335,7 @@ static size_t gateup_smem(const Dims& d) {
 }
 static size_t down_smem(const Dims& d) {
   const size_t H = d.hidden, K = d.top_k, ng = H / d.group;
-  return K * H + K * (H >> 5) * 4 + K * kDnRows * (ng + 1) * 4 + H * 4;
+  return K * H + K * (H >> 5) * 4 + K * kDnRows * (ng + 1) * 4;
 }
 
 void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s) {

@@ -1,0 +1,141 @@
+// libm_f32.h — single-precision tanh with the rounding of the host libm the
+// reference links (glibc), for host and device.
+//
+// The reference's attention soft-cap calls f32::tanh (src/tensor/activations.rs:
+// 133-135), which Rust on Linux takes from glibc. glibc's tanhf follows the
+// method of Sun's fdlibm: for |x| < 22, tanh is rebuilt from expm1 of 2|x|
+// (|x| >= 1: 1 - 2/(expm1(2|x|) + 2)) or of -2|x| (|x| < 1:
+// -expm1(-2|x|) / (expm1(-2|x|) + 2)); expm1 reduces its argument as
+// x = k*ln2 + r with ln2 split into a head exact in float and a tail, evaluates
+// a rational approximation of degree 5 in r^2/2 on |r| <= ln2/2, and rebuilds
+// 2^k * (expm1(r) + 1) - 1 with a correction term for the reduction error.
+// This file restates that published method in float arithmetic, operation by
+// operation, so the device reproduces the host's tanhf bit for bit (a host test
+// compares it against the system tanhf over millions of arguments).
+#pragma once
+
+#include <stdint.h>
+#include <string.h>
+
+#if defined(__CUDACC__)
+#define LIBM_FN __host__ __device__ __forceinline__
+#else
+#define LIBM_FN static inline
+#endif
+
+namespace chalot {
+namespace libm {
+
+#if defined(__CUDA_ARCH__)
+LIBM_FN float mul(float a, float b) { return __fmul_rn(a, b); }
+LIBM_FN float add(float a, float b) { return __fadd_rn(a, b); }
+LIBM_FN float sub(float a, float b) { return __fsub_rn(a, b); }
+LIBM_FN float dvd(float a, float b) { return __fdiv_rn(a, b); }
+LIBM_FN uint32_t bits(float f) { return __float_as_uint(f); }
+LIBM_FN float from_bits(uint32_t u) { return __uint_as_float(u); }
+#else
+// host: compiled with -ffp-contract=off, every operation rounds once
+LIBM_FN float mul(float a, float b) { return a * b; }
+LIBM_FN float add(float a, float b) { return a + b; }
+LIBM_FN float sub(float a, float b) { return a - b; }
+LIBM_FN float dvd(float a, float b) { return a / b; }
+LIBM_FN uint32_t bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+LIBM_FN float from_bits(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+#endif
+
+// expm1 for finite |x| < 88 (the range tanh needs), fdlibm's method.
+LIBM_FN float expm1_f32(float x) {
+  const float ln2_head = from_bits(0x3f317180u);  // ln 2 rounded so k*head is exact
+  const float ln2_tail = from_bits(0x3717f7d1u);  // ln 2 - head
+  const float inv_ln2 = from_bits(0x3fb8aa3bu);
+  // coefficients of the rational approximation in (r*r/2)
+  const float q1 = from_bits(0xbd088889u), q2 = from_bits(0x3ad00d01u),
+              q3 = from_bits(0xb8a670cdu), q4 = from_bits(0x36867e54u),
+              q5 = from_bits(0xb457edbbu);
+  const uint32_t ux = bits(x);
+  const bool neg = (ux >> 31) != 0;
+  const uint32_t ax = ux & 0x7fffffffu;
+  if (ax >= 0x4195b844u && neg) return -1.0f;  // x <= -27 ln2: expm1 rounds to -1
+  int k = 0;
+  float corr = 0.0f;
+  if (ax > 0x3eb17218u) {  // |x| > ln2/2: reduce
+    float hi, lo;
+    if (ax < 0x3f851592u) {  // |x| < 1.5 ln2: k = +-1
+      k = neg ? -1 : 1;
+      hi = neg ? add(x, ln2_head) : sub(x, ln2_head);
+      lo = neg ? -ln2_tail : ln2_tail;
+    } else {
+      k = (int)add(mul(inv_ln2, x), neg ? -0.5f : 0.5f);  // truncation toward zero
+      const float kf = (float)k;
+      hi = sub(x, mul(kf, ln2_head));
+      lo = mul(kf, ln2_tail);
+    }
+    const float r = sub(hi, lo);
+    corr = sub(sub(hi, r), lo);
+    x = r;
+  } else if (ax < 0x33000000u) {  // |x| < 2^-25
+    return x;
+  }
+  const float half_x = mul(0.5f, x);
+  const float hxs = mul(x, half_x);
+  const float r1 =
+      add(1.0f, mul(hxs, add(q1, mul(hxs, add(q2, mul(hxs, add(q3, mul(hxs, add(q4, mul(hxs, q5))))))))));
+  const float t = sub(3.0f, mul(r1, half_x));
+  float e = mul(hxs, dvd(sub(r1, t), sub(6.0f, mul(x, t))));
+  if (k == 0) return sub(x, sub(mul(x, e), hxs));
+  e = sub(mul(x, sub(e, corr)), corr);
+  e = sub(e, hxs);
+  if (k == -1) return sub(mul(0.5f, sub(x, e)), 0.5f);
+  if (k == 1) {
+    if (x < -0.25f) return mul(-2.0f, sub(e, add(x, 0.5f)));
+    return add(1.0f, mul(2.0f, sub(x, e)));
+  }
+  if (k <= -2 || k > 56) {
+    float y = sub(1.0f, sub(e, x));
+    y = from_bits(bits(y) + ((uint32_t)k << 23));
+    return sub(y, 1.0f);
+  }
+  float y;
+  if (k < 23) {
+    const float one_minus = from_bits(0x3f800000u - (0x1000000u >> k));  // 1 - 2^-k
+    y = sub(one_minus, sub(e, x));
+  } else {
+    const float two_mk = from_bits((uint32_t)(0x7f - k) << 23);  // 2^-k
+    y = sub(x, add(e, two_mk));
+    y = add(y, 1.0f);
+  }
+  return from_bits(bits(y) + ((uint32_t)k << 23));
+}
+
+// tanh for finite x, fdlibm's method (see the file comment).
+LIBM_FN float tanh_f32(float x) {
+  const uint32_t ux = bits(x);
+  const uint32_t ax = ux & 0x7fffffffu;
+  if (ax >= 0x7f800000u) return (ux >> 31) ? -1.0f : 1.0f;  // +-inf (NaN not expected)
+  float z;
+  if (ax < 0x41b00000u) {                 // |x| < 22
+    if (ax < 0x24000000u) return mul(x, add(1.0f, x));  // |x| < 2^-55
+    const float a = from_bits(ax);
+    if (ax >= 0x3f800000u) {              // |x| >= 1
+      const float t = expm1_f32(mul(2.0f, a));
+      z = sub(1.0f, dvd(2.0f, add(t, 2.0f)));
+    } else {
+      const float t = expm1_f32(mul(-2.0f, a));
+      z = dvd(-t, add(t, 2.0f));
+    }
+  } else {
+    z = 1.0f;  // 1 - tiny rounds to 1
+  }
+  return (ux >> 31) ? -z : z;
+}
+
+}  // namespace libm
+}  // namespace chalot
