@@ -283,6 +283,10 @@ def run_profile(args):
     for _ in range(2):
         toks = eng.generate(prompt, 8)
     print(json.dumps({"profile_tokens": toks}))
+    for pos in (40, 768):  # per-kernel device times (no programmatic overlap)
+        prof = eng.profile_forward(100, pos)
+        print(json.dumps({"pos": pos, "total_ms": sum(prof.values()),
+                          "per_kind_us": {k: round(v * 1000, 2) for k, v in prof.items()}}))
     eng.close()
 
 

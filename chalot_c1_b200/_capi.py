@@ -74,6 +74,8 @@ SIGNATURES = {
                                      C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     "chalot_bench_moe_layers": (C.c_int, [P, C.c_int, C.POINTER(C.c_double),
                                           C.POINTER(C.c_double)]),
+    "chalot_profile_forward": (C.c_int, [P, C.c_uint32, C.c_uint32, P, C.c_int,
+                                         C.POINTER(C.c_int)]),
     "chalot_matmul_i8": (C.c_int, [P, P, P, P, C.c_size_t, C.c_size_t, P]),
     "chalot_matmul_i4": (C.c_int, [P, P, P, P, C.c_size_t, C.c_size_t, C.c_size_t, P]),
     "chalot_quantize_i8": (C.c_int, [P, P, P, C.c_size_t, C.c_size_t, P]),

@@ -6,17 +6,43 @@
 
 namespace chalot {
 
+// Copies n floats (n % 4 == 0, 16-byte aligned) from global to shared memory
+// with every load of a thread issued before any store.
+__device__ __forceinline__ void load_f32(float* dst, const float* __restrict__ src, int n) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  const int n4 = n >> 2;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = s4[i];
+}
+
+// Same, reading through L2 only (__ldcg): for data other CTAs of the running
+// grid wrote, which the L1 of this SM may hold stale.
+__device__ __forceinline__ void load_f32_cg(float* dst, const float* src, int n) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  const int n4 = n >> 2;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
+}
+
 // rmsnorm_avx2 (src/tensor/normalization.rs:35-67) of x into xb (shared):
 // lane j of 8 accumulates x[8c+j]^2 over c, the lanes are combined by hsum8,
 // the tail is added in order, inv = 1/sqrt(ss/dim + 1e-5), xb = (x*inv)*w.
-__device__ __forceinline__ void rmsnorm_smem(const float* __restrict__ x,
-                                             const float* __restrict__ w, int dim, float* xb,
-                                             float* red) {
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) xb[i] = x[i];
+// dim % 32 == 0. `wbuf` is shared scratch of dim floats for the weights.
+__device__ __forceinline__ void rmsnorm_smem(const float* x, const float* __restrict__ w, int dim,
+                                             float* xb, float* wbuf, float* red,
+                                             bool x_coherent = false) {
+  if (x_coherent)
+    load_f32_cg(xb, x, dim);
+  else
+    load_f32(xb, x, dim);
+  load_f32(wbuf, w, dim);
   __syncthreads();
   const int chunks = dim >> 3;
   if (threadIdx.x < 8) {
     float s = 0.0f;
+#pragma unroll 8
     for (int c = 0; c < chunks; ++c) {
       float v = xb[c * 8 + threadIdx.x];
       s = __fadd_rn(s, __fmul_rn(v, v));
@@ -34,7 +60,7 @@ __device__ __forceinline__ void rmsnorm_smem(const float* __restrict__ x,
   __syncthreads();
   const float inv = red[8];
   for (int i = threadIdx.x; i < dim; i += blockDim.x)
-    xb[i] = __fmul_rn(__fmul_rn(xb[i], inv), w[i]);
+    xb[i] = __fmul_rn(__fmul_rn(xb[i], inv), wbuf[i]);
   __syncthreads();
 }
 
@@ -43,6 +69,19 @@ __device__ __forceinline__ float absmax_smem(const float* v, int n, float* red) 
   float m = 0.0f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(v[i]));
   return block_max(m, red);
+}
+
+// rmsnorm then quantize_f32_to_i8 of a vector other CTAs just finished
+// writing, into q_out/s_out (global). `xb`, `wbuf`: shared scratch of dim
+// floats each.
+__device__ __forceinline__ void norm_quant_tail(const float* x, const float* __restrict__ w, int dim,
+                                                int8_t* q_out, float* s_out, float* xb, float* wbuf,
+                                                float* red) {
+  rmsnorm_smem(x, w, dim, xb, wbuf, red, true);
+  float scale, inv;
+  quant_scale(absmax_smem(xb, dim, red), &scale, &inv);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) q_out[i] = quant_any(xb[i], inv, i, dim);
+  if (threadIdx.x == 0) *s_out = scale;
 }
 
 // quantize_f32_to_i8 of v[0..n) into q (shared or global); returns the scale.
@@ -123,6 +162,7 @@ __device__ __forceinline__ void router_logits(const float* __restrict__ W,
     const int e = t >> 4, l = t & 15, half = l >> 3, j = l & 7;
     const float* w = W + (size_t)e * dim;
     float s = 0.0f;
+#pragma unroll 8
     for (int c = 0; c < c16; ++c) {
       const int k = c * 16 + half * 8 + j;
       s = __fadd_rn(s, __fmul_rn(w[k], xb[k]));

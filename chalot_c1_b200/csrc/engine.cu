@@ -136,20 +136,42 @@ struct chalot_engine {
     return static_cast<T*>(p);
   }
 
-  void record_forward(cudaStream_t s, bool with_advance) {
+  // One forward: every kernel after the first is launched with programmatic
+  // dependent launch so it can load its weights while its predecessor runs.
+  // With `marks`, an event is recorded after every kernel (and PDL is off):
+  // the per-kernel profile of chalot_profile_forward.
+  void record_forward(cudaStream_t s, bool with_advance, cudaEvent_t* marks = nullptr) {
     const Dims& d = dims;
-    launch_embed(d, emb, emb_s, b, s);
+    const bool pdl = marks == nullptr;
+    int m = 0;
+    auto mark = [&]() {
+      if (marks) cudaEventRecordWithFlags(marks[m++], s, cudaEventRecordExternal);
+    };
+    mark();
+    launch_embed(d, emb, emb_s, layers[0].rms_attn, b, s);
+    mark();
     for (int l = 0; l < d.n_layers; ++l) {
       const LayerPtrs& L = layers[l];
-      launch_qkv(d, L, l, b, s);
-      launch_attention(d, l, b, s);
-      launch_oproj(d, L, b, s);
-      launch_router(d, L, l, b, s);
-      launch_gateup(d, L, b, s);
-      launch_down(d, L, b, s);
+      const float* next_norm = (l + 1 < d.n_layers) ? layers[l + 1].rms_attn : final_norm;
+      launch_qkv(d, L, l, b, s, pdl);
+      mark();
+      launch_scores(d, l, b, s, pdl);
+      mark();
+      launch_pv(d, l, b, s, pdl);
+      mark();
+      launch_oproj(d, L, l, b, s, pdl);
+      mark();
+      launch_gateup(d, L, b, s, pdl);
+      mark();
+      launch_down(d, L, next_norm, b, s, pdl);
+      mark();
     }
-    launch_lmhead(d, final_norm, out_w, out_s, b, num_sms, s);
-    if (with_advance) launch_advance(d, b, s);
+    launch_lmhead(d, out_w, out_s, b, num_sms, s, pdl);
+    mark();
+    if (with_advance) {
+      launch_advance(d, b, s, pdl);
+      mark();
+    }
   }
 
   cudaGraphExec_t capture(bool with_advance) {
@@ -202,7 +224,13 @@ bool check_shapes(const ModelConfig& c, std::string* err) {
   if (c.int4_group_size % 32) return bad("int4_group_size must be a multiple of 32");
   if (c.dim % c.int4_group_size || c.hidden_dim % c.int4_group_size)
     return bad("dim and hidden_dim must be multiples of int4_group_size");
-  if (c.head_dim % 8 || c.head_dim > 256) return bad("head_dim must be a multiple of 8 and <= 256");
+  if (c.head_dim % 8 || c.head_dim < 16 || c.head_dim > 256)
+    return bad("head_dim must be a multiple of 8 in [16, 256]");
+  if (c.dim > 4096) return bad("dim above 4096");
+  if (c.hidden_dim > 8192) return bad("hidden_dim above 8192");
+  if (c.top_k * c.hidden_dim > 16384) return bad("top_k * hidden_dim above 16384");
+  if (c.int4_group_size > 1024 || (c.int4_group_size & (c.int4_group_size - 1)))
+    return bad("int4_group_size must be a power of two in [32, 1024]");
   if (c.n_experts > 64) return bad("more than 64 experts");
   if (c.top_k > 8) return bad("top_k above 8");
   if (c.vocab_size >= (1u << 31)) return bad("vocab too large");
@@ -357,6 +385,7 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
         exs.push_back(p);
         all.push_back(p);
       }
+      for (size_t x = 0; x < std::min<size_t>(E, 16); ++x) L.ex[x] = exs[x];
       e->host_experts.push_back(exs);
       e->layers.push_back(L);
     }
@@ -387,8 +416,13 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.vc = e->dalloc<float>(c.n_layers * c.max_seq_len * dim);
     b.rope_cos = rc;
     b.rope_sin = rs;
+    b.xq_attn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
+    b.xs_attn = e->dalloc<float>(1);
+    b.xq_o = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
+    b.xs_o = e->dalloc<float>(1);
     b.xq_ffn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
     b.xs_ffn = e->dalloc<float>(1);
+    b.counters = e->dalloc<unsigned>(8);
     b.sel = e->dalloc<int32_t>(std::max<size_t>(c.top_k, 1));
     b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.h = e->dalloc<float>(std::max<size_t>(c.top_k, 1) * H);
@@ -644,8 +678,8 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
       bl.sel = sel + l * K;
       bl.selw = selw + l * K;
       CK(cudaMemsetAsync(bl.amax, 0, sizeof(unsigned) * K, e->stream));
-      launch_gateup(d, e->layers[l], bl, e->stream);
-      launch_down(d, e->layers[l], bl, e->stream);
+      launch_gateup(d, e->layers[l], bl, e->stream, false);
+      launch_down(d, e->layers[l], e->layers[l].rms_attn, bl, e->stream, true);
     }
     CK(cudaStreamEndCapture(e->stream, &g));
     CK(cudaGraphInstantiate(&ex, g, 0));
@@ -666,6 +700,42 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
   } catch (const CudaFail& f) {
     return fail(f);
   }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_profile_forward(chalot_engine* e, uint32_t token,
+                                                                  uint32_t pos, float* ms, int cap,
+                                                                  int* n_out) {
+  if (!e || !ms || !n_out) return set_error(CHALOT_ERR_ARG, "null argument");
+  if (token >= e->cfg.vocab_size || pos >= e->cfg.max_seq_len)
+    return set_error(CHALOT_ERR_ARG, "token or position out of range");
+  const int n = 2 + 6 * e->dims.n_layers + 1;  // kernels of one forward (no advance)
+  if (cap < n) return set_error(CHALOT_ERR_ARG, "profile buffer too small");
+  std::vector<cudaEvent_t> ev(n + 1, nullptr);
+  try {
+    CK(cudaSetDevice(e->device));
+    for (auto& x : ev) CK(cudaEventCreate(&x));
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ex = nullptr;
+    CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    e->record_forward(e->stream, false, ev.data());
+    CK(cudaStreamEndCapture(e->stream, &g));
+    CK(cudaGraphInstantiate(&ex, g, 0));
+    cudaGraphDestroy(g);
+    for (int rep = 0; rep < 2; ++rep) {  // the second replay is the one reported
+      e->set_state(pos, token, 0, 0);
+      CK(cudaGraphLaunch(ex, e->stream));
+    }
+    CK(cudaStreamSynchronize(e->stream));
+    for (int i = 0; i < n - 1; ++i) CK(cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]));
+    *n_out = n - 1;
+    cudaGraphExecDestroy(ex);
+  } catch (const CudaFail& f) {
+    for (auto& x : ev)
+      if (x) cudaEventDestroy(x);
+    return fail(f);
+  }
+  for (auto& x : ev) cudaEventDestroy(x);
   return CHALOT_OK;
 }
 

@@ -20,46 +20,60 @@
 
 #include "blockops.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 namespace chalot {
 namespace {
 
 constexpr int kScoreThreads = 128;
 
+// K row of (layer, t, head h): 16 floats per c16 step, loaded as float4.
+template <int C16>
+__device__ __forceinline__ void load_k_row(const float* k, float4 (&kr)[C16 * 4]) {
+#pragma unroll
+  for (int i = 0; i < C16 * 4; ++i) kr[i] = reinterpret_cast<const float4*>(k)[i];
+}
+
+template <int C16>  // head_dim / 16
 __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer, DecodeBufs b) {
   __shared__ __align__(16) float qh[256];
   const int h = blockIdx.y, hd = d.head_dim;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t pos = b.st->pos;
+  const float* k = b.kc + ((size_t)layer * d.max_seq + t) * d.dim + (size_t)h * hd;
+  float4 kr[C16 * 4];
+  // rows before pos were written by earlier forwards: load them before waiting
+  if ((uint32_t)t < pos) load_k_row<C16>(k, kr);
+  pdl_wait();
+  pdl_trigger();
   if (blockIdx.x * blockDim.x > pos) return;  // whole CTA beyond the causal range
-  for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = b.q[h * hd + i];
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = __ldcg(b.q + h * hd + i);
   __syncthreads();
   if ((uint32_t)t > pos) return;
-  const float* k = b.kc + ((size_t)layer * d.max_seq + t) * d.dim + (size_t)h * hd;
+  if ((uint32_t)t == pos) {  // this forward's key, written by the QKV kernel
+#pragma unroll
+    for (int i = 0; i < C16 * 4; ++i) kr[i] = __ldcg(reinterpret_cast<const float4*>(k) + i);
+  }
+  const float* kk = reinterpret_cast<const float*>(kr);
   float a0[8], a1[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) a0[j] = a1[j] = 0.0f;
-  const int c16 = hd >> 4, rem = c16 * 16;
-  for (int c = 0; c < c16; ++c) {
-    const float4* kv = reinterpret_cast<const float4*>(k + c * 16);
-    const float4 k0 = kv[0], k1 = kv[1], k2 = kv[2], k3 = kv[3];
-    const float kk[16] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w,
-                          k2.x, k2.y, k2.z, k2.w, k3.x, k3.y, k3.z, k3.w};
+#pragma unroll
+  for (int c = 0; c < C16; ++c)
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[c * 16 + j], kk[j]));
-      a1[j] = __fadd_rn(a1[j], __fmul_rn(qh[c * 16 + 8 + j], kk[8 + j]));
+      a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[c * 16 + j], kk[c * 16 + j]));
+      a1[j] = __fadd_rn(a1[j], __fmul_rn(qh[c * 16 + 8 + j], kk[c * 16 + 8 + j]));
     }
-  }
-  const bool extra = rem + 8 <= hd;
+  const int rem = C16 * 16;
+  const bool extra = rem + 8 <= hd;  // head_dim % 16 == 8: one more 8-chunk into a0
   if (extra)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[rem + j], k[rem + j]));
+    for (int j = 0; j < 8; ++j) a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[rem + j], __ldcg(k + rem + j)));
   float cmb[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) cmb[j] = __fadd_rn(a0[j], a1[j]);
-  float dot = hsum8(cmb);
-  for (int i = extra ? rem + 8 : rem; i < hd; ++i) dot = __fadd_rn(dot, __fmul_rn(qh[i], k[i]));
+  const float dot = hsum8(cmb);
   const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)hd));
   const float x = __fmul_rn(dot, inv_sqrt);
   b.scores[(size_t)h * d.max_seq + t] = __fmul_rn(30.0f, libm::tanh_f32(__fdiv_rn(x, 30.0f)));
@@ -69,19 +83,36 @@ constexpr int kPvThreads = 256;
 constexpr int kPvCols = 8;     // output columns per CTA: V loads spread over heads*hd/8 CTAs
 constexpr int kPvTile = 1024;  // V rows staged in shared memory at a time
 
+__device__ __forceinline__ void stage_v(float* vt, const float* vbase, int dim, int t0, int rows,
+                                        bool coherent) {
+#pragma unroll 8
+  for (int i = threadIdx.x; i < rows * (kPvCols / 4); i += blockDim.x) {
+    const int r = i / (kPvCols / 4), q = i % (kPvCols / 4);
+    const float4* src = reinterpret_cast<const float4*>(vbase + (size_t)(t0 + r) * dim + q * 4);
+    reinterpret_cast<float4*>(vt)[i] = coherent ? __ldcg(src) : *src;
+  }
+}
+
 __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, DecodeBufs b) {
   extern __shared__ __align__(16) float sm[];
-  float* p = sm;                      // [max_seq] probabilities
+  float* p = sm;                            // [max_seq] probabilities
   float* vt = sm + ((d.max_seq + 3) & ~3);  // [kPvTile][kPvCols] staged V (16-B aligned)
   __shared__ float red[40];
   __shared__ float inv_s;
   const int h = blockIdx.x, hd = d.head_dim, c0 = blockIdx.y * kPvCols;
   const int n = (int)b.st->pos + 1;
+  const float* vbase = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + c0;
+  // V rows 0..n-2 of the first tile were written by earlier forwards
+  stage_v(vt, vbase, d.dim, 0, min(n - 1, kPvTile), false);
+  pdl_wait();
+  pdl_trigger();
+  if (n - 1 < kPvTile) stage_v(vt + (n - 1) * kPvCols, vbase, d.dim, n - 1, 1, true);
   const float* s = b.scores + (size_t)h * d.max_seq;
   // softmax_avx2 over the n scores of this head (normalization.rs:106-160)
   float mx = -INFINITY;
+#pragma unroll 4
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = s[i];
+    const float v = __ldcg(s + i);
     p[i] = v;
     mx = fmaxf(mx, v);
   }
@@ -92,6 +123,7 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   __syncthreads();
   if (threadIdx.x < 8) {  // lane j sums elements 8c+j in c order
     float acc = 0.0f;
+#pragma unroll 8
     for (int c = 0; c < (full >> 3); ++c) acc = __fadd_rn(acc, p[c * 8 + threadIdx.x]);
     red[threadIdx.x] = acc;
   }
@@ -106,18 +138,16 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   __syncthreads();
   const float inv = inv_s;
   for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
-  // out[c] = sum_t p_t * V[t][c], added in t order; V staged tile by tile
-  const float* vbase = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + c0;
+  __syncthreads();
+  // out[c] = sum_t p_t * V[t][c], added in t order (engine.rs:302-308)
   float acc = 0.0f;
   for (int t0 = 0; t0 < n; t0 += kPvTile) {
     const int rows = min(kPvTile, n - t0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < rows * (kPvCols / 4); i += blockDim.x) {
-      const int r = i / (kPvCols / 4), q = i % (kPvCols / 4);
-      reinterpret_cast<float4*>(vt)[i] =
-          *reinterpret_cast<const float4*>(vbase + (size_t)(t0 + r) * d.dim + q * 4);
+    if (t0 > 0) {  // later tiles: stage now
+      __syncthreads();
+      stage_v(vt, vbase, d.dim, t0, rows, true);
+      __syncthreads();
     }
-    __syncthreads();
     if (threadIdx.x < kPvCols) {
       const float* pv = p + t0;
 #pragma unroll 8
@@ -125,17 +155,51 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
     }
   }
   if (threadIdx.x < kPvCols) b.att_out[h * hd + c0 + threadIdx.x] = acc;
+  // the last CTA quantizes the finished att_out for the O projection
+  if (!last_cta(b.counters + 0)) return;
+  float* a = sm;  // reuse
+  load_f32_cg(a, b.att_out, d.dim);
+  __syncthreads();
+  float scale, qinv;
+  quant_scale(absmax_smem(a, d.dim, red), &scale, &qinv);
+  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) b.xq_o[i] = quant_any(a[i], qinv, i, d.dim);
+  if (threadIdx.x == 0) *b.xs_o = scale;
 }
 
 }  // namespace
 
-void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s) {
+void launch_scores(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl) {
   dim3 g1((d.max_seq + kScoreThreads - 1) / kScoreThreads, d.n_heads);
-  k_attn_scores<<<g1, kScoreThreads, 0, s>>>(d, layer, b);
+  switch (d.head_dim / 16) {  // 16 <= head_dim <= 256, head_dim % 8 == 0
+    case 1: launch_k(k_attn_scores<1>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 2: launch_k(k_attn_scores<2>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 3: launch_k(k_attn_scores<3>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 4: launch_k(k_attn_scores<4>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 5: launch_k(k_attn_scores<5>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 6: launch_k(k_attn_scores<6>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 7: launch_k(k_attn_scores<7>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 8: launch_k(k_attn_scores<8>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 9: launch_k(k_attn_scores<9>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 10: launch_k(k_attn_scores<10>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 11: launch_k(k_attn_scores<11>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 12: launch_k(k_attn_scores<12>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 13: launch_k(k_attn_scores<13>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 14: launch_k(k_attn_scores<14>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    case 15: launch_k(k_attn_scores<15>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+    default: launch_k(k_attn_scores<16>, g1, dim3(kScoreThreads), 0, s, pdl, d, layer, b); break;
+  }
+}
+
+void launch_pv(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl) {
   dim3 g2(d.n_heads, d.head_dim / kPvCols);
   const size_t smem = ((((size_t)d.max_seq + 3) & ~size_t(3)) + (size_t)kPvTile * kPvCols) * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  k_attn_pv<<<g2, kPvThreads, smem, s>>>(d, layer, b);
+  launch_k(k_attn_pv, g2, dim3(kPvThreads), smem, s, pdl, d, layer, b);
+}
+
+void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl) {
+  launch_scores(d, layer, b, s, pdl);
+  launch_pv(d, layer, b, s, pdl);
 }
 
 }  // namespace chalot

@@ -19,6 +19,7 @@
 
 #include "blockops.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 namespace chalot {
 namespace {
@@ -26,11 +27,47 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// R consecutive rows of an int8 matrix dotted with xq (shared, 16-aligned);
-// in_dim % 16 == 0. Every lane returns the full int32 dots.
+// Loads the 16-byte chunks lane, lane+32, ... (IT of them) of R consecutive
+// int8 rows into registers (rows past n_rows or chunks past the row load 0).
+template <int R, int IT>
+__device__ __forceinline__ void rows_load_i8(const int8_t* __restrict__ W, int in_dim, int row0,
+                                             int n_rows, uint4 (&w)[R][IT]) {
+  const int lane = threadIdx.x & 31, chunks = in_dim >> 4;
+#pragma unroll
+  for (int i = 0; i < R; ++i)
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int c = lane + 32 * it;
+      w[i][it] = (row0 + i < n_rows && c < chunks)
+                     ? ldg_stream(W + (size_t)(row0 + i) * in_dim + (size_t)c * 16)
+                     : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// Exact int32 dots of the loaded rows with xq (shared, 16-aligned); every
+// lane returns the full sums. in_dim % 16 == 0 and in_dim <= 512 * IT.
+template <int R, int IT>
+__device__ __forceinline__ void rows_dot_i8(const uint4 (&w)[R][IT], int in_dim, const int8_t* xq,
+                                            int acc[R]) {
+  const int lane = threadIdx.x & 31, chunks = in_dim >> 4;
+  const uint4* xv = reinterpret_cast<const uint4*>(xq);
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = 0;
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int c = lane + 32 * it;
+    const uint4 x = (c < chunks) ? xv[c] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int i = 0; i < R; ++i) acc[i] = dot16_i8(w[i][it], x, acc[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) acc[i] = warp_sum_i(acc[i]);
+}
+
+// R consecutive rows dotted with xq for any in_dim % 16 == 0 (operator path).
 template <int R>
-__device__ __forceinline__ void rows_dot_i8(const int8_t* __restrict__ W, int in_dim, int row0,
-                                            int n_rows, const int8_t* xq, int acc[R]) {
+__device__ __forceinline__ void rows_dot_i8_loop(const int8_t* __restrict__ W, int in_dim, int row0,
+                                                 int n_rows, const int8_t* xq, int acc[R]) {
   const int lane = threadIdx.x & 31, chunks = in_dim >> 4;
   const uint4* xv = reinterpret_cast<const uint4*>(xq);
 #pragma unroll
@@ -50,43 +87,68 @@ __device__ __forceinline__ void rows_dot_i8(const int8_t* __restrict__ W, int in
   for (int i = 0; i < R; ++i) acc[i] = warp_sum_i(acc[i]);
 }
 
+// Copies a quantized vector (n bytes, n % 16 == 0) produced by another grid
+// into shared memory through L2.
+__device__ __forceinline__ void load_q(int8_t* dst, const int8_t* src, int n) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int i = threadIdx.x; i < (n >> 4); i += blockDim.x) d4[i] = __ldcg(s4 + i);
+}
+
 // ---------------------------------------------------------------------------
 
+// x = embedding row (engine.rs:201-210); then rmsnorm with the first layer's
+// attention norm and quantize_f32_to_i8 into xq_attn (one CTA).
 __global__ void __launch_bounds__(kThreads) k_embed(Dims d, const int8_t* __restrict__ emb,
-                                                    const float* __restrict__ emb_s, DecodeBufs b) {
+                                                    const float* __restrict__ emb_s,
+                                                    const float* __restrict__ rms0, DecodeBufs b) {
+  extern __shared__ __align__(16) float esm[];
+  __shared__ float red[40];
   const uint32_t tok = b.st->token;
   const float s = emb_s[tok];
   const int8_t* row = emb + (size_t)tok * d.dim;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < d.dim; i += gridDim.x * blockDim.x)
-    b.x[i] = __fmul_rn((float)row[i], s);  // engine.rs:207-209
-  if (blockIdx.x == 0 && threadIdx.x == 0) b.st->argmax_key = 0ull;
+  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) b.x[i] = __fmul_rn((float)row[i], s);
+  if (threadIdx.x == 0) b.st->argmax_key = 0ull;
+  __syncthreads();
+  norm_quant_tail(b.x, rms0, d.dim, b.xq_attn, b.xs_attn, esm, esm + d.dim, red);
 }
 
 constexpr int kQkvRows = 2;  // rows per warp: one RoPE pair
 
+template <int IT>
 __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* xb = reinterpret_cast<float*>(smem);
-  int8_t* xq = reinterpret_cast<int8_t*>(smem + d.dim * 4);
-  __shared__ float red[40];
-  rmsnorm_smem(b.x, L.rms_attn, d.dim, xb, red);
-  const float xs = quantize_smem(xb, d.dim, xq, red);
-
+  __shared__ __align__(16) int8_t xq[512 * IT];
   const int warp = threadIdx.x >> 5;
   const int r0 = (blockIdx.x * kWarps + warp) * kQkvRows;
   const int n_rows = 3 * d.dim;
-  if (r0 >= n_rows) return;
-  int acc[kQkvRows];
-  rows_dot_i8<kQkvRows>(L.qkv, d.dim, r0, n_rows, xq, acc);
-  if ((threadIdx.x & 31) != 0) return;
-  float v0 = __fmul_rn(__fmul_rn((float)acc[0], L.qkv_s[r0]), xs);
-  float v1 = __fmul_rn(__fmul_rn((float)acc[1], L.qkv_s[r0 + 1]), xs);
+  uint4 w[kQkvRows][IT];
+  rows_load_i8<kQkvRows, IT>(L.qkv, d.dim, r0, n_rows, w);  // weights do not depend on the token
+  // scales, position and rotation of this row pair: known before the token's x
   const int sec = r0 / d.dim, rr = r0 - sec * d.dim;
   const uint32_t pos = b.st->pos;
+  float s0 = 0.0f, s1 = 0.0f, c = 1.0f, sn = 0.0f;
+  if (r0 < n_rows && (threadIdx.x & 31) == 0) {
+    s0 = L.qkv_s[r0];
+    s1 = L.qkv_s[r0 + 1];
+    if (sec < 2) {
+      const int half = d.head_dim >> 1, i = (rr % d.head_dim) >> 1;
+      c = b.rope_cos[pos * half + i];
+      sn = b.rope_sin[pos * half + i];
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  load_q(xq, b.xq_attn, d.dim);
+  __syncthreads();
+  if (r0 >= n_rows) return;
+  const float xs = __ldcg(b.xs_attn);
+  int acc[kQkvRows];
+  rows_dot_i8<kQkvRows, IT>(w, d.dim, xq, acc);
+  if ((threadIdx.x & 31) != 0) return;
+  float v0 = __fmul_rn(__fmul_rn((float)acc[0], s0), xs);
+  float v1 = __fmul_rn(__fmul_rn((float)acc[1], s1), xs);
   if (sec < 2) {  // RoPE on the interleaved pair (engine.rs:252-271)
-    const int half = d.head_dim >> 1;
-    const int i = (rr % d.head_dim) >> 1;
-    const float c = b.rope_cos[pos * half + i], s = b.rope_sin[pos * half + i];
+    const float s = sn;
     const float a = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
     const float e = __fadd_rn(__fmul_rn(v0, s), __fmul_rn(v1, c));
     v0 = a;
@@ -105,48 +167,81 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer
 
 constexpr int kORows = 2;
 
-__global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, DecodeBufs b) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* a = reinterpret_cast<float*>(smem);
-  int8_t* xq = reinterpret_cast<int8_t*>(smem + d.dim * 4);
+// O rows + residual; the last CTA then runs the FFN prologue of the layer
+// once for every later kernel: xb = rmsnorm(x, rms_ffn), xq_ffn/xs_ffn =
+// quantize(xb), router logits and softmax_top_k -> sel/selw (engine.rs:325-344),
+// and clears the absmax slots of h.
+template <int IT>
+__global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
+  extern __shared__ __align__(16) float osm[];  // tail scratch: xb, wbuf [dim] each, lanes [16E], logit [E]
+  __shared__ __align__(16) int8_t xq[512 * IT];
   __shared__ float red[40];
-  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) a[i] = b.att_out[i];
-  __syncthreads();
-  const float xs = quantize_smem(a, d.dim, xq, red);
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = (blockIdx.x * kWarps + warp) * kORows;
-  if (r0 >= d.dim) return;
-  int acc[kORows];
-  rows_dot_i8<kORows>(L.o, d.dim, r0, d.dim, xq, acc);
-  const int lane = threadIdx.x & 31;
-  if (lane < kORows && r0 + lane < d.dim) {
-    const int r = r0 + lane;
-    int dot = acc[0];
+  uint4 w[kORows][IT];
+  rows_load_i8<kORows, IT>(L.o, d.dim, r0, d.dim, w);
+  pdl_wait();
+  pdl_trigger();
+  load_q(xq, b.xq_o, d.dim);
+  __syncthreads();
+  if (r0 < d.dim) {
+    const float xs = __ldcg(b.xs_o);
+    int acc[kORows];
+    rows_dot_i8<kORows, IT>(w, d.dim, xq, acc);
+    if (lane < kORows && r0 + lane < d.dim) {
+      const int r = r0 + lane;
+      int dot = acc[0];
 #pragma unroll
-    for (int i = 1; i < kORows; ++i) dot = (lane == i) ? acc[i] : dot;
-    const float v = __fmul_rn(__fmul_rn((float)dot, L.o_s[r]), xs);
-    b.x[r] = __fadd_rn(b.x[r], v);  // residual (engine.rs:320-322)
+      for (int i = 1; i < kORows; ++i) dot = (lane == i) ? acc[i] : dot;
+      const float v = __fmul_rn(__fmul_rn((float)dot, L.o_s[r]), xs);
+      b.x[r] = __fadd_rn(__ldcg(b.x + r), v);  // residual (engine.rs:320-322)
+    }
+  }
+  if (!last_cta(b.counters + 1)) return;
+  const int E = d.n_experts;
+  float* xb = osm;
+  float* wbuf = osm + d.dim;
+  float* lanes = wbuf + d.dim;
+  float* logit = lanes + 16 * E;
+  float* rw = logit + ((E + 3) & ~3);  // [E][dim] router weights staged before the norm
+  if (E >= 2) load_f32(rw, L.router_w, E * d.dim);
+  norm_quant_tail(b.x, L.rms_ffn, d.dim, b.xq_ffn, b.xs_ffn, xb, wbuf, red);
+  if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;
+  if (E >= 2) {
+    router_logits(rw, L.router_b, xb, d.dim, E, lanes, logit);
+    if (threadIdx.x == 0) {
+      if (b.router_trace)
+        for (int e = 0; e < E; ++e) b.router_trace[layer * E + e] = logit[e];
+      topk_serial(logit, E, d.top_k, b.sel, b.selw);
+    }
+  } else if (threadIdx.x == 0) {
+    b.sel[0] = 0;
+    b.selw[0] = 1.0f;
   }
 }
 
 constexpr int kLmRows = 4;
 
-__global__ void __launch_bounds__(kThreads) k_lmhead(Dims d, const float* __restrict__ norm_w,
-                                                     const int8_t* __restrict__ W,
+template <int IT>
+__global__ void __launch_bounds__(kThreads) k_lmhead(Dims d, const int8_t* __restrict__ W,
                                                      const float* __restrict__ ws, DecodeBufs b) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* xb = reinterpret_cast<float*>(smem);
-  int8_t* xq = reinterpret_cast<int8_t*>(smem + d.dim * 4);
-  __shared__ float red[40];
+  __shared__ __align__(16) int8_t xq[512 * IT];
   __shared__ unsigned long long best_w[kWarps];
-  rmsnorm_smem(b.x, norm_w, d.dim, xb, red);
-  const float xs = quantize_smem(xb, d.dim, xq, red);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  unsigned long long best = 0ull;
   const int step = gridDim.x * kWarps * kLmRows;
-  for (int r0 = (blockIdx.x * kWarps + warp) * kLmRows; r0 < d.vocab; r0 += step) {
+  int r0 = (blockIdx.x * kWarps + warp) * kLmRows;
+  uint4 w[kLmRows][IT];
+  rows_load_i8<kLmRows, IT>(W, d.dim, r0, d.vocab, w);
+  pdl_wait();
+  pdl_trigger();
+  load_q(xq, b.xq_attn, d.dim);  // rmsnorm(x, final_norm) quantized by the last down kernel
+  __syncthreads();
+  const float xs = __ldcg(b.xs_attn);
+  unsigned long long best = 0ull;
+  for (; r0 < d.vocab; r0 += step) {
     int acc[kLmRows];
-    rows_dot_i8<kLmRows>(W, d.dim, r0, d.vocab, xq, acc);
+    rows_dot_i8<kLmRows, IT>(w, d.dim, xq, acc);
+    if (r0 + step < d.vocab) rows_load_i8<kLmRows, IT>(W, d.dim, r0 + step, d.vocab, w);
 #pragma unroll
     for (int i = 0; i < kLmRows; ++i) {
       const int r = r0 + i;
@@ -175,6 +270,7 @@ __global__ void __launch_bounds__(kThreads) k_lmhead(Dims d, const float* __rest
 // Records the forward's argmax and picks the next token (engine.rs:509-545):
 // during prefill the next prompt token clamped to vocab-1, then the argmax.
 __global__ void k_advance(Dims d, DecodeBufs b) {
+  pdl_wait();
   StepState* st = b.st;
   const uint32_t idx = (uint32_t)(st->argmax_key & 0xffffffffull);
   const uint32_t step = st->step;
@@ -249,7 +345,7 @@ __global__ void __launch_bounds__(kThreads) k_matmul_i8_op(float* __restrict__ o
   for (int r0 = (blockIdx.x * kWarps + warp) * 2; r0 < out_dim; r0 += step) {
     int acc[2];
     if (vec) {
-      rows_dot_i8<2>(W, in_dim, r0, out_dim, xq, acc);
+      rows_dot_i8_loop<2>(W, in_dim, r0, out_dim, xq, acc);
     } else {
       for (int i = 0; i < 2; ++i) {
         int a = 0;
@@ -278,35 +374,64 @@ __global__ void __launch_bounds__(kThreads) k_quantize_op(int8_t* __restrict__ q
   if (threadIdx.x == 0) scale[blockIdx.x] = s;
 }
 
-size_t dense_smem(const Dims& d) { return (size_t)d.dim * 4 + (((size_t)d.dim + 15) & ~size_t(15)); }
-
 }  // namespace
 
-void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const DecodeBufs& b,
-                  cudaStream_t s) {
-  k_embed<<<std::max(1, (d.dim + kThreads - 1) / kThreads), kThreads, 0, s>>>(d, emb, emb_s, b);
+// in_dim of the dense projections is at most 4096: 16-byte chunks per lane
+static int dense_it(int dim) { return (dim + 511) / 512; }
+
+void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const float* rms0,
+                  const DecodeBufs& b, cudaStream_t s) {
+  launch_k(k_embed, dim3(1), dim3(kThreads), (size_t)d.dim * 8, s, false, d, emb, emb_s, rms0, b);
 }
 
-void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s) {
+#define CHALOT_IT_SWITCH(it, CALL) \
+  switch (it) {                    \
+    case 1: CALL(1); break;        \
+    case 2: CALL(2); break;        \
+    case 3: CALL(3); break;        \
+    case 4: CALL(4); break;        \
+    case 5: CALL(5); break;        \
+    case 6: CALL(6); break;        \
+    case 7: CALL(7); break;        \
+    default: CALL(8); break;       \
+  }
+
+void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
+                bool pdl) {
   const int rows_per_block = kWarps * kQkvRows;
   const int grid = (3 * d.dim + rows_per_block - 1) / rows_per_block;
-  k_qkv<<<grid, kThreads, dense_smem(d), s>>>(d, L, layer, b);
+#define QKV_CALL(IT) launch_k(k_qkv<IT>, dim3(grid), dim3(kThreads), 0, s, pdl, d, L, layer, b)
+  CHALOT_IT_SWITCH(dense_it(d.dim), QKV_CALL)
+#undef QKV_CALL
 }
 
-void launch_oproj(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s) {
+void launch_oproj(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b,
+                  cudaStream_t s, bool pdl) {
   const int rows_per_block = kWarps * kORows;
-  k_oproj<<<(d.dim + rows_per_block - 1) / rows_per_block, kThreads, dense_smem(d), s>>>(d, L, b);
+  const int grid = (d.dim + rows_per_block - 1) / rows_per_block;
+  const size_t E = d.n_experts;
+  const size_t smem = ((size_t)d.dim * 2 + 16 * E + ((E + 3) & ~size_t(3)) + E * d.dim) * 4;
+#define O_CALL(IT)                                                                           \
+  do {                                                                                      \
+    if (smem > 48 * 1024)                                                                   \
+      cudaFuncSetAttribute(k_oproj<IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    launch_k(k_oproj<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, b);        \
+  } while (0)
+  CHALOT_IT_SWITCH(dense_it(d.dim), O_CALL)
+#undef O_CALL
 }
 
-void launch_lmhead(const Dims& d, const float* final_norm, const int8_t* w, const float* ws,
-                   const DecodeBufs& b, int num_sms, cudaStream_t s) {
+void launch_lmhead(const Dims& d, const int8_t* w, const float* ws, const DecodeBufs& b,
+                   int num_sms, cudaStream_t s, bool pdl) {
   const int rows_per_block = kWarps * kLmRows;
   const int grid = std::min((d.vocab + rows_per_block - 1) / rows_per_block, num_sms * 4);
-  k_lmhead<<<grid, kThreads, dense_smem(d), s>>>(d, final_norm, w, ws, b);
+#define LM_CALL(IT) launch_k(k_lmhead<IT>, dim3(grid), dim3(kThreads), 0, s, pdl, d, w, ws, b)
+  CHALOT_IT_SWITCH(dense_it(d.dim), LM_CALL)
+#undef LM_CALL
 }
 
-void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s) {
-  k_advance<<<1, 1, 0, s>>>(d, b);
+void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s, bool pdl) {
+  launch_k(k_advance, dim3(1), dim3(1), 0, s, pdl, d, b);
 }
 
 void launch_penalty_argmax(const Dims& d, const DecodeBufs& b, const uint32_t* hist, int n_hist,

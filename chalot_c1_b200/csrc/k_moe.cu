@@ -8,10 +8,9 @@
 // 32-column chunk) at a time and compute exact group dots with dp4a; each group
 // leader writes p_g = ((float)gdot*s_g)*xs to shared memory, and one thread per
 // row then adds p_0, p_1, ... sequentially.
-//   k_router  rmsnorm(x) -> quantize -> router logits -> softmax top-k
-//             (engine.rs:325-344)
-//   k_gateup  gate and up rows of the selected experts -> SwiGLU -> h and
-//             absmax(h) (engine.rs:366-377)
+//   k_gateup  rmsnorm(x) -> quantize -> router logits -> softmax top-k
+//             (engine.rs:325-344), then gate and up rows of the selected
+//             experts -> SwiGLU -> h and absmax(h) (engine.rs:366-377)
 //   k_down    quantize(h) -> down rows of every selected expert -> gated sum in
 //             selection order -> x += (engine.rs:380-401)
 #include <cuda_runtime.h>
@@ -20,6 +19,7 @@
 
 #include "blockops.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 namespace chalot {
 namespace {
@@ -48,13 +48,15 @@ __device__ __forceinline__ void group_products(const RowJob* rows, int nrows, in
   for (int r0 = warp * R; r0 < nrows; r0 += kWarps * R) {
     for (int cb = 0; cb < chunks; cb += 32 * IT) {
       uint4 w[R][IT];
+      float sc[R][IT];
 #pragma unroll
       for (int i = 0; i < R; ++i)
 #pragma unroll
         for (int it = 0; it < IT; ++it) {
           const int c = cb + it * 32 + lane;
-          w[i][it] = (c < chunks && r0 + i < nrows) ? ldg_stream(rows[r0 + i].w + (size_t)c * 16)
-                                                    : make_uint4(0, 0, 0, 0);
+          const bool ok = c < chunks && r0 + i < nrows;
+          w[i][it] = ok ? ldg_stream(rows[r0 + i].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+          sc[i][it] = ok ? __ldg(rows[r0 + i].s + c / cpg) : 0.0f;  // this chunk's group scale
         }
 #pragma unroll
       for (int it = 0; it < IT; ++it) {
@@ -69,10 +71,8 @@ __device__ __forceinline__ void group_products(const RowJob* rows, int nrows, in
           if (c < chunks) dv = dot32_u4(w[i][it], xv[2 * c], xv[2 * c + 1], 0) - 8 * csum[xsel * chunks + c];
           // the chunks of one group sit in consecutive lanes: reduce them exactly
           for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-          if (live && c < chunks && (c % cpg) == 0) {
-            const int g = c / cpg;
-            P[(r0 + i) * ps + g] = __fmul_rn(__fmul_rn((float)dv, rows[r0 + i].s[g]), xs[xsel]);
-          }
+          if (live && c < chunks && (c % cpg) == 0)
+            P[(r0 + i) * ps + c / cpg] = __fmul_rn(__fmul_rn((float)dv, sc[i][it]), xs[xsel]);
         }
       }
     }
@@ -94,66 +94,64 @@ __device__ __forceinline__ void group_products_any(const RowJob* rows, int nrows
 // Ordered group sum of one row: t = t + p_g for g = 0..ng-1 (matmul.rs:576-577).
 __device__ __forceinline__ float ordered_sum(const float* p, int ng) {
   float t = 0.0f;
+#pragma unroll 8
   for (int g = 0; g < ng; ++g) t = __fadd_rn(t, p[g]);
   return t;
 }
 
-// ---------------------------------------------------------------------------
-
-__global__ void __launch_bounds__(kThreads) k_router(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* xb = reinterpret_cast<float*>(smem);
-  float* lanes = xb + d.dim;                 // [16*E]
-  float* logit = lanes + 16 * d.n_experts;  // [E]
-  __shared__ float red[40];
-  rmsnorm_smem(b.x, L.rms_ffn, d.dim, xb, red);  // engine.rs:325-329
-  const float xs = quantize_smem(xb, d.dim, b.xq_ffn, red);
-  if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;
-  if (threadIdx.x == 0) *b.xs_ffn = xs;
-  if (d.n_experts >= 2) {
-    router_logits(L.router_w, L.router_b, xb, d.dim, d.n_experts, lanes, logit);
-    if (threadIdx.x == 0) {
-      if (b.router_trace)
-        for (int e = 0; e < d.n_experts; ++e) b.router_trace[layer * d.n_experts + e] = logit[e];
-      topk_serial(logit, d.n_experts, d.top_k, b.sel, b.selw);
-    }
-  } else if (threadIdx.x == 0) {
-    b.sel[0] = 0;
-    b.selw[0] = 1.0f;
+// Sums of every 32-byte chunk of xp (n bytes): 8 dp4a per chunk.
+__device__ __forceinline__ void chunk_sums(const int8_t* xp, int n, int* csum) {
+  const int* w = reinterpret_cast<const int*>(xp);
+  for (int c = threadIdx.x; c < (n >> 5); c += blockDim.x) {
+    int s = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s = __dp4a(w[c * 8 + k], 0x01010101, s);
+    csum[c] = s;
   }
 }
 
+// ---------------------------------------------------------------------------
+
 constexpr int kGuPairs = 32;  // gate/up row pairs per CTA
 
+// Gate rows base..base+31 and the matching up rows of routed expert
+// sel[blockIdx.y], dotted with xq_ffn (engine.rs:366-374), then SwiGLU
+// (activations.rs:59-87); h goes to global memory and |h| into the expert's
+// absmax slot for the down kernel's quantization.
 __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, DecodeBufs b) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int ng = d.dim / d.group, ps = ng + 1;
-  int8_t* xp = reinterpret_cast<int8_t*>(smem);
-  int* csum = reinterpret_cast<int*>(smem + d.dim);
-  float* P = reinterpret_cast<float*>(smem + d.dim + (d.dim >> 5) * 4);
+  int8_t* xp = reinterpret_cast<int8_t*>(smem);              // [dim] permuted x_q
+  int* csum = reinterpret_cast<int*>(xp + d.dim);            // [dim/32]
+  float* P = reinterpret_cast<float*>(csum + (d.dim >> 5));  // [64][ng+1]
   __shared__ RowJob rows[2 * kGuPairs];
   __shared__ float xs_s[1];
   __shared__ float tots[2 * kGuPairs];
 
+  pdl_wait();  // the routing comes from the O-projection's last CTA
+  pdl_trigger();
   const int j = blockIdx.y;
-  const ExpertPtrs E = L.experts[b.sel[j]];
+  const ExpertPtrs X = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
   const int H = d.hidden, prow = d.dim >> 1;
   const int base = blockIdx.x * kGuPairs;
   const int npairs = min(kGuPairs, H - base);
   if (threadIdx.x < 2 * kGuPairs) {
     const int i = threadIdx.x, k = i % kGuPairs;
     const int r = (i < kGuPairs ? base : H + base) + min(k, npairs - 1);  // gate rows, then up rows
-    rows[i] = RowJob{E.gu + (size_t)r * prow, E.gu_s + (size_t)r * ng, 0};
+    rows[i] = RowJob{X.gu + (size_t)r * prow, X.gu_s + (size_t)r * ng, 0};
   }
-  // the quantized FFN input (xb of the router) in permuted order
-  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) xp[perm32(i)] = b.xq_ffn[i];
-  if (threadIdx.x == 0) xs_s[0] = *b.xs_ffn;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(b.xq_ffn);
+    for (int k = threadIdx.x; k < (d.dim >> 4); k += blockDim.x) {
+      const uint4 v = __ldcg(src + k);
+      const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
+#pragma unroll
+      for (int u = 0; u < 16; ++u) xp[perm32(k * 16 + u)] = vb[u];
+    }
+    if (threadIdx.x == 0) xs_s[0] = __ldcg(b.xs_ffn);
+  }
   __syncthreads();
-  for (int c = threadIdx.x; c < (d.dim >> 5); c += blockDim.x) {
-    int s = 0;
-    for (int i = 0; i < 32; ++i) s += xp[c * 32 + i];
-    csum[c] = s;
-  }
+  chunk_sums(xp, d.dim, csum);
   __syncthreads();
   group_products_any(rows, 2 * kGuPairs, d.dim, d.group, xp, csum, xs_s, P, ps);
   __syncthreads();
@@ -170,48 +168,104 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, Decode
   if (threadIdx.x == 0) atomicMax(&b.amax[j], __float_as_uint(m));
 }
 
-constexpr int kDnRows = 4;  // output rows per CTA (for every selected expert)
-
-__global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, DecodeBufs b, int dense) {
+// Output rows r0..r0+rpc-1 for every routed expert: the routing is two
+// launches old, so each warp loads its down row (all IT 32-lane strides)
+// before waiting for the gate/up kernel; then h is quantized with the
+// accumulated absmax (the input quantization of engine.rs:383-384), the group
+// products and ordered sums give y_j[r], and x[r] += sum_j w_j * y_j[r] in
+// selection order (engine.rs:390-401). The last CTA computes the next
+// layer's quantized attention input from the finished x.
+template <int IT>
+__global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, const float* next_norm,
+                                                   DecodeBufs b, int dense, int rpc) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int H = d.hidden, K = d.top_k, ng = H / d.group, ps = ng + 1;
-  int8_t* xp = reinterpret_cast<int8_t*>(smem);                        // [K][H]
-  int* csum = reinterpret_cast<int*>(smem + (size_t)K * H);             // [K][H/32]
-  float* P = reinterpret_cast<float*>(smem + (size_t)K * H + (size_t)K * (H >> 5) * 4);
-  __shared__ RowJob rows[8 * kDnRows];
+  int8_t* xp = reinterpret_cast<int8_t*>(smem);                          // [K][H]
+  int* csum = reinterpret_cast<int*>(smem + (size_t)K * H);               // [K][H/32]
+  float* P = reinterpret_cast<float*>(csum + (size_t)K * (H >> 5));       // [8][ng+1]
+  __shared__ RowJob rows[kWarps];
   __shared__ float xs_j[8];
-  __shared__ float y[8 * kDnRows];
+  __shared__ float selw_s[8];
+  __shared__ float y[kWarps];
+  __shared__ float red[40];
 
-  const int r0 = blockIdx.x * kDnRows;
-  const int nr = min(kDnRows, d.dim - r0);
-  const int prow = H >> 1;
-  if (threadIdx.x < K * kDnRows) {
-    const int j = threadIdx.x / kDnRows, i = threadIdx.x % kDnRows;
-    const ExpertPtrs E = L.experts[b.sel[j]];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * rpc;
+  const int nr = min(rpc, d.dim - r0);
+  const int nrow = K * rpc;  // <= kWarps: one row per warp
+  const int prow = H >> 1, chunks = H >> 5, cpg = d.group >> 5;
+  if (threadIdx.x < nrow) {
+    const int j = threadIdx.x / rpc, i = threadIdx.x % rpc;
+    const ExpertPtrs E = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
     const int r = r0 + min(i, nr - 1);
     rows[threadIdx.x] = RowJob{E.dn + (size_t)r * prow, E.dn_s + (size_t)r * ng, j};
   }
-  // quantize h of every selected expert with the absmax the gate/up kernel
-  // accumulated (quantize_f32_to_i8 of the down projection's input, engine.rs:383-384)
-  for (int j = 0; j < K; ++j) {
-    float scale, inv;
-    quant_scale(__uint_as_float(b.amax[j]), &scale, &inv);
-    const float* hj = b.h + (size_t)j * H;
-    int8_t* xj = xp + (size_t)j * H;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) xj[perm32(i)] = quant_any(hj[i], inv, i, H);
-    if (threadIdx.x == 0) xs_j[j] = scale;
+  if (threadIdx.x < K) selw_s[threadIdx.x] = __ldcg(b.selw + threadIdx.x);
+  __syncthreads();
+  uint4 w[IT];
+  float sc[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int c = lane + 32 * it;
+    const bool ok = warp < nrow && c < chunks;
+    w[it] = ok ? ldg_stream(rows[warp].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+    sc[it] = ok ? __ldg(rows[warp].s + c / cpg) : 0.0f;
+  }
+  pdl_wait();
+  pdl_trigger();
+  {
+    // all of h (K*H floats) in flight at once, then quantized per expert
+    constexpr int kMaxH4 = 16;  // float4 per thread: K*H <= 16384
+    const int n4 = (K * H) >> 2, h4 = H >> 2;
+    float4 hv[kMaxH4];
+    const float4* src = reinterpret_cast<const float4*>(b.h);
+#pragma unroll
+    for (int u = 0; u < kMaxH4; ++u) {
+      const int i4 = threadIdx.x + u * kThreads;
+      if (i4 < n4) hv[u] = __ldcg(src + i4);
+    }
+    float invs[8];
+    for (int j = 0; j < K; ++j) {
+      float scale;
+      quant_scale(__uint_as_float(__ldcg(b.amax + j)), &scale, &invs[j]);
+      if (threadIdx.x == 0) xs_j[j] = scale;
+    }
+#pragma unroll
+    for (int u = 0; u < kMaxH4; ++u) {
+      const int i4 = threadIdx.x + u * kThreads;
+      if (i4 < n4) {
+        const int j = i4 / h4, i = (i4 - j * h4) * 4;
+        int8_t* xj = xp + (size_t)j * H;
+        const float inv = invs[j];
+        xj[perm32(i)] = quant_any(hv[u].x, inv, i, H);
+        xj[perm32(i + 1)] = quant_any(hv[u].y, inv, i + 1, H);
+        xj[perm32(i + 2)] = quant_any(hv[u].z, inv, i + 2, H);
+        xj[perm32(i + 3)] = quant_any(hv[u].w, inv, i + 3, H);
+      }
+    }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < K * (H >> 5); c += blockDim.x) {
-    const int8_t* p = xp + (size_t)c * 32;
-    int s = 0;
-    for (int i = 0; i < 32; ++i) s += p[i];
-    csum[c] = s;
+  chunk_sums(xp, K * H, csum);
+  __syncthreads();
+  if (warp < nrow) {
+    const RowJob rj = rows[warp];
+    const uint4* xv = reinterpret_cast<const uint4*>(xp + (size_t)rj.x * H);
+    const int* cs = csum + rj.x * chunks;
+    const float xs = xs_j[rj.x];
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int c = lane + 32 * it;
+      int dv = 0;
+      if (c < chunks) dv = dot32_u4(w[it], xv[2 * c], xv[2 * c + 1], 0) - 8 * cs[c];
+      for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+      if (c < chunks && (c % cpg) == 0) {
+        const int g = c / cpg;
+        P[warp * ps + g] = __fmul_rn(__fmul_rn((float)dv, sc[it]), xs);
+      }
+    }
   }
   __syncthreads();
-  group_products_any(rows, K * kDnRows, H, d.group, xp, csum, xs_j, P, ps);
-  __syncthreads();
-  if (threadIdx.x < K * kDnRows) y[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
+  if (threadIdx.x < nrow) y[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
   __syncthreads();
   if (threadIdx.x < nr) {
     const int r = r0 + threadIdx.x;
@@ -220,10 +274,13 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, DecodeBu
       add = y[threadIdx.x];  // engine.rs:436-440
     } else {
       add = 0.0f;  // expert_out = sum_k w_k * y_k in selection order (engine.rs:390-396)
-      for (int j = 0; j < K; ++j) add = __fadd_rn(add, __fmul_rn(b.selw[j], y[j * kDnRows + threadIdx.x]));
+      for (int j = 0; j < K; ++j) add = __fadd_rn(add, __fmul_rn(selw_s[j], y[j * rpc + threadIdx.x]));
     }
-    b.x[r] = __fadd_rn(b.x[r], add);
+    b.x[r] = __fadd_rn(__ldcg(b.x + r), add);
   }
+  if (!last_cta(b.counters + 2)) return;
+  float* xb = reinterpret_cast<float*>(smem);  // the tail reuses the dynamic buffer
+  norm_quant_tail(b.x, next_norm, d.dim, b.xq_attn, b.xs_attn, xb, xb + d.dim, red);
 }
 
 // ---- operators ---------------------------------------------------------------
@@ -252,11 +309,7 @@ __global__ void __launch_bounds__(kThreads) k_matmul_i4_op(float* __restrict__ o
   for (int i = threadIdx.x; i < in_dim; i += blockDim.x) xp[perm32(i)] = quant_any(x[i], inv, i, in_dim);
   if (threadIdx.x == 0) xs_s[0] = scale;
   __syncthreads();
-  for (int c = threadIdx.x; c < (in_dim >> 5); c += blockDim.x) {
-    int s = 0;
-    for (int i = 0; i < 32; ++i) s += xp[c * 32 + i];
-    csum[c] = s;
-  }
+  chunk_sums(xp, in_dim, csum);
   __syncthreads();
   const int prow = in_dim >> 1;
   for (int rb = blockIdx.x * kOpRows; rb < out_dim; rb += gridDim.x * kOpRows) {
@@ -324,37 +377,48 @@ __global__ void __launch_bounds__(kThreads) k_router_op(int32_t* idx, float* w,
 
 }  // namespace
 
-void launch_router(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s) {
-  const size_t smem = ((size_t)d.dim + 17 * (size_t)d.n_experts) * 4;
-  k_router<<<1, kThreads, smem, s>>>(d, L, layer, b);
-}
-
 static size_t gateup_smem(const Dims& d) {
-  const int ng = d.dim / d.group;
+  const size_t ng = d.dim / d.group;
   return (size_t)d.dim + (size_t)(d.dim >> 5) * 4 + (size_t)2 * kGuPairs * (ng + 1) * 4;
 }
 static size_t down_smem(const Dims& d) {
   const size_t H = d.hidden, K = d.top_k, ng = H / d.group;
-  return K * H + K * (H >> 5) * 4 + K * kDnRows * (ng + 1) * 4;
+  const size_t main = K * H + K * (H >> 5) * 4 + (size_t)kWarps * (ng + 1) * 4;
+  return std::max(main, (size_t)d.dim * 8);  // the last CTA's norm scratch
 }
 
-void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s) {
+void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s,
+                   bool pdl) {
   const size_t smem = gateup_smem(d);
-  static unsigned long long done_mask = 0;  // devices whose attributes are set
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !(done_mask & (1ull << dev))) {
-    cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    __atomic_fetch_or(&done_mask, 1ull << dev, __ATOMIC_RELAXED);
-  }
+  if (smem > 48 * 1024) cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((d.hidden + kGuPairs - 1) / kGuPairs, d.top_k);
-  k_gateup<<<grid, kThreads, smem, s>>>(d, L, b);
+  launch_k(k_gateup, grid, dim3(kThreads), smem, s, pdl, d, L, b);
 }
 
-void launch_down(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s) {
-  k_down<<<(d.dim + kDnRows - 1) / kDnRows, kThreads, down_smem(d), s>>>(d, L, b,
-                                                                        d.n_experts < 2 ? 1 : 0);
+void launch_down(const Dims& d, const LayerPtrs& L, const float* next_norm, const DecodeBufs& b,
+                 cudaStream_t s, bool pdl) {
+  const int rpc = std::max(1, kWarps / d.top_k);  // rows per CTA: one row per warp over all experts
+  const size_t smem = down_smem(d);
+  const int grid = (d.dim + rpc - 1) / rpc;
+  const int dense = d.n_experts < 2 ? 1 : 0;
+  const int it = ((d.hidden >> 5) + 31) / 32;
+#define DOWN_CALL(IT)                                                                           \
+  do {                                                                                         \
+    if (smem > 48 * 1024)                                                                      \
+      cudaFuncSetAttribute(k_down<IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    launch_k(k_down<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, next_norm, b, dense, rpc); \
+  } while (0)
+  switch (it) {
+    case 1: DOWN_CALL(1); break;
+    case 2: DOWN_CALL(2); break;
+    case 3: DOWN_CALL(3); break;
+    case 4: DOWN_CALL(4); break;
+    case 5: DOWN_CALL(5); break;
+    case 6: DOWN_CALL(6); break;
+    case 7: DOWN_CALL(7); break;
+    default: DOWN_CALL(8); break;
+  }
+#undef DOWN_CALL
 }
 
 cudaError_t op_matmul_i4(float* out, const uint8_t* wp, const float* ws, const float* x,

@@ -32,7 +32,21 @@ struct LayerPtrs {
   const float* router_w;  // [E][dim] (MoE only)
   const float* router_b;  // [E]
   const ExpertPtrs* experts;  // device table of E entries
+  ExpertPtrs ex[16];          // the same pointers as kernel parameters (E <= 16)
 };
+
+// Pointers of expert e: from the kernel parameters when E <= 16 (no memory
+// round trip), else from the device table.
+__device__ __forceinline__ ExpertPtrs expert_ptrs(const LayerPtrs& L, int E, int e) {
+  if (E <= 16) {
+    ExpertPtrs r = L.ex[0];
+#pragma unroll
+    for (int i = 1; i < 16; ++i)
+      if (i == e) r = L.ex[i];
+    return r;
+  }
+  return L.experts[e];
+}
 
 // Per-engine device buffers of the batch-1 decode path.
 struct DecodeBufs {
@@ -44,8 +58,13 @@ struct DecodeBufs {
   float* vc;         // [n_layers][max_seq][dim] f32 value cache
   const float* rope_cos;  // [max_seq][head_dim/2]
   const float* rope_sin;
+  int8_t* xq_attn;   // [dim] quantized attention input (rmsnorm(x) of this layer)
+  float* xs_attn;    // [1] its scale
+  int8_t* xq_o;      // [dim] quantized attention output (O-projection input)
+  float* xs_o;       // [1]
   int8_t* xq_ffn;    // [dim] quantized FFN input
   float* xs_ffn;     // [1] its scale
+  unsigned* counters;  // [8] last-CTA tickets, one per kernel kind
   int32_t* sel;      // [top_k] selected experts
   float* selw;       // [top_k] their weights
   float* h;          // [top_k][hidden] SwiGLU output
@@ -58,18 +77,34 @@ struct DecodeBufs {
 };
 
 // ---- decode step (batch 1) ---------------------------------------------------
-void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const DecodeBufs& b,
-                  cudaStream_t s);
-void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s);
-void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s);
-void launch_oproj(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s);
-void launch_router(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s);
-void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s);
-void launch_down(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s);
-void launch_lmhead(const Dims& d, const float* final_norm, const int8_t* w, const float* ws,
-                   const DecodeBufs& b, int num_sms, cudaStream_t s);
+// Kernels after the first of a forward are launched with programmatic
+// dependent launch (`pdl`); see pdl.cuh for the rules they follow.
+// x = embedding(token); xq_attn = quantize(rmsnorm(x, rms_attn of layer 0)).
+void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const float* rms0,
+                  const DecodeBufs& b, cudaStream_t s);
+// Q/K/V rows from xq_attn, RoPE, KV-cache write.
+void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
+                bool pdl);
+// Scores and softmax.P.V; the last CTA quantizes att_out into xq_o.
+void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl);
+void launch_scores(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl);
+void launch_pv(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl);
+// O rows from xq_o, x += ; the last CTA computes the FFN norm, xq_ffn and the routing.
+void launch_oproj(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b,
+                  cudaStream_t s, bool pdl);
+// Gate/up rows of the routed experts + SwiGLU -> h, absmax(h).
+void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s,
+                   bool pdl);
+// Down rows of every routed expert, gated combine, x += ; the last CTA computes
+// xq_attn for the next layer (rmsnorm with `next_norm`: the next layer's
+// attention norm, or the final norm after the last layer).
+void launch_down(const Dims& d, const LayerPtrs& L, const float* next_norm, const DecodeBufs& b,
+                 cudaStream_t s, bool pdl);
+// Logits from xq_attn (the final-norm input) + argmax.
+void launch_lmhead(const Dims& d, const int8_t* w, const float* ws, const DecodeBufs& b,
+                   int num_sms, cudaStream_t s, bool pdl);
 // Records the argmax of the forward and selects the next token/position.
-void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s);
+void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s, bool pdl);
 // Repetition penalty on the logits followed by a fresh argmax into st->argmax_key.
 void launch_penalty_argmax(const Dims& d, const DecodeBufs& b, const uint32_t* hist, int n_hist,
                            float penalty, cudaStream_t s);

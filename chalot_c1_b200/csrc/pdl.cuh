@@ -1,0 +1,59 @@
+// pdl.cuh — programmatic dependent launch and last-CTA helpers.
+//
+// Every decode kernel is launched with programmatic stream serialization, so
+// it can be resident while its predecessor runs. Its code is split in two:
+// before pdl_wait() it may only touch data that existed before the
+// predecessor started (weights, older KV-cache rows, and outputs of kernels
+// two or more launches back, read through L2 with __ldcg); after pdl_wait()
+// the predecessor has completed and its writes are visible. Each kernel calls
+// pdl_trigger() right after its own pdl_wait(), so when its successor starts,
+// every kernel before this one has completed.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <utility>
+
+#include "common.cuh"
+
+namespace chalot {
+
+CHALOT_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+CHALOT_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// True in exactly one CTA of the grid: the last one to get here. The other
+// CTAs' global writes made before their call are visible to it (read them
+// with __ldcg). Resets the counter for the next launch.
+__device__ __forceinline__ bool last_cta(unsigned* counter) {
+  __shared__ bool is_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned n = gridDim.x * gridDim.y * gridDim.z;
+    const unsigned t = atomicAdd(counter, 1u);
+    is_last = (t == n - 1);
+    if (is_last) atomicExch(counter, 0u);
+  }
+  __syncthreads();
+  if (is_last) __threadfence();
+  return is_last;
+}
+
+// Launches `k` with programmatic stream serialization when `pdl` is set.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+}
+
+}  // namespace chalot

@@ -117,6 +117,20 @@ class Engine:
         return {"prefill_ms": a.value, "decode_ms": b.value, "n_prefill": n1.value,
                 "n_decode": n2.value}
 
+    def profile_forward(self, token: int, pos: int) -> dict:
+        """Per-kernel device ms of one forward, summed by kernel kind."""
+        n = 2 + 6 * self.config["n_layers"] + 1
+        ms = np.zeros(n, np.float32)
+        cnt = C.c_int()
+        check(lib().chalot_profile_forward(self._h, token, pos, ms.ctypes.data_as(C.c_void_p), n,
+                                           C.byref(cnt)))
+        names = ["embed"] + ["qkv", "attn_scores", "attn_pv", "oproj_route", "gateup", "down"] * \
+            self.config["n_layers"] + ["lmhead"]
+        out: dict = {}
+        for k, v in zip(names, ms[: cnt.value]):
+            out[k] = out.get(k, 0.0) + float(v)
+        return out
+
     def bench_moe_layers(self, reps: int = 20) -> tuple[float, float]:
         ms, by = C.c_double(), C.c_double()
         check(lib().chalot_bench_moe_layers(self._h, reps, C.byref(ms), C.byref(by)))

@@ -135,12 +135,20 @@ int chalot_get_logits(chalot_engine* e, float* dst, size_t n);
 int chalot_last_timing(chalot_engine* e, double* prefill_ms, double* decode_ms,
                        uint32_t* n_prefill, uint32_t* n_decode);
 
-/* Expert path of every layer at batch 1 (gate/up + down of top_k experts,
- * expert ids chosen round-robin per layer so successive layers stream
- * different weights), captured once and replayed `reps` times: mean device
- * time per layer and the weight bytes one layer streams. */
+/* Expert path of every layer at batch 1 (routing + gate/up + down of the
+ * top_k experts the router picks from the engine's current residual, on a
+ * private copy of it), captured once and replayed `reps` times: mean device
+ * time per layer and the expert weight bytes one layer streams. */
 int chalot_bench_moe_layers(chalot_engine* e, int reps, double* ms_per_layer,
                             double* bytes_per_layer);
+
+/* Device time of every kernel of one forward (token, pos), in launch order:
+ * embed, then per layer qkv, attention scores, attention softmax.PV, O
+ * projection (+ routing), gate/up, down; then lm_head. Runs the forward twice
+ * from a graph with an event after each kernel (no programmatic overlap) and
+ * reports the second run. *n_out = 1 + 6*n_layers + 1. */
+int chalot_profile_forward(chalot_engine* e, uint32_t token, uint32_t pos, float* ms, int cap,
+                           int* n_out);
 
 /* ---- operators (device pointers, caller-owned memory) ------------------- */
 /* `stream` is a cudaStream_t (NULL = the legacy default stream). The input
