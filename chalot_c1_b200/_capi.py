@@ -9,7 +9,7 @@ import ctypes as C
 import os
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_PKG, "_lib", "libchalot_b200.so")
+LIB_PATH = os.environ.get("CHALOT_LIB") or os.path.join(_PKG, "_lib", "libchalot_b200.so")
 
 CHALOT_OK = 0
 ERRORS = {-1: "CHALOT_ERR_ARG", -2: "CHALOT_ERR_IO", -3: "CHALOT_ERR_FORMAT",

@@ -20,9 +20,12 @@ import sys
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
-BUILD = os.path.join(PKG, "_build")
 LIBDIR = os.path.join(PKG, "_lib")
-LIB = os.path.join(LIBDIR, "libchalot_b200.so")
+# `python -m chalot_c1_b200.build --trace` builds a second library with the
+# per-CTA phase trace compiled in (CHALOT_PHASE_TRACE; chalot_phase_trace()).
+TRACE = os.environ.get("CHALOT_BUILD_TRACE") == "1"
+BUILD = os.path.join(PKG, "_build_trace" if TRACE else "_build")
+LIB = os.path.join(LIBDIR, "libchalot_b200_trace.so" if TRACE else "libchalot_b200.so")
 INCLUDE = os.path.join(os.path.dirname(PKG), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -56,7 +59,7 @@ def _compile(src: str, verbose: bool, ptxas_v: bool):
     if src.endswith(".cu"):
         cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "--fmad=false", "-std=c++17",
                "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I", CSRC, "-I", INCLUDE,
-               "-c", src, "-o", obj]
+               "-c", src, "-o", obj] + (["-DCHALOT_PHASE_TRACE"] if TRACE else [])
         if ptxas_v:
             cmd[1:1] = ["-Xptxas", "-v"]
     else:
@@ -99,5 +102,10 @@ if __name__ == "__main__":
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true", help="print register/smem use per kernel")
+    ap.add_argument("--trace", action="store_true", help="build the phase-trace library instead")
     a = ap.parse_args()
+    if a.trace and not TRACE:
+        os.environ["CHALOT_BUILD_TRACE"] = "1"
+        os.execv(sys.executable, [sys.executable, "-m", "chalot_c1_b200.build"] +
+                 [x for x in sys.argv[1:] if x != "--trace"])
     print(build(a.force, a.verbose, a.ptxas_v))

@@ -6,24 +6,61 @@
 
 namespace chalot {
 
-// Copies n floats (n % 4 == 0, 16-byte aligned) from global to shared memory
-// with every load of a thread issued before any store.
-__device__ __forceinline__ void load_f32(float* dst, const float* __restrict__ src, int n) {
-  const float4* s4 = reinterpret_cast<const float4*>(src);
-  float4* d4 = reinterpret_cast<float4*>(dst);
-  const int n4 = n >> 2;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = s4[i];
+// Copies n 16-byte elements from global memory to shared memory: each
+// thread issues up to 8 loads before its stores, so a copy costs about one
+// memory latency per 8*blockDim elements (through L2 only when `coherent`:
+// for data other CTAs of the running grid wrote).
+template <typename V>
+__device__ __forceinline__ void copy16(V* __restrict__ dst, const V* __restrict__ src, int n,
+                                       bool coherent) {
+  constexpr int U = 8;
+  for (int base = 0; base < n; base += U * (int)blockDim.x) {
+    V v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+      if (i < n) v[u] = coherent ? __ldcg(src + i) : __ldg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+      if (i < n) dst[i] = v[u];
+    }
+  }
 }
 
-// Same, reading through L2 only (__ldcg): for data other CTAs of the running
-// grid wrote, which the L1 of this SM may hold stale.
+// n floats (n % 4 == 0, 16-byte aligned) from global to shared memory.
+__device__ __forceinline__ void load_f32(float* dst, const float* __restrict__ src, int n) {
+  copy16(reinterpret_cast<float4*>(dst), reinterpret_cast<const float4*>(src), n >> 2, false);
+}
 __device__ __forceinline__ void load_f32_cg(float* dst, const float* src, int n) {
-  const float4* s4 = reinterpret_cast<const float4*>(src);
-  float4* d4 = reinterpret_cast<float4*>(dst);
-  const int n4 = n >> 2;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = __ldcg(s4 + i);
+  copy16(reinterpret_cast<float4*>(dst), reinterpret_cast<const float4*>(src), n >> 2, true);
+}
+
+// Quantizes n floats (n % 4 == 0) that other CTAs just wrote with a known
+// scale reciprocal into natural-order int8 words in global memory; loads are
+// batched 8 float4 per thread before the stores.
+__device__ __forceinline__ void quant_store_words(uint32_t* __restrict__ dst, const float4* src, int n4,
+                                                  float inv, int n) {
+  constexpr int U = 8;
+  for (int base = 0; base < n4; base += U * (int)blockDim.x) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+      if (i < n4) v[u] = __ldcg(src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i4 = base + u * (int)blockDim.x + (int)threadIdx.x;
+      if (i4 < n4) {
+        const int i = i4 * 4;
+        const uint32_t q0 = (uint8_t)quant_any(v[u].x, inv, i, n), q1 = (uint8_t)quant_any(v[u].y, inv, i + 1, n);
+        const uint32_t q2 = (uint8_t)quant_any(v[u].z, inv, i + 2, n), q3 = (uint8_t)quant_any(v[u].w, inv, i + 3, n);
+        dst[i4] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+      }
+    }
+  }
 }
 
 // rmsnorm_avx2 (src/tensor/normalization.rs:35-67) of x into xb (shared):
@@ -42,9 +79,16 @@ __device__ __forceinline__ void rmsnorm_smem(const float* x, const float* __rest
   const int chunks = dim >> 3;
   if (threadIdx.x < 8) {
     float s = 0.0f;
-#pragma unroll 8
-    for (int c = 0; c < chunks; ++c) {
-      float v = xb[c * 8 + threadIdx.x];
+    int c = 0;
+    for (; c + 8 <= chunks; c += 8) {  // 8 independent loads, then 8 dependent adds
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = xb[(c + u) * 8 + threadIdx.x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s = __fadd_rn(s, __fmul_rn(v[u], v[u]));
+    }
+    for (; c < chunks; ++c) {
+      const float v = xb[c * 8 + threadIdx.x];
       s = __fadd_rn(s, __fmul_rn(v, v));
     }
     red[threadIdx.x] = s;
@@ -78,6 +122,7 @@ __device__ __forceinline__ void norm_quant_tail(const float* x, const float* __r
                                                 int8_t* q_out, float* s_out, float* xb, float* wbuf,
                                                 float* red) {
   rmsnorm_smem(x, w, dim, xb, wbuf, red, true);
+
   float scale, inv;
   quant_scale(absmax_smem(xb, dim, red), &scale, &inv);
   for (int i = threadIdx.x; i < dim; i += blockDim.x) q_out[i] = quant_any(xb[i], inv, i, dim);
@@ -101,51 +146,57 @@ __device__ __forceinline__ int perm32(int i) {
   return chunk * 32 + ((t & 1) ? 16 : 0) + j * 4 + (t >> 1);
 }
 
-// softmax_avx2 over s[0..n) in place, serial (n is small):
-// fast_exp on the whole 8-chunks, libm exp on the tail, 8-lane sums + hsum8
-// (src/tensor/normalization.rs:106-160).
-__device__ __forceinline__ void softmax_serial(float* s, int n) {
-  if (n <= 0) return;
-  float mx = -INFINITY;
-  for (int i = 0; i < n; ++i) mx = fmaxf(mx, s[i]);
+// softmax_top_k (src/tensor/normalization.rs:203-216) of s[0..n) (n <= 32)
+// by one warp, in the reference's arithmetic order: softmax_avx2 with
+// fast_exp on whole 8-chunks and libm exp on the tail, 8-lane sums combined
+// by hsum8 (normalization.rs:106-160); then the k largest probabilities in
+// descending order, lower index first among equal values (the insertion sort
+// behind sort_unstable_by for <= 20 elements), renormalised by their sum when
+// it exceeds 1e-12. Called by all 32 lanes of one warp.
+__device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t* idx, float* w) {
+  const int lane = threadIdx.x & 31;
+  const float v = lane < n ? s[lane] : -INFINITY;
+  const float mx = warp_max(v);
   const int full = n & ~7;
-  float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  for (int i = 0; i < full; ++i) {
-    const float e = fast_exp(__fsub_rn(s[i], mx));
-    s[i] = e;
-    lanes[i & 7] = __fadd_rn(lanes[i & 7], e);
+  float e = 0.0f;
+  if (lane < n) e = (lane < full) ? fast_exp(__fsub_rn(v, mx)) : expf_cr(__fsub_rn(v, mx));
+  // lane j < 8 accumulates e[8c + j] over c in order
+  float acc = 0.0f;
+  for (int c = 0; c < (full >> 3); ++c) {
+    const float t = __shfl_sync(0xffffffffu, e, c * 8 + (lane & 7));
+    acc = __fadd_rn(acc, t);
   }
-  float sum = hsum8(lanes);
-  for (int i = full; i < n; ++i) {
-    const float e = expf_cr(__fsub_rn(s[i], mx));
-    s[i] = e;
-    sum = __fadd_rn(sum, e);
-  }
-  const float inv = __fdiv_rn(1.0f, sum);
-  for (int i = 0; i < n; ++i) s[i] = __fmul_rn(s[i], inv);
-}
-
-// softmax_top_k (src/tensor/normalization.rs:203-216) by one thread: the k
-// largest probabilities in descending order, lower index first among equal
-// values (what the insertion sort behind sort_unstable_by does for <= 20
-// elements), renormalised by their sum when it exceeds 1e-12.
-__device__ __forceinline__ void topk_serial(float* s, int n, int k, int32_t* idx, float* w) {
-  softmax_serial(s, n);
-  uint64_t taken = 0;  // n <= 64
-  float sum = -0.0f;
+  float l8[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) l8[j] = __shfl_sync(0xffffffffu, acc, j);
+  float sum = hsum8(l8);
+  for (int i = full; i < n; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, i));
+  const float p = __fmul_rn(e, __fdiv_rn(1.0f, sum));
+  // k rounds of (max probability, lowest index)
+  bool taken = lane >= n;
+  float tot = -0.0f;
   for (int j = 0; j < k; ++j) {
-    int best = -1;
-    for (int i = 0; i < n; ++i) {
-      if (taken & (1ull << i)) continue;
-      if (best < 0 || s[i] > s[best]) best = i;
+    float bv = taken ? -INFINITY : p;
+    int bi = taken ? 0x7fffffff : lane;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
     }
-    taken |= 1ull << best;
-    idx[j] = best;
-    w[j] = s[best];
-    sum = __fadd_rn(sum, s[best]);
+    if (lane == bi) taken = true;
+    tot = __fadd_rn(tot, bv);
+    if (lane == 0) {
+      idx[j] = bi;
+      w[j] = bv;
+    }
   }
-  if (sum > 1e-12f)
-    for (int j = 0; j < k; ++j) w[j] = __fdiv_rn(w[j], sum);
+  __syncwarp();
+  if (lane == 0 && tot > 1e-12f)
+    for (int j = 0; j < k; ++j) w[j] = __fdiv_rn(w[j], tot);
 }
 
 // Router logits of one token: logit[e] = b[e] + dot_f32(W[e], xb) with the

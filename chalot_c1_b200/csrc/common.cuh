@@ -167,13 +167,38 @@ CHALOT_DEV int dot32_u4(uint4 w, const uint4& xe, const uint4& xo, int acc) {
   return acc;
 }
 
-// Streaming 16-byte load that bypasses L1 allocation (weights are read once).
-CHALOT_DEV uint4 ldg_stream(const void* p) {
-  uint4 r;
-  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
-  return r;
+// Repacked int4 layout used by the engine (applied once at load): in every
+// 32-bit word (8 columns 8j..8j+7) byte b holds column 8j+b in its low nibble
+// and column 8j+4+b in its high nibble, each as a 4-bit two's complement
+// value. Then (w << 4) & 0xF0F0F0F0 is 16*w for columns 8j..8j+3 and
+// w & 0xF0F0F0F0 is 16*w for columns 8j+4..8j+7, as signed bytes, so dp4a
+// against the activations in natural order gives 16 * the exact int32 dot.
+CHALOT_DEV uint32_t repack_word(uint32_t w) {
+  const uint32_t lo0 = w & 0xF, hi0 = (w >> 4) & 0xF, lo1 = (w >> 8) & 0xF, hi1 = (w >> 12) & 0xF;
+  const uint32_t lo2 = (w >> 16) & 0xF, hi2 = (w >> 20) & 0xF, lo3 = (w >> 24) & 0xF, hi3 = (w >> 28) & 0xF;
+  // columns 0..7 of the word in the file: lo0 hi0 lo1 hi1 lo2 hi2 lo3 hi3 (value + 8)
+  const uint32_t b0 = lo0 | (lo2 << 4), b1 = hi0 | (hi2 << 4), b2 = lo1 | (lo3 << 4), b3 = hi1 | (hi3 << 4);
+  return (b0 | (b1 << 8) | (b2 << 16) | (b3 << 24)) ^ 0x88888888u;  // value + 8 -> two's complement
 }
+
+// Exact int32 dot of 32 repacked int4 weights (one uint4) with 32 int8
+// activations in natural order (x0: columns 0..15, x1: columns 16..31).
+CHALOT_DEV int dot32_rp(uint4 w, const uint4& x0, const uint4& x1) {
+  const uint32_t m = 0xF0F0F0F0u;
+  int acc = 0;
+  acc = __dp4a((int)((w.x << 4) & m), (int)x0.x, acc);
+  acc = __dp4a((int)(w.x & m), (int)x0.y, acc);
+  acc = __dp4a((int)((w.y << 4) & m), (int)x0.z, acc);
+  acc = __dp4a((int)(w.y & m), (int)x0.w, acc);
+  acc = __dp4a((int)((w.z << 4) & m), (int)x1.x, acc);
+  acc = __dp4a((int)(w.z & m), (int)x1.y, acc);
+  acc = __dp4a((int)((w.w << 4) & m), (int)x1.z, acc);
+  acc = __dp4a((int)(w.w & m), (int)x1.w, acc);
+  return acc >> 4;  // every product is 16 * w * x: the division is exact
+}
+
+// Streaming 16-byte load of a weight (read once: evict-first). A compiler
+// builtin, so it stays ordered with the griddepcontrol barriers.
+CHALOT_DEV uint4 ldg_stream(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
 
 }  // namespace chalot

@@ -31,6 +31,7 @@
 #include "capi_internal.h"
 #include "kernels.cuh"
 #include "myai.h"
+#include "pdl.cuh"
 
 namespace chalot {
 
@@ -83,6 +84,17 @@ class MappedFile {
 };
 
 }  // namespace chalot
+
+#ifdef CHALOT_PHASE_TRACE
+namespace chalot {
+cudaError_t trace_dense(unsigned long long*, size_t);
+cudaError_t trace_moe(unsigned long long*, size_t);
+cudaError_t trace_attn(unsigned long long*, size_t);
+cudaError_t trace_dense_clear();
+cudaError_t trace_moe_clear();
+cudaError_t trace_attn_clear();
+}  // namespace chalot
+#endif
 
 using namespace chalot;
 
@@ -161,9 +173,9 @@ struct chalot_engine {
       mark();
       launch_oproj(d, L, l, b, s, pdl);
       mark();
-      launch_gateup(d, L, b, s, pdl);
+      launch_gateup(d, L, l, b, s, pdl);
       mark();
-      launch_down(d, L, next_norm, b, s, pdl);
+      launch_down(d, L, l, next_norm, b, s, pdl);
       mark();
     }
     launch_lmhead(d, out_w, out_s, b, num_sms, s, pdl);
@@ -231,7 +243,7 @@ bool check_shapes(const ModelConfig& c, std::string* err) {
   if (c.top_k * c.hidden_dim > 16384) return bad("top_k * hidden_dim above 16384");
   if (c.int4_group_size > 1024 || (c.int4_group_size & (c.int4_group_size - 1)))
     return bad("int4_group_size must be a power of two in [32, 1024]");
-  if (c.n_experts > 64) return bad("more than 64 experts");
+  if (c.n_experts > 32) return bad("more than 32 experts");
   if (c.top_k > 8) return bad("top_k above 8");
   if (c.vocab_size >= (1u << 31)) return bad("vocab too large");
   return true;
@@ -390,6 +402,14 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
       e->layers.push_back(L);
     }
     CK(cudaMemcpy(e->d_experts, all.data(), all.size() * sizeof(ExpertPtrs), cudaMemcpyHostToDevice));
+    // expert int4 rows: file layout -> the kernels' repacked layout, once
+    for (size_t l = 0; l < c.n_layers; ++l)
+      for (size_t x = 0; x < E; ++x) {
+        const ExpertIndex& X = ix.layers[l].experts[x];
+        CK(repack_int4(W + loff[l].ex[x][0], X.gate_up_packed_bytes, e->stream));
+        CK(repack_int4(W + loff[l].ex[x][2], X.down_packed_bytes, e->stream));
+      }
+    CK(cudaStreamSynchronize(e->stream));
 
     // ---- RoPE tables (state.rs:53-60), computed with glibc powf/cosf/sinf ----
     const size_t half = c.head_dim / 2;
@@ -427,6 +447,8 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.h = e->dalloc<float>(std::max<size_t>(c.top_k, 1) * H);
     b.amax = e->dalloc<unsigned>(std::max<size_t>(c.top_k, 1));
+    b.xq_h = e->dalloc<int8_t>(std::max<size_t>(c.top_k, 1) * H);
+    b.xs_h = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.logits = e->dalloc<float>(V);
     b.st = e->dalloc<StepState>(1);
     b.prompt = e->dalloc<uint32_t>(c.max_seq_len);
@@ -678,8 +700,8 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
       bl.sel = sel + l * K;
       bl.selw = selw + l * K;
       CK(cudaMemsetAsync(bl.amax, 0, sizeof(unsigned) * K, e->stream));
-      launch_gateup(d, e->layers[l], bl, e->stream, false);
-      launch_down(d, e->layers[l], e->layers[l].rms_attn, bl, e->stream, true);
+      launch_gateup(d, e->layers[l], l, bl, e->stream, false);
+      launch_down(d, e->layers[l], l, e->layers[l].rms_attn, bl, e->stream, true);
     }
     CK(cudaStreamEndCapture(e->stream, &g));
     CK(cudaGraphInstantiate(&ex, g, 0));
@@ -702,6 +724,29 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
   }
   return CHALOT_OK;
 }
+
+#ifdef CHALOT_PHASE_TRACE
+// Copies the phase trace of the forwards since the last clear (instrumented
+// builds only): [slot = layer*8 + kind][cta][phase] %globaltimer values.
+__attribute__((visibility("default"))) int chalot_phase_trace(unsigned long long* dst, size_t n) {
+  n = std::min(n, (size_t)kTraceSlots * kTraceCtas * kTracePhases);
+  std::vector<unsigned long long> tmp(n);
+  std::memset(dst, 0, n * 8);
+  for (auto fn : {trace_dense, trace_moe, trace_attn}) {
+    cudaError_t r = fn(tmp.data(), n);
+    if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, cudaGetErrorString(r));
+    for (size_t i = 0; i < n; ++i) dst[i] += tmp[i];
+  }
+  return CHALOT_OK;
+}
+__attribute__((visibility("default"))) int chalot_phase_trace_clear(void) {
+  for (auto fn : {trace_dense_clear, trace_moe_clear, trace_attn_clear}) {
+    cudaError_t r = fn();
+    if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, cudaGetErrorString(r));
+  }
+  return CHALOT_OK;
+}
+#endif
 
 __attribute__((visibility("default"))) int chalot_profile_forward(chalot_engine* e, uint32_t token,
                                                                   uint32_t pos, float* ms, int cap,
@@ -789,8 +834,8 @@ __attribute__((visibility("default"))) int chalot_router_topk(int32_t* idx, floa
                                                               size_t dim, size_t n_experts,
                                                               size_t top_k, void* stream) {
   if (!idx || !weight || !x || !w || !b) return set_error(CHALOT_ERR_ARG, "null pointer");
-  if (n_experts == 0 || top_k == 0 || top_k > n_experts || n_experts > 64)
-    return set_error(CHALOT_ERR_ARG, "need 1 <= top_k <= n_experts <= 64");
+  if (n_experts == 0 || top_k == 0 || top_k > n_experts || n_experts > 32)
+    return set_error(CHALOT_ERR_ARG, "need 1 <= top_k <= n_experts <= 32");
   if (n_tok == 0) return CHALOT_OK;
   cudaError_t r = op_router_topk(idx, weight, x, w, b, n_tok, dim, n_experts, top_k,
                                  static_cast<cudaStream_t>(stream));

@@ -37,6 +37,8 @@ __device__ __forceinline__ void load_k_row(const float* k, float4 (&kr)[C16 * 4]
 template <int C16>  // head_dim / 16
 __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer, DecodeBufs b) {
   __shared__ __align__(16) float qh[256];
+  const int slot = layer * 8 + 1;
+  CHALOT_TRACE(slot, 0);
   const int h = blockIdx.y, hd = d.head_dim;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t pos = b.st->pos;
@@ -44,8 +46,10 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer
   float4 kr[C16 * 4];
   // rows before pos were written by earlier forwards: load them before waiting
   if ((uint32_t)t < pos) load_k_row<C16>(k, kr);
+  CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
+  CHALOT_TRACE(slot, 2);
   if (blockIdx.x * blockDim.x > pos) return;  // whole CTA beyond the causal range
   for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = __ldcg(b.q + h * hd + i);
   __syncthreads();
@@ -85,16 +89,31 @@ constexpr int kPvTile = 1024;  // V rows staged in shared memory at a time
 
 __device__ __forceinline__ void stage_v(float* vt, const float* vbase, int dim, int t0, int rows,
                                         bool coherent) {
-#pragma unroll 8
-  for (int i = threadIdx.x; i < rows * (kPvCols / 4); i += blockDim.x) {
-    const int r = i / (kPvCols / 4), q = i % (kPvCols / 4);
-    const float4* src = reinterpret_cast<const float4*>(vbase + (size_t)(t0 + r) * dim + q * 4);
-    reinterpret_cast<float4*>(vt)[i] = coherent ? __ldcg(src) : *src;
+  constexpr int U = 8;
+  const int n = rows * (kPvCols / 4);
+  for (int base = 0; base < n; base += U * kPvThreads) {
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * kPvThreads + (int)threadIdx.x;
+      if (i < n) {
+        const int r = i / (kPvCols / 4), q = i % (kPvCols / 4);
+        const float4* src = reinterpret_cast<const float4*>(vbase + (size_t)(t0 + r) * dim + q * 4);
+        v[u] = coherent ? __ldcg(src) : __ldg(src);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int i = base + u * kPvThreads + (int)threadIdx.x;
+      if (i < n) reinterpret_cast<float4*>(vt)[i] = v[u];
+    }
   }
 }
 
 __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, DecodeBufs b) {
   extern __shared__ __align__(16) float sm[];
+  const int slot = layer * 8 + 2;
+  CHALOT_TRACE(slot, 0);
   float* p = sm;                            // [max_seq] probabilities
   float* vt = sm + ((d.max_seq + 3) & ~3);  // [kPvTile][kPvCols] staged V (16-B aligned)
   __shared__ float red[40];
@@ -104,17 +123,27 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   const float* vbase = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + c0;
   // V rows 0..n-2 of the first tile were written by earlier forwards
   stage_v(vt, vbase, d.dim, 0, min(n - 1, kPvTile), false);
+  CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
+  CHALOT_TRACE(slot, 2);
   if (n - 1 < kPvTile) stage_v(vt + (n - 1) * kPvCols, vbase, d.dim, n - 1, 1, true);
   const float* s = b.scores + (size_t)h * d.max_seq;
   // softmax_avx2 over the n scores of this head (normalization.rs:106-160)
   float mx = -INFINITY;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = __ldcg(s + i);
-    p[i] = v;
-    mx = fmaxf(mx, v);
+  for (int base = 0; base < n; base += 8 * kPvThreads) {  // 8 loads in flight per thread
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * kPvThreads + (int)threadIdx.x;
+      v[u] = i < n ? __ldcg(s + i) : -INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * kPvThreads + (int)threadIdx.x;
+      if (i < n) p[i] = v[u];
+      mx = fmaxf(mx, v[u]);
+    }
   }
   mx = block_max(mx, red);
   const int full = n & ~7;
@@ -123,8 +152,16 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   __syncthreads();
   if (threadIdx.x < 8) {  // lane j sums elements 8c+j in c order
     float acc = 0.0f;
-#pragma unroll 8
-    for (int c = 0; c < (full >> 3); ++c) acc = __fadd_rn(acc, p[c * 8 + threadIdx.x]);
+    int c = 0;
+    const int nc = full >> 3;
+    for (; c + 8 <= nc; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = p[(c + u) * 8 + threadIdx.x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; c < nc; ++c) acc = __fadd_rn(acc, p[c * 8 + threadIdx.x]);
     red[threadIdx.x] = acc;
   }
   __syncthreads();
@@ -139,6 +176,7 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   const float inv = inv_s;
   for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
   __syncthreads();
+  CHALOT_TRACE(slot, 3);
   // out[c] = sum_t p_t * V[t][c], added in t order (engine.rs:302-308)
   float acc = 0.0f;
   for (int t0 = 0; t0 < n; t0 += kPvTile) {
@@ -150,13 +188,23 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
     }
     if (threadIdx.x < kPvCols) {
       const float* pv = p + t0;
-#pragma unroll 8
-      for (int t = 0; t < rows; ++t) acc = __fadd_rn(acc, __fmul_rn(pv[t], vt[t * kPvCols + threadIdx.x]));
+      int t = 0;
+      for (; t + 16 <= rows; t += 16) {  // 16 products first, then 16 dependent adds
+        float pr[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) pr[u] = __fmul_rn(pv[t + u], vt[(t + u) * kPvCols + threadIdx.x]);
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, pr[u]);
+      }
+      for (; t < rows; ++t) acc = __fadd_rn(acc, __fmul_rn(pv[t], vt[t * kPvCols + threadIdx.x]));
     }
   }
   if (threadIdx.x < kPvCols) b.att_out[h * hd + c0 + threadIdx.x] = acc;
+  CHALOT_TRACE(slot, 4);
   // the last CTA quantizes the finished att_out for the O projection
-  if (!last_cta(b.counters + 0)) return;
+  const bool tail = last_cta(b.counters + 0);
+  CHALOT_TRACE(slot, 5);
+  if (!tail) return;
   float* a = sm;  // reuse
   load_f32_cg(a, b.att_out, d.dim);
   __syncthreads();
@@ -164,6 +212,7 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   quant_scale(absmax_smem(a, d.dim, red), &scale, &qinv);
   for (int i = threadIdx.x; i < d.dim; i += blockDim.x) b.xq_o[i] = quant_any(a[i], qinv, i, d.dim);
   if (threadIdx.x == 0) *b.xs_o = scale;
+  CHALOT_TRACE(slot, 6);
 }
 
 }  // namespace
@@ -201,5 +250,9 @@ void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_
   launch_scores(d, layer, b, s, pdl);
   launch_pv(d, layer, b, s, pdl);
 }
+
+#ifdef CHALOT_PHASE_TRACE
+CHALOT_TRACE_EXPORT(trace_attn)
+#endif
 
 }  // namespace chalot

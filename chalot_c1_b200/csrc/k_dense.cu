@@ -90,9 +90,7 @@ __device__ __forceinline__ void rows_dot_i8_loop(const int8_t* __restrict__ W, i
 // Copies a quantized vector (n bytes, n % 16 == 0) produced by another grid
 // into shared memory through L2.
 __device__ __forceinline__ void load_q(int8_t* dst, const int8_t* src, int n) {
-  const uint4* s4 = reinterpret_cast<const uint4*>(src);
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
-  for (int i = threadIdx.x; i < (n >> 4); i += blockDim.x) d4[i] = __ldcg(s4 + i);
+  copy16(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n >> 4, true);
 }
 
 // ---------------------------------------------------------------------------
@@ -118,6 +116,8 @@ constexpr int kQkvRows = 2;  // rows per warp: one RoPE pair
 template <int IT>
 __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
   __shared__ __align__(16) int8_t xq[512 * IT];
+  const int slot = layer * 8 + 0;
+  CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5;
   const int r0 = (blockIdx.x * kWarps + warp) * kQkvRows;
   const int n_rows = 3 * d.dim;
@@ -136,10 +136,13 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer
       sn = b.rope_sin[pos * half + i];
     }
   }
+  CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
+  CHALOT_TRACE(slot, 2);
   load_q(xq, b.xq_attn, d.dim);
   __syncthreads();
+  CHALOT_TRACE(slot, 3);
   if (r0 >= n_rows) return;
   const float xs = __ldcg(b.xs_attn);
   int acc[kQkvRows];
@@ -176,14 +179,19 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   extern __shared__ __align__(16) float osm[];  // tail scratch: xb, wbuf [dim] each, lanes [16E], logit [E]
   __shared__ __align__(16) int8_t xq[512 * IT];
   __shared__ float red[40];
+  const int slot = layer * 8 + 3;
+  CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = (blockIdx.x * kWarps + warp) * kORows;
   uint4 w[kORows][IT];
   rows_load_i8<kORows, IT>(L.o, d.dim, r0, d.dim, w);
+  CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
+  CHALOT_TRACE(slot, 2);
   load_q(xq, b.xq_o, d.dim);
   __syncthreads();
+  CHALOT_TRACE(slot, 3);
   if (r0 < d.dim) {
     const float xs = __ldcg(b.xs_o);
     int acc[kORows];
@@ -197,27 +205,35 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
       b.x[r] = __fadd_rn(__ldcg(b.x + r), v);  // residual (engine.rs:320-322)
     }
   }
-  if (!last_cta(b.counters + 1)) return;
+  CHALOT_TRACE(slot, 4);
+  const bool tail = last_cta(b.counters + 1);
+  CHALOT_TRACE(slot, 5);
+  if (!tail) return;
   const int E = d.n_experts;
   float* xb = osm;
   float* wbuf = osm + d.dim;
   float* lanes = wbuf + d.dim;
   float* logit = lanes + 16 * E;
   float* rw = logit + ((E + 3) & ~3);  // [E][dim] router weights staged before the norm
+  const int tslot = layer * 8 + 6;
+  CHALOT_TRACE(tslot, 0);
   if (E >= 2) load_f32(rw, L.router_w, E * d.dim);
+  CHALOT_TRACE(tslot, 1);
   norm_quant_tail(b.x, L.rms_ffn, d.dim, b.xq_ffn, b.xs_ffn, xb, wbuf, red);
+  CHALOT_TRACE(tslot, 2);
   if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;
   if (E >= 2) {
     router_logits(rw, L.router_b, xb, d.dim, E, lanes, logit);
-    if (threadIdx.x == 0) {
-      if (b.router_trace)
-        for (int e = 0; e < E; ++e) b.router_trace[layer * E + e] = logit[e];
-      topk_serial(logit, E, d.top_k, b.sel, b.selw);
-    }
+    CHALOT_TRACE(tslot, 3);
+    if (threadIdx.x < 32) topk_warp(logit, E, d.top_k, b.sel, b.selw);
+    CHALOT_TRACE(tslot, 4);
+    if (b.router_trace)
+      for (int e = threadIdx.x; e < E; e += blockDim.x) b.router_trace[layer * E + e] = logit[e];
   } else if (threadIdx.x == 0) {
     b.sel[0] = 0;
     b.selw[0] = 1.0f;
   }
+  CHALOT_TRACE(slot, 6);
 }
 
 constexpr int kLmRows = 4;
@@ -461,5 +477,9 @@ cudaError_t op_quantize_i8(int8_t* q, float* scale, const float* x, size_t n_vec
   k_quantize_op<<<(unsigned)n_vec, kThreads, 0, s>>>(q, scale, x, (int)n);
   return cudaGetLastError();
 }
+
+#ifdef CHALOT_PHASE_TRACE
+CHALOT_TRACE_EXPORT(trace_dense)
+#endif
 
 }  // namespace chalot

@@ -45,6 +45,7 @@ __device__ __forceinline__ void group_products(const RowJob* rows, int nrows, in
                                                float* P, int ps) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunks = in_dim >> 5, cpg = group >> 5;
+  const int gsh = __ffs(cpg) - 1;  // group % 32 == 0 and a power of two: c / cpg == c >> gsh
   for (int r0 = warp * R; r0 < nrows; r0 += kWarps * R) {
     for (int cb = 0; cb < chunks; cb += 32 * IT) {
       uint4 w[R][IT];
@@ -56,7 +57,7 @@ __device__ __forceinline__ void group_products(const RowJob* rows, int nrows, in
           const int c = cb + it * 32 + lane;
           const bool ok = c < chunks && r0 + i < nrows;
           w[i][it] = ok ? ldg_stream(rows[r0 + i].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-          sc[i][it] = ok ? __ldg(rows[r0 + i].s + c / cpg) : 0.0f;  // this chunk's group scale
+          sc[i][it] = ok ? __ldg(rows[r0 + i].s + (c >> gsh)) : 0.0f;  // this chunk's group scale
         }
 #pragma unroll
       for (int it = 0; it < IT; ++it) {
@@ -71,8 +72,8 @@ __device__ __forceinline__ void group_products(const RowJob* rows, int nrows, in
           if (c < chunks) dv = dot32_u4(w[i][it], xv[2 * c], xv[2 * c + 1], 0) - 8 * csum[xsel * chunks + c];
           // the chunks of one group sit in consecutive lanes: reduce them exactly
           for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-          if (live && c < chunks && (c % cpg) == 0)
-            P[(r0 + i) * ps + c / cpg] = __fmul_rn(__fmul_rn((float)dv, sc[i][it]), xs[xsel]);
+          if (live && c < chunks && (c & (cpg - 1)) == 0)
+            P[(r0 + i) * ps + (c >> gsh)] = __fmul_rn(__fmul_rn((float)dv, sc[i][it]), xs[xsel]);
         }
       }
     }
@@ -91,11 +92,82 @@ __device__ __forceinline__ void group_products_any(const RowJob* rows, int nrows
     group_products<1, 8>(rows, nrows, in_dim, group, xp, csum, xs, P, ps);
 }
 
+// group_products for the engine's repacked weights (repack_word) against a
+// natural-order quantized vector: no per-chunk sums, no permutation.
+template <int R, int IT>
+__device__ __forceinline__ void group_products_rp(const RowJob* rows, int nrows, int in_dim,
+                                                  int group, const int8_t* xq, const float* xs,
+                                                  float* P, int ps, int tslot = -1) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int chunks = in_dim >> 5, cpg = group >> 5;
+  const int gsh = __ffs(cpg) - 1;  // group % 32 == 0 and a power of two: c / cpg == c >> gsh
+  for (int r0 = warp * R; r0 < nrows; r0 += kWarps * R) {
+    for (int cb = 0; cb < chunks; cb += 32 * IT) {
+      uint4 w[R][IT];
+      float sc[R][IT];
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+#pragma unroll
+        for (int it = 0; it < IT; ++it) {
+          const int c = cb + it * 32 + lane;
+          const bool ok = c < chunks && r0 + i < nrows;
+          w[i][it] = ok ? ldg_stream(rows[r0 + i].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+          sc[i][it] = ok ? __ldg(rows[r0 + i].s + (c >> gsh)) : 0.0f;
+        }
+      if (tslot >= 0 && r0 == 0 && cb == 0) CHALOT_TRACE(tslot, 0);  // loads issued
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int c = cb + it * 32 + lane;
+        if (cb + it * 32 >= chunks) break;  // warp-uniform
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const bool live = r0 + i < nrows;
+          const int xsel = live ? rows[r0 + i].x : 0;
+          const uint4* xv = reinterpret_cast<const uint4*>(xq + (size_t)xsel * in_dim);
+          int dv = 0;
+          if (c < chunks) dv = dot32_rp(w[i][it], xv[2 * c], xv[2 * c + 1]);
+          if (tslot >= 0 && r0 == 0 && cb == 0 && it == 0 && i == 0) CHALOT_TRACE(tslot, 1);  // first row's data used
+          for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+          if (live && c < chunks && (c & (cpg - 1)) == 0)
+            P[(r0 + i) * ps + (c >> gsh)] = __fmul_rn(__fmul_rn((float)dv, sc[i][it]), xs[xsel]);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void group_products_rp_any(const RowJob* rows, int nrows, int in_dim,
+                                                      int group, const int8_t* xq, const float* xs,
+                                                      float* P, int ps, int tslot = -1) {
+  const int chunks = in_dim >> 5;
+  if (chunks <= 32)
+    group_products_rp<8, 1>(rows, nrows, in_dim, group, xq, xs, P, ps, tslot);
+  else if (chunks <= 64)
+    group_products_rp<4, 2>(rows, nrows, in_dim, group, xq, xs, P, ps, tslot);
+  else
+    group_products_rp<1, 8>(rows, nrows, in_dim, group, xq, xs, P, ps, tslot);
+}
+
+// In-place conversion of packed int4 rows from the file layout to the
+// engine's repacked layout (repack_word), once at load.
+__global__ void k_repack_i4(uint32_t* p, size_t n_words) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_words;
+       i += (size_t)gridDim.x * blockDim.x)
+    p[i] = repack_word(p[i]);
+}
+
 // Ordered group sum of one row: t = t + p_g for g = 0..ng-1 (matmul.rs:576-577).
 __device__ __forceinline__ float ordered_sum(const float* p, int ng) {
   float t = 0.0f;
-#pragma unroll 8
-  for (int g = 0; g < ng; ++g) t = __fadd_rn(t, p[g]);
+  int g = 0;
+  for (; g + 8 <= ng; g += 8) {  // 8 independent loads, then 8 dependent adds
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = p[g + u];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) t = __fadd_rn(t, v[u]);
+  }
+  for (; g < ng; ++g) t = __fadd_rn(t, p[g]);
   return t;
 }
 
@@ -118,18 +190,20 @@ constexpr int kGuPairs = 32;  // gate/up row pairs per CTA
 // sel[blockIdx.y], dotted with xq_ffn (engine.rs:366-374), then SwiGLU
 // (activations.rs:59-87); h goes to global memory and |h| into the expert's
 // absmax slot for the down kernel's quantization.
-__global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, DecodeBufs b) {
+__global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
+  const int slot = layer * 8 + 4;
+  CHALOT_TRACE(slot, 0);
   extern __shared__ __align__(16) unsigned char smem[];
   const int ng = d.dim / d.group, ps = ng + 1;
-  int8_t* xp = reinterpret_cast<int8_t*>(smem);              // [dim] permuted x_q
-  int* csum = reinterpret_cast<int*>(xp + d.dim);            // [dim/32]
-  float* P = reinterpret_cast<float*>(csum + (d.dim >> 5));  // [64][ng+1]
+  int8_t* xq = reinterpret_cast<int8_t*>(smem);        // [dim] x_q in natural order
+  float* P = reinterpret_cast<float*>(xq + d.dim);     // [64][ng+1]
   __shared__ RowJob rows[2 * kGuPairs];
   __shared__ float xs_s[1];
   __shared__ float tots[2 * kGuPairs];
 
   pdl_wait();  // the routing comes from the O-projection's last CTA
   pdl_trigger();
+  CHALOT_TRACE(slot, 2);
   const int j = blockIdx.y;
   const ExpertPtrs X = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
   const int H = d.hidden, prow = d.dim >> 1;
@@ -140,23 +214,17 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, Decode
     const int r = (i < kGuPairs ? base : H + base) + min(k, npairs - 1);  // gate rows, then up rows
     rows[i] = RowJob{X.gu + (size_t)r * prow, X.gu_s + (size_t)r * ng, 0};
   }
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(b.xq_ffn);
-    for (int k = threadIdx.x; k < (d.dim >> 4); k += blockDim.x) {
-      const uint4 v = __ldcg(src + k);
-      const int8_t* vb = reinterpret_cast<const int8_t*>(&v);
-#pragma unroll
-      for (int u = 0; u < 16; ++u) xp[perm32(k * 16 + u)] = vb[u];
-    }
-    if (threadIdx.x == 0) xs_s[0] = __ldcg(b.xs_ffn);
-  }
+  copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_ffn), d.dim >> 4, true);
+  if (threadIdx.x == 0) xs_s[0] = __ldcg(b.xs_ffn);
   __syncthreads();
-  chunk_sums(xp, d.dim, csum);
+  CHALOT_TRACE(slot, 3);
+  group_products_rp_any(rows, 2 * kGuPairs, d.dim, d.group, xq, xs_s, P, ps, layer * 8 + 7);
+  CHALOT_TRACE(layer * 8 + 7, 2);  // warp 0 done
   __syncthreads();
-  group_products_any(rows, 2 * kGuPairs, d.dim, d.group, xp, csum, xs_s, P, ps);
-  __syncthreads();
+  CHALOT_TRACE(slot, 4);
   if (threadIdx.x < 2 * kGuPairs) tots[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
   __syncthreads();
+  CHALOT_TRACE(layer * 8 + 7, 3);
   float m = 0.0f;
   if (threadIdx.x < npairs) {
     const int r = base + threadIdx.x;
@@ -166,23 +234,38 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, Decode
   }
   m = warp_max(m);  // npairs <= 32: only warp 0 holds values
   if (threadIdx.x == 0) atomicMax(&b.amax[j], __float_as_uint(m));
+  // the last CTA quantizes every expert's finished h once for the down kernel
+  // (quantize_f32_to_i8 of the down projection's input, engine.rs:383-384)
+  const bool tail = last_cta(b.counters + 3);
+  CHALOT_TRACE(slot, 5);
+  if (!tail) return;
+  const int h4 = H >> 2;
+  for (int jj = 0; jj < d.top_k; ++jj) {
+    float scale, inv;
+    quant_scale(__uint_as_float(__ldcg(b.amax + jj)), &scale, &inv);
+    if (threadIdx.x == 0) b.xs_h[jj] = scale;
+    quant_store_words(reinterpret_cast<uint32_t*>(b.xq_h) + (size_t)jj * h4,
+                      reinterpret_cast<const float4*>(b.h) + (size_t)jj * h4, h4, inv, H);
+  }
+  CHALOT_TRACE(slot, 6);
 }
 
 // Output rows r0..r0+rpc-1 for every routed expert: the routing is two
 // launches old, so each warp loads its down row (all IT 32-lane strides)
-// before waiting for the gate/up kernel; then h is quantized with the
-// accumulated absmax (the input quantization of engine.rs:383-384), the group
-// products and ordered sums give y_j[r], and x[r] += sum_j w_j * y_j[r] in
-// selection order (engine.rs:390-401). The last CTA computes the next
+// before waiting for the gate/up kernel; then the group products against the
+// quantized h and the ordered sums give y_j[r], and x[r] += sum_j w_j * y_j[r]
+// in selection order (engine.rs:390-401). The last CTA computes the next
 // layer's quantized attention input from the finished x.
 template <int IT>
-__global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, const float* next_norm,
-                                                   DecodeBufs b, int dense, int rpc) {
+__global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, int layer,
+                                                   const float* next_norm, DecodeBufs b, int dense,
+                                                   int rpc) {
+  const int slot = layer * 8 + 5;
+  CHALOT_TRACE(slot, 0);
   extern __shared__ __align__(16) unsigned char smem[];
   const int H = d.hidden, K = d.top_k, ng = H / d.group, ps = ng + 1;
-  int8_t* xp = reinterpret_cast<int8_t*>(smem);                          // [K][H]
-  int* csum = reinterpret_cast<int*>(smem + (size_t)K * H);               // [K][H/32]
-  float* P = reinterpret_cast<float*>(csum + (size_t)K * (H >> 5));       // [8][ng+1]
+  int8_t* xq = reinterpret_cast<int8_t*>(smem);                    // [K][H] natural order
+  float* P = reinterpret_cast<float*>(smem + (size_t)K * H);       // [8][ng+1]
   __shared__ RowJob rows[kWarps];
   __shared__ float xs_j[8];
   __shared__ float selw_s[8];
@@ -193,7 +276,7 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, const fl
   const int r0 = blockIdx.x * rpc;
   const int nr = min(rpc, d.dim - r0);
   const int nrow = K * rpc;  // <= kWarps: one row per warp
-  const int prow = H >> 1, chunks = H >> 5, cpg = d.group >> 5;
+  const int prow = H >> 1, chunks = H >> 5, cpg = d.group >> 5, gsh = __ffs(cpg) - 1;
   if (threadIdx.x < nrow) {
     const int j = threadIdx.x / rpc, i = threadIdx.x % rpc;
     const ExpertPtrs E = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
@@ -209,64 +292,36 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, const fl
     const int c = lane + 32 * it;
     const bool ok = warp < nrow && c < chunks;
     w[it] = ok ? ldg_stream(rows[warp].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-    sc[it] = ok ? __ldg(rows[warp].s + c / cpg) : 0.0f;
+    sc[it] = ok ? __ldg(rows[warp].s + (c >> gsh)) : 0.0f;
   }
+  CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
+  CHALOT_TRACE(slot, 2);
   {
-    // all of h (K*H floats) in flight at once, then quantized per expert
-    constexpr int kMaxH4 = 16;  // float4 per thread: K*H <= 16384
-    const int n4 = (K * H) >> 2, h4 = H >> 2;
-    float4 hv[kMaxH4];
-    const float4* src = reinterpret_cast<const float4*>(b.h);
-#pragma unroll
-    for (int u = 0; u < kMaxH4; ++u) {
-      const int i4 = threadIdx.x + u * kThreads;
-      if (i4 < n4) hv[u] = __ldcg(src + i4);
-    }
-    float invs[8];
-    for (int j = 0; j < K; ++j) {
-      float scale;
-      quant_scale(__uint_as_float(__ldcg(b.amax + j)), &scale, &invs[j]);
-      if (threadIdx.x == 0) xs_j[j] = scale;
-    }
-#pragma unroll
-    for (int u = 0; u < kMaxH4; ++u) {
-      const int i4 = threadIdx.x + u * kThreads;
-      if (i4 < n4) {
-        const int j = i4 / h4, i = (i4 - j * h4) * 4;
-        int8_t* xj = xp + (size_t)j * H;
-        const float inv = invs[j];
-        xj[perm32(i)] = quant_any(hv[u].x, inv, i, H);
-        xj[perm32(i + 1)] = quant_any(hv[u].y, inv, i + 1, H);
-        xj[perm32(i + 2)] = quant_any(hv[u].z, inv, i + 2, H);
-        xj[perm32(i + 3)] = quant_any(hv[u].w, inv, i + 3, H);
-      }
-    }
+    // the quantized h of every routed expert (the gate/up kernel's last CTA)
+    copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_h), (K * H) >> 4, true);
+    if (threadIdx.x < K) xs_j[threadIdx.x] = __ldcg(b.xs_h + threadIdx.x);
   }
   __syncthreads();
-  chunk_sums(xp, K * H, csum);
-  __syncthreads();
+  CHALOT_TRACE(slot, 3);
   if (warp < nrow) {
     const RowJob rj = rows[warp];
-    const uint4* xv = reinterpret_cast<const uint4*>(xp + (size_t)rj.x * H);
-    const int* cs = csum + rj.x * chunks;
+    const uint4* xv = reinterpret_cast<const uint4*>(xq + (size_t)rj.x * H);
     const float xs = xs_j[rj.x];
 #pragma unroll
     for (int it = 0; it < IT; ++it) {
       const int c = lane + 32 * it;
       int dv = 0;
-      if (c < chunks) dv = dot32_u4(w[it], xv[2 * c], xv[2 * c + 1], 0) - 8 * cs[c];
+      if (c < chunks) dv = dot32_rp(w[it], xv[2 * c], xv[2 * c + 1]);
       for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-      if (c < chunks && (c % cpg) == 0) {
-        const int g = c / cpg;
-        P[warp * ps + g] = __fmul_rn(__fmul_rn((float)dv, sc[it]), xs);
-      }
+      if (c < chunks && (c & (cpg - 1)) == 0) P[warp * ps + (c >> gsh)] = __fmul_rn(__fmul_rn((float)dv, sc[it]), xs);
     }
   }
   __syncthreads();
   if (threadIdx.x < nrow) y[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
   __syncthreads();
+  CHALOT_TRACE(slot, 4);
   if (threadIdx.x < nr) {
     const int r = r0 + threadIdx.x;
     float add;
@@ -278,9 +333,12 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, const fl
     }
     b.x[r] = __fadd_rn(__ldcg(b.x + r), add);
   }
-  if (!last_cta(b.counters + 2)) return;
+  const bool tail = last_cta(b.counters + 2);
+  CHALOT_TRACE(slot, 5);
+  if (!tail) return;
   float* xb = reinterpret_cast<float*>(smem);  // the tail reuses the dynamic buffer
   norm_quant_tail(b.x, next_norm, d.dim, b.xq_attn, b.xs_attn, xb, xb + d.dim, red);
+  CHALOT_TRACE(slot, 6);
 }
 
 // ---- operators ---------------------------------------------------------------
@@ -372,31 +430,31 @@ __global__ void __launch_bounds__(kThreads) k_router_op(int32_t* idx, float* w,
   for (int i = threadIdx.x; i < dim; i += blockDim.x) xb[i] = xt[i];
   __syncthreads();
   router_logits(rw, rb, xb, dim, E, lanes, logit);
-  if (threadIdx.x == 0) topk_serial(logit, E, k, idx + (size_t)blockIdx.x * k, w + (size_t)blockIdx.x * k);
+  if (threadIdx.x < 32) topk_warp(logit, E, k, idx + (size_t)blockIdx.x * k, w + (size_t)blockIdx.x * k);
 }
 
 }  // namespace
 
 static size_t gateup_smem(const Dims& d) {
   const size_t ng = d.dim / d.group;
-  return (size_t)d.dim + (size_t)(d.dim >> 5) * 4 + (size_t)2 * kGuPairs * (ng + 1) * 4;
+  return (size_t)d.dim + (size_t)2 * kGuPairs * (ng + 1) * 4;
 }
 static size_t down_smem(const Dims& d) {
   const size_t H = d.hidden, K = d.top_k, ng = H / d.group;
-  const size_t main = K * H + K * (H >> 5) * 4 + (size_t)kWarps * (ng + 1) * 4;
+  const size_t main = K * H + (size_t)kWarps * (ng + 1) * 4;
   return std::max(main, (size_t)d.dim * 8);  // the last CTA's norm scratch
 }
 
-void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s,
+void launch_gateup(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
                    bool pdl) {
   const size_t smem = gateup_smem(d);
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((d.hidden + kGuPairs - 1) / kGuPairs, d.top_k);
-  launch_k(k_gateup, grid, dim3(kThreads), smem, s, pdl, d, L, b);
+  launch_k(k_gateup, grid, dim3(kThreads), smem, s, pdl, d, L, layer, b);
 }
 
-void launch_down(const Dims& d, const LayerPtrs& L, const float* next_norm, const DecodeBufs& b,
-                 cudaStream_t s, bool pdl) {
+void launch_down(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
+                 const DecodeBufs& b, cudaStream_t s, bool pdl) {
   const int rpc = std::max(1, kWarps / d.top_k);  // rows per CTA: one row per warp over all experts
   const size_t smem = down_smem(d);
   const int grid = (d.dim + rpc - 1) / rpc;
@@ -406,7 +464,7 @@ void launch_down(const Dims& d, const LayerPtrs& L, const float* next_norm, cons
   do {                                                                                         \
     if (smem > 48 * 1024)                                                                      \
       cudaFuncSetAttribute(k_down<IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    launch_k(k_down<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, next_norm, b, dense, rpc); \
+    launch_k(k_down<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc); \
   } while (0)
   switch (it) {
     case 1: DOWN_CALL(1); break;
@@ -421,9 +479,18 @@ void launch_down(const Dims& d, const LayerPtrs& L, const float* next_norm, cons
 #undef DOWN_CALL
 }
 
+cudaError_t repack_int4(uint8_t* p, size_t bytes, cudaStream_t s) {
+  const size_t words = bytes / 4;
+  if (words == 0) return cudaSuccess;
+  const int grid = (int)std::min<size_t>((words + 255) / 256, 4096);
+  k_repack_i4<<<grid, 256, 0, s>>>(reinterpret_cast<uint32_t*>(p), words);
+  return cudaGetLastError();
+}
+
 cudaError_t op_matmul_i4(float* out, const uint8_t* wp, const float* ws, const float* x,
                          size_t out_dim, size_t in_dim, size_t group, int num_sms, cudaStream_t s) {
-  const bool vec = in_dim % 32 == 0 && group % 32 == 0 && ((reinterpret_cast<uintptr_t>(wp) & 15) == 0);
+  const bool vec = in_dim % 32 == 0 && group % 32 == 0 && group <= 1024 && (group & (group - 1)) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(wp) & 15) == 0);
   if (vec) {
     const size_t ng = in_dim / group;
     const size_t smem = in_dim + (in_dim >> 5) * 4 + (size_t)kOpRows * (ng + 1) * 4;
@@ -446,7 +513,7 @@ cudaError_t op_matmul_i4(float* out, const uint8_t* wp, const float* ws, const f
 cudaError_t op_router_topk(int32_t* idx, float* w, const float* x, const float* rw,
                            const float* rb, size_t n_tok, size_t dim, size_t n_experts,
                            size_t top_k, cudaStream_t s) {
-  if (n_experts > 64 || top_k > n_experts || top_k == 0) return cudaErrorInvalidValue;
+  if (n_experts > 32 || top_k > n_experts || top_k == 0) return cudaErrorInvalidValue;
   const size_t smem = (dim + 17 * n_experts) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   cudaFuncSetAttribute(k_router_op, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -454,5 +521,9 @@ cudaError_t op_router_topk(int32_t* idx, float* w, const float* x, const float* 
                                                        (int)top_k);
   return cudaGetLastError();
 }
+
+#ifdef CHALOT_PHASE_TRACE
+CHALOT_TRACE_EXPORT(trace_moe)
+#endif
 
 }  // namespace chalot

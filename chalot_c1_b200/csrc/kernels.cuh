@@ -69,6 +69,8 @@ struct DecodeBufs {
   float* selw;       // [top_k] their weights
   float* h;          // [top_k][hidden] SwiGLU output
   unsigned* amax;    // [top_k] absmax bits of h
+  int8_t* xq_h;      // [top_k][hidden] quantized h (down-projection input)
+  float* xs_h;       // [top_k] its scales
   float* logits;     // [vocab]
   StepState* st;
   const uint32_t* prompt;  // [max_seq] prompt of the running generate call
@@ -93,13 +95,13 @@ void launch_pv(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bo
 void launch_oproj(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b,
                   cudaStream_t s, bool pdl);
 // Gate/up rows of the routed experts + SwiGLU -> h, absmax(h).
-void launch_gateup(const Dims& d, const LayerPtrs& L, const DecodeBufs& b, cudaStream_t s,
+void launch_gateup(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
                    bool pdl);
 // Down rows of every routed expert, gated combine, x += ; the last CTA computes
 // xq_attn for the next layer (rmsnorm with `next_norm`: the next layer's
 // attention norm, or the final norm after the last layer).
-void launch_down(const Dims& d, const LayerPtrs& L, const float* next_norm, const DecodeBufs& b,
-                 cudaStream_t s, bool pdl);
+void launch_down(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
+                 const DecodeBufs& b, cudaStream_t s, bool pdl);
 // Logits from xq_attn (the final-norm input) + argmax.
 void launch_lmhead(const Dims& d, const int8_t* w, const float* ws, const DecodeBufs& b,
                    int num_sms, cudaStream_t s, bool pdl);
@@ -108,6 +110,10 @@ void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s, bool pdl
 // Repetition penalty on the logits followed by a fresh argmax into st->argmax_key.
 void launch_penalty_argmax(const Dims& d, const DecodeBufs& b, const uint32_t* hist, int n_hist,
                            float penalty, cudaStream_t s);
+
+// Converts packed int4 rows (bytes % 4 == 0) in place from the file layout to
+// the engine's repacked layout (repack_word in common.cuh).
+cudaError_t repack_int4(uint8_t* p, size_t bytes, cudaStream_t s);
 
 // ---- operator entry points ------------------------------------------------------
 cudaError_t op_matmul_i8(float* out, const int8_t* w, const float* ws, const float* x,
