@@ -115,17 +115,50 @@ __device__ __forceinline__ float absmax_smem(const float* v, int n, float* red) 
   return block_max(m, red);
 }
 
-// rmsnorm then quantize_f32_to_i8 of a vector other CTAs just finished
-// writing, into q_out/s_out (global). `xb`, `wbuf`: shared scratch of dim
-// floats each.
-__device__ __forceinline__ void norm_quant_tail(const float* x, const float* __restrict__ w, int dim,
-                                                int8_t* q_out, float* s_out, float* xb, float* wbuf,
-                                                float* red) {
-  rmsnorm_smem(x, w, dim, xb, wbuf, red, true);
-
-  float scale, inv;
-  quant_scale(absmax_smem(xb, dim, red), &scale, &inv);
-  for (int i = threadIdx.x; i < dim; i += blockDim.x) q_out[i] = quant_any(xb[i], inv, i, dim);
+// rmsnorm then quantize_f32_to_i8 of a vector x other CTAs just finished
+// writing, into q_out/s_out (global). `wsm` holds the norm weights already in
+// shared memory (staged before the dependency wait); `xb`: shared scratch of
+// dim floats that ends up holding rmsnorm(x).
+__device__ __forceinline__ void norm_quant_tail(const float* x, const float* wsm, int dim,
+                                                int8_t* q_out, float* s_out, float* xb, float* red) {
+  load_f32_cg(xb, x, dim);
+  __syncthreads();
+  const int chunks = dim >> 3;
+  if (threadIdx.x < 8) {  // lane j accumulates x[8c+j]^2 over c in order
+    float s = 0.0f;
+    int c = 0;
+    for (; c + 8 <= chunks; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = xb[(c + u) * 8 + threadIdx.x];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) s = __fadd_rn(s, __fmul_rn(v[u], v[u]));
+    }
+    for (; c < chunks; ++c) {
+      const float v = xb[c * 8 + threadIdx.x];
+      s = __fadd_rn(s, __fmul_rn(v, v));
+    }
+    red[threadIdx.x] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float lanes[8];
+    for (int j = 0; j < 8; ++j) lanes[j] = red[j];
+    float ss = hsum8(lanes);
+    for (int i = chunks * 8; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
+    red[8] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), 1e-5f)));
+  }
+  __syncthreads();
+  const float inv = red[8];
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(xb[i], inv), wsm[i]);
+    xb[i] = v;
+    m = fmaxf(m, fabsf(v));
+  }
+  float scale, qinv;
+  quant_scale(block_max(m, red), &scale, &qinv);
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) q_out[i] = quant_any(xb[i], qinv, i, dim);
   if (threadIdx.x == 0) *s_out = scale;
 }
 
@@ -172,9 +205,10 @@ __device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t*
   float sum = hsum8(l8);
   for (int i = full; i < n; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, i));
   const float p = __fmul_rn(e, __fdiv_rn(1.0f, sum));
-  // k rounds of (max probability, lowest index)
+  // k rounds of (max probability, lowest index); lane j keeps round j's pick
   bool taken = lane >= n;
-  float tot = -0.0f;
+  float tot = -0.0f, my_w = 0.0f;
+  int my_i = 0;
   for (int j = 0; j < k; ++j) {
     float bv = taken ? -INFINITY : p;
     int bi = taken ? 0x7fffffff : lane;
@@ -189,14 +223,15 @@ __device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t*
     }
     if (lane == bi) taken = true;
     tot = __fadd_rn(tot, bv);
-    if (lane == 0) {
-      idx[j] = bi;
-      w[j] = bv;
+    if (lane == j) {
+      my_i = bi;
+      my_w = bv;
     }
   }
-  __syncwarp();
-  if (lane == 0 && tot > 1e-12f)
-    for (int j = 0; j < k; ++j) w[j] = __fdiv_rn(w[j], tot);
+  if (lane < k) {
+    idx[lane] = my_i;
+    w[lane] = (tot > 1e-12f) ? __fdiv_rn(my_w, tot) : my_w;
+  }
 }
 
 // Router logits of one token: logit[e] = b[e] + dot_f32(W[e], xb) with the

@@ -117,7 +117,9 @@ struct chalot_engine {
   const float* out_s = nullptr;
   DecodeBufs b{};
   std::vector<void*> allocs;
-  StepState* h_state = nullptr;  // pinned staging
+  StepState* h_state = nullptr;  // pinned: device-state readback
+  StepState* h_stage = nullptr;  // pinned: one StepState per in-flight host->device copy
+  size_t n_stage = 0, next_stage = 0;
   uint32_t* h_tokens = nullptr;  // pinned, [max_seq]
   uint32_t* d_hist = nullptr;    // [2*max_seq] token history for the penalty
   bool use_graph = true;
@@ -135,6 +137,7 @@ struct chalot_engine {
     for (void* p : allocs) cudaFree(p);
     if (d_weights) cudaFree(d_weights);
     if (h_state) cudaFreeHost(h_state);
+    if (h_stage) cudaFreeHost(h_stage);
     if (h_tokens) cudaFreeHost(h_tokens);
     if (stream) cudaStreamDestroy(stream);
   }
@@ -209,13 +212,29 @@ struct chalot_engine {
     }
   }
 
+  // After a synchronize: a bounded device wait that gave up leaves b.err set;
+  // report it and clear the error word and the last-CTA tickets.
+  void check_device_error() {
+    unsigned h = 0;
+    CK(cudaMemcpy(&h, b.err, sizeof h, cudaMemcpyDeviceToHost));
+    if (h) {
+      CK(cudaMemset(b.err, 0, 4 * sizeof(unsigned)));
+      CK(cudaMemset(b.counters, 0, 8 * sizeof(unsigned)));
+      throw CudaFail{CHALOT_ERR_TIMEOUT, "a device wait for a bulk copy timed out"};
+    }
+  }
+
+  // Stages the state of the next forward. Each call uses its own pinned slot
+  // (the copy is asynchronous: a slot is reused only after n_stage calls, and
+  // callers synchronize at least once per n_stage forwards).
   void set_state(uint32_t pos, uint32_t token, uint32_t n_prefill, uint32_t step) {
-    h_state->pos = pos;
-    h_state->token = token;
-    h_state->n_prefill = n_prefill;
-    h_state->step = step;
-    h_state->argmax_key = 0ull;
-    CK(cudaMemcpyAsync(b.st, h_state, sizeof(StepState), cudaMemcpyHostToDevice, stream));
+    StepState* h = h_stage + (next_stage++ % n_stage);
+    h->pos = pos;
+    h->token = token;
+    h->n_prefill = n_prefill;
+    h->step = step;
+    h->argmax_key = 0ull;
+    CK(cudaMemcpyAsync(b.st, h, sizeof(StepState), cudaMemcpyHostToDevice, stream));
   }
 };
 
@@ -241,6 +260,9 @@ bool check_shapes(const ModelConfig& c, std::string* err) {
   if (c.dim > 4096) return bad("dim above 4096");
   if (c.hidden_dim > 8192) return bad("hidden_dim above 8192");
   if (c.top_k * c.hidden_dim > 16384) return bad("top_k * hidden_dim above 16384");
+  if (c.dim / c.int4_group_size > 64) return bad("dim / int4_group_size above 64");
+  if (c.dim % 8) return bad("dim must be a multiple of 8");
+  if ((c.hidden_dim / c.int4_group_size) % 4) return bad("hidden_dim / int4_group_size must be a multiple of 4");
   if (c.int4_group_size > 1024 || (c.int4_group_size & (c.int4_group_size - 1)))
     return bad("int4_group_size must be a power of two in [32, 1024]");
   if (c.n_experts > 32) return bad("more than 32 experts");
@@ -443,6 +465,7 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.xq_ffn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
     b.xs_ffn = e->dalloc<float>(1);
     b.counters = e->dalloc<unsigned>(8);
+    b.err = e->dalloc<unsigned>(4);
     b.sel = e->dalloc<int32_t>(std::max<size_t>(c.top_k, 1));
     b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.h = e->dalloc<float>(std::max<size_t>(c.top_k, 1) * H);
@@ -456,6 +479,8 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.router_trace = nullptr;
     e->d_hist = e->dalloc<uint32_t>(2 * c.max_seq_len + 64);
     CK(cudaMallocHost(&e->h_state, sizeof(StepState)));
+    e->n_stage = c.max_seq_len + 2;  // a generate call stages at most max_seq states between syncs
+    CK(cudaMallocHost(&e->h_stage, e->n_stage * sizeof(StepState)));
     CK(cudaMallocHost(&e->h_tokens, (c.max_seq_len + 1) * sizeof(uint32_t)));
     for (auto& ev : e->ev) CK(cudaEventCreate(&ev));
     if (e->use_graph) {
@@ -509,6 +534,7 @@ __attribute__((visibility("default"))) int chalot_forward(chalot_engine* e, uint
     CK(cudaMemcpyAsync(e->h_tokens, e->b.out_tokens, sizeof(uint32_t), cudaMemcpyDeviceToHost,
                        e->stream));
     CK(cudaStreamSynchronize(e->stream));
+    e->check_device_error();
     if (out_token) *out_token = e->h_tokens[0];
   } catch (const CudaFail& f) {
     return fail(f);
@@ -578,6 +604,7 @@ __attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, con
   const bool stops = sp && sp->n_stop_tokens > 0 && sp->stop_tokens;
   try {
     CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->stream));  // every staged state of earlier calls is consumed
     std::vector<uint32_t> clamped(n_prefill);
     for (size_t i = 0; i < n_prefill; ++i) clamped[i] = std::min<uint32_t>(prompt[i], uint32_t(V - 1));
     if (n_prefill)
@@ -642,6 +669,7 @@ __attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, con
       CK(cudaStreamSynchronize(e->stream));
       *n_out = cnt;
     }
+    e->check_device_error();
     float a = 0, bb = 0;
     CK(cudaEventElapsedTime(&a, e->ev[0], e->ev[1]));
     CK(cudaEventElapsedTime(&bb, e->ev[1], e->ev[2]));

@@ -102,13 +102,14 @@ __global__ void __launch_bounds__(kThreads) k_embed(Dims d, const int8_t* __rest
                                                     const float* __restrict__ rms0, DecodeBufs b) {
   extern __shared__ __align__(16) float esm[];
   __shared__ float red[40];
+  load_f32(esm + d.dim, rms0, d.dim);
   const uint32_t tok = b.st->token;
   const float s = emb_s[tok];
   const int8_t* row = emb + (size_t)tok * d.dim;
   for (int i = threadIdx.x; i < d.dim; i += blockDim.x) b.x[i] = __fmul_rn((float)row[i], s);
   if (threadIdx.x == 0) b.st->argmax_key = 0ull;
   __syncthreads();
-  norm_quant_tail(b.x, rms0, d.dim, b.xq_attn, b.xs_attn, esm, esm + d.dim, red);
+  norm_quant_tail(b.x, esm + d.dim, d.dim, b.xq_attn, b.xs_attn, esm, red);
 }
 
 constexpr int kQkvRows = 2;  // rows per warp: one RoPE pair
@@ -183,8 +184,22 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = (blockIdx.x * kWarps + warp) * kORows;
+  const int E = d.n_experts;
+  float* xb = osm;
+  float* wbuf = osm + d.dim;
+  float* lanes = wbuf + d.dim;
+  float* logit = lanes + 16 * E;
+  float* rbias = logit + 32;
+  float* rw = rbias + 32;  // [E][dim] router weights
   uint4 w[kORows][IT];
   rows_load_i8<kORows, IT>(L.o, d.dim, r0, d.dim, w);
+  // whichever CTA finishes last runs the FFN prologue: every CTA stages its
+  // static inputs (norm weights, router weights and bias) before waiting
+  load_f32(wbuf, L.rms_ffn, d.dim);
+  if (E >= 2) {
+    load_f32(rw, L.router_w, E * d.dim);
+    if (threadIdx.x < E) rbias[threadIdx.x] = L.router_b[threadIdx.x];
+  }
   CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
@@ -209,21 +224,13 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   const bool tail = last_cta(b.counters + 1);
   CHALOT_TRACE(slot, 5);
   if (!tail) return;
-  const int E = d.n_experts;
-  float* xb = osm;
-  float* wbuf = osm + d.dim;
-  float* lanes = wbuf + d.dim;
-  float* logit = lanes + 16 * E;
-  float* rw = logit + ((E + 3) & ~3);  // [E][dim] router weights staged before the norm
   const int tslot = layer * 8 + 6;
   CHALOT_TRACE(tslot, 0);
-  if (E >= 2) load_f32(rw, L.router_w, E * d.dim);
-  CHALOT_TRACE(tslot, 1);
-  norm_quant_tail(b.x, L.rms_ffn, d.dim, b.xq_ffn, b.xs_ffn, xb, wbuf, red);
+  norm_quant_tail(b.x, wbuf, d.dim, b.xq_ffn, b.xs_ffn, xb, red);
   CHALOT_TRACE(tslot, 2);
   if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;
   if (E >= 2) {
-    router_logits(rw, L.router_b, xb, d.dim, E, lanes, logit);
+    router_logits(rw, rbias, xb, d.dim, E, lanes, logit);
     CHALOT_TRACE(tslot, 3);
     if (threadIdx.x < 32) topk_warp(logit, E, d.top_k, b.sel, b.selw);
     CHALOT_TRACE(tslot, 4);
@@ -426,7 +433,7 @@ void launch_oproj(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs
   const int rows_per_block = kWarps * kORows;
   const int grid = (d.dim + rows_per_block - 1) / rows_per_block;
   const size_t E = d.n_experts;
-  const size_t smem = ((size_t)d.dim * 2 + 16 * E + ((E + 3) & ~size_t(3)) + E * d.dim) * 4;
+  const size_t smem = ((size_t)d.dim * 2 + 16 * E + 64 + E * d.dim) * 4;
 #define O_CALL(IT)                                                                           \
   do {                                                                                      \
     if (smem > 48 * 1024)                                                                   \

@@ -20,6 +20,7 @@
 #include "blockops.cuh"
 #include "kernels.cuh"
 #include "pdl.cuh"
+#include "tma.cuh"
 
 namespace chalot {
 namespace {
@@ -92,62 +93,6 @@ __device__ __forceinline__ void group_products_any(const RowJob* rows, int nrows
     group_products<1, 8>(rows, nrows, in_dim, group, xp, csum, xs, P, ps);
 }
 
-// group_products for the engine's repacked weights (repack_word) against a
-// natural-order quantized vector: no per-chunk sums, no permutation.
-template <int R, int IT>
-__device__ __forceinline__ void group_products_rp(const RowJob* rows, int nrows, int in_dim,
-                                                  int group, const int8_t* xq, const float* xs,
-                                                  float* P, int ps, int tslot = -1) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int chunks = in_dim >> 5, cpg = group >> 5;
-  const int gsh = __ffs(cpg) - 1;  // group % 32 == 0 and a power of two: c / cpg == c >> gsh
-  for (int r0 = warp * R; r0 < nrows; r0 += kWarps * R) {
-    for (int cb = 0; cb < chunks; cb += 32 * IT) {
-      uint4 w[R][IT];
-      float sc[R][IT];
-#pragma unroll
-      for (int i = 0; i < R; ++i)
-#pragma unroll
-        for (int it = 0; it < IT; ++it) {
-          const int c = cb + it * 32 + lane;
-          const bool ok = c < chunks && r0 + i < nrows;
-          w[i][it] = ok ? ldg_stream(rows[r0 + i].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-          sc[i][it] = ok ? __ldg(rows[r0 + i].s + (c >> gsh)) : 0.0f;
-        }
-      if (tslot >= 0 && r0 == 0 && cb == 0) CHALOT_TRACE(tslot, 0);  // loads issued
-#pragma unroll
-      for (int it = 0; it < IT; ++it) {
-        const int c = cb + it * 32 + lane;
-        if (cb + it * 32 >= chunks) break;  // warp-uniform
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-          const bool live = r0 + i < nrows;
-          const int xsel = live ? rows[r0 + i].x : 0;
-          const uint4* xv = reinterpret_cast<const uint4*>(xq + (size_t)xsel * in_dim);
-          int dv = 0;
-          if (c < chunks) dv = dot32_rp(w[i][it], xv[2 * c], xv[2 * c + 1]);
-          if (tslot >= 0 && r0 == 0 && cb == 0 && it == 0 && i == 0) CHALOT_TRACE(tslot, 1);  // first row's data used
-          for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-          if (live && c < chunks && (c & (cpg - 1)) == 0)
-            P[(r0 + i) * ps + (c >> gsh)] = __fmul_rn(__fmul_rn((float)dv, sc[i][it]), xs[xsel]);
-        }
-      }
-    }
-  }
-}
-
-__device__ __forceinline__ void group_products_rp_any(const RowJob* rows, int nrows, int in_dim,
-                                                      int group, const int8_t* xq, const float* xs,
-                                                      float* P, int ps, int tslot = -1) {
-  const int chunks = in_dim >> 5;
-  if (chunks <= 32)
-    group_products_rp<8, 1>(rows, nrows, in_dim, group, xq, xs, P, ps, tslot);
-  else if (chunks <= 64)
-    group_products_rp<4, 2>(rows, nrows, in_dim, group, xq, xs, P, ps, tslot);
-  else
-    group_products_rp<1, 8>(rows, nrows, in_dim, group, xq, xs, P, ps, tslot);
-}
-
 // In-place conversion of packed int4 rows from the file layout to the
 // engine's repacked layout (repack_word), once at load.
 __global__ void k_repack_i4(uint32_t* p, size_t n_words) {
@@ -185,57 +130,109 @@ __device__ __forceinline__ void chunk_sums(const int8_t* xp, int n, int* csum) {
 // ---------------------------------------------------------------------------
 
 constexpr int kGuPairs = 32;  // gate/up row pairs per CTA
+constexpr int kSegs = 4;      // threads per gate/up row (the ordered sum is handed along)
+constexpr int kMaxSegGroups = 16;  // groups per thread: dim / group <= 64
+
+// Group dot of column group g of a repacked int4 row in shared memory with the
+// natural-order x_q in shared memory (cpg 32-column chunks per group).
+__device__ __forceinline__ int group_dot_smem(const uint8_t* wrow, const int8_t* xq, int g, int cpg) {
+  int dv = 0;
+  for (int cc = 0; cc < cpg; ++cc) {
+    const int c = g * cpg + cc;
+    const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (size_t)c * 16);
+    const uint4* xv = reinterpret_cast<const uint4*>(xq + (size_t)c * 32);
+    dv += dot32_rp(wv, xv[0], xv[1]);
+  }
+  return dv;
+}
 
 // Gate rows base..base+31 and the matching up rows of routed expert
-// sel[blockIdx.y], dotted with xq_ffn (engine.rs:366-374), then SwiGLU
-// (activations.rs:59-87); h goes to global memory and |h| into the expert's
-// absmax slot for the down kernel's quantization.
+// sel[blockIdx.y] (engine.rs:366-374), then SwiGLU (activations.rs:59-87): h
+// goes to global memory and |h| into the expert's absmax slot. The 64 rows
+// arrive in shared memory by TMA bulk copies (one per row, row stride padded
+// by 16 bytes); 4 threads share a row, each computing the exact products of a
+// quarter of its groups, and the running sum is handed from quarter to
+// quarter so the groups are added in order (matmul.rs:576-577). The last CTA
+// quantizes every expert's finished h once for the down kernel.
 __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
+  extern __shared__ __align__(16) unsigned char smem[];
   const int slot = layer * 8 + 4;
   CHALOT_TRACE(slot, 0);
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int ng = d.dim / d.group, ps = ng + 1;
-  int8_t* xq = reinterpret_cast<int8_t*>(smem);        // [dim] x_q in natural order
-  float* P = reinterpret_cast<float*>(xq + d.dim);     // [64][ng+1]
-  __shared__ RowJob rows[2 * kGuPairs];
-  __shared__ float xs_s[1];
+  const int ng = d.dim / d.group, cpg = d.group >> 5, prow = d.dim >> 1, wst = prow + 16;
+  uint8_t* W = smem;                                                 // [64][wst]
+  float* S = reinterpret_cast<float*>(smem + 2 * kGuPairs * wst);    // [64][ng]
+  int8_t* xq = reinterpret_cast<int8_t*>(S + 2 * kGuPairs * ng);     // [dim]
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float xs_s;
   __shared__ float tots[2 * kGuPairs];
+  __shared__ const uint8_t* gsrc[2];
+  __shared__ const float* ssrc[2];
 
+  const int H = d.hidden, j = blockIdx.y, base = blockIdx.x * kGuPairs;
+  const int npairs = min(kGuPairs, H - base);
+  if (threadIdx.x == 0) mbar_init(&bar);
   pdl_wait();  // the routing comes from the O-projection's last CTA
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  const int j = blockIdx.y;
-  const ExpertPtrs X = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
-  const int H = d.hidden, prow = d.dim >> 1;
-  const int base = blockIdx.x * kGuPairs;
-  const int npairs = min(kGuPairs, H - base);
-  if (threadIdx.x < 2 * kGuPairs) {
-    const int i = threadIdx.x, k = i % kGuPairs;
-    const int r = (i < kGuPairs ? base : H + base) + min(k, npairs - 1);  // gate rows, then up rows
-    rows[i] = RowJob{X.gu + (size_t)r * prow, X.gu_s + (size_t)r * ng, 0};
+  if (threadIdx.x == 0) {
+    const ExpertPtrs X = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
+    gsrc[0] = X.gu + (size_t)base * prow;        // gate rows
+    gsrc[1] = X.gu + (size_t)(H + base) * prow;  // up rows
+    ssrc[0] = X.gu_s + (size_t)base * ng;
+    ssrc[1] = X.gu_s + (size_t)(H + base) * ng;
+    // rows and scales: npairs == 32 (hidden % 32 == 0), the scale blocks are
+    // 32*ng floats (a multiple of 16 bytes) at 16-byte aligned offsets
+    mbar_expect_tx(&bar, (uint32_t)(2 * npairs * prow + 2 * npairs * ng * 4));
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * kGuPairs) {  // one bulk copy per row
+    const int half = threadIdx.x / kGuPairs, i = threadIdx.x % kGuPairs;
+    if (i < npairs) tma_load(W + threadIdx.x * wst, gsrc[half] + (size_t)i * prow, prow, &bar);
+  } else if (threadIdx.x < 2 * kGuPairs + 2) {  // the two scale blocks
+    const int half = threadIdx.x - 2 * kGuPairs;
+    tma_load(S + half * kGuPairs * ng, ssrc[half], (uint32_t)(npairs * ng * 4), &bar);
   }
   copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_ffn), d.dim >> 4, true);
-  if (threadIdx.x == 0) xs_s[0] = __ldcg(b.xs_ffn);
+  if (threadIdx.x == 0) xs_s = __ldcg(b.xs_ffn);
   __syncthreads();
   CHALOT_TRACE(slot, 3);
-  group_products_rp_any(rows, 2 * kGuPairs, d.dim, d.group, xq, xs_s, P, ps, layer * 8 + 7);
-  CHALOT_TRACE(layer * 8 + 7, 2);  // warp 0 done
+  if (!mbar_wait(&bar, 0, b.err)) return;
+  CHALOT_TRACE(layer * 8 + 7, 1);
+  // row r = t/4, quarter q = t%4 over groups [q*ng/4, (q+1)*ng/4)
+  const int r = threadIdx.x >> 2, q = threadIdx.x & 3;
+  const int g0 = q * ng / kSegs, g1 = (q + 1) * ng / kSegs;
+  const bool live = (r % kGuPairs) < npairs;
+  const float xs = xs_s;
+  float p[kMaxSegGroups];
+#pragma unroll
+  for (int i = 0; i < kMaxSegGroups; ++i) {
+    const int g = g0 + i;
+    p[i] = 0.0f;
+    if (live && g < g1)
+      p[i] = __fmul_rn(__fmul_rn((float)group_dot_smem(W + r * wst, xq, g, cpg), S[r * ng + g]), xs);
+  }
+  float acc = 0.0f;
+  const int lane = threadIdx.x & 31, lead = lane & ~3;
+#pragma unroll
+  for (int st = 0; st < kSegs; ++st) {
+    if (q == st)
+#pragma unroll
+      for (int i = 0; i < kMaxSegGroups; ++i)
+        if (g0 + i < g1) acc = __fadd_rn(acc, p[i]);
+    acc = __shfl_sync(0xffffffffu, acc, lead + st);
+  }
+  if (q == 0) tots[r] = acc;
   __syncthreads();
   CHALOT_TRACE(slot, 4);
-  if (threadIdx.x < 2 * kGuPairs) tots[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
-  __syncthreads();
-  CHALOT_TRACE(layer * 8 + 7, 3);
   float m = 0.0f;
   if (threadIdx.x < npairs) {
-    const int r = base + threadIdx.x;
-    const float hv = swiglu_elem(tots[threadIdx.x], tots[kGuPairs + threadIdx.x], r, H);
-    b.h[(size_t)j * H + r] = hv;
+    const int rr = base + threadIdx.x;
+    const float hv = swiglu_elem(tots[threadIdx.x], tots[kGuPairs + threadIdx.x], rr, H);
+    b.h[(size_t)j * H + rr] = hv;
     m = fabsf(hv);
   }
   m = warp_max(m);  // npairs <= 32: only warp 0 holds values
   if (threadIdx.x == 0) atomicMax(&b.amax[j], __float_as_uint(m));
-  // the last CTA quantizes every expert's finished h once for the down kernel
-  // (quantize_f32_to_i8 of the down projection's input, engine.rs:383-384)
   const bool tail = last_cta(b.counters + 3);
   CHALOT_TRACE(slot, 5);
   if (!tail) return;
@@ -250,23 +247,31 @@ __global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, int la
   CHALOT_TRACE(slot, 6);
 }
 
-// Output rows r0..r0+rpc-1 for every routed expert: the routing is two
-// launches old, so each warp loads its down row (all IT 32-lane strides)
-// before waiting for the gate/up kernel; then the group products against the
-// quantized h and the ordered sums give y_j[r], and x[r] += sum_j w_j * y_j[r]
-// in selection order (engine.rs:390-401). The last CTA computes the next
-// layer's quantized attention input from the finished x.
-template <int IT>
+// Output rows r0..r0+rpc-1 for every routed expert (one row per warp). The
+// routing is two launches old, so the rows are requested by TMA bulk copies
+// (and the scales and the next norm's weights staged) before waiting for the
+// gate/up kernel; then each warp forms the exact group products against the
+// quantized h and one thread per row adds them in group order; x[r] +=
+// sum_j w_j * y_j[r] in selection order (engine.rs:380-401). The last CTA
+// computes the next layer's quantized attention input from the finished x.
 __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, int layer,
                                                    const float* next_norm, DecodeBufs b, int dense,
                                                    int rpc) {
+  extern __shared__ __align__(16) unsigned char smem[];
   const int slot = layer * 8 + 5;
   CHALOT_TRACE(slot, 0);
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int H = d.hidden, K = d.top_k, ng = H / d.group, ps = ng + 1;
-  int8_t* xq = reinterpret_cast<int8_t*>(smem);                    // [K][H] natural order
-  float* P = reinterpret_cast<float*>(smem + (size_t)K * H);       // [8][ng+1]
-  __shared__ RowJob rows[kWarps];
+  const int H = d.hidden, K = d.top_k, ng = H / d.group, ps = ng + 1, cpg = d.group >> 5;
+  const int prow = H >> 1, wst = prow + 16;
+  const int nrow = K * rpc;  // <= kWarps
+  uint8_t* W = smem;                                          // [nrow][wst]
+  float* S = reinterpret_cast<float*>(W + kWarps * wst);      // [nrow][ng]
+  int8_t* xq = reinterpret_cast<int8_t*>(S + kWarps * ng);    // [K][H]
+  float* P = reinterpret_cast<float*>(xq + (size_t)K * H);    // [nrow][ng+1]
+  float* wn = P + kWarps * ps;                                // [dim] next norm weights
+  float* xb = wn + d.dim;                                     // [dim] tail scratch
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ const uint8_t* rsrc[kWarps];
+  __shared__ const float* ssrc[kWarps];
   __shared__ float xs_j[8];
   __shared__ float selw_s[8];
   __shared__ float y[kWarps];
@@ -275,53 +280,56 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, int laye
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * rpc;
   const int nr = min(rpc, d.dim - r0);
-  const int nrow = K * rpc;  // <= kWarps: one row per warp
-  const int prow = H >> 1, chunks = H >> 5, cpg = d.group >> 5, gsh = __ffs(cpg) - 1;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar);
+    // rows, and per expert one block of rpc scale rows (rpc*ng floats at a
+    // 16-byte aligned offset: dim % rpc == 0, rpc*ng*4 % 16 == 0)
+    mbar_expect_tx(&bar, (uint32_t)(nrow * prow + K * rpc * ng * 4));
+  }
   if (threadIdx.x < nrow) {
-    const int j = threadIdx.x / rpc, i = threadIdx.x % rpc;
-    const ExpertPtrs E = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
-    const int r = r0 + min(i, nr - 1);
-    rows[threadIdx.x] = RowJob{E.dn + (size_t)r * prow, E.dn_s + (size_t)r * ng, j};
+    const int jx = threadIdx.x / rpc, i = threadIdx.x % rpc;
+    const ExpertPtrs E = expert_ptrs(L, d.n_experts, __ldcg(b.sel + jx));
+    const int r = r0 + i;  // dim % rpc == 0: every CTA has rpc whole rows
+    rsrc[threadIdx.x] = E.dn + (size_t)r * prow;
+    ssrc[threadIdx.x] = E.dn_s + (size_t)r * ng;
   }
   if (threadIdx.x < K) selw_s[threadIdx.x] = __ldcg(b.selw + threadIdx.x);
   __syncthreads();
-  uint4 w[IT];
-  float sc[IT];
-#pragma unroll
-  for (int it = 0; it < IT; ++it) {
-    const int c = lane + 32 * it;
-    const bool ok = warp < nrow && c < chunks;
-    w[it] = ok ? ldg_stream(rows[warp].w + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
-    sc[it] = ok ? __ldg(rows[warp].s + (c >> gsh)) : 0.0f;
+  if (threadIdx.x < nrow) {
+    tma_load(W + threadIdx.x * wst, rsrc[threadIdx.x], prow, &bar);
+    if (threadIdx.x % rpc == 0)  // first row of each expert's block: its rpc scale rows
+      tma_load(S + threadIdx.x * ng, ssrc[threadIdx.x], (uint32_t)(rpc * ng * 4), &bar);
   }
+  load_f32(wn, next_norm, d.dim);
   CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  {
-    // the quantized h of every routed expert (the gate/up kernel's last CTA)
-    copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_h), (K * H) >> 4, true);
-    if (threadIdx.x < K) xs_j[threadIdx.x] = __ldcg(b.xs_h + threadIdx.x);
-  }
+  // the quantized h of every routed expert (the gate/up kernel's last CTA)
+  copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_h), (K * H) >> 4, true);
+  if (threadIdx.x < K) xs_j[threadIdx.x] = __ldcg(b.xs_h + threadIdx.x);
   __syncthreads();
   CHALOT_TRACE(slot, 3);
+  if (!mbar_wait(&bar, 0, b.err)) return;
+#ifdef CHALOT_PHASE_TRACE
+  long long c0_ = clock64();
+#endif
   if (warp < nrow) {
-    const RowJob rj = rows[warp];
-    const uint4* xv = reinterpret_cast<const uint4*>(xq + (size_t)rj.x * H);
-    const float xs = xs_j[rj.x];
-#pragma unroll
-    for (int it = 0; it < IT; ++it) {
-      const int c = lane + 32 * it;
-      int dv = 0;
-      if (c < chunks) dv = dot32_rp(w[it], xv[2 * c], xv[2 * c + 1]);
-      for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-      if (c < chunks && (c & (cpg - 1)) == 0) P[warp * ps + (c >> gsh)] = __fmul_rn(__fmul_rn((float)dv, sc[it]), xs);
-    }
+    const int jx = warp / rpc;
+    const int8_t* xj = xq + (size_t)jx * H;
+    const uint8_t* wrow = W + warp * wst;
+    const float xs = xs_j[jx];
+    for (int g = lane; g < ng; g += 32)
+      P[warp * ps + g] = __fmul_rn(__fmul_rn((float)group_dot_smem(wrow, xj, g, cpg), S[warp * ng + g]), xs);
   }
   __syncthreads();
   if (threadIdx.x < nrow) y[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
   __syncthreads();
   CHALOT_TRACE(slot, 4);
+#ifdef CHALOT_PHASE_TRACE
+  if (threadIdx.x == 0 && blockIdx.x == 0)  // SM cycles of the compute, next to its ns (phases 3..4)
+    g_phase_trace[((size_t)(layer * 8 + 7) * kTraceCtas + 1000) * kTracePhases] = clock64() - c0_;
+#endif
   if (threadIdx.x < nr) {
     const int r = r0 + threadIdx.x;
     float add;
@@ -336,8 +344,7 @@ __global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, int laye
   const bool tail = last_cta(b.counters + 2);
   CHALOT_TRACE(slot, 5);
   if (!tail) return;
-  float* xb = reinterpret_cast<float*>(smem);  // the tail reuses the dynamic buffer
-  norm_quant_tail(b.x, next_norm, d.dim, b.xq_attn, b.xs_attn, xb, xb + d.dim, red);
+  norm_quant_tail(b.x, wn, d.dim, b.xq_attn, b.xs_attn, xb, red);
   CHALOT_TRACE(slot, 6);
 }
 
@@ -436,13 +443,12 @@ __global__ void __launch_bounds__(kThreads) k_router_op(int32_t* idx, float* w,
 }  // namespace
 
 static size_t gateup_smem(const Dims& d) {
-  const size_t ng = d.dim / d.group;
-  return (size_t)d.dim + (size_t)2 * kGuPairs * (ng + 1) * 4;
+  const size_t ng = d.dim / d.group, wst = d.dim / 2 + 16;
+  return 2 * kGuPairs * wst + 2 * kGuPairs * ng * 4 + d.dim;
 }
 static size_t down_smem(const Dims& d) {
-  const size_t H = d.hidden, K = d.top_k, ng = H / d.group;
-  const size_t main = K * H + (size_t)kWarps * (ng + 1) * 4;
-  return std::max(main, (size_t)d.dim * 8);  // the last CTA's norm scratch
+  const size_t H = d.hidden, K = d.top_k, ng = H / d.group, wst = H / 2 + 16;
+  return kWarps * wst + kWarps * ng * 4 + K * H + kWarps * (ng + 1) * 4 + (size_t)d.dim * 8;
 }
 
 void launch_gateup(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
@@ -459,24 +465,9 @@ void launch_down(const Dims& d, const LayerPtrs& L, int layer, const float* next
   const size_t smem = down_smem(d);
   const int grid = (d.dim + rpc - 1) / rpc;
   const int dense = d.n_experts < 2 ? 1 : 0;
-  const int it = ((d.hidden >> 5) + 31) / 32;
-#define DOWN_CALL(IT)                                                                           \
-  do {                                                                                         \
-    if (smem > 48 * 1024)                                                                      \
-      cudaFuncSetAttribute(k_down<IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-    launch_k(k_down<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc); \
-  } while (0)
-  switch (it) {
-    case 1: DOWN_CALL(1); break;
-    case 2: DOWN_CALL(2); break;
-    case 3: DOWN_CALL(3); break;
-    case 4: DOWN_CALL(4); break;
-    case 5: DOWN_CALL(5); break;
-    case 6: DOWN_CALL(6); break;
-    case 7: DOWN_CALL(7); break;
-    default: DOWN_CALL(8); break;
-  }
-#undef DOWN_CALL
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_k(k_down, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc);
 }
 
 cudaError_t repack_int4(uint8_t* p, size_t bytes, cudaStream_t s) {

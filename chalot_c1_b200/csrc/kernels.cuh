@@ -65,6 +65,7 @@ struct DecodeBufs {
   int8_t* xq_ffn;    // [dim] quantized FFN input
   float* xs_ffn;     // [1] its scale
   unsigned* counters;  // [8] last-CTA tickets, one per kernel kind
+  unsigned* err;       // [1] set when a bounded wait gave up
   int32_t* sel;      // [top_k] selected experts
   float* selw;       // [top_k] their weights
   float* h;          // [top_k][hidden] SwiGLU output
