@@ -54,6 +54,12 @@ class Sampling(C.Structure):
                 ("n_stop_tokens", C.c_uint32)]
 
 
+class MoeDesc(C.Structure):
+    _fields_ = [("dim", C.c_uint32), ("hidden_dim", C.c_uint32), ("n_experts", C.c_uint32),
+                ("top_k", C.c_uint32), ("group", C.c_uint32), ("router_w", C.c_void_p),
+                ("router_b", C.c_void_p), ("experts", C.c_void_p)]
+
+
 # name -> (restype, argtypes); every function include/chalot_b200.h declares
 P = C.c_void_p
 SIGNATURES = {
@@ -81,6 +87,8 @@ SIGNATURES = {
     "chalot_quantize_i8": (C.c_int, [P, P, P, C.c_size_t, C.c_size_t, P]),
     "chalot_router_topk": (C.c_int, [P, P, P, P, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                      C.c_size_t, P]),
+    "chalot_moe_workspace_size": (C.c_size_t, [C.POINTER(MoeDesc), C.c_size_t]),
+    "chalot_moe_layer": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P, C.c_size_t, P]),
 }
 
 _lib = None

@@ -1,0 +1,437 @@
+// k_moe_layer.cu — one MoE FFN layer for a batch of T tokens (the operator
+// behind chalot_moe_layer): router, top-k gating, dispatch by expert, int4
+// SwiGLU expert products and the gated combine.
+//
+// Per token this is the expert block of Engine::forward
+// (src/model/engine.rs:334-401) applied to an already normalised input row:
+//   logits = b + dot_f32(Wr[e], x)      softmax_top_k(logits, k)
+//   for each selected (e, w): gate/up = matmul_int4(x), h = swiglu(gate, up),
+//   y = matmul_int4(down, h); out = 0 + w_0*y_0 + w_1*y_1 ... in selection order.
+// The batch is processed expert by expert: the T*k (token, choice) slots are
+// sorted by expert with a stable counting sort (histogram, prefix sum,
+// scatter), so each expert's weights are read once per tile of 32 slots.
+//
+// Kernels (all on one stream):
+//   k_ml_route     one CTA per token: router logits, top-k, quantize x
+//   k_ml_dispatch  one CTA: per-expert histogram, prefix sums, slot order,
+//                  and the table of 32-slot blocks (expert, first slot, count)
+//   k_ml_gemm<GU>  tiles of 32 slots x 128 weight rows: exact int32 group dots
+//                  (dp4a on unpacked int4), the f32 group epilogue in group
+//                  order; GU=true writes swiglu(gate, up), else y
+//   k_ml_quant     one CTA per slot: quantize h (quantize_f32_to_i8)
+//   k_ml_combine   one CTA per token: gated sum in selection order
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <string>
+
+#include "blockops.cuh"
+#include "capi_internal.h"
+#include "common.cuh"
+#include "moe_layer.h"
+
+namespace chalot {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kBM = 32;    // slots per tile
+constexpr int kBN = 128;   // weight rows per tile (gate/up: 64 gate rows + the 64 matching up rows)
+constexpr int kKC = 256;   // columns staged per chunk
+constexpr int kWS = kKC + 16;  // shared row stride of unpacked weights (16-B aligned, 4 banks apart)
+constexpr int kSS = kKC / 32 + 1;  // shared row stride of group scales
+
+// (float)v for |v| < 2^22: the integer is placed in the mantissa of 1.5*2^23
+// and that bias is subtracted; both steps are exact.
+__device__ __forceinline__ float i2f_exact(int v) {
+  return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+
+// 16 packed int4 bytes (32 columns, low nibble = even column, value = nibble-8)
+// to 32 int8 in column order.
+__device__ __forceinline__ void unpack32(uint4 p, uint4* dst) {
+  const uint32_t in[4] = {p.x, p.y, p.z, p.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = in[i] & 0x0F0F0F0Fu, hi = (in[i] >> 4) & 0x0F0F0F0Fu;
+    // bytes [lo0 hi0 lo1 hi1] and [lo2 hi2 lo3 hi3]; nibble-8 per byte without borrows
+    o[2 * i] = (__byte_perm(lo, hi, 0x5140) + 0x78787878u) ^ 0x80808080u;
+    o[2 * i + 1] = (__byte_perm(lo, hi, 0x7362) + 0x78787878u) ^ 0x80808080u;
+  }
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+__global__ void __launch_bounds__(kThreads) k_ml_route(MlDims d, const float* __restrict__ x,
+                                                       const float* __restrict__ rw,
+                                                       const float* __restrict__ rb, MlWork w) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* xb = reinterpret_cast<float*>(smem);
+  float* lanes = xb + d.dim;
+  float* logit = lanes + 16 * d.E;
+  float* red = logit + 32;
+  const int t = blockIdx.x;
+  const float* xt = x + (size_t)t * d.dim;
+  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) xb[i] = xt[i];
+  __syncthreads();
+  router_logits(rw, rb, xb, d.dim, d.E, lanes, logit);
+  if (threadIdx.x < 32) topk_warp(logit, d.E, d.K, w.sel + (size_t)t * d.K, w.selw + (size_t)t * d.K);
+  const float s = quantize_smem(xb, d.dim, w.xq + (size_t)t * d.dim, red);
+  if (threadIdx.x == 0) w.xs[t] = s;
+}
+
+// Stable counting sort of the N = T*k slots by expert. Warp v walks slots
+// [v*chunk, (v+1)*chunk) in order; lanes holding the same expert are grouped
+// with __match_any_sync, so positions follow slot order within each expert.
+__global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w) {
+  __shared__ int cnt[32][33];
+  __shared__ int off[33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int N = d.T * d.K;
+  const int chunk = ((N + 1023) / 1024) * 32;
+  const int beg = warp * chunk, end = min(N, beg + chunk);
+  for (int i = threadIdx.x; i < 32 * 33; i += blockDim.x) (&cnt[0][0])[i] = 0;
+  __syncthreads();
+  for (int i0 = beg; i0 < end; i0 += 32) {
+    const int i = i0 + lane;
+    const int e = i < end ? w.sel[i] : -1;
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(m) - 1) cnt[warp][e] += __popc(m);
+    __syncwarp();
+  }
+  __syncthreads();
+  if (threadIdx.x < d.E) {  // exclusive prefix over warps, per expert
+    const int e = threadIdx.x;
+    int run = 0;
+    for (int v = 0; v < 32; ++v) {
+      const int c = cnt[v][e];
+      cnt[v][e] = run;
+      run += c;
+    }
+    off[e + 1] = run;  // totals, turned into offsets below
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    off[0] = 0;
+    for (int e = 0; e < d.E; ++e) off[e + 1] += off[e];
+    int n = 0;
+    for (int e = 0; e < d.E; ++e)
+      for (int p = off[e]; p < off[e + 1]; p += kBM) {
+        w.mb_e[n] = e;
+        w.mb_p0[n] = p;
+        w.mb_n[n] = min(kBM, off[e + 1] - p);
+        ++n;
+      }
+    *w.n_mb = n;
+  }
+  __syncthreads();
+  for (int i0 = beg; i0 < end; i0 += 32) {
+    const int i = i0 + lane;
+    const int e = i < end ? w.sel[i] : -1;
+    const unsigned m = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      const int pos = off[e] + cnt[warp][e] + __popc(m & ((1u << lane) - 1u));
+      w.perm[pos] = i;
+      w.inv[i] = pos;
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(m) - 1) cnt[warp][e] += __popc(m);
+    __syncwarp();
+  }
+}
+
+// One tile: slots [p0, p0+cnt) of expert e against 128 weight rows.
+// Thread (warp v, lane l) owns slots 4v..4v+3 and tile rows l, l+32, l+64,
+// l+96. For gate/up, tile rows 0..63 are gate rows r0.. and 64..127 are the
+// up rows of the same hidden units, so a thread holds gate and up of the
+// hidden units r0+l and r0+l+32 for its four slots.
+template <bool GU>
+__global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const uint8_t* __restrict__ experts,
+                                                      size_t ex_bytes, MlWork w) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int mb = blockIdx.y;
+  if (mb >= *w.n_mb) return;
+  const int e = w.mb_e[mb], p0 = w.mb_p0[mb], cnt = w.mb_n[mb];
+  const int in_dim = GU ? d.dim : d.H;
+  const int out_rows = GU ? d.H : d.dim;
+  const int ng = in_dim / d.group;
+  const int r0 = blockIdx.x * (GU ? kBN / 2 : kBN);
+  const uint8_t* eb = experts + (size_t)e * ex_bytes;
+  const size_t gu_bytes = (size_t)2 * d.H * (d.dim / 2);
+  const size_t gu_scales = (size_t)2 * d.H * (d.dim / d.group) * 4;
+  const uint8_t* wmat = GU ? eb : eb + gu_bytes + gu_scales;
+  const float* smat = reinterpret_cast<const float*>(GU ? eb + gu_bytes
+                                                         : eb + gu_bytes + gu_scales + (size_t)d.dim * (d.H / 2));
+  const int8_t* amat = GU ? w.xq : w.hq;
+  const float* ascale = GU ? w.xs : w.hs;
+
+  int8_t* X = reinterpret_cast<int8_t*>(smem);              // [kBM][kKC]
+  int8_t* W = X + kBM * kKC;                                 // [kBN][kWS]
+  float* S = reinterpret_cast<float*>(W + kBN * kWS);        // [kBN][kSS]
+  const uint8_t** wrow = reinterpret_cast<const uint8_t**>(S + kBN * kSS);  // [kBN]
+  const float** srow = reinterpret_cast<const float**>(wrow + kBN);          // [kBN]
+  const int8_t** arow = reinterpret_cast<const int8_t**>(srow + kBN);        // [kBM]
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < kBN) {  // weight row of tile row tid, or null past the matrix
+    const int hr = GU ? r0 + (tid & 63) : r0 + tid;
+    const int mrow = GU ? (tid < 64 ? hr : d.H + hr) : hr;
+    const bool ok = hr < out_rows;
+    wrow[tid] = ok ? wmat + (size_t)mrow * (in_dim / 2) : nullptr;
+    srow[tid] = ok ? smat + (size_t)mrow * ng : nullptr;
+  } else if (tid < kBN + kBM) {
+    const int s = tid - kBN;
+    const int p = p0 + s;
+    arow[s] = s < cnt ? (GU ? amat + (size_t)(w.perm[p] / d.K) * in_dim : amat + (size_t)p * in_dim)
+                      : nullptr;
+  }
+  float xsv[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int sl = warp * 4 + s;
+    xsv[s] = sl < cnt ? (GU ? ascale[w.perm[p0 + sl] / d.K] : ascale[p0 + sl]) : 0.0f;
+  }
+  float acc[4][4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[s][i] = 0.0f;
+
+  const int gw = d.group >> 2;  // 32-bit words per group
+  for (int k0 = 0; k0 < in_dim; k0 += kKC) {
+    const int kc = min(kKC, in_dim - k0);  // a multiple of group
+    __syncthreads();
+    // activations: kBM rows of kc int8
+    const int xch = kc >> 4;
+    for (int c = tid; c < kBM * xch; c += kThreads) {
+      const int s = c / xch, j = c - s * xch;
+      const int8_t* a = arow[s];
+      *reinterpret_cast<uint4*>(X + s * kKC + j * 16) =
+          a ? __ldg(reinterpret_cast<const uint4*>(a + k0 + j * 16)) : make_uint4(0, 0, 0, 0);
+    }
+    // weights: kBN rows of kc/2 packed bytes, unpacked to int8
+    const int wch = kc >> 5;
+    for (int c = tid; c < kBN * wch; c += kThreads) {
+      const int r = c / wch, j = c - r * wch;
+      const uint8_t* wr = wrow[r];
+      uint4* dst = reinterpret_cast<uint4*>(W + r * kWS + j * 32);
+      if (wr) {
+        unpack32(ldg_stream(wr + (k0 >> 1) + j * 16), dst);
+      } else {
+        dst[0] = make_uint4(0, 0, 0, 0);
+        dst[1] = make_uint4(0, 0, 0, 0);
+      }
+    }
+    const int gpc = kc / d.group;
+    for (int c = tid; c < kBN * gpc; c += kThreads) {
+      const int r = c / gpc, g = c - r * gpc;
+      S[r * kSS + g] = srow[r] ? __ldg(srow[r] + k0 / d.group + g) : 0.0f;
+    }
+    __syncthreads();
+    for (int g = 0; g < gpc; ++g) {
+      int dots[4][4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dots[s][i] = 0;
+      for (int q = 0; q < gw; q += 4) {
+        const int col = g * d.group + q * 4;
+        uint4 xv[4], wv[4];
+#pragma unroll
+        for (int s = 0; s < 4; ++s) xv[s] = *reinterpret_cast<const uint4*>(X + (warp * 4 + s) * kKC + col);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint4*>(W + (lane + 32 * i) * kWS + col);
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            int t = dots[s][i];
+            t = __dp4a((int)wv[i].x, (int)xv[s].x, t);
+            t = __dp4a((int)wv[i].y, (int)xv[s].y, t);
+            t = __dp4a((int)wv[i].z, (int)xv[s].z, t);
+            t = __dp4a((int)wv[i].w, (int)xv[s].w, t);
+            dots[s][i] = t;
+          }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float sc = S[(lane + 32 * i) * kSS + g];
+#pragma unroll
+        for (int s = 0; s < 4; ++s)
+          acc[s][i] = __fadd_rn(acc[s][i], __fmul_rn(__fmul_rn(i2f_exact(dots[s][i]), sc), xsv[s]));
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < 4; ++s) {
+    const int sl = warp * 4 + s;
+    if (sl >= cnt) continue;
+    const size_t p = (size_t)(p0 + sl);
+    if (GU) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int hr = r0 + lane + 32 * i;
+        if (hr < d.H) w.h[p * d.H + hr] = swiglu_elem(acc[s][i], acc[s][i + 2], hr, d.H);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = r0 + lane + 32 * i;
+        if (r < d.dim) w.y[p * d.dim + r] = acc[s][i];
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_ml_quant(MlDims d, MlWork w) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* v = reinterpret_cast<float*>(smem);
+  float* red = v + d.H;
+  const size_t p = blockIdx.x;
+  const float* h = w.h + p * d.H;
+  for (int i = threadIdx.x; i < d.H; i += blockDim.x) v[i] = h[i];
+  __syncthreads();
+  const float s = quantize_smem(v, d.H, w.hq + p * d.H, red);
+  if (threadIdx.x == 0) w.hs[p] = s;
+}
+
+__global__ void __launch_bounds__(kThreads) k_ml_combine(MlDims d, MlWork w, float* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < d.K; ++j) {
+      const int slot = t * d.K + j;
+      acc = __fadd_rn(acc, __fmul_rn(w.selw[slot], w.y[(size_t)w.inv[slot] * d.dim + i]));
+    }
+    out[(size_t)t * d.dim + i] = acc;
+  }
+}
+
+size_t gemm_smem() {
+  return (size_t)kBM * kKC + (size_t)kBN * kWS + (size_t)kBN * kSS * 4 + (2 * kBN + kBM) * sizeof(void*);
+}
+
+}  // namespace
+
+size_t ml_expert_bytes(const MlDims& d) {
+  const size_t ng_d = d.dim / d.group, ng_h = d.H / d.group;
+  return (size_t)2 * d.H * (d.dim / 2) + (size_t)2 * d.H * ng_d * 4 + (size_t)d.dim * (d.H / 2) +
+         (size_t)d.dim * ng_h * 4;
+}
+
+// Workspace regions, each 256-byte aligned; with base == nullptr only the
+// total size is computed.
+size_t ml_layout(const MlDims& d, void* base, MlWork* w) {
+  const size_t N = (size_t)d.T * d.K, nmb = N / kBM + d.E + 1;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return base ? static_cast<unsigned char*>(base) + o : nullptr;
+  };
+  MlWork t{};
+  t.sel = reinterpret_cast<int32_t*>(take(N * 4));
+  t.selw = reinterpret_cast<float*>(take(N * 4));
+  t.xq = reinterpret_cast<int8_t*>(take((size_t)d.T * d.dim));
+  t.xs = reinterpret_cast<float*>(take((size_t)d.T * 4));
+  t.perm = reinterpret_cast<int32_t*>(take(N * 4));
+  t.inv = reinterpret_cast<int32_t*>(take(N * 4));
+  t.mb_e = reinterpret_cast<int32_t*>(take(nmb * 4));
+  t.mb_p0 = reinterpret_cast<int32_t*>(take(nmb * 4));
+  t.mb_n = reinterpret_cast<int32_t*>(take(nmb * 4));
+  t.n_mb = reinterpret_cast<int32_t*>(take(4));
+  t.h = reinterpret_cast<float*>(take(N * d.H * 4));
+  t.hq = reinterpret_cast<int8_t*>(take(N * d.H));
+  t.hs = reinterpret_cast<float*>(take(N * 4));
+  t.y = reinterpret_cast<float*>(take(N * d.dim * 4));
+  if (w) *w = t;
+  return off;
+}
+
+const char* ml_check(const MlDims& d) {
+  if (d.dim <= 0 || d.H <= 0) return "dim and hidden_dim must be positive";
+  if (d.dim % 32 || d.H % 32) return "dim and hidden_dim must be multiples of 32";
+  if (d.group < 32 || d.group > 256 || (d.group & (d.group - 1)))
+    return "group must be a power of two in [32, 256]";
+  if (d.dim % d.group || d.H % d.group) return "group must divide dim and hidden_dim";
+  if (d.E < 2 || d.E > 32) return "n_experts must be in [2, 32]";
+  if (d.K < 1 || d.K > d.E) return "top_k must be in [1, n_experts]";
+  if (d.dim > 16384 || d.H > 16384) return "dim and hidden_dim must be at most 16384";
+  return nullptr;
+}
+
+cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
+                   const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s) {
+  if (d.T == 0) return cudaSuccess;
+  const size_t N = (size_t)d.T * d.K;
+  const size_t rsm = ((size_t)d.dim + 16 * d.E + 32 + 40) * 4;
+  cudaFuncSetAttribute(k_ml_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+  k_ml_route<<<d.T, kThreads, rsm, s>>>(d, x, rw, rb, w);
+  k_ml_dispatch<<<1, 1024, 0, s>>>(d, w);
+  const size_t gsm = gemm_smem();
+  cudaFuncSetAttribute(k_ml_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+  cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+  const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
+  const size_t ex = ml_expert_bytes(d);
+  k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+  const size_t qsm = ((size_t)d.H + 40) * 4;
+  cudaFuncSetAttribute(k_ml_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm);
+  k_ml_quant<<<(unsigned)N, kThreads, qsm, s>>>(d, w);
+  k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+  k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
+  return cudaGetLastError();
+}
+
+}  // namespace chalot
+
+using namespace chalot;
+
+static int ml_prepare(const chalot_moe_desc* desc, size_t n_tok, MlDims* d) {
+  if (!desc) return set_error(CHALOT_ERR_ARG, "null descriptor");
+  if (n_tok * std::max<uint32_t>(desc->top_k, 1) > (size_t)(1 << 20))
+    return set_error(CHALOT_ERR_ARG, "moe_layer: n_tok * top_k above 2^20");
+  *d = MlDims{(int)n_tok, (int)desc->dim, (int)desc->hidden_dim, (int)desc->n_experts,
+              (int)desc->top_k, (int)(desc->group ? desc->group : 32)};
+  if (const char* m = ml_check(*d)) return set_error(CHALOT_ERR_ARG, std::string("moe_layer: ") + m);
+  if (!desc->router_w || !desc->router_b || !desc->experts)
+    return set_error(CHALOT_ERR_ARG, "moe_layer: null weight pointer");
+  if (reinterpret_cast<uintptr_t>(desc->experts) & 15)
+    return set_error(CHALOT_ERR_ARG, "moe_layer: experts must be 16-byte aligned");
+  return CHALOT_OK;
+}
+
+extern "C" {
+
+__attribute__((visibility("default"))) size_t chalot_moe_workspace_size(const chalot_moe_desc* desc,
+                                                                         size_t n_tok) {
+  MlDims d;
+  if (ml_prepare(desc, n_tok, &d) != CHALOT_OK) return 0;
+  return ml_layout(d, nullptr, nullptr);
+}
+
+__attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_desc* desc, const float* x,
+                                                            size_t n_tok, float* out, int32_t* sel_out,
+                                                            float* selw_out, void* workspace,
+                                                            size_t workspace_bytes, void* stream) {
+  MlDims d;
+  if (int rc = ml_prepare(desc, n_tok, &d)) return rc;
+  if (n_tok == 0) return CHALOT_OK;
+  if (!x || !out) return set_error(CHALOT_ERR_ARG, "moe_layer: null x or out");
+  const size_t need = ml_layout(d, nullptr, nullptr);
+  if (!workspace || workspace_bytes < need)
+    return set_error(CHALOT_ERR_ARG, "moe_layer: workspace too small (need " + std::to_string(need) +
+                                         " bytes)");
+  if (reinterpret_cast<uintptr_t>(workspace) & 255)
+    return set_error(CHALOT_ERR_ARG, "moe_layer: workspace must be 256-byte aligned");
+  MlWork w;
+  ml_layout(d, workspace, &w);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t r = ml_run(d, x, desc->router_w, desc->router_b, desc->experts, w, out, s);
+  const size_t N = n_tok * d.K;
+  if (r == cudaSuccess && sel_out) r = cudaMemcpyAsync(sel_out, w.sel, N * 4, cudaMemcpyDeviceToDevice, s);
+  if (r == cudaSuccess && selw_out) r = cudaMemcpyAsync(selw_out, w.selw, N * 4, cudaMemcpyDeviceToDevice, s);
+  if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
+  return CHALOT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,38 @@
+// moe_layer.h — host-side interface of the batched MoE layer kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace chalot {
+
+struct MlDims {
+  int T, dim, H, E, K, group;
+};
+
+// Device pointers into a caller-provided workspace (ml_layout).
+struct MlWork {
+  int32_t* sel;   // [T*k] expert of each (token, choice) slot
+  float* selw;    // [T*k] its gate weight
+  int8_t* xq;     // [T][dim] quantized input rows
+  float* xs;      // [T] their scales
+  int32_t* perm;  // [T*k] expert-sorted position -> slot
+  int32_t* inv;   // [T*k] slot -> position
+  int32_t* mb_e;  // 32-slot blocks: expert, first position, slot count
+  int32_t* mb_p0;
+  int32_t* mb_n;
+  int32_t* n_mb;  // number of blocks
+  float* h;       // [T*k][H] swiglu(gate, up), by position
+  int8_t* hq;     // [T*k][H] quantized h
+  float* hs;      // [T*k]
+  float* y;       // [T*k][dim] expert outputs, by position
+};
+
+size_t ml_expert_bytes(const MlDims& d);
+size_t ml_layout(const MlDims& d, void* base, MlWork* w);
+const char* ml_check(const MlDims& d);
+cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
+                   const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s);
+
+}  // namespace chalot

@@ -176,6 +176,37 @@ int chalot_router_topk(int32_t* idx, float* weight, const float* x, const float*
                        const float* b, size_t n_tok, size_t dim, size_t n_experts,
                        size_t top_k, void* stream);
 
+/* ---- batched MoE layer (device pointers, caller-owned memory) ----------- */
+
+/* One MoE FFN layer as a .myai file stores it (src/model/weight_index.rs:
+ * 126-160): router W [E][dim] f32 and b [E] f32, then E experts back to back,
+ * each {gate+up packed int4 [2*hidden][dim/2] (gate rows first), their scales
+ * [2*hidden][dim/group] f32, down packed [dim][hidden/2], scales
+ * [dim][hidden/group]}. `experts` must be 16-byte aligned. group 0 selects 32. */
+typedef struct chalot_moe_desc {
+  uint32_t dim, hidden_dim, n_experts, top_k, group;
+  const float* router_w;
+  const float* router_b;
+  const uint8_t* experts;
+} chalot_moe_desc;
+
+/* Bytes of device workspace chalot_moe_layer needs for n_tok tokens (0 when
+ * the descriptor is invalid; chalot_last_error says why). */
+size_t chalot_moe_workspace_size(const chalot_moe_desc* desc, size_t n_tok);
+
+/* The expert block of Engine::forward (src/model/engine.rs:334-401) for n_tok
+ * input rows x[n_tok][dim] that are already the FFN's normalised input:
+ * router logits, softmax_top_k, then per selected expert gate/up matmul_int4,
+ * swiglu, down matmul_int4, and out[t] = 0 + w_0*y_0 + w_1*y_1 ... in
+ * selection order (the residual add is the caller's). Bit-exact with the
+ * reference's per-token arithmetic. sel_out/selw_out ([n_tok][top_k], may be
+ * NULL) receive the router's choices. `workspace` (256-byte aligned, at least
+ * chalot_moe_workspace_size bytes) is scratch owned by the caller; calls that
+ * share it must not overlap. Asynchronous on `stream`. */
+int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, float* out,
+                     int32_t* sel_out, float* selw_out, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
