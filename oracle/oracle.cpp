@@ -22,6 +22,7 @@
 //   apply_repetition_penalty  src/tensor/sampling.rs:168-178
 //   InferenceState::new RoPE  src/model/state.rs:41-60
 //   Engine::forward           src/model/engine.rs:173-494
+//   expert block, T tokens    src/model/engine.rs:334-401 (orc_moe_forward)
 //   Engine::generate          src/model/engine.rs:497-548
 //   sample_from_logits        src/model/engine.rs:551-569
 //   header/config/index       src/model/header.rs:40-133, config.rs:40-69,
@@ -31,6 +32,12 @@
 // -ffast-math each lane operation rounds exactly as the SIMD instruction does.
 // Transcendentals call glibc (expf, tanhf, powf, cosf, sinf), the libm Rust's
 // std links on Linux. Integer dot products are exact in any order.
+//
+// Pinning: the operators are pinned by the reference's own known-answer tests
+// (src/tensor/tests.rs, src/model/memory.rs tests; tests/test_oracle.py) and by
+// an independent numpy restatement; the reference holds no end-to-end outputs
+// and cannot be run here, so whole-model decode parity is unpinned beyond this
+// restatement.
 #include <fcntl.h>
 #include <immintrin.h>
 #include <omp.h>
