@@ -89,6 +89,7 @@ SIGNATURES = {
                                      C.c_size_t, P]),
     "chalot_moe_workspace_size": (C.c_size_t, [C.POINTER(MoeDesc), C.c_size_t]),
     "chalot_moe_layer": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P, C.c_size_t, P]),
+    "chalot_moe_layer_noalloc": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P]),
 }
 
 _lib = None

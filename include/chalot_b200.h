@@ -207,6 +207,22 @@ int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, 
                      int32_t* sel_out, float* selw_out, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* chalot_moe_layer without a workspace argument. This entry point has no
+ * counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they run a layer, such as a host whose own allocator
+ * owns the device's whole memory budget, or a host binding only plain
+ * pointers through an FFI. Its scratch is a fixed 4 MiB array inside the
+ * library on each device (held by every GPU that loads the library until the
+ * process exits); calls needing more (chalot_moe_workspace_size > 4 MiB,
+ * e.g. more than 73 tokens at dim 896, hidden 4864, top-2) fail with
+ * CHALOT_ERR_ARG. It allocates nothing. The first call on a device looks up
+ * the array's device address, so make that call before any stream capture on
+ * the device. All calls on a device share the array: calls that overlap on
+ * the GPU (other streams or threads without ordering) race. Output matches
+ * chalot_moe_layer's bit for bit. */
+int chalot_moe_layer_noalloc(const chalot_moe_desc* desc, const float* x, size_t n_tok,
+                             float* out, int32_t* sel_out, float* selw_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
