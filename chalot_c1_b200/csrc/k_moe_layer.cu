@@ -14,7 +14,9 @@
 // Kernels (all on one stream):
 //   k_ml_route     one CTA per token: router logits, top-k, quantize x
 //   k_ml_dispatch  one CTA: per-expert histogram, prefix sums, slot order,
-//                  and the table of 32-slot blocks (expert, first slot, count)
+//                  and the table of slot blocks (expert, first slot, count):
+//                  32 slots for the tile GEMMs below, 128 for the tensor-core
+//                  path (k_moe_tc.cu), which replaces k_ml_gemm for large T
 //   k_ml_gemm<GU>  tiles of 32 slots x 128 weight rows: exact int32 group dots
 //                  (dp4a on unpacked int4), the f32 group epilogue in group
 //                  order; GU=true writes swiglu(gate, up), else y
@@ -23,6 +25,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "blockops.cuh"
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) k_ml_route(MlDims d, const float* __
 // Stable counting sort of the N = T*k slots by expert. Warp v walks slots
 // [v*chunk, (v+1)*chunk) in order; lanes holding the same expert are grouped
 // with __match_any_sync, so positions follow slot order within each expert.
-__global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w) {
+__global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm) {
   __shared__ int cnt[32][33];
   __shared__ int off[33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -116,10 +120,10 @@ __global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w) {
     for (int e = 0; e < d.E; ++e) off[e + 1] += off[e];
     int n = 0;
     for (int e = 0; e < d.E; ++e)
-      for (int p = off[e]; p < off[e + 1]; p += kBM) {
+      for (int p = off[e]; p < off[e + 1]; p += bm) {
         w.mb_e[n] = e;
         w.mb_p0[n] = p;
-        w.mb_n[n] = min(kBM, off[e + 1] - p);
+        w.mb_n[n] = min(bm, off[e + 1] - p);
         ++n;
       }
     *w.n_mb = n;
@@ -360,24 +364,51 @@ const char* ml_check(const MlDims& d) {
   return nullptr;
 }
 
+static void route_and_dispatch(const MlDims& d, const float* x, const float* rw, const float* rb,
+                               const MlWork& w, int bm, cudaStream_t s) {
+  const size_t rsm = ((size_t)d.dim + 16 * d.E + 32 + 40) * 4;
+  cudaFuncSetAttribute(k_ml_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+  k_ml_route<<<d.T, kThreads, rsm, s>>>(d, x, rw, rb, w);
+  k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm);
+}
+
+static void quantize_h(const MlDims& d, const MlWork& w, cudaStream_t s) {
+  const size_t qsm = ((size_t)d.H + 40) * 4;
+  cudaFuncSetAttribute(k_ml_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm);
+  k_ml_quant<<<(unsigned)((size_t)d.T * d.K), kThreads, qsm, s>>>(d, w);
+}
+
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
                    const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
-  const size_t rsm = ((size_t)d.dim + 16 * d.E + 32 + 40) * 4;
-  cudaFuncSetAttribute(k_ml_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
-  k_ml_route<<<d.T, kThreads, rsm, s>>>(d, x, rw, rb, w);
-  k_ml_dispatch<<<1, 1024, 0, s>>>(d, w);
+  route_and_dispatch(d, x, rw, rb, w, kBM, s);
   const size_t gsm = gemm_smem();
   cudaFuncSetAttribute(k_ml_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
   cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
   const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
   const size_t ex = ml_expert_bytes(d);
   k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, experts, ex, w);
-  const size_t qsm = ((size_t)d.H + 40) * 4;
-  cudaFuncSetAttribute(k_ml_quant, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsm);
-  k_ml_quant<<<(unsigned)N, kThreads, qsm, s>>>(d, w);
+  quantize_h(d, w, s);
   k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+  k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
+  return cudaGetLastError();
+}
+
+// The same layer with the expert products on the tensor cores.
+cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const float* rb,
+                      const uint8_t* experts, const MlWork& w, const MlTcWork& t, float* out,
+                      cudaStream_t s) {
+  if (d.T == 0) return cudaSuccess;
+  const size_t N = (size_t)d.T * d.K;
+  cudaError_t r = cudaMemsetAsync(t.err, 0, 16, s);
+  if (r != cudaSuccess) return r;
+  route_and_dispatch(d, x, rw, rb, w, 128, s);
+  if ((r = ml_tc_prepare(d, experts, w, t, s)) != cudaSuccess) return r;
+  const unsigned nmb = (unsigned)std::min(N, N / 128 + d.E);
+  if ((r = ml_tc_gemm(d, true, w, t, nmb, s)) != cudaSuccess) return r;
+  quantize_h(d, w, s);
+  if ((r = ml_tc_gemm(d, false, w, t, nmb, s)) != cudaSuccess) return r;
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
   return cudaGetLastError();
 }
@@ -400,13 +431,27 @@ static int ml_prepare(const chalot_moe_desc* desc, size_t n_tok, MlDims* d) {
   return CHALOT_OK;
 }
 
+// Tensor-core expert products from this many (token, choice) slots on, when
+// the shape allows them (group 32, dim and hidden_dim multiples of 128).
+// CHALOT_MOE_PATH=simt|tc overrides the choice (tests use it to cover both).
+static constexpr size_t kTcMinSlots = 1024;
+
+static bool use_tc(const MlDims& d) {
+  const char* env = std::getenv("CHALOT_MOE_PATH");
+  if (env && !std::strcmp(env, "simt")) return false;
+  if (!ml_tc_eligible(d)) return false;
+  if (env && !std::strcmp(env, "tc")) return true;
+  return (size_t)d.T * d.K >= kTcMinSlots;
+}
+
 extern "C" {
 
 __attribute__((visibility("default"))) size_t chalot_moe_workspace_size(const chalot_moe_desc* desc,
                                                                          size_t n_tok) {
   MlDims d;
   if (ml_prepare(desc, n_tok, &d) != CHALOT_OK) return 0;
-  return ml_layout(d, nullptr, nullptr);
+  const size_t simt = ml_layout(d, nullptr, nullptr);
+  return use_tc(d) ? ml_tc_layout(d, simt, nullptr, nullptr) : simt;
 }
 
 __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_desc* desc, const float* x,
@@ -417,7 +462,9 @@ __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_des
   if (int rc = ml_prepare(desc, n_tok, &d)) return rc;
   if (n_tok == 0) return CHALOT_OK;
   if (!x || !out) return set_error(CHALOT_ERR_ARG, "moe_layer: null x or out");
-  const size_t need = ml_layout(d, nullptr, nullptr);
+  const bool tc = use_tc(d);
+  const size_t simt = ml_layout(d, nullptr, nullptr);
+  const size_t need = tc ? ml_tc_layout(d, simt, nullptr, nullptr) : simt;
   if (!workspace || workspace_bytes < need)
     return set_error(CHALOT_ERR_ARG, "moe_layer: workspace too small (need " + std::to_string(need) +
                                          " bytes)");
@@ -426,11 +473,21 @@ __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_des
   MlWork w;
   ml_layout(d, workspace, &w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t r = ml_run(d, x, desc->router_w, desc->router_b, desc->experts, w, out, s);
+  MlTcWork t{};
+  if (tc) ml_tc_layout(d, simt, workspace, &t);
+  cudaError_t r = tc ? ml_run_tc(d, x, desc->router_w, desc->router_b, desc->experts, w, t, out, s)
+                     : ml_run(d, x, desc->router_w, desc->router_b, desc->experts, w, out, s);
   const size_t N = n_tok * d.K;
   if (r == cudaSuccess && sel_out) r = cudaMemcpyAsync(sel_out, w.sel, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess && selw_out) r = cudaMemcpyAsync(selw_out, w.selw, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
+  if (tc && std::getenv("CHALOT_MOE_SYNC_CHECK")) {  // tests: surface a bounded-wait timeout
+    unsigned err = 0;
+    r = cudaMemcpyAsync(&err, t.err, 4, cudaMemcpyDeviceToHost, s);
+    if (r == cudaSuccess) r = cudaStreamSynchronize(s);
+    if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
+    if (err) return set_error(CHALOT_ERR_TIMEOUT, "moe_layer: a tensor-core pipeline wait timed out");
+  }
   return CHALOT_OK;
 }
 

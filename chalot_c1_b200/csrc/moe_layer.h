@@ -29,10 +29,28 @@ struct MlWork {
   float* y;       // [T*k][dim] expert outputs, by position
 };
 
+// Extra workspace of the tensor-core path (k_moe_tc.cu).
+struct MlTcWork {
+  int8_t* xp;     // [T*k][dim] quantized x rows in expert-sorted order
+  float* xsp;     // [T*k] their scales
+  int8_t* w8gu;   // [E*2H][dim] gate/up weights as int8, gate/up interleaved per 64 units
+  float* sgu;     // [E*dim/group][2H] their group scales, transposed
+  int8_t* w8dn;   // [E*dim][H] down weights as int8
+  float* sdn;     // [E*H/group][dim] their group scales, transposed
+  unsigned* err;  // nonzero when a bounded wait ran out
+};
+
 size_t ml_expert_bytes(const MlDims& d);
 size_t ml_layout(const MlDims& d, void* base, MlWork* w);
 const char* ml_check(const MlDims& d);
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
                    const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s);
+
+bool ml_tc_eligible(const MlDims& d);
+size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t);
+cudaError_t ml_tc_prepare(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork& t,
+                          cudaStream_t s);
+cudaError_t ml_tc_gemm(const MlDims& d, bool gate_up, const MlWork& w, const MlTcWork& t,
+                       unsigned n_mblocks, cudaStream_t s);
 
 }  // namespace chalot

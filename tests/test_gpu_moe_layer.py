@@ -95,3 +95,60 @@ def test_moe_layer_argument_errors(moe, chalot):
     with pytest.raises(ChalotError, match="group"):
         check(lib().chalot_moe_layer(C.byref(bad), x.data_ptr(), 8, out.data_ptr(), None, None,
                                      dev.workspace.data_ptr(), need, None))
+
+
+# ---- tensor-core path (tcgen05 kind::i8 group dots + f32 group epilogue) ----
+
+TC_CASES = [
+    # dim, hidden, E, K, T
+    (256, 1024, 8, 2, 1),
+    (256, 1024, 8, 2, 100),
+    (256, 1024, 8, 2, 700),
+    (256, 512, 4, 1, 260),
+    (896, 4864, 8, 2, 300),
+    (2048, 5632, 16, 2, 64),
+]
+
+
+@pytest.fixture
+def tc_path(monkeypatch):
+    monkeypatch.setenv("CHALOT_MOE_PATH", "tc")
+    monkeypatch.setenv("CHALOT_MOE_SYNC_CHECK", "1")
+
+
+@pytest.mark.parametrize("dim,hidden,E,K,T", TC_CASES)
+def test_moe_layer_tensor_core_bit_exact(moe, oracle_lib, tc_path, dim, hidden, E, K, T):
+    ref, ref_sel, out, sel, _ = _run(moe, oracle_lib, dim, hidden, E, K, 32, T, seed=T + 7 * E)
+    assert (sel == ref_sel).all()
+    assert (out.view(np.uint32) == ref.view(np.uint32)).all()
+
+
+def test_moe_layer_tensor_core_skewed(moe, oracle_lib, tc_path):
+    # every token on experts 3 and 5: several 128-slot blocks of one expert,
+    # a partial last block, and experts with no slots at all
+    import torch
+    dim, hidden, E, K, T = 256, 512, 8, 2, 333
+    layer = moe.synthetic_moe_layer(dim, hidden, E, K, 32, seed=19)
+    layer.router_b[3], layer.router_b[5] = 50.0, 40.0
+    x = np.random.default_rng(3).standard_normal((T, dim), dtype=np.float32)
+    ref, ref_sel = oracle_lib.moe_forward(x, layer.layer_bytes(), dim, hidden, E, K, 32,
+                                          threads=oracle_lib.hw_threads())
+    out, sel, _ = moe.MoeLayer(layer, T)(torch.from_numpy(x).cuda())
+    assert (sel.cpu().numpy() == ref_sel).all()
+    assert (out.cpu().numpy().view(np.uint32) == ref.view(np.uint32)).all()
+
+
+def test_moe_layer_paths_agree_at_prefill_size(moe, monkeypatch):
+    # 4096 tokens of the Qwen-shaped layer: the tensor-core path against the
+    # tile-GEMM path (both bit-exact restatements of the same arithmetic)
+    import torch
+    layer = moe.synthetic_moe_layer(896, 4864, 8, 2, 32, seed=3)
+    x = torch.from_numpy(np.random.default_rng(3).standard_normal((4096, 896), dtype=np.float32)).cuda()
+    monkeypatch.setenv("CHALOT_MOE_PATH", "simt")
+    a, sa, _ = moe.MoeLayer(layer, 4096)(x)
+    monkeypatch.setenv("CHALOT_MOE_PATH", "tc")
+    monkeypatch.setenv("CHALOT_MOE_SYNC_CHECK", "1")
+    b, sb, _ = moe.MoeLayer(layer, 4096)(x)
+    torch.cuda.synchronize()
+    assert torch.equal(sa, sb)
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32))
