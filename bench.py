@@ -290,16 +290,93 @@ def run_profile(args):
     eng.close()
 
 
+MOE_T, MOE_DIM, MOE_H, MOE_E, MOE_K = 4096, 896, 4864, 8, 2
+# int dot work of one layer call: T tokens x top-2 x (gate+up+down = 3 x dim x H) MACs x 2
+MOE_OPS = MOE_T * MOE_K * 3 * MOE_DIM * MOE_H * 2
+
+
+def bench_moe_prefill(reps: int = 10, warmup: int = 3, path: str | None = None,
+                      cpu_tokens: int = 0) -> dict:
+    """Single MoE layer prefill: 4096 tokens of N(0,1) activations (seed 3)
+    through chalot_moe_layer with the Qwen-shaped layer (router 896->8
+    N(0,0.02), experts int4 g32 SwiGLU 896->4864->896, top-2). Device time
+    by CUDA events around each call (inputs resident), plus an end-to-end
+    time with the activations copied in from pinned host memory and the
+    output copied back."""
+    import numpy as np
+    import torch
+    from chalot_c1_b200 import moe
+    old = os.environ.get("CHALOT_MOE_PATH")
+    if path:
+        os.environ["CHALOT_MOE_PATH"] = path
+    try:
+        layer = moe.synthetic_moe_layer(MOE_DIM, MOE_H, MOE_E, MOE_K, 32, seed=3)
+        xh = np.random.default_rng(3).standard_normal((MOE_T, MOE_DIM), dtype=np.float32)
+        dev = moe.MoeLayer(layer, MOE_T)
+        x = torch.from_numpy(xh).cuda()
+        out = torch.empty((MOE_T, MOE_DIM), dtype=torch.float32, device="cuda")
+        x_pin = torch.from_numpy(xh).pin_memory()
+        out_pin = torch.empty((MOE_T, MOE_DIM), dtype=torch.float32).pin_memory()
+        for _ in range(warmup):
+            dev(x, out=out)
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * reps)]
+        for i in range(reps):
+            ev[2 * i].record()
+            dev(x, out=out)
+            ev[2 * i + 1].record()
+        torch.cuda.synchronize()
+        ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(reps))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            x.copy_(x_pin, non_blocking=True)
+            dev(x, out=out)
+            out_pin.copy_(out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / reps
+        res = {"tokens": MOE_T, "ms": ms, "tok_s": MOE_T / (ms * 1e-3),
+               "tops": MOE_OPS / (ms * 1e-3) / 1e12, "e2e_ms": e2e_ms,
+               "e2e_tok_s": MOE_T / (e2e_ms * 1e-3),
+               "path": os.environ.get("CHALOT_MOE_PATH", "auto")}
+        if cpu_tokens:
+            from oracle import oracle as orc
+            t0 = time.perf_counter()
+            orc.moe_forward(xh[:cpu_tokens], layer.layer_bytes(), MOE_DIM, MOE_H, MOE_E, MOE_K, 32,
+                            threads=orc.hw_threads())
+            dt = time.perf_counter() - t0
+            res["cpu"] = {"tok_s": cpu_tokens / dt, "cores": orc.hw_threads(), "kind": "port",
+                          "sample": f"{cpu_tokens} tokens ({dt:.2f} s)"}
+        return res
+    finally:
+        if path:
+            if old is None:
+                os.environ.pop("CHALOT_MOE_PATH", None)
+            else:
+                os.environ["CHALOT_MOE_PATH"] = old
+
+
+def run_moe(args):
+    for path in ("tc", "simt"):
+        r = bench_moe_prefill(reps=args.steps, warmup=args.warmup, path=path,
+                              cpu_tokens=256 if path == "tc" else 0)
+        print(json.dumps(r), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="bench", choices=["bench", "profile"])
+    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe"])
     a = ap.parse_args()
     if a.mode == "profile":
         run_profile(a)
+        return
+    if a.mode == "moe":
+        run_moe(a)
         return
     ws, rank, local = dist_setup()
     try:

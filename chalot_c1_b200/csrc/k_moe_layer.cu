@@ -402,12 +402,13 @@ cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const fl
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
   cudaError_t r = cudaMemsetAsync(t.err, 0, 16, s);
+  if (r == cudaSuccess) r = cudaMemsetAsync(t.amax, 0, N * 4, s);
   if (r != cudaSuccess) return r;
   route_and_dispatch(d, x, rw, rb, w, 128, s);
   if ((r = ml_tc_prepare(d, experts, w, t, s)) != cudaSuccess) return r;
   const unsigned nmb = (unsigned)std::min(N, N / 128 + d.E);
   if ((r = ml_tc_gemm(d, true, w, t, nmb, s)) != cudaSuccess) return r;
-  quantize_h(d, w, s);
+  if ((r = ml_tc_quant(d, w, t, s)) != cudaSuccess) return r;
   if ((r = ml_tc_gemm(d, false, w, t, nmb, s)) != cudaSuccess) return r;
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
   return cudaGetLastError();

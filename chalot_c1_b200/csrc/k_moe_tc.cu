@@ -7,8 +7,8 @@
 // come from the tensor cores: one M=128 x N=128 x K=32 MMA per group writes
 // the int32 dots of a 128-slot x 128-row tile into TMEM (overwrite, not
 // accumulate), and eight epilogue warps read them back and run the f32 group
-// epilogue in registers, in group order. The MMA for group g+1 (second TMEM
-// buffer) overlaps the epilogue of group g; the epilogue is the bound.
+// epilogue in registers, in group order. Four TMEM buffers let the MMAs run
+// up to three groups ahead of the epilogue, which is the bound.
 //
 // Operands are int8 in HBM, K-major, loaded by 2-D TMA with the 128-byte
 // swizzle into a 4-stage ring (128 columns = 4 groups per stage):
@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "blockops.cuh"
@@ -39,11 +40,12 @@ constexpr int kTcThreads = 320;
 constexpr int kStages = 4;        // A/B ring depth (128 columns each)
 constexpr int kSRing = 4;         // scale ring depth
 constexpr int kTileBytes = 128 * 128;
-constexpr uint32_t kTmemCols = 256;  // two 128-column int32 buffers
+constexpr int kTBufs = 4;            // TMEM accumulator buffers (128 columns each)
+constexpr uint32_t kTmemCols = 128 * kTBufs;
 constexpr uint32_t kIdesc = tc_idesc_i8(128, 128);
 
 struct TcSmem {
-  uint64_t full[kStages], empty[kStages], s_full[kSRing], s_empty[kSRing], t_full[2], t_empty[2], done;
+  uint64_t full[kStages], empty[kStages], s_full[kSRing], s_empty[kSRing], t_full[kTBufs], t_empty[kTBufs], done;
   uint32_t tmem;
   int abort;
 };
@@ -123,20 +125,26 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, un
   return false;
 }
 
+constexpr uint32_t kMagic = 0x4B400000u;  // bits of 1.5 * 2^23
+
+// Persistent kernel: CTA b takes tiles b, b + gridDim.x, ... of the
+// (128-slot block, 128-row tile) grid, row tiles fastest. The TMA ring, the
+// scale ring and the two TMEM buffers run continuously across tiles, so the
+// next tile's loads and first MMAs overlap this tile's last groups and its
+// stores. Each TMEM buffer holds 1.5*2^23 in every element before an MMA
+// accumulates a group's int32 dots onto it; the bits then read back as the
+// float 12582912 + gdot (exact, |gdot| < 2^22), so one packed subtraction
+// gives (float)gdot, and the epilogue refills the buffer after reading it.
 template <bool GU>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
-              const __grid_constant__ CUtensorMap tS, MlDims d, MlWork w, MlTcWork t) {
+              const __grid_constant__ CUtensorMap tS, MlDims d, MlWork w, MlTcWork t, int ntn) {
   extern __shared__ unsigned char smem_raw[];
-  const int mb = blockIdx.y;
-  if (mb >= *w.n_mb) return;
-  const int e = w.mb_e[mb], p0 = w.mb_p0[mb], cnt = w.mb_n[mb];
-  const int nb = blockIdx.x;
+  const int total = *w.n_mb * ntn;
+  if ((int)blockIdx.x >= total) return;
   const int K = GU ? d.dim : d.H;
   const int nchunks = K >> 7, ngroups = K >> 5;
   const int ng = K / d.group;
-  const int brow0 = GU ? e * 2 * d.H + nb * 128 : e * d.dim + nb * 128;
-  const int srow0 = e * ng;
 
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   unsigned char* sbase = smem_raw + (base - smem_u32(smem_raw));
@@ -155,7 +163,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init_n(&sm->s_full[i], 1);
       mbar_init_n(&sm->s_empty[i], 8);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kTBufs; ++i) {
       mbar_init_n(&sm->t_full[i], 1);
       mbar_init_n(&sm->t_empty[i], 8);
     }
@@ -171,117 +179,168 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
-      int issued = 0, s_issued = 0;
-      for (int c = 0; c < nchunks && !aborted(sm); ++c) {
-        const int st = c % kStages, n = c / kStages;
-        if (n > 0 && !wait_or_abort(&sm->empty[st], (n - 1) & 1, t.err, sm)) break;
-        mbar_expect_tx(&sm->full[st], 2 * kTileBytes);
-        tma_load_2d(A + st * kTileBytes, &tA, c * 128, p0, &sm->full[st]);
-        tma_load_2d(B + st * kTileBytes, &tB, c * 128, brow0, &sm->full[st]);
-        issued = c + 1;
-        const int ss = c % kSRing, m = c / kSRing;
-        if (m > 0 && !wait_or_abort(&sm->s_empty[ss], (m - 1) & 1, t.err, sm)) break;
-        mbar_expect_tx(&sm->s_full[ss], 4 * 128 * 4);
-        tma_load_2d(S + ss * 4 * 128, &tS, nb * 128, srow0 + c * 4, &sm->s_full[ss]);
-        s_issued = c + 1;
+      int it = 0, s_issued = 0;
+      for (int tile = blockIdx.x; tile < total && !aborted(sm); tile += gridDim.x) {
+        const int mb = tile / ntn, nb = tile - mb * ntn;
+        const int e = w.mb_e[mb], p0 = w.mb_p0[mb];
+        const int brow0 = GU ? e * 2 * d.H + nb * 128 : e * d.dim + nb * 128;
+        bool ok = true;
+        for (int c = 0; c < nchunks; ++c, ++it) {
+          const int st = it % kStages, n = it / kStages;
+          if (n > 0 && !wait_or_abort(&sm->empty[st], (n - 1) & 1, t.err, sm)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&sm->full[st], 2 * kTileBytes);
+          tma_load_2d(A + st * kTileBytes, &tA, c * 128, p0, &sm->full[st]);
+          tma_load_2d(B + st * kTileBytes, &tB, c * 128, brow0, &sm->full[st]);
+          const int m = it / kSRing, ss = it % kSRing;
+          if (m > 0 && !wait_or_abort(&sm->s_empty[ss], (m - 1) & 1, t.err, sm)) {
+            ok = false;
+            ++it;
+            break;
+          }
+          mbar_expect_tx(&sm->s_full[ss], 4 * 128 * 4);
+          tma_load_2d(S + ss * 4 * 128, &tS, nb * 128, e * ng + c * 4, &sm->s_full[ss]);
+          ++s_issued;
+        }
+        if (!ok) break;
       }
       // copies still in flight land before the CTA exits
-      for (int c = max(0, issued - kStages); c < issued; ++c)
+      for (int c = max(0, it - kStages); c < it; ++c)
         mbar_wait(&sm->full[c % kStages], (c / kStages) & 1, t.err);
       for (int c = max(0, s_issued - kSRing); c < s_issued; ++c)
         mbar_wait(&sm->s_full[c % kSRing], (c / kSRing) & 1, t.err);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
-      for (int c = 0; c < nchunks && !aborted(sm); ++c) {
-        const int st = c % kStages;
-        if (!wait_or_abort(&sm->full[st], (c / kStages) & 1, t.err, sm)) break;
-        tc_fence_after();
-        const uint32_t a0 = smem_u32(A + st * kTileBytes), b0 = smem_u32(B + st * kTileBytes);
+      int it = 0, gall = 0;
+      for (int tile = blockIdx.x; tile < total && !aborted(sm); tile += gridDim.x) {
         bool ok = true;
-        for (int j = 0; j < 4; ++j) {
-          const int g = c * 4 + j, buf = g & 1, u = g >> 1;
-          if (u > 0) {
-            if (!wait_or_abort(&sm->t_empty[buf], (u - 1) & 1, t.err, sm)) {
+        for (int c = 0; c < nchunks && ok; ++c, ++it) {
+          const int st = it % kStages;
+          if (!wait_or_abort(&sm->full[st], (it / kStages) & 1, t.err, sm)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(A + st * kTileBytes), b0 = smem_u32(B + st * kTileBytes);
+          for (int j = 0; j < 4; ++j, ++gall) {
+            const int buf = gall % kTBufs;
+            if (!wait_or_abort(&sm->t_empty[buf], (gall / kTBufs) & 1, t.err, sm)) {
               ok = false;
               break;
             }
             tc_fence_after();
+            tc_mma_i8(tmem + buf * 128, tc_desc_sw128(a0 + j * 32), tc_desc_sw128(b0 + j * 32), kIdesc, 1);
+            tc_commit(&sm->t_full[buf]);
           }
-          tc_mma_i8(tmem + buf * 128, tc_desc_sw128(a0 + j * 32), tc_desc_sw128(b0 + j * 32), kIdesc, 0);
-          tc_commit(&sm->t_full[buf]);
+          if (ok) tc_commit(&sm->empty[st]);
         }
         if (!ok) break;
-        tc_commit(&sm->empty[st]);
       }
       tc_commit(&sm->done);  // every MMA issued has completed before TMEM is freed
       mbar_wait(&sm->done, 0, t.err);
     }
   } else {  // epilogue
     const int ew = warp - 2, q = warp & 3, half = ew >> 2;
-    const int row = 32 * q + lane;
-    const bool live = row < cnt;
-    const float xs = live ? (GU ? t.xsp[p0 + row] : w.hs[p0 + row]) : 0.0f;
     const int col_a = GU ? 32 * half : 64 * half;
     const int col_b = GU ? 64 + 32 * half : 64 * half + 32;
-    float acc0[32], acc1[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) acc0[j] = acc1[j] = 0.0f;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
-    for (int g = 0; g < ngroups; ++g) {
-      const int buf = g & 1, c = g >> 2, gl = g & 3, ss = c % kSRing;
-      if (!wait_or_abort(&sm->t_full[buf], (g >> 1) & 1, t.err, sm)) break;
-      tc_fence_after();
-      if (gl == 0 && !wait_or_abort(&sm->s_full[ss], (c / kSRing) & 1, t.err, sm)) break;
-      uint32_t r0[32], r1[32];
-      tc_ld32(lane_addr + buf * 128 + col_a, r0);
-      tc_ld32(lane_addr + buf * 128 + col_b, r1);
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm->t_empty[buf]);
-      const float4* sa = reinterpret_cast<const float4*>(S + (ss * 4 + gl) * 128 + col_a);
-      const float4* sb = reinterpret_cast<const float4*>(S + (ss * 4 + gl) * 128 + col_b);
-#pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 va = sa[j4], vb = sb[j4];
-        const float fa[4] = {va.x, va.y, va.z, va.w}, fb[4] = {vb.x, vb.y, vb.z, vb.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = j4 * 4 + u;
-          acc0[j] = __fadd_rn(acc0[j], __fmul_rn(__fmul_rn(i2f_exact((int)r0[j]), fa[u]), xs));
-          acc1[j] = __fadd_rn(acc1[j], __fmul_rn(__fmul_rn(i2f_exact((int)r1[j]), fb[u]), xs));
-        }
-      }
-      if (gl == 3) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sm->s_empty[ss]);
-      }
+    // every buffer starts at the bias
+    for (int b = 0; b < kTBufs; ++b) {
+      tc_st32_fill(lane_addr + b * 128 + col_a, kMagic);
+      tc_st32_fill(lane_addr + b * 128 + col_b, kMagic);
     }
-    if (live && !aborted(sm)) {
-      const size_t p = (size_t)(p0 + row);
-      if (GU) {
-        const int hu0 = nb * 64 + 32 * half;
-        float4* o = reinterpret_cast<float4*>(w.h + p * d.H + hu0);
+    tc_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (int b = 0; b < kTBufs; ++b) mbar_arrive(&sm->t_empty[b]);
+    const f32x2 bias = f2_pack(12582912.0f, 12582912.0f);
+    int it = 0, gall = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      const int mb = tile / ntn, nb = tile - mb * ntn;
+      const int p0 = w.mb_p0[mb], cnt = w.mb_n[mb];
+      const int row = 32 * q + lane;
+      const bool live = row < cnt;
+      const float xs1 = live ? (GU ? t.xsp[p0 + row] : w.hs[p0 + row]) : 0.0f;
+      const f32x2 xs = f2_pack(xs1, xs1);
+      f32x2 acc0[16], acc1[16];
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          float v[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int j = j4 * 4 + u;
-            v[u] = swiglu_elem(acc0[j], acc1[j], hu0 + j, d.H);
-          }
-          o[j4] = make_float4(v[0], v[1], v[2], v[3]);
+      for (int j = 0; j < 16; ++j) acc0[j] = acc1[j] = 0ull;
+      for (int g = 0; g < ngroups; ++g, ++gall) {
+        const int buf = gall % kTBufs, gl = g & 3, ss = it % kSRing;
+        if (!wait_or_abort(&sm->t_full[buf], (gall / kTBufs) & 1, t.err, sm)) {
+          ok = false;
+          break;
         }
-      } else {
-        float4* o = reinterpret_cast<float4*>(w.y + p * d.dim + nb * 128 + col_a);
+        tc_fence_after();
+        if (gl == 0 && !wait_or_abort(&sm->s_full[ss], (it / kSRing) & 1, t.err, sm)) {
+          ok = false;
+          break;
+        }
+        // one 32-column half at a time keeps the live registers under the
+        // 168 a thread gets with 3 warps per SM sub-partition
+        const uint32_t ta = lane_addr + buf * 128;
+        const f32x2* sa = reinterpret_cast<const f32x2*>(S + (ss * 4 + gl) * 128 + col_a);
+        const f32x2* sb = reinterpret_cast<const f32x2*>(S + (ss * 4 + gl) * 128 + col_b);
+        uint32_t r[32];
+        tc_ld32(ta + col_a, r);
+        tc_wait_ld();
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4)
-          o[j4] = make_float4(acc0[4 * j4], acc0[4 * j4 + 1], acc0[4 * j4 + 2], acc0[4 * j4 + 3]);
-        o += 8;
+        for (int j = 0; j < 16; ++j) {  // acc = acc + ((float)gdot * s) * xs, lane-wise in f32
+          const f32x2 ga = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
+          acc0[j] = f2_add_nc(acc0[j], f2_mul(f2_mul(ga, sa[j]), xs));
+        }
+        tc_ld32(ta + col_b, r);
+        tc_wait_ld();
+        tc_st32_fill(ta + col_a, kMagic);
+        tc_st32_fill(ta + col_b, kMagic);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->t_empty[buf]);
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4)
-          o[j4] = make_float4(acc1[4 * j4], acc1[4 * j4 + 1], acc1[4 * j4 + 2], acc1[4 * j4 + 3]);
+        for (int j = 0; j < 16; ++j) {
+          const f32x2 gb = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
+          acc1[j] = f2_add_nc(acc1[j], f2_mul(f2_mul(gb, sb[j]), xs));
+        }
+        if (gl == 3) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm->s_empty[ss]);
+          ++it;
+        }
+      }
+      if (!ok || aborted(sm)) break;
+      if (live) {
+        const size_t p = (size_t)(p0 + row);
+        if (GU) {
+          const int hu0 = nb * 64 + 32 * half;
+          float4* o = reinterpret_cast<float4*>(w.h + p * d.H + hu0);
+          float amax = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            float g0, g1, g2, g3, u0, u1, u2, u3;
+            f2_unpack(acc0[j], g0, g1);
+            f2_unpack(acc0[j + 1], g2, g3);
+            f2_unpack(acc1[j], u0, u1);
+            f2_unpack(acc1[j + 1], u2, u3);
+            const int k = hu0 + 2 * j;
+            const float4 v = make_float4(swiglu_elem(g0, u0, k, d.H), swiglu_elem(g1, u1, k + 1, d.H),
+                                         swiglu_elem(g2, u2, k + 2, d.H), swiglu_elem(g3, u3, k + 3, d.H));
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            o[j >> 1] = v;
+          }
+          atomicMax(t.amax + p, __float_as_uint(amax));  // non-negative floats order as their bits
+        } else {
+          f32x2* o = reinterpret_cast<f32x2*>(w.y + p * d.dim + nb * 128 + col_a);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[j] = acc0[j];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) o[16 + j] = acc1[j];
+        }
       }
     }
   }
@@ -291,6 +350,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc_fence_after();
     tc_dealloc(tmem, kTmemCols);
   }
+}
+
+// quantize_f32_to_i8 of each h row with its absmax already reduced by the
+// gate/up epilogue: 16 elements per thread, one 16-byte store.
+__global__ void __launch_bounds__(256) k_tc_quant(MlDims d, MlWork w, MlTcWork t) {
+  const int per_row = d.H >> 4;
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)d.T * d.K * per_row) return;
+  const long p = i / per_row;
+  const int c = (int)(i - p * per_row);
+  float scale, inv;
+  quant_scale(__uint_as_float(t.amax[p]), &scale, &inv);
+  const float4* src = reinterpret_cast<const float4*>(w.h + p * d.H + c * 16);
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 v = src[k];
+    o[k] = (uint32_t)(uint8_t)quant_elem(v.x, inv) | ((uint32_t)(uint8_t)quant_elem(v.y, inv) << 8) |
+           ((uint32_t)(uint8_t)quant_elem(v.z, inv) << 16) | ((uint32_t)(uint8_t)quant_elem(v.w, inv) << 24);
+  }
+  *reinterpret_cast<uint4*>(w.hq + p * d.H + c * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (c == 0) w.hs[p] = scale;
 }
 
 // ---- host: tensor maps -------------------------------------------------------
@@ -348,6 +429,7 @@ size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t) {
   w.sgu = reinterpret_cast<float*>(take((size_t)d.E * ngd * 2 * d.H * 4));
   w.w8dn = reinterpret_cast<int8_t*>(take((size_t)d.E * d.dim * d.H));
   w.sdn = reinterpret_cast<float*>(take((size_t)d.E * ngh * d.dim * 4));
+  w.amax = reinterpret_cast<unsigned*>(take(N * 4));
   w.err = reinterpret_cast<unsigned*>(take(16));
   if (t) *t = w;
   return off;
@@ -384,8 +466,18 @@ cudaError_t ml_tc_gemm(const MlDims& d, bool gate_up, const MlWork& w, const MlT
   auto k = gate_up ? k_tc_gemm<true> : k_tc_gemm<false>;
   cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (r != cudaSuccess) return r;
-  const unsigned ntiles = gate_up ? (unsigned)(d.H / 64) : (unsigned)(d.dim / 128);
-  k<<<dim3(ntiles, n_mblocks), kTcThreads, smem, s>>>(mA, mB, mS, d, w, t);
+  const int ntn = gate_up ? d.H / 64 : d.dim / 128;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned grid = (unsigned)std::min<size_t>((size_t)n_mblocks * ntn, (size_t)sms);
+  k<<<grid, kTcThreads, smem, s>>>(mA, mB, mS, d, w, t, ntn);
+  return cudaGetLastError();
+}
+
+cudaError_t ml_tc_quant(const MlDims& d, const MlWork& w, const MlTcWork& t, cudaStream_t s) {
+  const long n = (long)d.T * d.K * (d.H / 16);
+  k_tc_quant<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(d, w, t);
   return cudaGetLastError();
 }
 

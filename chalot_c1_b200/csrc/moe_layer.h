@@ -37,6 +37,7 @@ struct MlTcWork {
   float* sgu;     // [E*dim/group][2H] their group scales, transposed
   int8_t* w8dn;   // [E*dim][H] down weights as int8
   float* sdn;     // [E*H/group][dim] their group scales, transposed
+  unsigned* amax; // [T*k] absmax of each h row (float bits), reduced by the gate/up epilogue
   unsigned* err;  // nonzero when a bounded wait ran out
 };
 
@@ -52,5 +53,6 @@ cudaError_t ml_tc_prepare(const MlDims& d, const uint8_t* experts, const MlWork&
                           cudaStream_t s);
 cudaError_t ml_tc_gemm(const MlDims& d, bool gate_up, const MlWork& w, const MlTcWork& t,
                        unsigned n_mblocks, cudaStream_t s);
+cudaError_t ml_tc_quant(const MlDims& d, const MlWork& w, const MlTcWork& t, cudaStream_t s);
 
 }  // namespace chalot

@@ -94,4 +94,59 @@ CHALOT_DEV void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 CHALOT_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Writes the value v to 32 consecutive 32-bit TMEM columns of this thread's lane.
+CHALOT_DEV void tc_st32_fill(uint32_t taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+CHALOT_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Packed pairs of f32 (sm_100a f32x2 arithmetic, each lane rounded to nearest
+// as the scalar .rn instruction rounds).
+typedef unsigned long long f32x2;
+CHALOT_DEV f32x2 f2_pack(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+CHALOT_DEV f32x2 f2_pack_bits(uint32_t lo, uint32_t hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+CHALOT_DEV void f2_unpack(f32x2 v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+CHALOT_DEV f32x2 f2_add(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+CHALOT_DEV f32x2 f2_sub(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+CHALOT_DEV f32x2 f2_mul(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+CHALOT_DEV f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// acc + p lane-wise with scalar add.rn.f32. A packed add (or fma(p, 1, acc))
+// fed by a packed multiply was contracted into one fused multiply-add by the
+// assembler despite .rn (measured: results then equal fma(x, y, acc)); a
+// scalar add with an explicit rounding modifier is never contracted.
+CHALOT_DEV f32x2 f2_add_nc(f32x2 acc, f32x2 p) {
+  float a0, a1, p0, p1;
+  f2_unpack(acc, a0, a1);
+  f2_unpack(p, p0, p1);
+  return f2_pack(__fadd_rn(a0, p0), __fadd_rn(a1, p1));
+}
+
 }  // namespace chalot
