@@ -357,6 +357,77 @@ def bench_moe_prefill(reps: int = 10, warmup: int = 3, path: str | None = None,
                 os.environ["CHALOT_MOE_PATH"] = old
 
 
+PG_SEQ, PG_TOK, PG_P, PG_H, PG_HD, PG_LAYERS = 32, 8192, 16, 14, 64, 24
+
+
+def bench_paged(reps: int = 5, warmup: int = 3, layers: int = PG_LAYERS) -> dict:
+    """Long-context paged int8 KV attention: 32 sequences x 8192 cached tokens,
+    pages of 16 tokens, 14 heads of 64; K/V ~ N(0,1) (torch generator seed 5)
+    quantized per (page, K|V, head); queries ~ N(0,1). One step = decode-step
+    attention of all sequences in each of 24 layers (one pool per layer).
+    The pools (11.3 GB) are far larger than L2, so no flush is needed."""
+    import numpy as np
+    import torch
+    from chalot_c1_b200 import paged
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    pages_per_seq = PG_TOK // PG_P
+    n_pages = PG_SEQ * pages_per_seq
+    pools = []
+    chunk = 2048
+    for _ in range(layers):
+        pool = paged.PagedKVPool(n_pages, PG_P, PG_H, PG_HD)
+        for c0 in range(0, n_pages, chunk):
+            n = min(chunk, n_pages - c0)
+            k = torch.randn((n, PG_P, PG_H, PG_HD), generator=g, device="cuda")
+            v = torch.randn((n, PG_P, PG_H, PG_HD), generator=g, device="cuda")
+            pool.store(torch.arange(c0, c0 + n, dtype=torch.int32, device="cuda"), k, v)
+        pools.append(pool)
+        del k, v
+    # sequence s owns a shuffled set of pages (numpy seed 5)
+    perm = np.random.default_rng(5).permutation(n_pages).astype(np.int32).reshape(PG_SEQ, pages_per_seq)
+    table = torch.from_numpy(perm).cuda()
+    lens = torch.full((PG_SEQ,), PG_TOK, dtype=torch.int32, device="cuda")
+    q = torch.randn((layers, PG_SEQ, PG_H, PG_HD), generator=g, device="cuda")
+    out = torch.empty_like(q)
+    for p in pools:
+        p.workspace(PG_SEQ, pages_per_seq)
+
+    def step():
+        for li, p in enumerate(pools):
+            p.attention(q[li], table, lens, out=out[li])
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record()
+        step()
+        b.record()
+    torch.cuda.synchronize()
+    ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+    kv_bytes = layers * n_pages * (pools[0].page_bytes + 2 * PG_H * 4)
+    q_pin = q.cpu().pin_memory()
+    out_pin = torch.empty(out.shape, dtype=torch.float32).pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        q.copy_(q_pin, non_blocking=True)
+        step()
+        out_pin.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / reps
+    return {"seqs": PG_SEQ, "tokens": PG_TOK, "layers": layers, "ms": ms,
+            "kv_gb": kv_bytes / 1e9, "gbs": kv_bytes / (ms * 1e-3) / 1e9, "e2e_ms": e2e_ms,
+            "tok_s": PG_SEQ / (ms * 1e-3), "e2e_tok_s": PG_SEQ / (e2e_ms * 1e-3)}
+
+
+def run_paged(args):
+    print(json.dumps(bench_paged(reps=args.steps, warmup=args.warmup)), flush=True)
+
+
 def run_moe(args):
     for path in ("tc", "simt"):
         r = bench_moe_prefill(reps=args.steps, warmup=args.warmup, path=path,
@@ -370,13 +441,16 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe"])
+    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe", "paged"])
     a = ap.parse_args()
     if a.mode == "profile":
         run_profile(a)
         return
     if a.mode == "moe":
         run_moe(a)
+        return
+    if a.mode == "paged":
+        run_paged(a)
         return
     ws, rank, local = dist_setup()
     try:

@@ -60,6 +60,11 @@ class MoeDesc(C.Structure):
                 ("router_b", C.c_void_p), ("experts", C.c_void_p)]
 
 
+class PagedKV(C.Structure):
+    _fields_ = [("n_pages", C.c_uint32), ("page_tokens", C.c_uint32), ("n_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("data", C.c_void_p), ("scales", C.c_void_p)]
+
+
 # name -> (restype, argtypes); every function include/chalot_b200.h declares
 P = C.c_void_p
 SIGNATURES = {
@@ -90,6 +95,10 @@ SIGNATURES = {
     "chalot_moe_workspace_size": (C.c_size_t, [C.POINTER(MoeDesc), C.c_size_t]),
     "chalot_moe_layer": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P, C.c_size_t, P]),
     "chalot_moe_layer_noalloc": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P]),
+    "chalot_paged_kv_store": (C.c_int, [C.POINTER(PagedKV), P, C.c_size_t, P, P, P]),
+    "chalot_paged_attention_workspace_size": (C.c_size_t, [C.POINTER(PagedKV), C.c_size_t, C.c_size_t]),
+    "chalot_paged_attention": (C.c_int, [C.POINTER(PagedKV), P, C.c_size_t, P, C.c_size_t, P, P, P,
+                                         C.c_size_t, P]),
 }
 
 _lib = None

@@ -223,6 +223,45 @@ int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, 
 int chalot_moe_layer_noalloc(const chalot_moe_desc* desc, const float* x, size_t n_tok,
                              float* out, int32_t* sel_out, float* selw_out, void* stream);
 
+/* ---- paged int8 KV cache for long-context decode ------------------------ */
+
+/* A device page pool in the long-context format (new; the reference's own
+ * PagedKVCache, src/model/memory.rs:100-201, keeps 256-token pages with one
+ * scale per token row): pages of page_tokens (8, 16 or 32) tokens; the K block
+ * and the V block of each head in a page (page_tokens x head_dim values,
+ * token-major) are int8 with one f32 scale per block (quantize_f32_to_i8's
+ * rule: absmax/127, round to nearest even).
+ *   data   [n_pages][2 (K, V)][n_heads][page_tokens][head_dim] int8, 16-B aligned
+ *   scales [n_pages][2][n_heads] f32
+ * head_dim 64 or 128, n_heads at most 31. Memory is owned by the caller. */
+typedef struct chalot_paged_kv {
+  uint32_t n_pages, page_tokens, n_heads, head_dim;
+  int8_t* data;
+  float* scales;
+} chalot_paged_kv;
+
+/* Quantizes n whole pages into the pool: k and v are f32
+ * [n][page_tokens][n_heads][head_dim] (device), the tokens of page page_ids[i]
+ * (device int32) in order. Synchronous, as KVPage::write_token
+ * (memory.rs:76-84) is. Out-of-range page ids are skipped and reported. */
+int chalot_paged_kv_store(const chalot_paged_kv* kv, const int32_t* page_ids, size_t n,
+                          const float* k, const float* v, void* stream);
+
+/* Device workspace bytes of chalot_paged_attention (0 on a bad pool). */
+size_t chalot_paged_attention_workspace_size(const chalot_paged_kv* kv, size_t n_seq,
+                                             size_t max_pages);
+
+/* Decode-step attention of n_seq sequences over the pool: per sequence s and
+ * head h, the attention of Engine::forward (src/model/engine.rs:283-309) over
+ * the dequantized rows of tokens [0, seq_lens[s]), whose pages are
+ * page_table[s][0..] ([n_seq][max_pages] int32, device):
+ * s_t = 30*tanh((q.k_t / sqrt(head_dim)) / 30), softmax, out = sum_t p_t v_t.
+ * q, out: [n_seq][n_heads][head_dim] f32 (device). Float sums are reordered
+ * (split pages, online softmax): agreement is to float tolerance, not bits. */
+int chalot_paged_attention(const chalot_paged_kv* kv, const float* q, size_t n_seq,
+                           const int32_t* page_table, size_t max_pages, const int32_t* seq_lens,
+                           float* out, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

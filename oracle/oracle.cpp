@@ -23,6 +23,7 @@
 //   InferenceState::new RoPE  src/model/state.rs:41-60
 //   Engine::forward           src/model/engine.rs:173-494
 //   expert block, T tokens    src/model/engine.rs:334-401 (orc_moe_forward)
+//   paged int8 KV attention   engine.rs:283-309 over memory.rs:69-74 dequantized rows
 //   Engine::generate          src/model/engine.rs:497-548
 //   sample_from_logits        src/model/engine.rs:551-569
 //   header/config/index       src/model/header.rs:40-133, config.rs:40-69,
@@ -942,6 +943,67 @@ ORC_API int orc_moe_forward(const float* x, size_t T, const uint8_t* layer_base,
     std::memcpy(out + size_t(t) * dim, acc.data(), dim * 4);
   }
   return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Paged int8 KV cache of the long-context decode workload (a new format, not
+// the reference's PagedKVCache): pages of P tokens; the K block and the V block
+// of each head in a page (P x hd values, token-major) are quantized as one
+// vector with quantize_f32_to_i8's rule (absmax/127, round to nearest even).
+// data [page][K|V][head][P][hd] int8, scales [page][K|V][head] f32.
+// k, v: [n][P][H][hd] f32, the tokens of page page_ids[i] in order.
+ORC_API void orc_paged_store(int8_t* data, float* scales, const int32_t* page_ids, size_t n, size_t P,
+                             size_t H, size_t hd, const float* k, const float* v) {
+  std::vector<float> blk(P * hd);
+  for (size_t i = 0; i < n; ++i) {
+    const size_t page = size_t(page_ids[i]);
+    for (size_t kv = 0; kv < 2; ++kv) {
+      const float* src = kv ? v : k;
+      for (size_t h = 0; h < H; ++h) {
+        for (size_t t = 0; t < P; ++t)
+          std::memcpy(&blk[t * hd], src + ((i * P + t) * H + h) * hd, hd * 4);
+        const size_t b = (page * 2 + kv) * H + h;
+        scales[b] = quantize_i8(blk.data(), data + b * P * hd, P * hd);
+      }
+    }
+  }
+}
+
+// Decode-step attention of n_seq sequences over that cache: the attention of
+// Engine::forward (engine.rs:283-309) on the dequantized rows (value as f32 *
+// scale, as KVPage::dequantize_row does, memory.rs:69-74): per head, scores
+// soft_cap(dot_f32(q, k_t) / sqrt(hd), 30), softmax, o = sum_t w_t * v_t in t
+// order. q, out: [n_seq][H][hd].
+ORC_API void orc_paged_attention(const int8_t* data, const float* scales, const int32_t* page_table,
+                                 size_t max_pages, const int32_t* lens, size_t n_seq, size_t P, size_t H,
+                                 size_t hd, const float* q, float* out, int threads) {
+  const float inv_sqrt = 1.0f / std::sqrt(float(hd));
+  const int nt = threads > 0 ? threads : 1;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt) if (nt > 1)
+  for (long sh = 0; sh < long(n_seq * H); ++sh) {
+    const size_t s = size_t(sh) / H, h = size_t(sh) % H;
+    const size_t L = size_t(lens[s]);
+    const float* qh = q + (s * H + h) * hd;
+    std::vector<float> sc(L), row(hd), o(hd, 0.0f);
+    for (size_t t = 0; t < L; ++t) {
+      const size_t page = size_t(page_table[s * max_pages + t / P]), off = t % P;
+      const size_t b = (page * 2 + 0) * H + h;
+      const int8_t* kr = data + b * P * hd + off * hd;
+      for (size_t d = 0; d < hd; ++d) row[d] = float(kr[d]) * scales[b];
+      sc[t] = soft_cap(dot_f32(qh, row.data(), hd) * inv_sqrt, 30.0f);
+    }
+    softmax(sc.data(), L);
+    for (size_t t = 0; t < L; ++t) {
+      const size_t page = size_t(page_table[s * max_pages + t / P]), off = t % P;
+      const size_t b = (page * 2 + 1) * H + h;
+      const int8_t* vr = data + b * P * hd + off * hd;
+      for (size_t d = 0; d < hd; ++d) {
+        float p = sc[t] * (float(vr[d]) * scales[b]);
+        o[d] += p;
+      }
+    }
+    std::memcpy(out + (s * H + h) * hd, o.data(), hd * 4);
+  }
 }
 
 ORC_API int orc_hw_threads(void) { return omp_get_num_procs(); }

@@ -77,6 +77,9 @@ def lib():
         L.orc_moe_forward.restype = C.c_int
         L.orc_moe_forward.argtypes = [P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_size_t, C.c_size_t, P, P, C.c_int]
+        L.orc_paged_store.argtypes = [P, P, P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, P, P]
+        L.orc_paged_attention.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
+                                          C.c_size_t, P, P, C.c_int]
         L.orc_hw_threads.restype = C.c_int
         L.orc_fill_kv_random.argtypes = [P, C.c_size_t, C.c_uint64]
         _lib = L
@@ -210,6 +213,23 @@ def moe_forward(x, layer_bytes, dim, hidden, n_experts, top_k, group, threads=1)
     lib().orc_moe_forward(_p(x), T, _p(lb), dim, hidden, n_experts, top_k, group, _p(out),
                           _p(sel), threads)
     return out, sel
+
+
+def paged_store(data, scales, page_ids, P, H, hd, k, v):
+    """Quantizes whole pages into data [pages][2][H][P][hd] / scales [pages][2][H]."""
+    pid = np.ascontiguousarray(page_ids, np.int32)
+    lib().orc_paged_store(_p(data), _p(scales), _p(pid), pid.size, P, H, hd, _p(_f32(k)), _p(_f32(v)))
+
+
+def paged_attention(data, scales, page_table, lens, P, H, hd, q, threads=1):
+    pt = np.ascontiguousarray(page_table, np.int32)
+    ln = np.ascontiguousarray(lens, np.int32)
+    q = _f32(q)
+    n_seq = ln.size
+    out = np.zeros((n_seq, H, hd), np.float32)
+    lib().orc_paged_attention(_p(data), _p(scales), _p(pt), pt.shape[1], _p(ln), n_seq, P, H, hd, _p(q),
+                              _p(out), threads)
+    return out
 
 
 def hw_threads() -> int:

@@ -173,3 +173,27 @@ def test_golden_tiny_greedy(oracle_lib, tiny_model):
     assert e.generate(g["prompt"], g["max_new"]) == g["tokens"]
     pen = e.generate(g["prompt"], g["max_new"], repetition_penalty=1.15, repetition_window=64)
     assert pen == g["tokens_penalty_1_15"]
+
+
+def test_oracle_paged_attention_matches_f32_attention(oracle_lib):
+    # the paged oracle over dequantized pages equals the plain attention
+    # restatement (engine.rs:283-309) run on those dequantized rows
+    P, H, hd, L = 16, 2, 64, 40
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((3, P, H, hd), dtype=np.float32)
+    v = rng.standard_normal((3, P, H, hd), dtype=np.float32)
+    data = np.zeros((3, 2, H, P, hd), np.int8)
+    sc = np.zeros((3, 2, H), np.float32)
+    oracle_lib.paged_store(data, sc, [0, 1, 2], P, H, hd, k, v)
+    q = rng.standard_normal((1, H, hd), dtype=np.float32)
+    out = oracle_lib.paged_attention(data, sc, np.array([[0, 1, 2]], np.int32), [L], P, H, hd, q)
+    for h in range(H):
+        kd = (data[:, 0, h].astype(np.float32) * sc[:, 0, h, None, None]).reshape(-1, hd)[:L]
+        vd = (data[:, 1, h].astype(np.float32) * sc[:, 1, h, None, None]).reshape(-1, hd)[:L]
+        s = np.array([oracle_lib.soft_cap(oracle_lib.dot_f32(q[0, h], kd[t]) * np.float32(1 / np.sqrt(np.float32(hd))), 30.0)
+                      for t in range(L)], np.float32)
+        w = oracle_lib.softmax(s)
+        ref = np.zeros(hd, np.float32)
+        for t in range(L):
+            ref = (ref + (w[t] * vd[t]).astype(np.float32)).astype(np.float32)
+        assert np.allclose(out[0, h], ref, rtol=1e-5, atol=1e-6)
