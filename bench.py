@@ -425,7 +425,7 @@ def bench_paged(reps: int = 5, warmup: int = 3, layers: int = PG_LAYERS) -> dict
 
 
 def run_paged(args):
-    print(json.dumps(bench_paged(reps=args.steps, warmup=args.warmup)), flush=True)
+    print(json.dumps(bench_paged(reps=args.steps, warmup=args.warmup, layers=args.paged_layers)), flush=True)
 
 
 def run_moe(args):
@@ -442,6 +442,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe", "paged"])
+    ap.add_argument("--paged-layers", type=int, default=PG_LAYERS,
+                    help="--mode paged: layers (one 470 MB page pool each)")
     a = ap.parse_args()
     if a.mode == "profile":
         run_profile(a)

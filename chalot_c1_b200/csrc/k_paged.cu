@@ -7,7 +7,8 @@
 // token-major) are int8 with one f32 scale per block, quantized with
 // quantize_f32_to_i8's rule (absmax/127, round to nearest even,
 // src/tensor/quantization.rs:56-104).
-//   data   [page][K|V][head][P][head_dim] int8   (one page is contiguous)
+//   data   [page][K|V][head][P x head_dim] int8 (one page is contiguous); K
+//          blocks token-major [P][head_dim], V blocks dim-major [head_dim][P]
 //   scales [page][K|V][head] f32
 //
 // Attention per (sequence, head) is the attention of Engine::forward
@@ -16,8 +17,13 @@
 // split-page flash decoding: CTA (split, seq) streams its share of the
 // sequence's pages through shared memory with 1-D bulk copies (one copy per
 // page, a multi-stage ring), warp h computes head h with an online softmax,
-// and k_paged_combine merges the splits. The kernel is bound by HBM reads of
-// the pages; the softmax reorders the reference's sums (float tolerance).
+// and k_paged_combine merges the splits. The dot products run on dp4a: the
+// query is split into two int8 planes (q ~ s1*q1 + s2*q2, s2 = s1/254, error
+// below max|q|*1.6e-5 per element) against the int8 K rows, and the softmax
+// weights p in [0, 1] into two planes (p ~ (p1 + p2/254)/127) against the
+// dim-major int8 V rows, so the kernel stays bound by HBM reads of the pages.
+// The sums are reordered and the planes round q and p slightly: agreement with
+// the reference's f32 arithmetic is to float tolerance, not bits.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -33,6 +39,7 @@ namespace chalot {
 namespace {
 
 constexpr int kMaxStages = 8;
+constexpr int kMaxCtaPages = 64;  // pages one CTA streams; sets the split count
 constexpr size_t kMaxSmem = 227 * 1024;
 
 // Set by k_paged_store when a page id is out of range (that page is skipped).
@@ -63,18 +70,14 @@ __global__ void __launch_bounds__(256) k_paged_store(PagedDims d, int8_t* data, 
   }
   __syncthreads();
   const size_t b = ((size_t)page * 2 + kv) * d.H + h;
-  const float s = quantize_smem(blk, n, data + b * n, red);
-  if (threadIdx.x == 0) scales[b] = s;
-}
-
-// int8 x 4 (one word) to floats, exactly: bytes biased to unsigned are placed
-// in the mantissa of 2^23 and the bias 2^23 + 128 is subtracted.
-__device__ __forceinline__ void i8x4_to_f32(uint32_t w, float* f) {
-  const uint32_t u = w ^ 0x80808080u;
-  f[0] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)), 8388736.0f);
-  f[1] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)), 8388736.0f);
-  f[2] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)), 8388736.0f);
-  f[3] = __fsub_rn(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)), 8388736.0f);
+  float scale, inv;
+  quant_scale(absmax_smem(blk, n, red), &scale, &inv);
+  int8_t* dst = data + b * n;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const int t = j / d.hd, c = j - t * d.hd;
+    dst[kv ? c * d.P + t : j] = quant_any(blk[j], inv, j, n);  // V blocks dim-major
+  }
+  if (threadIdx.x == 0) scales[b] = scale;
 }
 
 struct PagedBars {
@@ -93,14 +96,13 @@ __device__ __forceinline__ int checked_page(const PagedDims& d, int page, unsign
 // Partial results (running max m, sum l, unnormalised o) go to `part`.
 template <int HD, int P>
 __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_t* __restrict__ data,
-                                                     const float* __restrict__ scales,
-                                                     const int32_t* __restrict__ page_table,
-                                                     const int32_t* __restrict__ lens,
-                                                     const float* __restrict__ q, float* part,
-                                                     unsigned* err) {
-  constexpr int LPT = 32 / P;    // lanes per token
-  constexpr int DPL = HD / LPT;  // q.k dims per lane
-  constexpr int DPO = HD / 32;   // output dims per lane
+                                                        const float* __restrict__ scales,
+                                                        const int32_t* __restrict__ page_table,
+                                                        const int32_t* __restrict__ lens,
+                                                        const float* __restrict__ q, float* part,
+                                                        unsigned* err) {
+  constexpr int PPI = 32 / P;    // pages per step: one token per lane
+  constexpr int DPO = HD / 32;   // output dims per lane (lane + 32 j)
   extern __shared__ unsigned char smem_raw[];
   const size_t PB = (size_t)2 * d.H * P * HD;
   unsigned char* stage0 = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
@@ -114,6 +116,10 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int32_t* pt = page_table + (size_t)s * d.max_pages;
 
+  // this CTA's page ids and their scales, staged once (at most kMaxCtaPages pages)
+  int* spage = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(bars) + sizeof(PagedBars) +
+                                      (size_t)d.H * (2 * HD + 64));
+  float* sscale = reinterpret_cast<float*>(spage + kMaxCtaPages);
   if (threadIdx.x == 0) {
     for (int i = 0; i < d.stages; ++i) {
       mbar_init_n(&bars->full[i], 1);
@@ -121,6 +127,10 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
     }
     mbar_fence_init();
   }
+  for (int i = threadIdx.x; i < pe - pb; i += blockDim.x) spage[i] = checked_page(d, pt[pb + i], err);
+  __syncthreads();
+  for (int j = threadIdx.x; j < (pe - pb) * 2 * d.H; j += blockDim.x)
+    sscale[j] = __ldg(scales + (size_t)spage[j / (2 * d.H)] * 2 * d.H + j % (2 * d.H));
   __syncthreads();
 
   if (warp == d.H) {
@@ -129,9 +139,8 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
       for (int i = pb; i < pe; ++i, ++issued) {
         const int st = issued % d.stages, n = issued / d.stages;
         if (n > 0 && !mbar_wait(&bars->empty[st], (n - 1) & 1, err)) break;
-        const int page = checked_page(d, pt[i], err);
         mbar_expect_tx(&bars->full[st], (uint32_t)PB);
-        tma_load(stage0 + st * PB, data + (size_t)page * PB, (uint32_t)PB, &bars->full[st]);
+        tma_load(stage0 + st * PB, data + (size_t)spage[i - pb] * PB, (uint32_t)PB, &bars->full[st]);
       }
       for (int c = max(0, issued - d.stages); c < issued; ++c)  // copies in flight land first
         mbar_wait(&bars->full[c % d.stages], (c / d.stages) & 1, err);
@@ -139,85 +148,125 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
     return;
   }
 
-  // consumer: head h = warp
+  // consumer: head h = warp; lane = (page j of the step, token t)
   const int h = warp;
-  const int t = lane / LPT, lp = lane % LPT;
-  // this head's query in shared memory (lanes of a token part read the same words)
-  float* qsm = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(bars) + sizeof(PagedBars)) + h * HD;
-  for (int j = lane; j < HD; j += 32) qsm[j] = q[((size_t)s * d.H + h) * HD + j];
-  __syncwarp();
-  const float4* qv4 = reinterpret_cast<const float4*>(qsm + lp * DPL);
-  const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  const int jp = lane / P, t = lane % P;
+  // per-warp shared scratch: query planes q1, q2 (HD bytes each), weight planes p1, p2 (32 bytes each)
+  int8_t* wsm = reinterpret_cast<int8_t*>(reinterpret_cast<unsigned char*>(bars) + sizeof(PagedBars)) +
+                h * (2 * HD + 64);
+  int8_t *q1 = wsm, *q2 = wsm + HD, *p1 = wsm + 2 * HD, *p2 = wsm + 2 * HD + 32;
+  float s1, s2;
+  {
+    float qv[DPO], amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < DPO; ++j) {
+      qv[j] = q[((size_t)s * d.H + h) * HD + lane + 32 * j];
+      amax = fmaxf(amax, fabsf(qv[j]));
+    }
+    amax = warp_max(amax);
+    s1 = amax > 0.0f ? amax / 127.0f : 1.0f;
+    s2 = s1 / 254.0f;
+#pragma unroll
+    for (int j = 0; j < DPO; ++j) {
+      const float a = fminf(fmaxf(rintf(qv[j] / s1), -127.0f), 127.0f);
+      const float r = qv[j] - a * s1;
+      q1[lane + 32 * j] = (int8_t)a;
+      q2[lane + 32 * j] = (int8_t)fminf(fmaxf(rintf(r / s2), -127.0f), 127.0f);
+    }
+    __syncwarp();
+  }
+  const float kscale = 1.0f / (sqrtf((float)HD) * 30.0f);  // q.k / sqrt(hd) / 30
   float m = -INFINITY, l = 0.0f, o[DPO];
 #pragma unroll
   for (int j = 0; j < DPO; ++j) o[j] = 0.0f;
-  int used = 0;
-  for (int i = pb; i < pe; ++i, ++used) {
-    const int st = used % d.stages;
-    if (!mbar_wait(&bars->full[st], (used / d.stages) & 1, err)) break;
-    const int page = checked_page(d, pt[i], err);
-    const float sk = __ldg(scales + ((size_t)page * 2) * d.H + h);
-    const float sv = __ldg(scales + ((size_t)page * 2 + 1) * d.H + h);
-    const unsigned char* kb = stage0 + st * PB + (size_t)h * P * HD;
-    const unsigned char* vb = stage0 + st * PB + (size_t)(d.H + h) * P * HD;
-    // q . k8 for this lane's token and dims
-    float dot = 0.0f;
-    const uint4* kr = reinterpret_cast<const uint4*>(kb + t * HD + lp * DPL);
-#pragma unroll
-    for (int c = 0; c < DPL / 16; ++c) {
-      const uint4 w = kr[c];
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float f[4];
-        i8x4_to_f32(ws[u], f);
-        const float4 qq = qv4[c * 4 + u];
-        dot = __fadd_rn(dot, __fmul_rn(qq.x, f[0]));
-        dot = __fadd_rn(dot, __fmul_rn(qq.y, f[1]));
-        dot = __fadd_rn(dot, __fmul_rn(qq.z, f[2]));
-        dot = __fadd_rn(dot, __fmul_rn(qq.w, f[3]));
-      }
+  const uint4* q1w = reinterpret_cast<const uint4*>(q1);
+  const uint4* q2w = reinterpret_cast<const uint4*>(q2);
+  for (int i0 = pb; i0 < pe; i0 += PPI) {
+    const int np = min(PPI, pe - i0);  // pages in this step
+    bool ok = true;
+    for (int j = 0; j < np; ++j) {
+      const int u = i0 + j - pb;
+      ok = ok && mbar_wait(&bars->full[u % d.stages], (u / d.stages) & 1, err);
     }
-#pragma unroll
-    for (int off = 1; off < LPT; off <<= 1) dot = __fadd_rn(dot, __shfl_xor_sync(0xffffffffu, dot, off));
-    const bool valid = i * P + t < L;
+    if (!ok) break;
+    const int i = i0 + jp;
+    const bool have = jp < np;
+    const bool valid = have && i * P + t < L;
     float sc = -INFINITY;
     if (valid) {
-      const float x = __fmul_rn(__fmul_rn(dot, sk), inv_sqrt);
-      sc = __fmul_rn(30.0f, libm::tanh_f32(__fdiv_rn(x, 30.0f)));
+      const int u = i - pb;
+      const unsigned char* kb = stage0 + (u % d.stages) * PB + (size_t)h * P * HD;
+      const uint4* kr = reinterpret_cast<const uint4*>(kb + t * HD);
+      int i1 = 0, i2 = 0;  // q.k_t as two exact int32 dot products
+#pragma unroll
+      for (int c0 = 0; c0 < HD / 16; ++c0) {
+        const int c = (c0 + t) & (HD / 16 - 1);  // rotated so neighbouring rows hit different banks
+        const uint4 w = kr[c], a = q1w[c], b2 = q2w[c];
+        i1 = __dp4a((int)w.x, (int)a.x, i1);
+        i1 = __dp4a((int)w.y, (int)a.y, i1);
+        i1 = __dp4a((int)w.z, (int)a.z, i1);
+        i1 = __dp4a((int)w.w, (int)a.w, i1);
+        i2 = __dp4a((int)w.x, (int)b2.x, i2);
+        i2 = __dp4a((int)w.y, (int)b2.y, i2);
+        i2 = __dp4a((int)w.z, (int)b2.z, i2);
+        i2 = __dp4a((int)w.w, (int)b2.w, i2);
+      }
+      const float dot = fmaf(s1, (float)i1, s2 * (float)i2);
+      sc = 30.0f * tanhf(dot * sscale[u * 2 * d.H + h] * kscale);
     }
     const float m_new = fmaxf(m, warp_max(sc));
-    const float c = (m == -INFINITY) ? 0.0f : fast_exp(__fsub_rn(m, m_new));
-    const float p = valid ? fast_exp(__fsub_rn(sc, m_new)) : 0.0f;
-    float ps = (lp == 0) ? p : 0.0f;
+    const float c = (m == -INFINITY) ? 0.0f : __expf(m - m_new);
+    const float p = valid ? __expf(sc - m_new) : 0.0f;
+    float ps = p;
 #pragma unroll
-    for (int off = 16; off; off >>= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, off));
-    l = __fadd_rn(__fmul_rn(l, c), ps);
+    for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+    l = fmaf(l, c, ps);
+    {  // p in [0, 1] as two int8 planes
+      const float a = rintf(p * 127.0f);
+      p1[lane] = (int8_t)a;
+      p2[lane] = (int8_t)fminf(fmaxf(rintf((p * 127.0f - a) * 254.0f), -127.0f), 127.0f);
+    }
+    __syncwarp();
     float acc[DPO];
 #pragma unroll
     for (int j = 0; j < DPO; ++j) acc[j] = 0.0f;
+    for (int jj = 0; jj < np; ++jj) {
+      const int u = i0 + jj - pb;
+      const unsigned char* vb = stage0 + (u % d.stages) * PB + (size_t)(d.H + h) * P * HD;
+      const float sv = sscale[u * 2 * d.H + d.H + h];
 #pragma unroll
-    for (int tt = 0; tt < P; ++tt) {
-      const float ptt = __shfl_sync(0xffffffffu, p, tt * LPT);
-      const unsigned char* vr = vb + tt * HD + lane * DPO;
-      if (DPO == 4) {
-        float f[4];
-        i8x4_to_f32(*reinterpret_cast<const uint32_t*>(vr), f);
+      for (int j = 0; j < DPO; ++j) {
+        int vw[P / 4];  // the dim's row of P int8 in one shared load
+        const unsigned char* vr = vb + (size_t)(lane + 32 * j) * P;
+        if (P == 8) {
+          const uint2 x = *reinterpret_cast<const uint2*>(vr);
+          vw[0] = (int)x.x;
+          vw[1 % (P / 4)] = (int)x.y;
+        } else {
 #pragma unroll
-        for (int j = 0; j < DPO; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(ptt, f[j]));
-      } else {
-        const uint32_t w2 = *reinterpret_cast<const uint16_t*>(vr);
-        float f[4];
-        i8x4_to_f32(w2, f);
+          for (int w4 = 0; w4 < P / 16; ++w4) {
+            const uint4 x = reinterpret_cast<const uint4*>(vr)[w4];
+            vw[(4 * w4) % (P / 4)] = (int)x.x;
+            vw[(4 * w4 + 1) % (P / 4)] = (int)x.y;
+            vw[(4 * w4 + 2) % (P / 4)] = (int)x.z;
+            vw[(4 * w4 + 3) % (P / 4)] = (int)x.w;
+          }
+        }
+        int a1 = 0, a2 = 0;
 #pragma unroll
-        for (int j = 0; j < DPO; ++j) acc[j] = __fadd_rn(acc[j], __fmul_rn(ptt, f[j]));
+        for (int w = 0; w < P / 4; ++w) {
+          a1 = __dp4a(vw[w], *reinterpret_cast<const int*>(p1 + jj * P + 4 * w), a1);
+          a2 = __dp4a(vw[w], *reinterpret_cast<const int*>(p2 + jj * P + 4 * w), a2);
+        }
+        acc[j] = fmaf(fmaf((float)a1, 1.0f / 127.0f, (float)a2 * (1.0f / (127.0f * 254.0f))), sv, acc[j]);
       }
     }
 #pragma unroll
-    for (int j = 0; j < DPO; ++j) o[j] = __fadd_rn(__fmul_rn(o[j], c), __fmul_rn(acc[j], sv));
+    for (int j = 0; j < DPO; ++j) o[j] = fmaf(o[j], c, acc[j]);
     m = m_new;
     __syncwarp();
-    if (lane == 0) mbar_arrive(&bars->empty[st]);
+    if (lane == 0)
+      for (int j = 0; j < np; ++j) mbar_arrive(&bars->empty[(i0 + j - pb) % d.stages]);
   }
   float* pp = part + (((size_t)s * d.H + h) * d.n_split + split) * (HD + 2);
   if (lane == 0) {
@@ -225,7 +274,7 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
     pp[1] = l;
   }
 #pragma unroll
-  for (int j = 0; j < DPO; ++j) pp[2 + lane * DPO + j] = o[j];
+  for (int j = 0; j < DPO; ++j) pp[2 + lane + 32 * j] = o[j];
 }
 
 // Merges the splits of each (sequence, head): o = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M).
@@ -239,7 +288,7 @@ __global__ void k_paged_combine(PagedDims d, const float* __restrict__ part, flo
     for (int i = 0; i < d.n_split; ++i) {
       const float* pi = pp + i * (d.hd + 2);
       if (pi[0] == -INFINITY) continue;
-      const float w = fast_exp(__fsub_rn(pi[0], M));
+      const float w = __expf(pi[0] - M);
       L = __fadd_rn(L, __fmul_rn(pi[1], w));
       O = __fadd_rn(O, __fmul_rn(pi[2 + j], w));
     }
@@ -262,7 +311,8 @@ const char* paged_check(const chalot_paged_kv* kv) {
   if (kv->n_pages < 1) return "n_pages must be positive";
   if (reinterpret_cast<uintptr_t>(kv->data) & 15) return "data must be 16-byte aligned";
   if (2 * ((size_t)2 * kv->n_heads * kv->page_tokens * kv->head_dim) + 128 + 2 * kMaxStages * 8 +
-          (size_t)kv->n_heads * kv->head_dim * 4 > kMaxSmem)
+          (size_t)kv->n_heads * (2 * kv->head_dim + 64) + kMaxCtaPages * 4 +
+          (size_t)kMaxCtaPages * 2 * kv->n_heads * 4 > kMaxSmem)
     return "two pages do not fit in shared memory (n_heads * page_tokens * head_dim too large)";
   return nullptr;
 }
@@ -275,10 +325,12 @@ PagedDims paged_dims(const chalot_paged_kv* kv, size_t n_seq, size_t max_pages) 
   d.n_pages = (int)kv->n_pages;
   d.n_seq = (int)n_seq;
   d.max_pages = (int)max_pages;
-  const int want = (4 * sm_count() + (int)std::max<size_t>(n_seq, 1) - 1) / (int)std::max<size_t>(n_seq, 1);
+  // two CTAs per SM (three page stages each), about four full waves of them
+  const int want = (8 * sm_count() + (int)std::max<size_t>(n_seq, 1) - 1) / (int)std::max<size_t>(n_seq, 1);
   d.n_split = std::max(1, std::min(want, (int)std::max<size_t>(max_pages, 1)));
+  d.n_split = std::max(d.n_split, (int)((max_pages + kMaxCtaPages - 1) / kMaxCtaPages));
   const size_t pb = (size_t)2 * d.H * d.P * d.hd;
-  d.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (size_t)(192 * 1024) / pb));
+  d.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (size_t)(96 * 1024) / pb));
   return d;
 }
 
@@ -287,7 +339,8 @@ size_t part_bytes(const PagedDims& d) { return (size_t)d.n_seq * d.H * d.n_split
 template <int HD, int P>
 cudaError_t launch_attn(const PagedDims& d, const chalot_paged_kv* kv, const int32_t* pt, const int32_t* lens,
                         const float* q, float* part, unsigned* err, cudaStream_t s) {
-  const size_t smem = 128 + (size_t)d.stages * 2 * d.H * P * HD + sizeof(PagedBars) + (size_t)d.H * HD * 4;
+  const size_t smem = 128 + (size_t)d.stages * 2 * d.H * P * HD + sizeof(PagedBars) + (size_t)d.H * (2 * HD + 64) +
+                      kMaxCtaPages * 4 + (size_t)kMaxCtaPages * 2 * d.H * 4;
   cudaError_t r = cudaFuncSetAttribute(k_paged_attn<HD, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (r != cudaSuccess) return r;
   k_paged_attn<HD, P><<<dim3(d.n_split, d.n_seq), (d.H + 1) * 32, smem, s>>>(d, kv->data, kv->scales, pt, lens, q,

@@ -950,8 +950,8 @@ ORC_API int orc_moe_forward(const float* x, size_t T, const uint8_t* layer_base,
 // the reference's PagedKVCache): pages of P tokens; the K block and the V block
 // of each head in a page (P x hd values, token-major) are quantized as one
 // vector with quantize_f32_to_i8's rule (absmax/127, round to nearest even).
-// data [page][K|V][head][P][hd] int8, scales [page][K|V][head] f32.
-// k, v: [n][P][H][hd] f32, the tokens of page page_ids[i] in order.
+// data [page][K|V][head][P x hd] int8 (K blocks token-major [P][hd], V blocks
+// dim-major [hd][P]), scales [page][K|V][head] f32. k, v: [n][P][H][hd] f32, the tokens of page page_ids[i] in order.
 ORC_API void orc_paged_store(int8_t* data, float* scales, const int32_t* page_ids, size_t n, size_t P,
                              size_t H, size_t hd, const float* k, const float* v) {
   std::vector<float> blk(P * hd);
@@ -963,7 +963,14 @@ ORC_API void orc_paged_store(int8_t* data, float* scales, const int32_t* page_id
         for (size_t t = 0; t < P; ++t)
           std::memcpy(&blk[t * hd], src + ((i * P + t) * H + h) * hd, hd * 4);
         const size_t b = (page * 2 + kv) * H + h;
-        scales[b] = quantize_i8(blk.data(), data + b * P * hd, P * hd);
+        if (kv == 0) {
+          scales[b] = quantize_i8(blk.data(), data + b * P * hd, P * hd);
+        } else {  // V blocks are stored dim-major: [hd][P]
+          std::vector<int8_t> qb(P * hd);
+          scales[b] = quantize_i8(blk.data(), qb.data(), P * hd);
+          for (size_t t = 0; t < P; ++t)
+            for (size_t d = 0; d < hd; ++d) data[b * P * hd + d * P + t] = qb[t * hd + d];
+        }
       }
     }
   }
@@ -996,9 +1003,9 @@ ORC_API void orc_paged_attention(const int8_t* data, const float* scales, const 
     for (size_t t = 0; t < L; ++t) {
       const size_t page = size_t(page_table[s * max_pages + t / P]), off = t % P;
       const size_t b = (page * 2 + 1) * H + h;
-      const int8_t* vr = data + b * P * hd + off * hd;
+      const int8_t* vb = data + b * P * hd;
       for (size_t d = 0; d < hd; ++d) {
-        float p = sc[t] * (float(vr[d]) * scales[b]);
+        float p = sc[t] * (float(vb[d * P + off]) * scales[b]);
         o[d] += p;
       }
     }

@@ -189,7 +189,8 @@ def test_oracle_paged_attention_matches_f32_attention(oracle_lib):
     out = oracle_lib.paged_attention(data, sc, np.array([[0, 1, 2]], np.int32), [L], P, H, hd, q)
     for h in range(H):
         kd = (data[:, 0, h].astype(np.float32) * sc[:, 0, h, None, None]).reshape(-1, hd)[:L]
-        vd = (data[:, 1, h].astype(np.float32) * sc[:, 1, h, None, None]).reshape(-1, hd)[:L]
+        vd = (data[:, 1, h].reshape(3, hd, P).transpose(0, 2, 1).astype(np.float32)
+              * sc[:, 1, h, None, None]).reshape(-1, hd)[:L]
         s = np.array([oracle_lib.soft_cap(oracle_lib.dot_f32(q[0, h], kd[t]) * np.float32(1 / np.sqrt(np.float32(hd))), 30.0)
                       for t in range(L)], np.float32)
         w = oracle_lib.softmax(s)
