@@ -95,6 +95,12 @@ SIGNATURES = {
     "chalot_moe_workspace_size": (C.c_size_t, [C.POINTER(MoeDesc), C.c_size_t]),
     "chalot_moe_layer": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P, C.c_size_t, P]),
     "chalot_moe_layer_noalloc": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P]),
+    "chalot_moe_route": (C.c_int, [C.POINTER(MoeDesc), P, C.c_size_t, P, P, P, P, P]),
+    "chalot_moe_plan": (C.c_int, [P, C.c_size_t, C.c_uint32, C.c_uint32, P, P, P, P]),
+    "chalot_moe_gather": (C.c_int, [P, P, P, C.c_size_t, C.c_uint32, C.c_size_t, P, P, P]),
+    "chalot_moe_experts_workspace_size": (C.c_size_t, [C.POINTER(MoeDesc), C.c_size_t]),
+    "chalot_moe_experts": (C.c_int, [C.POINTER(MoeDesc), P, P, P, C.c_size_t, P, P, C.c_size_t, P]),
+    "chalot_moe_combine": (C.c_int, [P, P, P, C.c_size_t, C.c_uint32, C.c_size_t, P, P]),
     "chalot_paged_kv_store": (C.c_int, [C.POINTER(PagedKV), P, C.c_size_t, P, P, P]),
     "chalot_paged_attention_workspace_size": (C.c_size_t, [C.POINTER(PagedKV), C.c_size_t, C.c_size_t]),
     "chalot_paged_attention": (C.c_int, [C.POINTER(PagedKV), P, C.c_size_t, P, C.c_size_t, P, P, P,

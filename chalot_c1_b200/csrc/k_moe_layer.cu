@@ -87,7 +87,16 @@ __global__ void __launch_bounds__(kThreads) k_ml_route(MlDims d, const float* __
 // Stable counting sort of the N = T*k slots by expert. Warp v walks slots
 // [v*chunk, (v+1)*chunk) in order; lanes holding the same expert are grouped
 // with __match_any_sync, so positions follow slot order within each expert.
-__global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm) {
+// With n_ranks > 1 the sort key of expert e is (e % n_ranks) * (E / n_ranks) +
+// e / n_ranks: slots come out grouped by the rank that holds their expert
+// (expert e lives on rank e % n_ranks), then by that rank's local expert.
+// Expert ids outside [0, E) get no position (key -1) and their slot's inv is -1.
+__device__ __forceinline__ int dispatch_key(int e, int E, int n_ranks) {
+  if (e < 0 || e >= E) return -1;
+  return n_ranks > 1 ? (e % n_ranks) * (E / n_ranks) + e / n_ranks : e;
+}
+
+__global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm, int n_ranks, int32_t* offs_out) {
   __shared__ int cnt[32][33];
   __shared__ int off[33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -98,7 +107,7 @@ __global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm
   __syncthreads();
   for (int i0 = beg; i0 < end; i0 += 32) {
     const int i = i0 + lane;
-    const int e = i < end ? w.sel[i] : -1;
+    const int e = i < end ? dispatch_key(w.sel[i], d.E, n_ranks) : -1;
     const unsigned m = __match_any_sync(0xffffffffu, e);
     if (e >= 0 && lane == __ffs(m) - 1) cnt[warp][e] += __popc(m);
     __syncwarp();
@@ -118,25 +127,31 @@ __global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm
   if (threadIdx.x == 0) {
     off[0] = 0;
     for (int e = 0; e < d.E; ++e) off[e + 1] += off[e];
-    int n = 0;
-    for (int e = 0; e < d.E; ++e)
-      for (int p = off[e]; p < off[e + 1]; p += bm) {
-        w.mb_e[n] = e;
-        w.mb_p0[n] = p;
-        w.mb_n[n] = min(bm, off[e + 1] - p);
-        ++n;
-      }
-    *w.n_mb = n;
+    if (offs_out)
+      for (int e = 0; e <= d.E; ++e) offs_out[e] = off[e];
+    if (w.mb_e) {
+      int n = 0;
+      for (int e = 0; e < d.E; ++e)
+        for (int p = off[e]; p < off[e + 1]; p += bm) {
+          w.mb_e[n] = e;
+          w.mb_p0[n] = p;
+          w.mb_n[n] = min(bm, off[e + 1] - p);
+          ++n;
+        }
+      *w.n_mb = n;
+    }
   }
   __syncthreads();
   for (int i0 = beg; i0 < end; i0 += 32) {
     const int i = i0 + lane;
-    const int e = i < end ? w.sel[i] : -1;
+    const int e = i < end ? dispatch_key(w.sel[i], d.E, n_ranks) : -1;
     const unsigned m = __match_any_sync(0xffffffffu, e);
     if (e >= 0) {
       const int pos = off[e] + cnt[warp][e] + __popc(m & ((1u << lane) - 1u));
       w.perm[pos] = i;
       w.inv[i] = pos;
+    } else if (i < end) {
+      w.inv[i] = -1;
     }
     __syncwarp();
     if (e >= 0 && lane == __ffs(m) - 1) cnt[warp][e] += __popc(m);
@@ -305,7 +320,8 @@ __global__ void __launch_bounds__(kThreads) k_ml_combine(MlDims d, MlWork w, flo
     float acc = 0.0f;
     for (int j = 0; j < d.K; ++j) {
       const int slot = t * d.K + j;
-      acc = __fadd_rn(acc, __fmul_rn(w.selw[slot], w.y[(size_t)w.inv[slot] * d.dim + i]));
+      const int p = w.inv[slot];
+      if (p >= 0) acc = __fadd_rn(acc, __fmul_rn(w.selw[slot], w.y[(size_t)p * d.dim + i]));
     }
     out[(size_t)t * d.dim + i] = acc;
   }
@@ -369,7 +385,7 @@ static void route_and_dispatch(const MlDims& d, const float* x, const float* rw,
   const size_t rsm = ((size_t)d.dim + 16 * d.E + 32 + 40) * 4;
   cudaFuncSetAttribute(k_ml_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
   k_ml_route<<<d.T, kThreads, rsm, s>>>(d, x, rw, rb, w);
-  k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm);
+  k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
 }
 
 static void quantize_h(const MlDims& d, const MlWork& w, cudaStream_t s) {
@@ -414,6 +430,68 @@ cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const fl
   return cudaGetLastError();
 }
 
+__global__ void k_fill_f32(float* p, size_t n, float v) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+void ml_launch_route(const MlDims& d, const float* x, const float* rw, const float* rb, const MlWork& w,
+                     cudaStream_t s) {
+  const size_t rsm = ((size_t)d.dim + 16 * d.E + 32 + 40) * 4;
+  cudaFuncSetAttribute(k_ml_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+  k_ml_route<<<d.T, kThreads, rsm, s>>>(d, x, rw, rb, w);
+}
+
+void ml_launch_plan(const MlDims& d, const MlWork& w, int n_ranks, int32_t* offs, cudaStream_t s) {
+  k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, kBM, n_ranks, offs);
+}
+
+void ml_launch_combine(const MlDims& d, const MlWork& w, float* out, cudaStream_t s) {
+  k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
+}
+
+// Expert products of rows whose input is already quantized: w.sel holds each
+// row's (local) expert, w.xq / w.xs the rows; d.K == 1. y[row] (the expert
+// output) is written in row order through the combine with weight 1.0, which
+// reproduces y exactly (0 + 1*y).
+cudaError_t ml_run_rows(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork* t, float* y,
+                        cudaStream_t s) {
+  if (d.T == 0) return cudaSuccess;
+  const size_t N = (size_t)d.T;
+  k_fill_f32<<<(unsigned)std::min<size_t>((N + 255) / 256, 1024), 256, 0, s>>>(w.selw, N, 1.0f);
+  if (t) {
+    cudaError_t r = cudaMemsetAsync(t->err, 0, 16, s);
+    if (r == cudaSuccess) r = cudaMemsetAsync(t->amax, 0, N * 4, s);
+    if (r != cudaSuccess) return r;
+    k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, 128, 1, nullptr);
+    if ((r = ml_tc_prepare(d, experts, w, *t, s)) != cudaSuccess) return r;
+    const unsigned nmb = (unsigned)std::min(N, N / 128 + d.E);
+    if ((r = ml_tc_gemm(d, true, w, *t, nmb, s)) != cudaSuccess) return r;
+    if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
+    if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
+  } else {
+    k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, kBM, 1, nullptr);
+    const size_t gsm = gemm_smem();
+    cudaFuncSetAttribute(k_ml_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
+    const size_t ex = ml_expert_bytes(d);
+    k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+    quantize_h(d, w, s);
+    k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+  }
+  k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, y);
+  return cudaGetLastError();
+}
+
+bool ml_use_tc(const MlDims& d) {
+  const char* env = std::getenv("CHALOT_MOE_PATH");
+  if (env && !std::strcmp(env, "simt")) return false;
+  if (!ml_tc_eligible(d)) return false;
+  if (env && !std::strcmp(env, "tc")) return true;
+  return (size_t)d.T * d.K >= 1024;
+}
+
 }  // namespace chalot
 
 using namespace chalot;
@@ -432,18 +510,10 @@ static int ml_prepare(const chalot_moe_desc* desc, size_t n_tok, MlDims* d) {
   return CHALOT_OK;
 }
 
-// Tensor-core expert products from this many (token, choice) slots on, when
-// the shape allows them (group 32, dim and hidden_dim multiples of 128).
+// Tensor-core expert products from 1024 (token, choice) slots on, when the
+// shape allows them (group 32, dim and hidden_dim multiples of 128);
 // CHALOT_MOE_PATH=simt|tc overrides the choice (tests use it to cover both).
-static constexpr size_t kTcMinSlots = 1024;
-
-static bool use_tc(const MlDims& d) {
-  const char* env = std::getenv("CHALOT_MOE_PATH");
-  if (env && !std::strcmp(env, "simt")) return false;
-  if (!ml_tc_eligible(d)) return false;
-  if (env && !std::strcmp(env, "tc")) return true;
-  return (size_t)d.T * d.K >= kTcMinSlots;
-}
+static bool use_tc(const MlDims& d) { return ml_use_tc(d); }
 
 extern "C" {
 

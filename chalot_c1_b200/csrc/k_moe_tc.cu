@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(256) k_tc_gather(MlDims d, MlWork w, MlTcWork 
   const long p = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (p >= (long)d.T * d.K) return;
   const int tok = w.perm[p] / d.K;
+  if (tok < 0 || tok >= d.T) return;  // a position no valid slot filled
   const uint4* s = reinterpret_cast<const uint4*>(w.xq + (size_t)tok * d.dim);
   uint4* o = reinterpret_cast<uint4*>(t.xp + (size_t)p * d.dim);
   for (int j = lane; j < d.dim / 16; j += 32) o[j] = __ldg(s + j);
@@ -440,6 +441,13 @@ cudaError_t ml_tc_prepare(const MlDims& d, const uint8_t* experts, const MlWork&
   const long rows = (long)d.E * 2 * d.H + (long)d.E * d.dim;
   k_tc_unpack<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(d, experts, ml_expert_bytes(d), t);
   const long N = (long)d.T * d.K;
+  k_tc_gather<<<(unsigned)((N + 7) / 8), 256, 0, s>>>(d, w, t);
+  return cudaGetLastError();
+}
+
+cudaError_t ml_tc_gather_rows(const MlDims& d, const MlWork& w, const MlTcWork& t, cudaStream_t s) {
+  const long N = (long)d.T * d.K;
+  if (N == 0) return cudaSuccess;
   k_tc_gather<<<(unsigned)((N + 7) / 8), 256, 0, s>>>(d, w, t);
   return cudaGetLastError();
 }

@@ -47,6 +47,16 @@ const char* ml_check(const MlDims& d);
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
                    const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s);
 
+// Building blocks of the expert-parallel layer (k_moe_layer.cu).
+void ml_launch_route(const MlDims& d, const float* x, const float* rw, const float* rb, const MlWork& w,
+                     cudaStream_t s);
+void ml_launch_plan(const MlDims& d, const MlWork& w, int n_ranks, int32_t* offs, cudaStream_t s);
+void ml_launch_combine(const MlDims& d, const MlWork& w, float* out, cudaStream_t s);
+cudaError_t ml_run_rows(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork* t, float* y,
+                        cudaStream_t s);
+bool ml_use_tc(const MlDims& d);
+cudaError_t ml_tc_gather_rows(const MlDims& d, const MlWork& w, const MlTcWork& t, cudaStream_t s);
+
 bool ml_tc_eligible(const MlDims& d);
 size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t);
 cudaError_t ml_tc_prepare(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork& t,

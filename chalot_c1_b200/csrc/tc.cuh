@@ -3,7 +3,7 @@
 // Only what the int8 expert GEMM needs: TMEM allocation, the kind::i8 MMA
 // with both operands K-major in 128-byte-swizzled shared memory, commits to
 // mbarriers, TMEM loads of the 32x32b shape, and tiled 2-D TMA loads (no
-// multicast; every load reads this GPU's own memory).
+// copy to other CTAs; every load reads this GPU's own memory).
 #pragma once
 
 #include <cuda.h>

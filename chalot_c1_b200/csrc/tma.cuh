@@ -1,8 +1,8 @@
 // tma.cuh — 1-D bulk copies (cp.async.bulk, the TMA engine) into shared
 // memory, completed on an mbarrier, with bounded waits.
 //
-// No multicast anywhere: every copy reads this GPU's own memory into the
-// issuing CTA's shared memory. Sources and destinations are 16-byte aligned
+// Every copy reads this GPU's own memory into the issuing CTA's own shared
+// memory. Sources and destinations are 16-byte aligned
 // and sizes are multiples of 16 bytes (checked by the callers' layouts).
 #pragma once
 

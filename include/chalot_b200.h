@@ -223,6 +223,47 @@ int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, 
 int chalot_moe_layer_noalloc(const chalot_moe_desc* desc, const float* x, size_t n_tok,
                              float* out, int32_t* sel_out, float* selw_out, void* stream);
 
+/* ---- expert-parallel MoE layer: building blocks ------------------------- */
+/* Expert e lives on rank e % n_ranks. Per layer each rank routes its tokens,
+ * plans and gathers its (token, choice) slots by destination, exchanges
+ * counts, int8 rows and scales with the other ranks (the caller's NCCL
+ * all-to-all), runs chalot_moe_experts on the rows it received, sends the
+ * outputs back and combines them. Together: the expert block of
+ * Engine::forward (src/model/engine.rs:334-401), bit-identical to
+ * chalot_moe_layer. All pointers are device memory; all calls are
+ * asynchronous on `stream`. */
+
+/* Router, softmax_top_k and quantize_f32_to_i8 of n_tok rows:
+ * sel/selw [n_tok][top_k], xq [n_tok][dim] int8, xs [n_tok]. */
+int chalot_moe_route(const chalot_moe_desc* desc, const float* x, size_t n_tok, int32_t* sel,
+                     float* selw, int8_t* xq, float* xs, void* stream);
+
+/* Stable order of the n_slots slots (sel flattened) by (rank, local expert):
+ * order[p] = slot at position p, pos[slot] = its position (-1 for an expert id
+ * outside [0, n_experts)), offsets[n_experts + 1] = position where the key
+ * (rank, local expert) = rank * (n_experts / n_ranks) + local starts. */
+int chalot_moe_plan(const int32_t* sel, size_t n_slots, uint32_t n_experts, uint32_t n_ranks,
+                    int32_t* order, int32_t* pos, int32_t* offsets, void* stream);
+
+/* rows[p] = xq[order[p] / top_k], row_scales[p] = xs[order[p] / top_k];
+ * dim % 16 == 0, 16-byte aligned rows. */
+int chalot_moe_gather(const int8_t* xq, const float* xs, const int32_t* order, size_t n_slots,
+                      uint32_t top_k, size_t dim, int8_t* rows, float* row_scales, void* stream);
+
+/* Expert outputs y[i] = down(swiglu(gate(x_i), up(x_i))) of expert
+ * row_expert[i] for n_rows already-quantized rows (matmul_int4 on rows[i] with
+ * scale row_scales[i], engine.rs:366-380). `local` describes the experts this
+ * rank holds (n_experts = its count, router pointers unused). */
+size_t chalot_moe_experts_workspace_size(const chalot_moe_desc* local, size_t n_rows);
+int chalot_moe_experts(const chalot_moe_desc* local, const int8_t* rows, const float* row_scales,
+                       const int32_t* row_expert, size_t n_rows, float* y, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* out[t] = 0 + selw[t][0] * y[pos[t*top_k]] + selw[t][1] * y[pos[t*top_k+1]] ...
+ * in selection order (slots with pos < 0 are skipped). */
+int chalot_moe_combine(const float* y, const int32_t* pos, const float* selw, size_t n_tok,
+                       uint32_t top_k, size_t dim, float* out, void* stream);
+
 /* ---- paged int8 KV cache for long-context decode ------------------------ */
 
 /* A device page pool in the long-context format (new; the reference's own

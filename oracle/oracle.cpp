@@ -945,6 +945,32 @@ ORC_API int orc_moe_forward(const float* x, size_t T, const uint8_t* layer_base,
   return 0;
 }
 
+// The expert block (engine.rs:366-380) for rows whose input is already
+// quantized (xq, xs, as quantize_f32_to_i8 left it): y = down(swiglu(gate, up))
+// of expert[i], experts laid out back to back as in a .myai layer.
+ORC_API void orc_expert_rows(const int8_t* xq, const float* xs, const int32_t* expert, size_t n,
+                             const uint8_t* experts, size_t dim, size_t hidden, size_t group, float* y,
+                             int threads) {
+  const size_t ng_d = (dim + group - 1) / group, ng_h = (hidden + group - 1) / group;
+  const size_t gu_bytes = 2 * hidden * ((dim + 1) / 2), gu_cnt = 2 * hidden * ng_d;
+  const size_t dn_bytes = dim * ((hidden + 1) / 2), dn_cnt = dim * ng_h;
+  const size_t ex_bytes = gu_bytes + gu_cnt * 4 + dn_bytes + dn_cnt * 4;
+  const int nt = threads > 0 ? threads : 1;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt) if (nt > 1)
+  for (long i = 0; i < long(n); ++i) {
+    std::vector<float> g(hidden), u(hidden);
+    const uint8_t* eb = experts + size_t(expert[i]) * ex_bytes;
+    const float* gus = reinterpret_cast<const float*>(eb + gu_bytes);
+    const uint8_t* dn = eb + gu_bytes + gu_cnt * 4;
+    const float* dns = reinterpret_cast<const float*>(dn + dn_bytes);
+    const int8_t* xr = xq + size_t(i) * dim;
+    matmul_i4_q(g.data(), nullptr, eb, gus, xr, xs[i], hidden, dim, group, 1);
+    matmul_i4_q(u.data(), nullptr, eb + gu_bytes / 2, gus + gu_cnt / 2, xr, xs[i], hidden, dim, group, 1);
+    swiglu(g.data(), u.data(), hidden);
+    matmul_i4(y + size_t(i) * dim, dn, dns, g.data(), dim, hidden, group, 1);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Paged int8 KV cache of the long-context decode workload (a new format, not
 // the reference's PagedKVCache): pages of P tokens; the K block and the V block

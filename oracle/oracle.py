@@ -77,6 +77,7 @@ def lib():
         L.orc_moe_forward.restype = C.c_int
         L.orc_moe_forward.argtypes = [P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_size_t, C.c_size_t, P, P, C.c_int]
+        L.orc_expert_rows.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t, P, C.c_int]
         L.orc_paged_store.argtypes = [P, P, P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, P, P]
         L.orc_paged_attention.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                           C.c_size_t, P, P, C.c_int]
@@ -213,6 +214,16 @@ def moe_forward(x, layer_bytes, dim, hidden, n_experts, top_k, group, threads=1)
     lib().orc_moe_forward(_p(x), T, _p(lb), dim, hidden, n_experts, top_k, group, _p(out),
                           _p(sel), threads)
     return out, sel
+
+
+def expert_rows(xq, xs, expert, experts, dim, hidden, group, threads=1):
+    """Expert outputs y [n][dim] of already-quantized rows (xq int8 [n][dim], xs [n])."""
+    xq = np.ascontiguousarray(xq, np.int8)
+    n = xq.shape[0]
+    y = np.zeros((n, dim), np.float32)
+    lib().orc_expert_rows(_p(xq), _p(_f32(xs)), _p(np.ascontiguousarray(expert, np.int32)), n,
+                          _p(np.ascontiguousarray(experts, np.uint8)), dim, hidden, group, _p(y), threads)
+    return y
 
 
 def paged_store(data, scales, page_ids, P, H, hd, k, v):
