@@ -44,7 +44,7 @@ sys.path.insert(0, ROOT)
 
 PROMPT_LEN = 512
 NEW_TOKENS = 512
-KERNELS_PER_LAYER = 7  # qkv, attn scores, attn softmax+PV, o-proj, router, gate/up, down
+KERNELS_PER_LAYER = 6  # qkv, attn scores, attn softmax+PV, o-proj + routing, gate/up, down
 
 
 def model_dir() -> str:
@@ -119,7 +119,8 @@ def dist_setup():
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        # gloo for the host-side timing reductions, NCCL for the expert-parallel exchange
+        dist.init_process_group("cpu:gloo,cuda:nccl", timeout=datetime.timedelta(seconds=600))
     return ws, rank, local
 
 
@@ -229,6 +230,7 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     barrier(ws)
     clocks = clk.summary()
+    ep_res = bench_moe_ep(ws, rank) if ws > 1 else None
     decode_s = allmax(ws, dev_decode_ms / 1000.0)
     e2e_s = allmax(ws, wall - dev_prefill_ms / 1000.0)
     step_s = allmax(ws, t_all / args.steps)
@@ -266,8 +268,81 @@ def run_ours(args, ws, rank, local):
         "gpu_launches": fwd * ws * (1 + cfg["n_layers"] * KERNELS_PER_LAYER + 2),
         "clocks": clocks,
     }
-    print(json.dumps(line), flush=True)
+    if ep_res is not None:
+        line["moe_layer_prefill_ep"] = dict(ep_res, workload="expert-parallel MoE layer prefill over NCCL, "
+                                            "4096 tokens per rank, experts e on rank e % n_gpus", scaling="weak")
     eng.close()
+    if ws == 1:
+        mo = bench_moe_prefill(reps=10, warmup=3, cpu_tokens=1024)
+        line["moe_layer_prefill"] = {
+            "workload": "single MoE layer, 4096 tokens N(0,1) at dim 896, router 896->8, experts int4 g32 "
+                        "SwiGLU 896->4864->896, top-2 (tensor-core path)",
+            "tok_s": mo["tok_s"], "ms": mo["ms"], "e2e_tok_s": mo["e2e_tok_s"],
+            "roofline": {"bound": "cuda-core f32 group epilogue (exact per-group order); int8 tensor ops",
+                         "achieved": mo["tops"], "unit": "TOP/s", "peak": 4500.0,
+                         "peak_source": "nominal dense int8", "frac": mo["tops"] / 4500.0},
+            "cpu_baseline": mo.get("cpu")}
+        pg = bench_paged(reps=5, warmup=3)
+        cpu_tok_s, cpu_sample_s = paged_cpu_sample()
+        line["paged_kv_attention"] = {
+            "workload": "24 layers of decode-step attention, 32 sequences x 8192 cached tokens, pages of 16, "
+                        "14 heads x 64, int8 K/V per (page, K|V, head)",
+            "tok_s": pg["tok_s"], "ms": pg["ms"], "e2e_tok_s": pg["e2e_tok_s"],
+            "roofline": {"bound": "hbm", "achieved": pg["gbs"], "unit": "GB/s", "peak": pk["hbm_gbs"],
+                         "frac": pg["gbs"] / pk["hbm_gbs"], "peak_source": pk["source"],
+                         "bytes_per_step": pg["kv_gb"] * 1e9},
+            "cpu_baseline": {"value": cpu_tok_s, "unit": "tok/s", "cores": orc.hw_threads(), "kind": "port",
+                             "sample": cpu_sample_s}}
+    print(json.dumps(line), flush=True)
+
+
+def paged_cpu_sample():
+    """The oracle's paged attention on the host: 2 sequences x 8192 tokens,
+    one layer, all host threads; returned as tok/s of a 24-layer step."""
+    import numpy as np
+    from oracle import oracle as orc
+    rng = np.random.default_rng(5)
+    P, H, hd, L = PG_P, PG_H, PG_HD, PG_TOK
+    npg = 2 * L // P
+    data = rng.integers(-127, 128, (npg, 2, H, P, hd)).astype(np.int8)
+    sc = rng.uniform(0.01, 0.03, (npg, 2, H)).astype(np.float32)
+    table = np.arange(npg, dtype=np.int32).reshape(2, L // P)
+    q = rng.standard_normal((2, H, hd), dtype=np.float32)
+    t0, n = time.perf_counter(), 0
+    while time.perf_counter() - t0 < 8.0:  # a bounded sample: about 8 s of host work
+        orc.paged_attention(data, sc, table, [L, L], P, H, hd, q, threads=orc.hw_threads())
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return 2 / (dt * PG_LAYERS), (f"{n} runs of 2 sequences x 8192 tokens, 1 layer ({dt * 1e3:.1f} ms each), "
+                                  f"scaled to a 24-layer step")
+
+
+def bench_moe_ep(ws: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
+    """Expert-parallel MoE layer prefill over NCCL: every rank holds 4096
+    tokens (weak scaling) and experts e % ws == rank of the Qwen-shaped
+    layer. Device time per call, max over ranks."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from chalot_c1_b200 import ep, moe
+    layer = moe.synthetic_moe_layer(MOE_DIM, MOE_H, MOE_E, MOE_K, 32, seed=3)
+    x = torch.from_numpy(np.random.default_rng(100 + rank).standard_normal((MOE_T, MOE_DIM),
+                                                                           dtype=np.float32)).cuda()
+    be = ep.GpuBackend(layer, ws, rank)
+    a2a = ep.dist_all_to_all()
+    for _ in range(warmup):
+        ep.ep_forward(be, x, a2a, ws)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        ep.ep_forward(be, x, a2a, ws)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = allmax(ws, e0.elapsed_time(e1) / reps)
+    return {"tokens_per_rank": MOE_T, "ms": ms, "tok_s": MOE_T * ws / (ms * 1e-3),
+            "tops": MOE_OPS * ws / (ms * 1e-3) / 1e12}
 
 
 def run_profile(args):
@@ -342,12 +417,14 @@ def bench_moe_prefill(reps: int = 10, warmup: int = 3, path: str | None = None,
                "path": os.environ.get("CHALOT_MOE_PATH", "auto")}
         if cpu_tokens:
             from oracle import oracle as orc
-            t0 = time.perf_counter()
-            orc.moe_forward(xh[:cpu_tokens], layer.layer_bytes(), MOE_DIM, MOE_H, MOE_E, MOE_K, 32,
-                            threads=orc.hw_threads())
+            blob = layer.layer_bytes()
+            t0, n = time.perf_counter(), 0
+            while time.perf_counter() - t0 < 8.0:  # a bounded sample: about 8 s of host work
+                orc.moe_forward(xh[:cpu_tokens], blob, MOE_DIM, MOE_H, MOE_E, MOE_K, 32, threads=orc.hw_threads())
+                n += 1
             dt = time.perf_counter() - t0
-            res["cpu"] = {"tok_s": cpu_tokens / dt, "cores": orc.hw_threads(), "kind": "port",
-                          "sample": f"{cpu_tokens} tokens ({dt:.2f} s)"}
+            res["cpu"] = {"tok_s": n * cpu_tokens / dt, "cores": orc.hw_threads(), "kind": "port",
+                          "sample": f"{n} x {cpu_tokens} tokens ({dt:.1f} s)"}
         return res
     finally:
         if path:
@@ -431,7 +508,7 @@ def run_paged(args):
 def run_moe(args):
     for path in ("tc", "simt"):
         r = bench_moe_prefill(reps=args.steps, warmup=args.warmup, path=path,
-                              cpu_tokens=256 if path == "tc" else 0)
+                              cpu_tokens=1024 if path == "tc" else 0)
         print(json.dumps(r), flush=True)
 
 
