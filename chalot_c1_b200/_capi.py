@@ -101,6 +101,15 @@ SIGNATURES = {
     "chalot_moe_experts_workspace_size": (C.c_size_t, [C.POINTER(MoeDesc), C.c_size_t]),
     "chalot_moe_experts": (C.c_int, [C.POINTER(MoeDesc), P, P, P, C.c_size_t, P, P, C.c_size_t, P]),
     "chalot_moe_combine": (C.c_int, [P, P, P, C.c_size_t, C.c_uint32, C.c_size_t, P, P]),
+    "chalot_kv_create": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.c_int, C.POINTER(P)]),
+    "chalot_kv_free": (None, [P]),
+    "chalot_kv_write": (C.c_int, [P, C.c_uint32, C.c_uint32, P, P]),
+    "chalot_kv_read": (C.c_int, [P, C.c_uint32, C.c_uint32, P, P, C.POINTER(C.c_int)]),
+    "chalot_kv_write_batch": (C.c_int, [P, C.c_uint32, P, C.c_size_t, P, P, P]),
+    "chalot_kv_gather": (C.c_int, [P, C.c_uint32, P, C.c_size_t, P, P, P, P]),
+    "chalot_kv_clear": (C.c_int, [P]),
+    "chalot_kv_active_pages": (C.c_size_t, [P]),
+    "chalot_kv_memory_mb": (C.c_float, [P]),
     "chalot_paged_kv_store": (C.c_int, [C.POINTER(PagedKV), P, C.c_size_t, P, P, P]),
     "chalot_paged_attention_workspace_size": (C.c_size_t, [C.POINTER(PagedKV), C.c_size_t, C.c_size_t]),
     "chalot_paged_attention": (C.c_int, [C.POINTER(PagedKV), P, C.c_size_t, P, C.c_size_t, P, P, P,

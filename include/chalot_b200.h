@@ -264,6 +264,39 @@ int chalot_moe_experts(const chalot_moe_desc* local, const int8_t* rows, const f
 int chalot_moe_combine(const float* y, const int32_t* pos, const float* selw, size_t n_tok,
                        uint32_t top_k, size_t dim, float* out, void* stream);
 
+/* ---- PagedKVCache (the reference's paged KV manager) -------------------- */
+/* PagedKVCache (src/model/memory.rs:100-201) with its pages in device memory:
+ * 256-token pages per layer, K and V rows int8 with one scale per row
+ * (max|x|/127, 1.0 for a zero row; (x/scale).clamp(-128, 127) truncated, as
+ * `as i8`), LRU eviction of the least recently written page once the cache
+ * holds max_pages_per_layer * n_layers pages (0 selects the reference's 16),
+ * checked before every write. Reads leave the LRU order alone. One cache per
+ * host thread, as the reference's &mut self. */
+typedef struct chalot_kv_cache chalot_kv_cache;
+
+/* PagedKVCache::new(kv_dim, n_layers) (memory.rs:119-127). */
+int chalot_kv_create(uint32_t kv_dim, uint32_t n_layers, uint32_t max_pages_per_layer, int device,
+                     chalot_kv_cache** out);
+void chalot_kv_free(chalot_kv_cache* c);
+/* PagedKVCache::write (memory.rs:163-171); k, v: host rows of kv_dim f32. */
+int chalot_kv_write(chalot_kv_cache* c, uint32_t layer, uint32_t pos, const float* k, const float* v);
+/* PagedKVCache::read (memory.rs:174-185): *found = 0 (outputs untouched) when
+ * the page is absent; k_out, v_out: host rows. */
+int chalot_kv_read(chalot_kv_cache* c, uint32_t layer, uint32_t pos, float* k_out, float* v_out,
+                   int* found);
+/* n writes in order, as n calls of chalot_kv_write would leave the cache;
+ * pos: host array; k, v: device rows [n][kv_dim]. */
+int chalot_kv_write_batch(chalot_kv_cache* c, uint32_t layer, const uint32_t* pos, size_t n,
+                          const float* k, const float* v, void* stream);
+/* n reads: k_out, v_out device rows [n][kv_dim] (rows whose page is absent are
+ * left untouched), found: host array of n flags. */
+int chalot_kv_gather(chalot_kv_cache* c, uint32_t layer, const uint32_t* pos, size_t n, float* k_out,
+                     float* v_out, uint8_t* found, void* stream);
+/* PagedKVCache::clear, active_pages, memory_mb (memory.rs:129-133, 188-201). */
+int chalot_kv_clear(chalot_kv_cache* c);
+size_t chalot_kv_active_pages(const chalot_kv_cache* c);
+float chalot_kv_memory_mb(const chalot_kv_cache* c);
+
 /* ---- paged int8 KV cache for long-context decode ------------------------ */
 
 /* A device page pool in the long-context format (new; the reference's own

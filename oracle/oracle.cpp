@@ -24,6 +24,7 @@
 //   Engine::forward           src/model/engine.rs:173-494
 //   expert block, T tokens    src/model/engine.rs:334-401 (orc_moe_forward)
 //   paged int8 KV attention   engine.rs:283-309 over memory.rs:69-74 dequantized rows
+//   PagedKVCache              src/model/memory.rs:26-201 (orc_kvc_*)
 //   Engine::generate          src/model/engine.rs:497-548
 //   sample_from_logits        src/model/engine.rs:551-569
 //   header/config/index       src/model/header.rs:40-133, config.rs:40-69,
@@ -48,6 +49,8 @@
 
 #include <algorithm>
 #include <cmath>
+#include <deque>
+#include <map>
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -1037,6 +1040,93 @@ ORC_API void orc_paged_attention(const int8_t* data, const float* scales, const 
     }
     std::memcpy(out + (s * H + h) * hd, o.data(), hd * 4);
   }
+}
+
+// ---------------------------------------------------------------------------
+// PagedKVCache (src/model/memory.rs:26-201), restated: pages of 256 tokens per
+// layer in a map, an LRU queue of (layer, page), eviction of the queue's front
+// when the cache holds 16 * n_layers pages (checked before every write, even
+// to a page that exists), per-row int8 quantization with scale = max|x|/127
+// (1.0 for an all-zero row) and a truncating `as i8` after clamp [-128, 127].
+// ---------------------------------------------------------------------------
+struct orc_kvc {
+  size_t dim, n_layers, max_pages;
+  std::vector<std::map<size_t, std::pair<std::vector<int8_t>, std::vector<float>>>> pages;  // k|v, scales
+  std::deque<std::pair<size_t, size_t>> lru;
+};
+
+namespace {
+constexpr size_t kRefPage = 256;
+
+// KVPage::quantize_row (memory.rs:58-66)
+void kv_quantize_row(const float* row, size_t n, int8_t* out, float* scale) {
+  float mx = 0.0f;
+  for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, std::fabs(row[i]));  // fold(0.0, f32::max)
+  const float s = mx > 0.0f ? mx / 127.0f : 1.0f;
+  *scale = s;
+  for (size_t i = 0; i < n; ++i) {
+    float v = row[i] / s;
+    if (v != v) {
+      out[i] = 0;
+      continue;
+    }
+    v = std::min(std::max(v, -128.0f), 127.0f);
+    out[i] = int8_t(v);  // truncation toward zero, as `as i8`
+  }
+}
+}  // namespace
+
+ORC_API orc_kvc* orc_kvc_create(size_t kv_dim, size_t n_layers, size_t max_pages_per_layer) {
+  orc_kvc* c = new orc_kvc;
+  c->dim = kv_dim;
+  c->n_layers = n_layers;
+  c->max_pages = (max_pages_per_layer ? max_pages_per_layer : 16) * n_layers;
+  c->pages.resize(n_layers);
+  return c;
+}
+ORC_API void orc_kvc_free(orc_kvc* c) { delete c; }
+
+ORC_API void orc_kvc_write(orc_kvc* c, size_t layer, size_t pos, const float* k, const float* v) {
+  const size_t page = pos / kRefPage, off = pos % kRefPage, d = c->dim;
+  size_t total = 0;
+  for (auto& m : c->pages) total += m.size();
+  if (total >= c->max_pages && !c->lru.empty()) {  // evict_if_full (memory.rs:137-145)
+    auto lp = c->lru.front();
+    c->lru.pop_front();
+    c->pages[lp.first].erase(lp.second);
+  }
+  for (auto it = c->lru.begin(); it != c->lru.end();)
+    it = (it->first == layer && it->second == page) ? c->lru.erase(it) : it + 1;
+  c->lru.push_back({layer, page});
+  auto& m = c->pages[layer];
+  auto f = m.find(page);
+  if (f == m.end())
+    f = m.emplace(page, std::make_pair(std::vector<int8_t>(2 * kRefPage * d, 0), std::vector<float>(2 * kRefPage, 1.0f)))
+            .first;
+  kv_quantize_row(k, d, f->second.first.data() + off * d, &f->second.second[off]);
+  kv_quantize_row(v, d, f->second.first.data() + (kRefPage + off) * d, &f->second.second[kRefPage + off]);
+}
+
+ORC_API int orc_kvc_read(const orc_kvc* c, size_t layer, size_t pos, float* k_out, float* v_out) {
+  const size_t page = pos / kRefPage, off = pos % kRefPage, d = c->dim;
+  auto f = c->pages[layer].find(page);
+  if (f == c->pages[layer].end()) return 0;
+  for (size_t i = 0; i < d; ++i) {
+    k_out[i] = float(f->second.first[off * d + i]) * f->second.second[off];
+    v_out[i] = float(f->second.first[(kRefPage + off) * d + i]) * f->second.second[kRefPage + off];
+  }
+  return 1;
+}
+
+ORC_API void orc_kvc_clear(orc_kvc* c) {
+  for (auto& m : c->pages) m.clear();
+  c->lru.clear();
+}
+
+ORC_API size_t orc_kvc_active_pages(const orc_kvc* c) {
+  size_t t = 0;
+  for (auto& m : c->pages) t += m.size();
+  return t;
 }
 
 ORC_API int orc_hw_threads(void) { return omp_get_num_procs(); }

@@ -78,6 +78,15 @@ def lib():
         L.orc_moe_forward.argtypes = [P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_size_t, C.c_size_t, P, P, C.c_int]
         L.orc_expert_rows.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t, P, C.c_int]
+        L.orc_kvc_create.restype = P
+        L.orc_kvc_create.argtypes = [C.c_size_t, C.c_size_t, C.c_size_t]
+        L.orc_kvc_free.argtypes = [P]
+        L.orc_kvc_write.argtypes = [P, C.c_size_t, C.c_size_t, P, P]
+        L.orc_kvc_read.restype = C.c_int
+        L.orc_kvc_read.argtypes = [P, C.c_size_t, C.c_size_t, P, P]
+        L.orc_kvc_clear.argtypes = [P]
+        L.orc_kvc_active_pages.restype = C.c_size_t
+        L.orc_kvc_active_pages.argtypes = [P]
         L.orc_paged_store.argtypes = [P, P, P, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t, P, P]
         L.orc_paged_attention.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                           C.c_size_t, P, P, C.c_int]
@@ -224,6 +233,34 @@ def expert_rows(xq, xs, expert, experts, dim, hidden, group, threads=1):
     lib().orc_expert_rows(_p(xq), _p(_f32(xs)), _p(np.ascontiguousarray(expert, np.int32)), n,
                           _p(np.ascontiguousarray(experts, np.uint8)), dim, hidden, group, _p(y), threads)
     return y
+
+
+class RefPagedKVCache:
+    """PagedKVCache (src/model/memory.rs:100-201) restated: write/read/clear."""
+
+    def __init__(self, kv_dim: int, n_layers: int, max_pages_per_layer: int = 16):
+        self.dim = kv_dim
+        self.h = lib().orc_kvc_create(kv_dim, n_layers, max_pages_per_layer)
+
+    def write(self, layer, pos, k, v):
+        lib().orc_kvc_write(self.h, layer, pos, _p(_f32(k)), _p(_f32(v)))
+
+    def read(self, layer, pos):
+        k = np.zeros(self.dim, np.float32)
+        v = np.zeros(self.dim, np.float32)
+        ok = lib().orc_kvc_read(self.h, layer, pos, _p(k), _p(v))
+        return bool(ok), k, v
+
+    def clear(self):
+        lib().orc_kvc_clear(self.h)
+
+    def active_pages(self) -> int:
+        return int(lib().orc_kvc_active_pages(self.h))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().orc_kvc_free(self.h)
+            self.h = None
 
 
 def paged_store(data, scales, page_ids, P, H, hd, k, v):

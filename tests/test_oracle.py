@@ -198,3 +198,42 @@ def test_oracle_paged_attention_matches_f32_attention(oracle_lib):
         for t in range(L):
             ref = (ref + (w[t] * vd[t]).astype(np.float32)).astype(np.float32)
         assert np.allclose(out[0, h], ref, rtol=1e-5, atol=1e-6)
+
+
+# ---- PagedKVCache (src/model/memory.rs tests) ---------------------------------
+
+def test_kvcache_quantization_kat(oracle_lib):
+    # memory.rs:210-225: a row round-trips within 0.1
+    c = oracle_lib.RefPagedKVCache(4, 1)
+    row = np.array([0.5, -1.2, 3.4, 0.0], np.float32)
+    c.write(0, 0, row, row)
+    ok, k, v = c.read(0, 0)
+    assert ok and np.all(np.abs(k - row) < 0.1) and np.all(np.abs(v - row) < 0.1)
+
+
+def test_kvcache_paging_kat(oracle_lib):
+    # memory.rs:227-243: position 300 lives in page 1
+    c = oracle_lib.RefPagedKVCache(64, 4)
+    c.write(0, 300, np.ones(64, np.float32), np.full(64, 2.0, np.float32))
+    ok, k, v = c.read(0, 300)
+    assert ok and abs(k[0] - 1.0) < 0.1 and abs(v[0] - 2.0) < 0.1
+    assert not c.read(0, 0)[0] and not c.read(1, 300)[0]
+
+
+def test_kvcache_lru_eviction_kat(oracle_lib):
+    # memory.rs:245-260: 21 pages into a 1-layer cache keep at most 16
+    c = oracle_lib.RefPagedKVCache(32, 1)
+    for i in range(16 + 5):
+        c.write(0, i * 256, np.ones(32, np.float32), np.full(32, 2.0, np.float32))
+    assert c.active_pages() <= 16
+    assert not c.read(0, 0)[0] and c.read(0, 20 * 256)[0]
+
+
+def test_kvcache_truncating_quantizer(oracle_lib):
+    # (val / scale).clamp(-128, 127) as i8 truncates toward zero: 0.9 * 127 -> 114
+    c = oracle_lib.RefPagedKVCache(2, 1)
+    c.write(0, 0, np.array([1.0, 0.9], np.float32), np.zeros(2, np.float32))
+    ok, k, v = c.read(0, 0)
+    s = np.float32(1.0) / np.float32(127.0)
+    assert k[1] == np.float32(np.float32(int(np.float32(0.9) / s)) * s)
+    assert (v == 0).all()  # an all-zero row keeps scale 1.0 and zeros
