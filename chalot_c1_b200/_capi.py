@@ -81,6 +81,9 @@ SIGNATURES = {
     "chalot_sample_from_logits": (C.c_int, [P, C.POINTER(Sampling), P, C.c_size_t,
                                             C.POINTER(C.c_uint32)]),
     "chalot_get_logits": (C.c_int, [P, P, C.c_size_t]),
+    "chalot_batch_reserve": (C.c_int, [P, C.c_uint32]),
+    "chalot_forward_batch": (C.c_int, [P, P, P, P, C.c_uint32, P]),
+    "chalot_get_batch_logits": (C.c_int, [P, C.c_uint32, P, C.c_size_t]),
     "chalot_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_double),
                                      C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     "chalot_bench_moe_layers": (C.c_int, [P, C.c_int, C.POINTER(C.c_double),

@@ -1,0 +1,29 @@
+// batch.h — launchers of the batched-decode kernels (k_batch.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace chalot {
+
+struct BatchDims {
+  int dim, n_layers, n_heads, head_dim, max_seq;
+};
+
+void b_embed(const BatchDims& d, int B, const uint32_t* toks, const int8_t* emb, const float* emb_s,
+             const float* rms0, float* x, int8_t* xq, float* xs, cudaStream_t s);
+void b_norm_quant(const BatchDims& d, int B, const float* x, const float* w, int8_t* xq, float* xs,
+                  cudaStream_t s);
+void b_gemm_i8(int B, int R, int C, const int8_t* W, const float* ws, const int8_t* xq, const float* xs,
+               float* out, int ldo, bool add, cudaStream_t s);
+void b_rope_kv(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* qkv,
+               float* q, float* kc, float* vc, const float* rcos, const float* rsin, cudaStream_t s);
+void b_attention(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* q,
+                 const float* kc, const float* vc, float* scores, float* att, cudaStream_t s);
+void b_rmsnorm(const BatchDims& d, int B, const float* x, const float* w, float* xb, cudaStream_t s);
+void b_add(long n, float* x, const float* y, cudaStream_t s);
+void b_argmax(int B, int V, const float* logits, uint32_t* out, cudaStream_t s);
+
+}  // namespace chalot

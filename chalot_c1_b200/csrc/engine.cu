@@ -28,8 +28,10 @@
 #include <string>
 #include <vector>
 
+#include "batch.h"
 #include "capi_internal.h"
 #include "kernels.cuh"
+#include "moe_layer.h"
 #include "myai.h"
 #include "pdl.cuh"
 
@@ -128,6 +130,18 @@ struct chalot_engine {
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   double last_prefill_ms = 0, last_decode_ms = 0;
   uint32_t last_n_prefill = 0, last_n_decode = 0;
+  // batched decode (chalot_batch_reserve / chalot_forward_batch)
+  struct Batch {
+    int cap = 0;
+    float *kc = nullptr, *vc = nullptr, *x = nullptr, *qkv = nullptr, *q = nullptr, *scores = nullptr;
+    float *att = nullptr, *xb = nullptr, *eout = nullptr, *logits = nullptr, *xs = nullptr;
+    int8_t* xq = nullptr;
+    int32_t *pos = nullptr, *slot = nullptr;
+    uint32_t *toks = nullptr, *out = nullptr;
+    void* moe_ws = nullptr;
+    uint32_t* h_io = nullptr;  // pinned staging: slots, tokens, positions, results
+    std::vector<MlExperts> experts;  // per layer, the engine's repacked experts
+  } bt;
 
   ~chalot_engine() {
     if (g_fwd) cudaGraphExecDestroy(g_fwd);
@@ -139,6 +153,7 @@ struct chalot_engine {
     if (h_state) cudaFreeHost(h_state);
     if (h_stage) cudaFreeHost(h_stage);
     if (h_tokens) cudaFreeHost(h_tokens);
+    if (bt.h_io) cudaFreeHost(bt.h_io);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -809,6 +824,138 @@ __attribute__((visibility("default"))) int chalot_profile_forward(chalot_engine*
     return fail(f);
   }
   for (auto& x : ev) cudaEventDestroy(x);
+  return CHALOT_OK;
+}
+
+// ---- batched decode -------------------------------------------------------------
+
+static MlDims batch_moe_dims(const chalot_engine* e, int n) {
+  const ModelConfig& c = e->cfg;
+  return MlDims{n, (int)c.dim, (int)c.hidden_dim, (int)c.n_experts, (int)c.top_k, (int)c.int4_group_size};
+}
+
+__attribute__((visibility("default"))) int chalot_batch_reserve(chalot_engine* e, uint32_t max_seqs) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
+  const ModelConfig& c = e->cfg;
+  if (c.n_experts < 2) return set_error(CHALOT_ERR_ARG, "batch_reserve: batched decode needs a MoE model");
+  if (max_seqs == 0 || max_seqs > 1024) return set_error(CHALOT_ERR_ARG, "batch_reserve: max_seqs in [1, 1024]");
+  if ((int)max_seqs <= e->bt.cap) return CHALOT_OK;
+  if (e->bt.cap) return set_error(CHALOT_ERR_STATE, "batch_reserve: already reserved with fewer slots");
+  if (const char* m = ml_check(batch_moe_dims(e, (int)max_seqs)))
+    return set_error(CHALOT_ERR_ARG, std::string("batch_reserve: ") + m);
+  try {
+    CK(cudaSetDevice(e->device));
+    auto& b = e->bt;
+    const size_t S = max_seqs, D = c.dim, L = c.n_layers, M = c.max_seq_len, H = c.n_heads;
+    b.kc = e->dalloc<float>(S * L * M * D);
+    b.vc = e->dalloc<float>(S * L * M * D);
+    b.x = e->dalloc<float>(S * D);
+    b.qkv = e->dalloc<float>(S * 3 * D);
+    b.q = e->dalloc<float>(S * D);
+    b.scores = e->dalloc<float>(S * H * M);
+    b.att = e->dalloc<float>(S * D);
+    b.xb = e->dalloc<float>(S * D);
+    b.eout = e->dalloc<float>(S * D);
+    b.logits = e->dalloc<float>(S * c.vocab_size);
+    b.xs = e->dalloc<float>(S);
+    b.xq = e->dalloc<int8_t>(S * D);
+    b.pos = e->dalloc<int32_t>(S);
+    b.slot = e->dalloc<int32_t>(S);
+    b.toks = e->dalloc<uint32_t>(S);
+    b.out = e->dalloc<uint32_t>(S);
+    const MlDims md = batch_moe_dims(e, (int)max_seqs);
+    const size_t simt = ml_layout(md, nullptr, nullptr);
+    const size_t need = ml_tc_eligible(md) ? ml_tc_layout(md, simt, nullptr, nullptr) : simt;
+    b.moe_ws = e->dalloc<unsigned char>(need);
+    CK(cudaMallocHost(&b.h_io, 4 * S * sizeof(uint32_t)));
+    b.experts.assign(L, MlExperts{});
+    for (size_t l = 0; l < L; ++l) {
+      for (size_t x = 0; x < c.n_experts && x < 32; ++x) {
+        const ExpertPtrs& p = e->host_experts[l][x];
+        b.experts[l].ex[x] = MlExpert{p.gu, p.gu_s, p.dn, p.dn_s};
+      }
+      b.experts[l].repacked = 1;
+    }
+    b.cap = (int)max_seqs;
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e, const uint32_t* slots,
+                                                                const uint32_t* toks, const uint32_t* pos,
+                                                                uint32_t n, uint32_t* out_toks) {
+  if (!e || (n && (!slots || !toks || !pos || !out_toks))) return set_error(CHALOT_ERR_ARG, "null argument");
+  auto& b = e->bt;
+  if (!b.cap) return set_error(CHALOT_ERR_STATE, "forward_batch: call chalot_batch_reserve first");
+  if ((int)n > b.cap) return set_error(CHALOT_ERR_ARG, "forward_batch: more tokens than reserved slots");
+  const ModelConfig& c = e->cfg;
+  for (uint32_t i = 0; i < n; ++i) {
+    if ((int)slots[i] >= b.cap) return set_error(CHALOT_ERR_ARG, "forward_batch: slot out of range");
+    if (pos[i] >= c.max_seq_len) return set_error(CHALOT_ERR_ARG, "forward_batch: position beyond max_seq_len");
+    if (toks[i] >= c.vocab_size) return set_error(CHALOT_ERR_ARG, "forward_batch: token out of range");
+    for (uint32_t j = 0; j < i; ++j)
+      if (slots[j] == slots[i]) return set_error(CHALOT_ERR_ARG, "forward_batch: a slot appears twice");
+  }
+  if (n == 0) return CHALOT_OK;
+  try {
+    CK(cudaSetDevice(e->device));
+    cudaStream_t s = e->stream;
+    CK(cudaStreamSynchronize(s));  // the pinned staging may still feed a previous call
+    uint32_t* io = b.h_io;
+    std::memcpy(io, slots, n * 4);
+    std::memcpy(io + b.cap, toks, n * 4);
+    std::memcpy(io + 2 * b.cap, pos, n * 4);
+    CK(cudaMemcpyAsync(b.slot, io, n * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(b.toks, io + b.cap, n * 4, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(b.pos, io + 2 * b.cap, n * 4, cudaMemcpyHostToDevice, s));
+    const int B = (int)n, D = (int)c.dim;
+    const BatchDims bd{D, (int)c.n_layers, (int)c.n_heads, (int)c.head_dim, (int)c.max_seq_len};
+    b_embed(bd, B, b.toks, e->emb, e->emb_s, e->layers[0].rms_attn, b.x, b.xq, b.xs, s);
+    const MlDims md = batch_moe_dims(e, B);
+    MlWork w;
+    const size_t simt = ml_layout(md, b.moe_ws, &w);
+    const bool tc = ml_use_tc(md);
+    MlTcWork t{};
+    if (tc) ml_tc_layout(md, simt, b.moe_ws, &t);
+    for (int l = 0; l < (int)c.n_layers; ++l) {
+      const LayerPtrs& L = e->layers[l];
+      b_gemm_i8(B, 3 * D, D, L.qkv, L.qkv_s, b.xq, b.xs, b.qkv, 3 * D, false, s);
+      b_rope_kv(bd, l, B, b.pos, b.slot, b.qkv, b.q, b.kc, b.vc, e->b.rope_cos, e->b.rope_sin, s);
+      b_attention(bd, l, B, b.pos, b.slot, b.q, b.kc, b.vc, b.scores, b.att, s);
+      CK(op_quantize_i8(b.xq, b.xs, b.att, B, D, s));
+      b_gemm_i8(B, D, D, L.o, L.o_s, b.xq, b.xs, b.x, D, true, s);  // residual (engine.rs:312-322)
+      b_rmsnorm(bd, B, b.x, L.rms_ffn, b.xb, s);
+      CK(tc ? ml_run_tc(md, b.xb, L.router_w, L.router_b, b.experts[l], w, t, b.eout, s)
+            : ml_run(md, b.xb, L.router_w, L.router_b, b.experts[l], w, b.eout, s));
+      b_add((long)B * D, b.x, b.eout, s);  // x += expert_out (engine.rs:401)
+      b_norm_quant(bd, B, b.x, l + 1 < (int)c.n_layers ? e->layers[l + 1].rms_attn : e->final_norm, b.xq, b.xs, s);
+    }
+    b_gemm_i8(B, (int)c.vocab_size, D, e->out_w, e->out_s, b.xq, b.xs, b.logits, (int)c.vocab_size, false, s);
+    b_argmax(B, (int)c.vocab_size, b.logits, b.out, s);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(io + 3 * b.cap, b.out, n * 4, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    std::memcpy(out_toks, io + 3 * b.cap, n * 4);
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst,
+                                                                   size_t n) {
+  if (!e || !dst) return set_error(CHALOT_ERR_ARG, "null argument");
+  if ((int)row >= e->bt.cap) return set_error(CHALOT_ERR_ARG, "get_batch_logits: row out of range");
+  try {
+    CK(cudaSetDevice(e->device));
+    CK(cudaMemcpyAsync(dst, e->bt.logits + (size_t)row * e->cfg.vocab_size,
+                       std::min(n, e->cfg.vocab_size) * 4, cudaMemcpyDeviceToHost, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
   return CHALOT_OK;
 }
 

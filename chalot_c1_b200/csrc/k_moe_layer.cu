@@ -33,6 +33,7 @@
 #include "capi_internal.h"
 #include "common.cuh"
 #include "moe_layer.h"
+#include "unpack.cuh"
 
 namespace chalot {
 namespace {
@@ -48,22 +49,6 @@ constexpr int kSS = kKC / 32 + 1;  // shared row stride of group scales
 // and that bias is subtracted; both steps are exact.
 __device__ __forceinline__ float i2f_exact(int v) {
   return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
-}
-
-// 16 packed int4 bytes (32 columns, low nibble = even column, value = nibble-8)
-// to 32 int8 in column order.
-__device__ __forceinline__ void unpack32(uint4 p, uint4* dst) {
-  const uint32_t in[4] = {p.x, p.y, p.z, p.w};
-  uint32_t o[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = in[i] & 0x0F0F0F0Fu, hi = (in[i] >> 4) & 0x0F0F0F0Fu;
-    // bytes [lo0 hi0 lo1 hi1] and [lo2 hi2 lo3 hi3]; nibble-8 per byte without borrows
-    o[2 * i] = (__byte_perm(lo, hi, 0x5140) + 0x78787878u) ^ 0x80808080u;
-    o[2 * i + 1] = (__byte_perm(lo, hi, 0x7362) + 0x78787878u) ^ 0x80808080u;
-  }
-  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 __global__ void __launch_bounds__(kThreads) k_ml_route(MlDims d, const float* __restrict__ x,
@@ -165,8 +150,7 @@ __global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm
 // up rows of the same hidden units, so a thread holds gate and up of the
 // hidden units r0+l and r0+l+32 for its four slots.
 template <bool GU>
-__global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const uint8_t* __restrict__ experts,
-                                                      size_t ex_bytes, MlWork w) {
+__global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts XP, MlWork w) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int mb = blockIdx.y;
   if (mb >= *w.n_mb) return;
@@ -175,12 +159,8 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const uint8_t* _
   const int out_rows = GU ? d.H : d.dim;
   const int ng = in_dim / d.group;
   const int r0 = blockIdx.x * (GU ? kBN / 2 : kBN);
-  const uint8_t* eb = experts + (size_t)e * ex_bytes;
-  const size_t gu_bytes = (size_t)2 * d.H * (d.dim / 2);
-  const size_t gu_scales = (size_t)2 * d.H * (d.dim / d.group) * 4;
-  const uint8_t* wmat = GU ? eb : eb + gu_bytes + gu_scales;
-  const float* smat = reinterpret_cast<const float*>(GU ? eb + gu_bytes
-                                                         : eb + gu_bytes + gu_scales + (size_t)d.dim * (d.H / 2));
+  const uint8_t* wmat = GU ? XP.ex[e].gu : XP.ex[e].dn;
+  const float* smat = GU ? XP.ex[e].gus : XP.ex[e].dns;
   const int8_t* amat = GU ? w.xq : w.hq;
   const float* ascale = GU ? w.xs : w.hs;
 
@@ -235,7 +215,7 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const uint8_t* _
       const uint8_t* wr = wrow[r];
       uint4* dst = reinterpret_cast<uint4*>(W + r * kWS + j * 32);
       if (wr) {
-        unpack32(ldg_stream(wr + (k0 >> 1) + j * 16), dst);
+        unpack32_any(ldg_stream(wr + (k0 >> 1) + j * 16), dst, XP.repacked != 0);
       } else {
         dst[0] = make_uint4(0, 0, 0, 0);
         dst[1] = make_uint4(0, 0, 0, 0);
@@ -333,6 +313,21 @@ size_t gemm_smem() {
 
 }  // namespace
 
+MlExperts ml_experts_from_blob(const MlDims& d, const uint8_t* blob) {
+  MlExperts X{};
+  const size_t ng_d = d.dim / d.group, ng_h = d.H / d.group, ex = ml_expert_bytes(d);
+  const size_t gu_bytes = (size_t)2 * d.H * (d.dim / 2), gu_sc = (size_t)2 * d.H * ng_d * 4;
+  const size_t dn_bytes = (size_t)d.dim * (d.H / 2);
+  for (int e = 0; e < d.E && e < 32; ++e) {
+    const uint8_t* eb = blob + (size_t)e * ex;
+    X.ex[e] = MlExpert{eb, reinterpret_cast<const float*>(eb + gu_bytes), eb + gu_bytes + gu_sc,
+                       reinterpret_cast<const float*>(eb + gu_bytes + gu_sc + dn_bytes)};
+  }
+  (void)ng_h;
+  X.repacked = 0;
+  return X;
+}
+
 size_t ml_expert_bytes(const MlDims& d) {
   const size_t ng_d = d.dim / d.group, ng_h = d.H / d.group;
   return (size_t)2 * d.H * (d.dim / 2) + (size_t)2 * d.H * ng_d * 4 + (size_t)d.dim * (d.H / 2) +
@@ -395,7 +390,7 @@ static void quantize_h(const MlDims& d, const MlWork& w, cudaStream_t s) {
 }
 
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
-                   const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s) {
+                   const MlExperts& X, const MlWork& w, float* out, cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
   route_and_dispatch(d, x, rw, rb, w, kBM, s);
@@ -403,17 +398,16 @@ cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float
   cudaFuncSetAttribute(k_ml_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
   cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
   const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
-  const size_t ex = ml_expert_bytes(d);
-  k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+  k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, X, w);
   quantize_h(d, w, s);
-  k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+  k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, X, w);
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
   return cudaGetLastError();
 }
 
 // The same layer with the expert products on the tensor cores.
 cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const float* rb,
-                      const uint8_t* experts, const MlWork& w, const MlTcWork& t, float* out,
+                      const MlExperts& X, const MlWork& w, const MlTcWork& t, float* out,
                       cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
@@ -421,7 +415,7 @@ cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const fl
   if (r == cudaSuccess) r = cudaMemsetAsync(t.amax, 0, N * 4, s);
   if (r != cudaSuccess) return r;
   route_and_dispatch(d, x, rw, rb, w, 128, s);
-  if ((r = ml_tc_prepare(d, experts, w, t, s)) != cudaSuccess) return r;
+  if ((r = ml_tc_prepare(d, X, w, t, s)) != cudaSuccess) return r;
   const unsigned nmb = (unsigned)std::min(N, N / 128 + d.E);
   if ((r = ml_tc_gemm(d, true, w, t, nmb, s)) != cudaSuccess) return r;
   if ((r = ml_tc_quant(d, w, t, s)) != cudaSuccess) return r;
@@ -454,7 +448,7 @@ void ml_launch_combine(const MlDims& d, const MlWork& w, float* out, cudaStream_
 // row's (local) expert, w.xq / w.xs the rows; d.K == 1. y[row] (the expert
 // output) is written in row order through the combine with weight 1.0, which
 // reproduces y exactly (0 + 1*y).
-cudaError_t ml_run_rows(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork* t, float* y,
+cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork* t, float* y,
                         cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T;
@@ -464,7 +458,7 @@ cudaError_t ml_run_rows(const MlDims& d, const uint8_t* experts, const MlWork& w
     if (r == cudaSuccess) r = cudaMemsetAsync(t->amax, 0, N * 4, s);
     if (r != cudaSuccess) return r;
     k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, 128, 1, nullptr);
-    if ((r = ml_tc_prepare(d, experts, w, *t, s)) != cudaSuccess) return r;
+    if ((r = ml_tc_prepare(d, X, w, *t, s)) != cudaSuccess) return r;
     const unsigned nmb = (unsigned)std::min(N, N / 128 + d.E);
     if ((r = ml_tc_gemm(d, true, w, *t, nmb, s)) != cudaSuccess) return r;
     if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
@@ -476,9 +470,9 @@ cudaError_t ml_run_rows(const MlDims& d, const uint8_t* experts, const MlWork& w
     cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
     const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
     const size_t ex = ml_expert_bytes(d);
-    k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+    k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, X, w);
     quantize_h(d, w, s);
-    k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, experts, ex, w);
+    k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, X, w);
   }
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, y);
   return cudaGetLastError();
@@ -546,8 +540,9 @@ __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_des
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   MlTcWork t{};
   if (tc) ml_tc_layout(d, simt, workspace, &t);
-  cudaError_t r = tc ? ml_run_tc(d, x, desc->router_w, desc->router_b, desc->experts, w, t, out, s)
-                     : ml_run(d, x, desc->router_w, desc->router_b, desc->experts, w, out, s);
+  const MlExperts X = ml_experts_from_blob(d, desc->experts);
+  cudaError_t r = tc ? ml_run_tc(d, x, desc->router_w, desc->router_b, X, w, t, out, s)
+                     : ml_run(d, x, desc->router_w, desc->router_b, X, w, out, s);
   const size_t N = n_tok * d.K;
   if (r == cudaSuccess && sel_out) r = cudaMemcpyAsync(sel_out, w.sel, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess && selw_out) r = cudaMemcpyAsync(selw_out, w.selw, N * 4, cudaMemcpyDeviceToDevice, s);

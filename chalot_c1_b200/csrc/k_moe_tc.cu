@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "moe_layer.h"
 #include "tc.cuh"
+#include "unpack.cuh"
 
 namespace chalot {
 namespace {
@@ -59,47 +60,31 @@ __device__ __forceinline__ float i2f_exact(int v) {
   return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
 }
 
-__device__ __forceinline__ void unpack32(uint4 p, uint4* dst) {
-  const uint32_t in[4] = {p.x, p.y, p.z, p.w};
-  uint32_t o[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = in[i] & 0x0F0F0F0Fu, hi = (in[i] >> 4) & 0x0F0F0F0Fu;
-    o[2 * i] = (__byte_perm(lo, hi, 0x5140) + 0x78787878u) ^ 0x80808080u;
-    o[2 * i + 1] = (__byte_perm(lo, hi, 0x7362) + 0x78787878u) ^ 0x80808080u;
-  }
-  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-}
-
-// One warp per destination row: int4 (file layout) -> int8, scales transposed.
-__global__ void __launch_bounds__(256) k_tc_unpack(MlDims d, const uint8_t* __restrict__ experts,
-                                                   size_t ex_bytes, MlTcWork t) {
+// One warp per destination row: int4 -> int8, scales transposed.
+__global__ void __launch_bounds__(256) k_tc_unpack(MlDims d, const MlExperts X, MlTcWork t) {
   const int lane = threadIdx.x & 31;
   const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const long gu_rows = (long)d.E * 2 * d.H, dn_rows = (long)d.E * d.dim;
   const int ngd = d.dim / d.group, ngh = d.H / d.group;
-  const size_t gu_bytes = (size_t)2 * d.H * (d.dim / 2), gu_sc = (size_t)2 * d.H * ngd * 4;
+  const bool rp = X.repacked != 0;
   if (row < gu_rows) {
     const int e = (int)(row / (2 * d.H)), r = (int)(row % (2 * d.H));
     const int hb = r >> 7, rr = r & 127;
     const int src = rr < 64 ? hb * 64 + rr : d.H + hb * 64 + (rr - 64);
-    const uint8_t* eb = experts + (size_t)e * ex_bytes;
-    const uint8_t* s = eb + (size_t)src * (d.dim / 2);
+    const uint8_t* s = X.ex[e].gu + (size_t)src * (d.dim / 2);
     int8_t* dst = t.w8gu + (size_t)row * d.dim;
     for (int j = lane; j < d.dim / 32; j += 32)
-      unpack32(__ldg(reinterpret_cast<const uint4*>(s + j * 16)), reinterpret_cast<uint4*>(dst + j * 32));
-    const float* sc = reinterpret_cast<const float*>(eb + gu_bytes) + (size_t)src * ngd;
+      unpack32_any(__ldg(reinterpret_cast<const uint4*>(s + j * 16)), reinterpret_cast<uint4*>(dst + j * 32), rp);
+    const float* sc = X.ex[e].gus + (size_t)src * ngd;
     for (int g = lane; g < ngd; g += 32) t.sgu[((size_t)e * ngd + g) * 2 * d.H + r] = __ldg(sc + g);
   } else if (row < gu_rows + dn_rows) {
     const long rr = row - gu_rows;
     const int e = (int)(rr / d.dim), i = (int)(rr % d.dim);
-    const uint8_t* eb = experts + (size_t)e * ex_bytes + gu_bytes + gu_sc;
-    const uint8_t* s = eb + (size_t)i * (d.H / 2);
+    const uint8_t* s = X.ex[e].dn + (size_t)i * (d.H / 2);
     int8_t* dst = t.w8dn + (size_t)rr * d.H;
     for (int j = lane; j < d.H / 32; j += 32)
-      unpack32(__ldg(reinterpret_cast<const uint4*>(s + j * 16)), reinterpret_cast<uint4*>(dst + j * 32));
-    const float* sc = reinterpret_cast<const float*>(eb + (size_t)d.dim * (d.H / 2)) + (size_t)i * ngh;
+      unpack32_any(__ldg(reinterpret_cast<const uint4*>(s + j * 16)), reinterpret_cast<uint4*>(dst + j * 32), rp);
+    const float* sc = X.ex[e].dns + (size_t)i * ngh;
     for (int g = lane; g < ngh; g += 32) t.sdn[((size_t)e * ngh + g) * d.dim + i] = __ldg(sc + g);
   }
 }
@@ -436,10 +421,10 @@ size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t) {
   return off;
 }
 
-cudaError_t ml_tc_prepare(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork& t,
+cudaError_t ml_tc_prepare(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork& t,
                           cudaStream_t s) {
   const long rows = (long)d.E * 2 * d.H + (long)d.E * d.dim;
-  k_tc_unpack<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(d, experts, ml_expert_bytes(d), t);
+  k_tc_unpack<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(d, X, t);
   const long N = (long)d.T * d.K;
   k_tc_gather<<<(unsigned)((N + 7) / 8), 256, 0, s>>>(d, w, t);
   return cudaGetLastError();

@@ -11,6 +11,20 @@ struct MlDims {
   int T, dim, H, E, K, group;
 };
 
+// Where each expert's tensors are: gate+up packed int4 [2H][dim/2] (gate rows
+// first) and their scales [2H][dim/group], down [dim][H/2] and its scales
+// [dim][H/group]. Passed by value to the kernels (32 experts at most).
+struct MlExpert {
+  const uint8_t* gu;
+  const float* gus;
+  const uint8_t* dn;
+  const float* dns;
+};
+struct MlExperts {
+  MlExpert ex[32];
+  int repacked;  // 0: the file's int4 layout, 1: the engine's repacked layout
+};
+
 // Device pointers into a caller-provided workspace (ml_layout).
 struct MlWork {
   int32_t* sel;   // [T*k] expert of each (token, choice) slot
@@ -42,24 +56,28 @@ struct MlTcWork {
 };
 
 size_t ml_expert_bytes(const MlDims& d);
+// E experts back to back in the file layout from `blob`.
+MlExperts ml_experts_from_blob(const MlDims& d, const uint8_t* blob);
 size_t ml_layout(const MlDims& d, void* base, MlWork* w);
 const char* ml_check(const MlDims& d);
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
-                   const uint8_t* experts, const MlWork& w, float* out, cudaStream_t s);
+                   const MlExperts& X, const MlWork& w, float* out, cudaStream_t s);
 
 // Building blocks of the expert-parallel layer (k_moe_layer.cu).
 void ml_launch_route(const MlDims& d, const float* x, const float* rw, const float* rb, const MlWork& w,
                      cudaStream_t s);
 void ml_launch_plan(const MlDims& d, const MlWork& w, int n_ranks, int32_t* offs, cudaStream_t s);
 void ml_launch_combine(const MlDims& d, const MlWork& w, float* out, cudaStream_t s);
-cudaError_t ml_run_rows(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork* t, float* y,
+cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork* t, float* y,
                         cudaStream_t s);
 bool ml_use_tc(const MlDims& d);
+cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const float* rb, const MlExperts& X,
+                      const MlWork& w, const MlTcWork& t, float* out, cudaStream_t s);
 cudaError_t ml_tc_gather_rows(const MlDims& d, const MlWork& w, const MlTcWork& t, cudaStream_t s);
 
 bool ml_tc_eligible(const MlDims& d);
 size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t);
-cudaError_t ml_tc_prepare(const MlDims& d, const uint8_t* experts, const MlWork& w, const MlTcWork& t,
+cudaError_t ml_tc_prepare(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork& t,
                           cudaStream_t s);
 cudaError_t ml_tc_gemm(const MlDims& d, bool gate_up, const MlWork& w, const MlTcWork& t,
                        unsigned n_mblocks, cudaStream_t s);

@@ -89,7 +89,7 @@ __attribute__((visibility("default"))) int chalot_moe_layer_noalloc(const chalot
   MlWork w;
   ml_layout(d, base, &w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  r = ml_run(d, x, desc->router_w, desc->router_b, desc->experts, w, out, s);
+  r = ml_run(d, x, desc->router_w, desc->router_b, ml_experts_from_blob(d, desc->experts), w, out, s);
   const size_t N = n_tok * d.K;
   if (r == cudaSuccess && sel_out) r = cudaMemcpyAsync(sel_out, w.sel, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess && selw_out)

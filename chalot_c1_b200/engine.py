@@ -101,6 +101,56 @@ class Engine:
         del keep
         return out[: n.value].tolist()
 
+    # ---- batched decode: many sequences, one KV slot each ----
+
+    def reserve_batch(self, max_seqs: int) -> None:
+        check(lib().chalot_batch_reserve(self._h, max_seqs))
+
+    def forward_batch(self, slots: Sequence[int], tokens: Sequence[int], positions: Sequence[int]) -> list[int]:
+        """Engine::forward for several sequences at once (one token each)."""
+        s, t, p = _u32(slots), _u32(tokens), _u32(positions)
+        out = np.zeros(max(1, s.size), np.uint32)
+        check(lib().chalot_forward_batch(self._h, s.ctypes.data_as(C.c_void_p), t.ctypes.data_as(C.c_void_p),
+                                         p.ctypes.data_as(C.c_void_p), s.size, out.ctypes.data_as(C.c_void_p)))
+        return out[: s.size].tolist()
+
+    def batch_logits(self, row: int) -> np.ndarray:
+        v = np.empty(self.config["vocab_size"], np.float32)
+        check(lib().chalot_get_batch_logits(self._h, row, v.ctypes.data_as(C.c_void_p), v.size))
+        return v
+
+    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new: int) -> list[list[int]]:
+        """Greedy Engine::generate (engine.rs:497-548) of every prompt at once:
+        sequence i uses slot i; each call advances every sequence that still
+        has a prompt token or a token to decode. Returns the new tokens."""
+        n = len(prompts)
+        self.reserve_batch(n)
+        prompts = [list(p) or [0] for p in prompts]
+        nxt = [0] * n
+        out = [[] for _ in range(n)]
+        steps = max(len(p) for p in prompts) + max_new - 1
+        for step in range(steps + 1):
+            slots, toks, pos, who = [], [], [], []
+            for i, p in enumerate(prompts):
+                if step < len(p):
+                    tok = p[step]
+                elif step - len(p) < max_new - 1 and len(out[i]) < max_new:
+                    tok = nxt[i]
+                else:
+                    continue
+                slots.append(i)
+                toks.append(tok)
+                pos.append(step)
+                who.append(i)
+            if not slots:
+                break
+            res = self.forward_batch(slots, toks, pos)
+            for i, r in zip(who, res):
+                nxt[i] = r
+                if step >= len(prompts[i]) - 1 and len(out[i]) < max_new:
+                    out[i].append(r)
+        return out
+
     def sample_from_logits(self, sampling: SamplingConfig | None, history: Sequence[int]) -> int:
         h = _u32(list(history) or [0])
         tok = C.c_uint32()

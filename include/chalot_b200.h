@@ -130,6 +130,25 @@ int chalot_sample_from_logits(chalot_engine* e, const chalot_sampling* sampling,
 /* Copies the logits of the last forward (state.logits) to host memory. */
 int chalot_get_logits(chalot_engine* e, float* dst, size_t n);
 
+/* ---- batched decode --------------------------------------------------- */
+/* Several sequences through one engine, one token each per call. The
+ * reference runs one Engine per sequence (Engine::forward, engine.rs:173,
+ * has no batch); here each sequence owns a KV cache slot and a call advances
+ * n of them at once with the same per-token arithmetic, so every sequence
+ * decodes exactly as it would alone. MoE models only. */
+
+/* Allocates max_seqs KV cache slots (f32, [slot][layer][max_seq_len][dim])
+ * and the batch buffers; once per engine. */
+int chalot_batch_reserve(chalot_engine* e, uint32_t max_seqs);
+
+/* Engine::forward for n sequences: token toks[i] at position pos[i] of the
+ * sequence in slot slots[i] (distinct slots); writes each argmax token. */
+int chalot_forward_batch(chalot_engine* e, const uint32_t* slots, const uint32_t* toks,
+                         const uint32_t* pos, uint32_t n, uint32_t* out_toks);
+
+/* Logits of row `row` (the i-th token) of the last chalot_forward_batch. */
+int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst, size_t n);
+
 /* Device time of the prefill and decode phases of the last chalot_generate,
  * measured with CUDA events on the engine's stream, and the forward counts. */
 int chalot_last_timing(chalot_engine* e, double* prefill_ms, double* decode_ms,
