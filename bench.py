@@ -507,6 +507,56 @@ def run_paged(args):
     print(json.dumps(bench_paged(reps=args.steps, warmup=args.warmup, layers=args.paged_layers)), flush=True)
 
 
+BT_SEQS, BT_PROMPT, BT_NEW = 64, 256, 256
+
+
+def bench_batch(decode_steps: int = 64, warmup: int = 3, cpu: bool = True) -> dict:
+    """Batched decode of the 1B-class MoE (d2048 L16 H16 V32000 E16 top-2
+    g32, seed 2): 64 sequences with 256-token prompts (numpy seed 2) prefilled
+    together, position by position, then decoded together. Device time of
+    `decode_steps` batched decode forwards (64 tokens each) after the prompt;
+    the end-to-end figure is the wall time of chalot_forward_batch calls with
+    host tokens in and out."""
+    import numpy as np
+    import torch
+
+    import chalot_c1_b200 as cb
+    path = cb.ensure_shape(model_dir(), "1b")
+    eng = cb.Engine.load(path)
+    V = eng.config["vocab_size"]
+    prompts = np.random.default_rng(2).integers(0, V, (BT_SEQS, BT_PROMPT))
+    eng.reserve_batch(BT_SEQS)
+    slots = list(range(BT_SEQS))
+    nxt = None
+    for p in range(BT_PROMPT):
+        nxt = eng.forward_batch(slots, prompts[:, p].tolist(), [p] * BT_SEQS)
+    pos = BT_PROMPT
+    for _ in range(warmup):
+        nxt = eng.forward_batch(slots, nxt, [pos] * BT_SEQS)
+        pos += 1
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(decode_steps):
+        nxt = eng.forward_batch(slots, nxt, [pos] * BT_SEQS)
+        pos += 1
+    dt = time.perf_counter() - t0
+    eng.close()
+    res = {"seqs": BT_SEQS, "prompt": BT_PROMPT, "decode_steps": decode_steps,
+           "ms_per_step": dt / decode_steps * 1000, "tok_s": BT_SEQS * decode_steps / dt}
+    if cpu:
+        # the reference runs one Engine per sequence, one after another: its
+        # rate is one sequence's decode rate on all host threads
+        from oracle import oracle as orc
+        v, cdt = cpu_sample(path, orc.hw_threads(), n_tokens=8, start=BT_PROMPT)
+        res["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": orc.hw_threads(), "kind": "port",
+                               "sample": f"8 decode forwards of one sequence at positions 257-264 ({cdt:.1f} s)"}
+    return res
+
+
+def run_batch(args):
+    print(json.dumps(bench_batch(decode_steps=max(args.steps, 8), warmup=args.warmup)), flush=True)
+
+
 def run_moe(args):
     for path in ("tc", "simt"):
         r = bench_moe_prefill(reps=args.steps, warmup=args.warmup, path=path,
@@ -520,7 +570,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe", "paged"])
+    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe", "paged", "batch"])
     ap.add_argument("--paged-layers", type=int, default=PG_LAYERS,
                     help="--mode paged: layers (one 470 MB page pool each)")
     a = ap.parse_args()
@@ -532,6 +582,9 @@ def main():
         return
     if a.mode == "paged":
         run_paged(a)
+        return
+    if a.mode == "batch":
+        run_batch(a)
         return
     ws, rank, local = dist_setup()
     try:

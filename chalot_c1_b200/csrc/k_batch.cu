@@ -5,7 +5,7 @@
 //   k_b_embed       embedding row * scale, rmsnorm, quantize (engine.rs:201-210)
 //   k_b_norm_quant  rmsnorm + quantize of each token's residual
 //   k_b_gemm_i8     int8 GEMM for B tokens: exact int32 dots (dp4a over shared
-//                   tiles of 32 tokens x 128 rows), then (dot*ws)*xs; stores,
+//                   tiles of 32 tokens x 32 or 128 rows), then (dot*ws)*xs; stores,
 //                   or adds to the residual (matmul.rs:183-298, engine.rs:320-322)
 //   k_b_rope_kv     RoPE on q and k, K/V rows into the sequence's cache slot
 //   k_b_scores      s[b][h][t] = 30*tanh((dot_f32(q, k_t)/sqrt(hd))/30)
@@ -52,23 +52,25 @@ __global__ void __launch_bounds__(kT) k_b_norm_quant(int dim, const float* x, co
   norm_quant_tail(x + (size_t)b * dim, esm, dim, xq + (size_t)b * dim, xs + b, esm + dim, red);
 }
 
-constexpr int kGT = 32, kGR = 128, kGK = 256, kGWS = kGK + 16;
+constexpr int kGT = 32, kGK = 256, kGWS = kGK + 16;
 
 // out[t][r] (=|+=) ((float)dot(W[r], xq[t]) * ws[r]) * xs[t] for t < B, r < R.
-// Thread (warp v, lane l): tokens 4v..4v+3 of the tile, rows l, l+32, l+64, l+96.
-template <bool ADD>
+// Tiles of 32 tokens x 32*RPL rows; thread (warp v, lane l): tokens 4v..4v+3,
+// rows l, l+32, ... (RPL of them).
+template <bool ADD, int RPL>
 __global__ void __launch_bounds__(kT) k_b_gemm_i8(int B, int R, int C, const int8_t* __restrict__ W,
                                                   const float* __restrict__ ws, const int8_t* __restrict__ xq,
                                                   const float* __restrict__ xs, float* out, int ldo) {
+  constexpr int GR = 32 * RPL;
   __shared__ __align__(16) int8_t X[kGT * kGK];
-  __shared__ __align__(16) int8_t Wt[kGR * kGWS];
-  const int r0 = blockIdx.x * kGR, t0 = blockIdx.y * kGT;
+  __shared__ __align__(16) int8_t Wt[GR * kGWS];
+  const int r0 = blockIdx.x * GR, t0 = blockIdx.y * kGT;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  int acc[4][4];
+  int acc[4][RPL];
 #pragma unroll
   for (int s = 0; s < 4; ++s)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[s][i] = 0;
+    for (int i = 0; i < RPL; ++i) acc[s][i] = 0;
   for (int k0 = 0; k0 < C; k0 += kGK) {
     const int kc = min(kGK, C - k0), ch = kc >> 4;
     __syncthreads();
@@ -78,22 +80,22 @@ __global__ void __launch_bounds__(kT) k_b_gemm_i8(int B, int R, int C, const int
           t0 + s < B ? __ldg(reinterpret_cast<const uint4*>(xq + (size_t)(t0 + s) * C + k0 + j * 16))
                      : make_uint4(0, 0, 0, 0);
     }
-    for (int c = tid; c < kGR * ch; c += kT) {
+    for (int c = tid; c < GR * ch; c += kT) {
       const int r = c / ch, j = c - r * ch;
       *reinterpret_cast<uint4*>(Wt + r * kGWS + j * 16) =
           r0 + r < R ? ldg_stream(W + (size_t)(r0 + r) * C + k0 + j * 16) : make_uint4(0, 0, 0, 0);
     }
     __syncthreads();
     for (int q = 0; q < ch; ++q) {
-      uint4 xv[4], wv[4];
+      uint4 xv[4], wv[RPL];
 #pragma unroll
       for (int s = 0; s < 4; ++s) xv[s] = *reinterpret_cast<const uint4*>(X + (warp * 4 + s) * kGK + q * 16);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint4*>(Wt + (lane + 32 * i) * kGWS + q * 16);
+      for (int i = 0; i < RPL; ++i) wv[i] = *reinterpret_cast<const uint4*>(Wt + (lane + 32 * i) * kGWS + q * 16);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < RPL; ++i) {
           int t = acc[s][i];
           t = __dp4a((int)wv[i].x, (int)xv[s].x, t);
           t = __dp4a((int)wv[i].y, (int)xv[s].y, t);
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(kT) k_b_gemm_i8(int B, int R, int C, const int
     if (tok >= B) continue;
     const float xsc = xs[tok];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < RPL; ++i) {
       const int r = r0 + lane + 32 * i;
       if (r >= R) continue;
       const float v = __fmul_rn(__fmul_rn(__int2float_rn(acc[s][i]), ws[r]), xsc);
@@ -303,11 +305,17 @@ void b_norm_quant(const BatchDims& d, int B, const float* x, const float* w, int
 
 void b_gemm_i8(int B, int R, int C, const int8_t* W, const float* ws, const int8_t* xq, const float* xs,
                float* out, int ldo, bool add, cudaStream_t s) {
-  dim3 grid((R + kGR - 1) / kGR, (B + kGT - 1) / kGT);
-  if (add)
-    k_b_gemm_i8<true><<<grid, kT, 0, s>>>(B, R, C, W, ws, xq, xs, out, ldo);
-  else
-    k_b_gemm_i8<false><<<grid, kT, 0, s>>>(B, R, C, W, ws, xq, xs, out, ldo);
+  const int tt = (B + kGT - 1) / kGT;
+  // 128-row tiles while they give two waves of CTAs, else 32-row tiles
+  const bool wide = (long)((R + 127) / 128) * tt >= 296;
+  const dim3 grid(wide ? (R + 127) / 128 : (R + 31) / 32, tt);
+  if (wide) {
+    if (add) k_b_gemm_i8<true, 4><<<grid, kT, 0, s>>>(B, R, C, W, ws, xq, xs, out, ldo);
+    else k_b_gemm_i8<false, 4><<<grid, kT, 0, s>>>(B, R, C, W, ws, xq, xs, out, ldo);
+  } else {
+    if (add) k_b_gemm_i8<true, 1><<<grid, kT, 0, s>>>(B, R, C, W, ws, xq, xs, out, ldo);
+    else k_b_gemm_i8<false, 1><<<grid, kT, 0, s>>>(B, R, C, W, ws, xq, xs, out, ldo);
+  }
 }
 
 void b_rope_kv(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* qkv,

@@ -145,11 +145,12 @@ __global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm
 }
 
 // One tile: slots [p0, p0+cnt) of expert e against 128 weight rows.
-// Thread (warp v, lane l) owns slots 4v..4v+3 and tile rows l, l+32, l+64,
+// Thread (warp v, lane l) owns slots SPW*v..SPW*v+SPW-1 (tiles of 8*SPW slots:
+// 32 for prefill, 8 when an expert gets few slots) and tile rows l, l+32, l+64,
 // l+96. For gate/up, tile rows 0..63 are gate rows r0.. and 64..127 are the
 // up rows of the same hidden units, so a thread holds gate and up of the
 // hidden units r0+l and r0+l+32 for its four slots.
-template <bool GU>
+template <bool GU, int SPW>
 __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts XP, MlWork w) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int mb = blockIdx.y;
@@ -171,6 +172,7 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
   const float** srow = reinterpret_cast<const float**>(wrow + kBN);          // [kBN]
   const int8_t** arow = reinterpret_cast<const int8_t**>(srow + kBN);        // [kBM]
 
+  constexpr int BM = 8 * SPW;  // slots per tile: SPW per warp
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < kBN) {  // weight row of tile row tid, or null past the matrix
     const int hr = GU ? r0 + (tid & 63) : r0 + tid;
@@ -178,21 +180,21 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
     const bool ok = hr < out_rows;
     wrow[tid] = ok ? wmat + (size_t)mrow * (in_dim / 2) : nullptr;
     srow[tid] = ok ? smat + (size_t)mrow * ng : nullptr;
-  } else if (tid < kBN + kBM) {
+  } else if (tid < kBN + BM) {
     const int s = tid - kBN;
     const int p = p0 + s;
     arow[s] = s < cnt ? (GU ? amat + (size_t)(w.perm[p] / d.K) * in_dim : amat + (size_t)p * in_dim)
                       : nullptr;
   }
-  float xsv[4];
+  float xsv[SPW];
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const int sl = warp * 4 + s;
+  for (int s = 0; s < SPW; ++s) {
+    const int sl = warp * SPW + s;
     xsv[s] = sl < cnt ? (GU ? ascale[w.perm[p0 + sl] / d.K] : ascale[p0 + sl]) : 0.0f;
   }
-  float acc[4][4];
+  float acc[SPW][4];
 #pragma unroll
-  for (int s = 0; s < 4; ++s)
+  for (int s = 0; s < SPW; ++s)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[s][i] = 0.0f;
 
@@ -202,7 +204,7 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
     __syncthreads();
     // activations: kBM rows of kc int8
     const int xch = kc >> 4;
-    for (int c = tid; c < kBM * xch; c += kThreads) {
+    for (int c = tid; c < BM * xch; c += kThreads) {
       const int s = c / xch, j = c - s * xch;
       const int8_t* a = arow[s];
       *reinterpret_cast<uint4*>(X + s * kKC + j * 16) =
@@ -228,20 +230,20 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
     }
     __syncthreads();
     for (int g = 0; g < gpc; ++g) {
-      int dots[4][4];
+      int dots[SPW][4];
 #pragma unroll
-      for (int s = 0; s < 4; ++s)
+      for (int s = 0; s < SPW; ++s)
 #pragma unroll
         for (int i = 0; i < 4; ++i) dots[s][i] = 0;
       for (int q = 0; q < gw; q += 4) {
         const int col = g * d.group + q * 4;
-        uint4 xv[4], wv[4];
+        uint4 xv[SPW], wv[4];
 #pragma unroll
-        for (int s = 0; s < 4; ++s) xv[s] = *reinterpret_cast<const uint4*>(X + (warp * 4 + s) * kKC + col);
+        for (int s = 0; s < SPW; ++s) xv[s] = *reinterpret_cast<const uint4*>(X + (warp * SPW + s) * kKC + col);
 #pragma unroll
         for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint4*>(W + (lane + 32 * i) * kWS + col);
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
+        for (int s = 0; s < SPW; ++s)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             int t = dots[s][i];
@@ -256,14 +258,14 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
       for (int i = 0; i < 4; ++i) {
         const float sc = S[(lane + 32 * i) * kSS + g];
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
+        for (int s = 0; s < SPW; ++s)
           acc[s][i] = __fadd_rn(acc[s][i], __fmul_rn(__fmul_rn(i2f_exact(dots[s][i]), sc), xsv[s]));
       }
     }
   }
 #pragma unroll
-  for (int s = 0; s < 4; ++s) {
-    const int sl = warp * 4 + s;
+  for (int s = 0; s < SPW; ++s) {
+    const int sl = warp * SPW + s;
     if (sl >= cnt) continue;
     const size_t p = (size_t)(p0 + sl);
     if (GU) {
@@ -337,7 +339,7 @@ size_t ml_expert_bytes(const MlDims& d) {
 // Workspace regions, each 256-byte aligned; with base == nullptr only the
 // total size is computed.
 size_t ml_layout(const MlDims& d, void* base, MlWork* w) {
-  const size_t N = (size_t)d.T * d.K, nmb = N / kBM + d.E + 1;
+  const size_t N = (size_t)d.T * d.K, nmb = N / 8 + d.E + 1;  // blocks of 8 slots at the smallest
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -389,18 +391,39 @@ static void quantize_h(const MlDims& d, const MlWork& w, cudaStream_t s) {
   k_ml_quant<<<(unsigned)((size_t)d.T * d.K), kThreads, qsm, s>>>(d, w);
 }
 
+// Slots per tile of the tile GEMMs: 8 when the experts get few slots each
+// (batched decode), else 32.
+static int tile_slots(const MlDims& d) { return (size_t)d.T * d.K / d.E < 24 ? 8 : kBM; }
+
+// gate/up tile GEMM, quantize h, down tile GEMM, with tiles of bm slots.
+static void tile_gemms(const MlDims& d, const MlExperts& X, const MlWork& w, int bm, cudaStream_t s) {
+  const size_t N = (size_t)d.T * d.K;
+  const size_t gsm = gemm_smem();
+  const unsigned nmb = (unsigned)std::min(N, N / bm + d.E);
+  const dim3 ggu((d.H + kBN / 2 - 1) / (kBN / 2), nmb), gdn((d.dim + kBN - 1) / kBN, nmb);
+  if (bm == 8) {
+    cudaFuncSetAttribute(k_ml_gemm<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    cudaFuncSetAttribute(k_ml_gemm<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    k_ml_gemm<true, 1><<<ggu, kThreads, gsm, s>>>(d, X, w);
+    quantize_h(d, w, s);
+    k_ml_gemm<false, 1><<<gdn, kThreads, gsm, s>>>(d, X, w);
+  } else {
+    cudaFuncSetAttribute(k_ml_gemm<true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    cudaFuncSetAttribute(k_ml_gemm<false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
+    k_ml_gemm<true, 4><<<ggu, kThreads, gsm, s>>>(d, X, w);
+    quantize_h(d, w, s);
+    k_ml_gemm<false, 4><<<gdn, kThreads, gsm, s>>>(d, X, w);
+  }
+}
+
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
                    const MlExperts& X, const MlWork& w, float* out, cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
-  route_and_dispatch(d, x, rw, rb, w, kBM, s);
-  const size_t gsm = gemm_smem();
-  cudaFuncSetAttribute(k_ml_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
-  cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
-  const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
-  k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, X, w);
-  quantize_h(d, w, s);
-  k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, X, w);
+  const int bm = tile_slots(d);
+  route_and_dispatch(d, x, rw, rb, w, bm, s);
+  tile_gemms(d, X, w, bm, s);
+  (void)N;
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
   return cudaGetLastError();
 }
@@ -464,15 +487,9 @@ cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, co
     if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
     if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
   } else {
-    k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, kBM, 1, nullptr);
-    const size_t gsm = gemm_smem();
-    cudaFuncSetAttribute(k_ml_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
-    cudaFuncSetAttribute(k_ml_gemm<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
-    const unsigned nmb = (unsigned)std::min(N, N / kBM + d.E);
-    const size_t ex = ml_expert_bytes(d);
-    k_ml_gemm<true><<<dim3((d.H + kBN / 2 - 1) / (kBN / 2), nmb), kThreads, gsm, s>>>(d, X, w);
-    quantize_h(d, w, s);
-    k_ml_gemm<false><<<dim3((d.dim + kBN - 1) / kBN, nmb), kThreads, gsm, s>>>(d, X, w);
+    const int bm = tile_slots(d);
+    k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
+    tile_gemms(d, X, w, bm, s);
   }
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, y);
   return cudaGetLastError();
