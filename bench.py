@@ -275,6 +275,8 @@ def run_ours(args, ws, rank, local):
                                             "4096 tokens per rank, experts e on rank e % n_gpus", scaling="weak")
     eng.close()
     if ws == 1:
+        td = bench_tiny()
+        line["tiny_decode"] = td
         mo = bench_moe_prefill(reps=10, warmup=3, cpu_tokens=1024)
         line["moe_layer_prefill"] = {
             "workload": "single MoE layer, 4096 tokens N(0,1) at dim 896, router 896->8, experts int4 g32 "
@@ -296,6 +298,37 @@ def run_ours(args, ws, rank, local):
             "cpu_baseline": {"value": cpu_tok_s, "unit": "tok/s", "cores": orc.hw_threads(), "kind": "port",
                              "sample": cpu_sample_s}}
     print(json.dumps(line), flush=True)
+
+
+def bench_tiny() -> dict:
+    """Config 1: the tiny MoE (d256 L4 E8 top-2 g32, seed 0), a 32-token
+    prompt (numpy seed 0) and 128 greedy tokens. The weights (19 MB) sit in L2,
+    so this is a latency figure: device decode time per token."""
+    import numpy as np
+
+    import chalot_c1_b200 as cb
+    path = cb.ensure_shape(model_dir(), "tiny")
+    eng = cb.Engine.load(path)
+    prompt = np.random.default_rng(0).integers(0, 4096, 32).tolist()
+    for _ in range(3):
+        eng.generate(prompt, 128)
+    dec, n = 0.0, 0
+    for _ in range(5):
+        eng.generate(prompt, 128)
+        t = eng.last_timing()
+        dec += t["decode_ms"]
+        n += t["n_decode"]
+    eng.close()
+    from oracle import oracle as orc
+    o = orc.OracleEngine(path, threads=0)
+    t0 = time.perf_counter()
+    o.generate(prompt, 128)
+    cdt = time.perf_counter() - t0
+    o.close()
+    return {"workload": "tiny MoE d256 L4 E8, 32-token prompt + 128 greedy tokens", "tok_s": n / (dec / 1000),
+            "us_per_token": dec * 1000 / n,
+            "cpu_baseline": {"value": 128 / cdt, "unit": "tok/s (prompt + 128 tokens)", "cores": 1, "kind": "port",
+                             "sample": f"one generate of 32 + 128 tokens ({cdt:.2f} s)"}}
 
 
 def paged_cpu_sample():
