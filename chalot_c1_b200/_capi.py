@@ -51,7 +51,7 @@ class Sampling(C.Structure):
     _fields_ = [("strategy", C.c_int), ("temperature", C.c_float), ("top_k", C.c_uint32),
                 ("top_p", C.c_float), ("min_p", C.c_float), ("repetition_penalty", C.c_float),
                 ("repetition_window", C.c_uint32), ("stop_tokens", C.POINTER(C.c_uint32)),
-                ("n_stop_tokens", C.c_uint32)]
+                ("n_stop_tokens", C.c_uint32), ("seed", C.c_uint64)]
 
 
 class MoeDesc(C.Structure):
@@ -81,6 +81,7 @@ SIGNATURES = {
     "chalot_sample_from_logits": (C.c_int, [P, C.POINTER(Sampling), P, C.c_size_t,
                                             C.POINTER(C.c_uint32)]),
     "chalot_get_logits": (C.c_int, [P, P, C.c_size_t]),
+    "chalot_sample": (C.c_int, [P, C.c_size_t, C.POINTER(Sampling), C.c_float, C.POINTER(C.c_uint32), P]),
     "chalot_batch_reserve": (C.c_int, [P, C.c_uint32]),
     "chalot_forward_batch": (C.c_int, [P, P, P, P, C.c_uint32, P]),
     "chalot_get_batch_logits": (C.c_int, [P, C.c_uint32, P, C.c_size_t]),

@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <array>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -130,6 +131,7 @@ struct chalot_engine {
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
   double last_prefill_ms = 0, last_decode_ms = 0;
   uint32_t last_n_prefill = 0, last_n_decode = 0;
+  uint64_t rng = 0;  // splitmix64 state of the sampling draws
   // batched decode (chalot_batch_reserve / chalot_forward_batch)
   struct Batch {
     int cap = 0;
@@ -571,16 +573,42 @@ __attribute__((visibility("default"))) int chalot_get_logits(chalot_engine* e, f
   return CHALOT_OK;
 }
 
+// Uniform draw in [0, 1) from splitmix64 (24 bits, exact in f32).
+static float next_draw(uint64_t* st) {
+  uint64_t z = (*st += 0x9E3779B97F4A7C15ull);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+static uint64_t seed_of(const chalot_sampling* sp) {
+  if (sp && sp->seed) return sp->seed;
+  return (uint64_t)std::chrono::high_resolution_clock::now().time_since_epoch().count();
+}
+
+// Greedy argmax, or the configured strategy for one draw, of the engine's
+// logits (the penalty already applied); the token lands in st->argmax_key.
+static void launch_pick(chalot_engine* e, const chalot_sampling* sp) {
+  if (!sp || sp->strategy == CHALOT_GREEDY || (sp->strategy == CHALOT_MIN_P && sp->min_p > 1.0f)) {
+    launch_penalty_argmax(e->dims, e->b, e->d_hist, 0, 1.0f, e->stream);  // argmax only
+    return;
+  }
+  CK(launch_sample(e->b.logits, (int)e->cfg.vocab_size, sp->strategy, sp->temperature, (int)sp->top_k,
+                   sp->top_p, sp->min_p, next_draw(&e->rng), &e->b.st->argmax_key, e->stream));
+}
+
 __attribute__((visibility("default"))) int chalot_sample_from_logits(chalot_engine* e,
                                                                      const chalot_sampling* sp,
                                                                      const uint32_t* history,
                                                                      size_t n_history,
                                                                      uint32_t* out_token) {
   if (!e || !out_token) return set_error(CHALOT_ERR_ARG, "null argument");
-  if (sp && sp->strategy != CHALOT_GREEDY)
-    return set_error(CHALOT_ERR_ARG, "only the greedy strategy is implemented");
+  if (sp && (sp->strategy < CHALOT_GREEDY || sp->strategy > CHALOT_MIN_P))
+    return set_error(CHALOT_ERR_ARG, "unknown sampling strategy");
   try {
     CK(cudaSetDevice(e->device));
+    if (!e->rng) e->rng = seed_of(sp);
     const float pen = sp ? sp->repetition_penalty : 1.0f;
     size_t w = 0;
     if (pen > 1.0f && n_history > 0 && history) {  // engine.rs:555-560
@@ -590,6 +618,7 @@ __attribute__((visibility("default"))) int chalot_sample_from_logits(chalot_engi
                          e->stream));
     }
     launch_penalty_argmax(e->dims, e->b, e->d_hist, int(w), w ? pen : 1.0f, e->stream);
+    if (sp && sp->strategy != CHALOT_GREEDY) launch_pick(e, sp);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(e->h_state, e->b.st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
     CK(cudaStreamSynchronize(e->stream));
@@ -606,8 +635,9 @@ __attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, con
                                                            size_t* n_out) {
   if (!e || !n_out || (n_prompt && !prompt) || (max_new && !out))
     return set_error(CHALOT_ERR_ARG, "null argument");
-  if (sp && sp->strategy != CHALOT_GREEDY)
-    return set_error(CHALOT_ERR_ARG, "only the greedy strategy is implemented");
+  if (sp && (sp->strategy < CHALOT_GREEDY || sp->strategy > CHALOT_MIN_P))
+    return set_error(CHALOT_ERR_ARG, "unknown sampling strategy");
+  const bool greedy = !sp || sp->strategy == CHALOT_GREEDY;
   const size_t max_seq = e->cfg.max_seq_len, V = e->cfg.vocab_size;
   *n_out = 0;
   // engine.rs:509: n_prefill = min(len, max(max_seq - max_new, 1))
@@ -630,7 +660,8 @@ __attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, con
     std::vector<uint32_t> hist(prompt, prompt + n_prompt);
     const size_t total = n_prefill + n_decode;
     CK(cudaEventRecord(e->ev[0], e->stream));
-    if (!penalty && !stops) {
+    e->rng = seed_of(sp);
+    if (greedy && !penalty && !stops) {
       for (size_t f = 0; f < total; ++f) {
         e->run_forward(true);
         if (f + 1 == n_prefill) CK(cudaEventRecord(e->ev[1], e->stream));
@@ -646,7 +677,8 @@ __attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, con
         out[cnt++] = (n_prefill == 0 && s == 0) ? 1u : e->h_tokens[n_prefill + s - 1];
       *n_out = cnt;
     } else {
-      // host-driven loop: the penalty needs the history, stop tokens end early
+      // host-driven loop: the penalty needs the history, stop tokens end early,
+      // and the sampling strategies need one draw per token
       if (n_prefill == 0) CK(cudaEventRecord(e->ev[1], e->stream));
       uint32_t next = 1;
       size_t cnt = 0;
@@ -659,6 +691,7 @@ __attribute__((visibility("default"))) int chalot_generate(chalot_engine* e, con
                              cudaMemcpyHostToDevice, e->stream));
         }
         launch_penalty_argmax(e->dims, e->b, e->d_hist, int(w), w ? pen : 1.0f, e->stream);
+        if (!greedy) launch_pick(e, sp);
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(e->h_state, e->b.st, sizeof(StepState), cudaMemcpyDeviceToHost, e->stream));
         CK(cudaStreamSynchronize(e->stream));
@@ -956,6 +989,34 @@ __attribute__((visibility("default"))) int chalot_get_batch_logits(chalot_engine
   } catch (const CudaFail& f) {
     return fail(f);
   }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_sample(const float* logits, size_t vocab,
+                                                         const chalot_sampling* cfg, float r, uint32_t* out_token,
+                                                         void* stream) {
+  if (!logits || !cfg || !out_token) return set_error(CHALOT_ERR_ARG, "sample: null argument");
+  if (vocab == 0 || vocab > (1u << 30)) return set_error(CHALOT_ERR_ARG, "sample: bad vocab size");
+  if (cfg->strategy < CHALOT_GREEDY || cfg->strategy > CHALOT_MIN_P)
+    return set_error(CHALOT_ERR_ARG, "sample: unknown strategy");
+  if (!(r >= 0.0f && r < 1.0f)) return set_error(CHALOT_ERR_ARG, "sample: r must be in [0, 1)");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned long long* d = nullptr;
+  unsigned long long h = 0;
+  cudaError_t rc = cudaMallocAsync(reinterpret_cast<void**>(&d), 8, s);
+  if (rc == cudaSuccess) rc = cudaMemsetAsync(d, 0, 8, s);
+  if (rc == cudaSuccess) {
+    if (cfg->strategy == CHALOT_GREEDY || (cfg->strategy == CHALOT_MIN_P && cfg->min_p > 1.0f))
+      rc = launch_argmax_op(logits, (int)vocab, d, s);
+    else
+      rc = launch_sample(logits, (int)vocab, cfg->strategy, cfg->temperature, (int)cfg->top_k, cfg->top_p,
+                         cfg->min_p, r, d, s);
+  }
+  if (rc == cudaSuccess) rc = cudaMemcpyAsync(&h, d, 8, cudaMemcpyDeviceToHost, s);
+  if (d) cudaFreeAsync(d, s);
+  if (rc == cudaSuccess) rc = cudaStreamSynchronize(s);
+  if (rc != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("sample: ") + cudaGetErrorString(rc));
+  *out_token = uint32_t(h & 0xffffffffull);
   return CHALOT_OK;
 }
 

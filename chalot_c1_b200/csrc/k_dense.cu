@@ -464,6 +464,11 @@ void launch_penalty_argmax(const Dims& d, const DecodeBufs& b, const uint32_t* h
       b.logits, d.vocab, &b.st->argmax_key);
 }
 
+cudaError_t launch_argmax_op(const float* logits, int V, unsigned long long* out, cudaStream_t s) {
+  k_argmax<<<std::min(148, (V + kThreads - 1) / kThreads), kThreads, 0, s>>>(logits, V, out);
+  return cudaGetLastError();
+}
+
 cudaError_t op_matmul_i8(float* out, const int8_t* w, const float* ws, const float* x,
                          size_t out_dim, size_t in_dim, int num_sms, cudaStream_t s) {
   const int vec = (in_dim % 16 == 0) && ((reinterpret_cast<uintptr_t>(w) & 15) == 0);

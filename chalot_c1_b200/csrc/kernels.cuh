@@ -109,6 +109,11 @@ void launch_lmhead(const Dims& d, const int8_t* w, const float* ws, const Decode
 // Records the argmax of the forward and selects the next token/position.
 void launch_advance(const Dims& d, const DecodeBufs& b, cudaStream_t s, bool pdl);
 // Repetition penalty on the logits followed by a fresh argmax into st->argmax_key.
+// One draw of a sampling strategy (k_sample.cu); the token goes to *out.
+cudaError_t launch_sample(const float* logits, int V, int strategy, float temperature, int top_k, float top_p,
+                          float min_p, float r, unsigned long long* out, cudaStream_t s);
+// argmax with ties to the last index into *out (cleared by the caller).
+cudaError_t launch_argmax_op(const float* logits, int V, unsigned long long* out, cudaStream_t s);
 void launch_penalty_argmax(const Dims& d, const DecodeBufs& b, const uint32_t* hist, int n_hist,
                            float penalty, cudaStream_t s);
 

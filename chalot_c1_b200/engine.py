@@ -21,9 +21,9 @@ GREEDY, TOP_K, TOP_P, MIN_P = 0, 1, 2, 3
 
 @dataclass
 class SamplingConfig:
-    """SamplingConfig (src/model/engine.rs:37-62). Only GREEDY is sampled here;
-    the reference's default (TopP, penalty 1.15) is not, so the default below
-    is greedy without a penalty."""
+    """SamplingConfig (src/model/engine.rs:37-62) plus the seed of the draws
+    (0: from the clock, as the reference). The default here is greedy without
+    a penalty (the reference's default is TopP with penalty 1.15)."""
     strategy: int = GREEDY
     temperature: float = 0.7
     top_k: int = 40
@@ -32,12 +32,13 @@ class SamplingConfig:
     repetition_penalty: float = 1.0
     repetition_window: int = 64
     stop_tokens: Sequence[int] = field(default_factory=list)
+    seed: int = 0
 
     def _c(self):
         stops = (C.c_uint32 * max(1, len(self.stop_tokens)))(*self.stop_tokens)
         s = Sampling(self.strategy, self.temperature, self.top_k, self.top_p, self.min_p,
                      self.repetition_penalty, self.repetition_window,
-                     C.cast(stops, C.POINTER(C.c_uint32)), len(self.stop_tokens))
+                     C.cast(stops, C.POINTER(C.c_uint32)), len(self.stop_tokens), self.seed)
         return s, stops
 
 

@@ -85,7 +85,7 @@ typedef struct chalot_opts {
 } chalot_opts;
 
 typedef enum chalot_strategy {
-  CHALOT_GREEDY = 0, /* the only strategy this build samples with */
+  CHALOT_GREEDY = 0,
   CHALOT_TOP_K = 1,
   CHALOT_TOP_P = 2,
   CHALOT_MIN_P = 3
@@ -102,6 +102,10 @@ typedef struct chalot_sampling {
   uint32_t repetition_window;
   const uint32_t* stop_tokens;
   uint32_t n_stop_tokens;
+  /* Seed of the draws of the TOP_K / TOP_P / MIN_P strategies (splitmix64,
+   * one draw per sampled token). 0 seeds from the clock, as the reference's
+   * random_f32 (src/tensor/sampling.rs:15-30) does. */
+  uint64_t seed;
 } chalot_sampling;
 
 /* Engine::load: parse the header, upload the weights to the device, build
@@ -126,6 +130,14 @@ int chalot_generate(chalot_engine* e, const uint32_t* prompt, size_t n_prompt,
 int chalot_sample_from_logits(chalot_engine* e, const chalot_sampling* sampling,
                               const uint32_t* history, size_t n_history,
                               uint32_t* out_token);
+
+/* One token from device logits [V] with the strategy of `cfg` (its penalty,
+ * window and stop tokens are ignored) for the uniform draw r in [0, 1):
+ * sample_argmax / sample_top_k / sample_top_p / sample_min_p
+ * (src/tensor/sampling.rs:34-165). The logits are not modified. Synchronous;
+ * *out_token receives the token. */
+int chalot_sample(const float* logits, size_t vocab, const chalot_sampling* cfg, float r,
+                  uint32_t* out_token, void* stream);
 
 /* Copies the logits of the last forward (state.logits) to host memory. */
 int chalot_get_logits(chalot_engine* e, float* dst, size_t n);

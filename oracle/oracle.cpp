@@ -25,6 +25,7 @@
 //   expert block, T tokens    src/model/engine.rs:334-401 (orc_moe_forward)
 //   paged int8 KV attention   engine.rs:283-309 over memory.rs:69-74 dequantized rows
 //   PagedKVCache              src/model/memory.rs:26-201 (orc_kvc_*)
+//   sampling strategies       src/tensor/sampling.rs:45-165 (orc_sample, given the draw)
 //   Engine::generate          src/model/engine.rs:497-548
 //   sample_from_logits        src/model/engine.rs:551-569
 //   header/config/index       src/model/header.rs:40-133, config.rs:40-69,
@@ -1127,6 +1128,97 @@ ORC_API size_t orc_kvc_active_pages(const orc_kvc* c) {
   size_t t = 0;
   for (auto& m : c->pages) t += m.size();
   return t;
+}
+
+// ---------------------------------------------------------------------------
+// Sampling strategies (src/tensor/sampling.rs:45-165) for a given draw r in
+// [0, 1) instead of the clock-seeded random_f32. The descending sorts are
+// stable with the lower index first among equal values (sort_unstable_by
+// leaves that order unspecified). *margin receives how far r lies from the
+// running-sum boundaries of the chosen token (the normalised units r is
+// compared in): a draw closer than rounding to a boundary may legitimately
+// pick the neighbour in another summation order.
+// strategy: 0 greedy, 1 top-k, 2 top-p, 3 min-p.
+ORC_API long orc_sample(const float* logits_in, size_t n, int strategy, float temperature, size_t top_k,
+                        float top_p, float min_p, float r, float* margin) {
+  std::vector<float> l(logits_in, logits_in + n);
+  *margin = 1.0f;
+  if (strategy == 0) return argmax(l.data(), n);
+  auto desc = [&](std::vector<size_t>& idx) {
+    std::stable_sort(idx.begin(), idx.end(), [&](size_t a, size_t b) { return l[a] > l[b]; });
+  };
+  auto pick = [&](const std::vector<size_t>& idx, const std::vector<float>& probs) -> long {
+    float cum = 0.0f;
+    for (size_t i = 0; i < probs.size(); ++i) {
+      const float before = cum;
+      cum += probs[i];
+      if (r < cum) {
+        *margin = std::min(r - before, cum - r);
+        return long(idx[i]);
+      }
+    }
+    *margin = 0.0f;
+    return long(idx.back());
+  };
+  if (strategy == 1) {  // sample_top_k (sampling.rs:45-78)
+    if (temperature > 0.0f) {
+      const float inv_t = 1.0f / temperature;
+      for (auto& v : l) v *= inv_t;
+    }
+    std::vector<size_t> idx(n);
+    for (size_t i = 0; i < n; ++i) idx[i] = i;
+    desc(idx);
+    idx.resize(std::min(top_k, n));
+    const float mx = l[idx[0]];
+    std::vector<float> probs;
+    for (size_t i : idx) probs.push_back(std::exp(l[i] - mx));
+    float sum = 0.0f;
+    for (float p : probs) sum += p;
+    for (auto& p : probs) p /= sum;
+    return pick(idx, probs);
+  }
+  if (temperature > 0.0f && temperature != 1.0f) {
+    const float inv_t = 1.0f / temperature;
+    for (auto& v : l) v *= inv_t;
+  }
+  softmax(l.data(), n);
+  if (strategy == 2) {  // sample_top_p (sampling.rs:83-124)
+    std::vector<size_t> idx(n);
+    for (size_t i = 0; i < n; ++i) idx[i] = i;
+    desc(idx);
+    float cumulative = 0.0f;
+    size_t cutoff = n;
+    for (size_t rank = 0; rank < n; ++rank) {
+      cumulative += l[idx[rank]];
+      if (cumulative > top_p) {
+        cutoff = rank + 1;
+        break;
+      }
+    }
+    idx.resize(cutoff);
+    std::vector<float> probs;
+    for (size_t i : idx) probs.push_back(l[i]);
+    float sum = 0.0f;
+    for (float p : probs) sum += p;
+    if (sum > 1e-12f)
+      for (auto& p : probs) p /= sum;
+    return pick(idx, probs);
+  }
+  // sample_min_p (sampling.rs:129-165)
+  float max_prob = 0.0f;
+  for (float v : l) max_prob = std::fmax(max_prob, v);
+  const float threshold = max_prob * min_p;
+  std::vector<size_t> idx;
+  for (size_t i = 0; i < n; ++i)
+    if (l[i] >= threshold) idx.push_back(i);
+  if (idx.empty()) return argmax(l.data(), n);
+  std::vector<float> probs;
+  for (size_t i : idx) probs.push_back(l[i]);
+  float sum = 0.0f;
+  for (float p : probs) sum += p;
+  if (sum > 1e-12f)
+    for (auto& p : probs) p /= sum;
+  return pick(idx, probs);
 }
 
 ORC_API int orc_hw_threads(void) { return omp_get_num_procs(); }

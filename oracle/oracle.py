@@ -78,6 +78,9 @@ def lib():
         L.orc_moe_forward.argtypes = [P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t,
                                       C.c_size_t, C.c_size_t, P, P, C.c_int]
         L.orc_expert_rows.argtypes = [P, P, P, C.c_size_t, P, C.c_size_t, C.c_size_t, C.c_size_t, P, C.c_int]
+        L.orc_sample.restype = C.c_long
+        L.orc_sample.argtypes = [P, C.c_size_t, C.c_int, C.c_float, C.c_size_t, C.c_float, C.c_float, C.c_float,
+                                 C.POINTER(C.c_float)]
         L.orc_kvc_create.restype = P
         L.orc_kvc_create.argtypes = [C.c_size_t, C.c_size_t, C.c_size_t]
         L.orc_kvc_free.argtypes = [P]
@@ -233,6 +236,14 @@ def expert_rows(xq, xs, expert, experts, dim, hidden, group, threads=1):
     lib().orc_expert_rows(_p(xq), _p(_f32(xs)), _p(np.ascontiguousarray(expert, np.int32)), n,
                           _p(np.ascontiguousarray(experts, np.uint8)), dim, hidden, group, _p(y), threads)
     return y
+
+
+def sample(logits, strategy, temperature=0.7, top_k=40, top_p=0.9, min_p=0.05, r=0.5):
+    """sampling.rs's strategies for the draw r; returns (token, margin)."""
+    lg = _f32(logits)
+    m = C.c_float()
+    t = lib().orc_sample(_p(lg), lg.size, strategy, temperature, top_k, top_p, min_p, r, C.byref(m))
+    return int(t), float(m.value)
 
 
 class RefPagedKVCache:
