@@ -197,6 +197,22 @@ CHALOT_DEV int dot32_rp(uint4 w, const uint4& x0, const uint4& x1) {
   return acc >> 4;  // every product is 16 * w * x: the division is exact
 }
 
+// One 16-byte shared-memory load as a single vector instruction. Passing
+// *(const uint4*)p straight into a helper that reads the four words one by
+// one lets the compiler emit four 32-bit loads instead, which at a 32-byte
+// lane stride is an 8-way bank conflict.
+CHALOT_DEV uint4 lds16(const void* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)));
+  return v;
+}
+CHALOT_DEV float4 lds16f(const float* p) {
+  const uint4 v = lds16(p);
+  return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+}
+
 // Streaming 16-byte load of a weight (read once: evict-first). A compiler
 // builtin, so it stays ordered with the griddepcontrol barriers.
 CHALOT_DEV uint4 ldg_stream(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }

@@ -487,8 +487,6 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.h = e->dalloc<float>(std::max<size_t>(c.top_k, 1) * H);
     b.amax = e->dalloc<unsigned>(std::max<size_t>(c.top_k, 1));
-    b.xq_h = e->dalloc<int8_t>(std::max<size_t>(c.top_k, 1) * H);
-    b.xs_h = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.logits = e->dalloc<float>(V);
     b.st = e->dalloc<StepState>(1);
     b.prompt = e->dalloc<uint32_t>(c.max_seq_len);

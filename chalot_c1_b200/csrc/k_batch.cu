@@ -89,9 +89,9 @@ __global__ void __launch_bounds__(kT) k_b_gemm_i8(int B, int R, int C, const int
     for (int q = 0; q < ch; ++q) {
       uint4 xv[4], wv[RPL];
 #pragma unroll
-      for (int s = 0; s < 4; ++s) xv[s] = *reinterpret_cast<const uint4*>(X + (warp * 4 + s) * kGK + q * 16);
+      for (int s = 0; s < 4; ++s) xv[s] = lds16(X + (warp * 4 + s) * kGK + q * 16);
 #pragma unroll
-      for (int i = 0; i < RPL; ++i) wv[i] = *reinterpret_cast<const uint4*>(Wt + (lane + 32 * i) * kGWS + q * 16);
+      for (int i = 0; i < RPL; ++i) wv[i] = lds16(Wt + (lane + 32 * i) * kGWS + q * 16);
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll

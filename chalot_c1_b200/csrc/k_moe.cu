@@ -68,9 +68,12 @@ __device__ __forceinline__ void group_products(const RowJob* rows, int nrows, in
         for (int i = 0; i < R; ++i) {
           const bool live = r0 + i < nrows;
           const int xsel = live ? rows[r0 + i].x : 0;
-          const uint4* xv = reinterpret_cast<const uint4*>(xp + (size_t)xsel * in_dim);
+          const int8_t* xv = xp + (size_t)xsel * in_dim;
           int dv = 0;
-          if (c < chunks) dv = dot32_u4(w[i][it], xv[2 * c], xv[2 * c + 1], 0) - 8 * csum[xsel * chunks + c];
+          if (c < chunks) {
+            const uint4 xe = lds16(xv + (size_t)c * 32), xo = lds16(xv + (size_t)c * 32 + 16);
+            dv = dot32_u4(w[i][it], xe, xo, 0) - 8 * csum[xsel * chunks + c];
+          }
           // the chunks of one group sit in consecutive lanes: reduce them exactly
           for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
           if (live && c < chunks && (c & (cpg - 1)) == 0)
@@ -128,223 +131,264 @@ __device__ __forceinline__ void chunk_sums(const int8_t* xp, int n, int* csum) {
 }
 
 // ---------------------------------------------------------------------------
+// Decode expert kernels (one token). Both stream every weight byte once and
+// keep the exact group arithmetic of matmul_int4: per group g an exact int32
+// dot, p_g = ((float)gdot_g * s_g) * xs, and the row result t = t + p_g in
+// group order (matmul.rs:576-577).
 
-constexpr int kGuPairs = 32;  // gate/up row pairs per CTA
-constexpr int kSegs = 4;      // threads per gate/up row (the ordered sum is handed along)
-constexpr int kMaxSegGroups = 16;  // groups per thread: dim / group <= 64
+constexpr int kMaxGroups = 64;  // dim / group (checked at load)
 
-// Group dot of column group g of a repacked int4 row in shared memory with the
-// natural-order x_q in shared memory (cpg 32-column chunks per group).
-__device__ __forceinline__ int group_dot_smem(const uint8_t* wrow, const int8_t* xq, int g, int cpg) {
-  int dv = 0;
-  for (int cc = 0; cc < cpg; ++cc) {
-    const int c = g * cpg + cc;
-    const uint4 wv = *reinterpret_cast<const uint4*>(wrow + (size_t)c * 16);
-    const uint4* xv = reinterpret_cast<const uint4*>(xq + (size_t)c * 32);
-    dv += dot32_rp(wv, xv[0], xv[1]);
-  }
-  return dv;
-}
-
-// Gate rows base..base+31 and the matching up rows of routed expert
-// sel[blockIdx.y] (engine.rs:366-374), then SwiGLU (activations.rs:59-87): h
-// goes to global memory and |h| into the expert's absmax slot. The 64 rows
-// arrive in shared memory by TMA bulk copies (one per row, row stride padded
-// by 16 bytes); 4 threads share a row, each computing the exact products of a
-// quarter of its groups, and the running sum is handed from quarter to
-// quarter so the groups are added in order (matmul.rs:576-577). The last CTA
-// quantizes every expert's finished h once for the down kernel.
-__global__ void __launch_bounds__(kThreads) k_gateup(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
-  extern __shared__ __align__(16) unsigned char smem[];
+// Gate and up rows of routed expert sel[blockIdx.y] (engine.rs:366-374), then
+// SwiGLU (activations.rs:59-87) into h and |h| into the expert's absmax slot.
+// Warp w owns PPW = 4/IT row pairs (gate rows i and up rows H+i); lane l holds
+// the 32-column chunks l, l+32, ... (IT of them) of each of its rows in
+// registers, loaded straight from HBM with streaming loads, and the matching
+// chunks of the quantized input. A chunk is one group when group == 32 (else
+// the group's chunks, on consecutive lanes, are reduced exactly by shuffles).
+// The group products go to shared memory and one lane per row adds them in
+// group order.
+template <int IT>
+__global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
+  constexpr int RW = 8 / IT, PPW = RW / 2, PPC = kWarps * PPW, PS = kMaxGroups + 1;
+  __shared__ float P[kWarps * RW * PS];
+  __shared__ float wmax[kWarps];
   const int slot = layer * 8 + 4;
   CHALOT_TRACE(slot, 0);
-  const int ng = d.dim / d.group, cpg = d.group >> 5, prow = d.dim >> 1, wst = prow + 16;
-  uint8_t* W = smem;                                                 // [64][wst]
-  float* S = reinterpret_cast<float*>(smem + 2 * kGuPairs * wst);    // [64][ng]
-  int8_t* xq = reinterpret_cast<int8_t*>(S + 2 * kGuPairs * ng);     // [dim]
-  __shared__ __align__(8) uint64_t bar;
-  __shared__ float xs_s;
-  __shared__ float tots[2 * kGuPairs];
-  __shared__ const uint8_t* gsrc[2];
-  __shared__ const float* ssrc[2];
-
-  const int H = d.hidden, j = blockIdx.y, base = blockIdx.x * kGuPairs;
-  const int npairs = min(kGuPairs, H - base);
-  if (threadIdx.x == 0) mbar_init(&bar);
-  pdl_wait();  // the routing comes from the O-projection's last CTA
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = d.hidden, chunks = d.dim >> 5, cpg = d.group >> 5, gsh = __ffs(cpg) - 1;
+  const int ng = d.dim / d.group, prow = d.dim >> 1, j = blockIdx.y;
+  const int i0 = blockIdx.x * PPC + warp * PPW;  // first pair of this warp
+  pdl_wait();  // the routing and the quantized FFN input come from the O-projection's last CTA
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  if (threadIdx.x == 0) {
-    const ExpertPtrs X = expert_ptrs(L, d.n_experts, __ldcg(b.sel + j));
-    gsrc[0] = X.gu + (size_t)base * prow;        // gate rows
-    gsrc[1] = X.gu + (size_t)(H + base) * prow;  // up rows
-    ssrc[0] = X.gu_s + (size_t)base * ng;
-    ssrc[1] = X.gu_s + (size_t)(H + base) * ng;
-    // rows and scales: npairs == 32 (hidden % 32 == 0), the scale blocks are
-    // 32*ng floats (a multiple of 16 bytes) at 16-byte aligned offsets
-    mbar_expect_tx(&bar, (uint32_t)(2 * npairs * prow + 2 * npairs * ng * 4));
+  const int e = __ldcg(b.sel + j);
+  const float xs = __ldcg(b.xs_ffn);
+  uint4 xa[IT], xb[IT];
+#pragma unroll
+  for (int it = 0; it < IT; ++it) {
+    const int c = lane + 32 * it;
+    const uint4* xv = reinterpret_cast<const uint4*>(b.xq_ffn) + 2 * c;
+    xa[it] = c < chunks ? __ldcg(xv) : make_uint4(0, 0, 0, 0);
+    xb[it] = c < chunks ? __ldcg(xv + 1) : make_uint4(0, 0, 0, 0);
   }
-  __syncthreads();
-  if (threadIdx.x < 2 * kGuPairs) {  // one bulk copy per row
-    const int half = threadIdx.x / kGuPairs, i = threadIdx.x % kGuPairs;
-    if (i < npairs) tma_load(W + threadIdx.x * wst, gsrc[half] + (size_t)i * prow, prow, &bar);
-  } else if (threadIdx.x < 2 * kGuPairs + 2) {  // the two scale blocks
-    const int half = threadIdx.x - 2 * kGuPairs;
-    tma_load(S + half * kGuPairs * ng, ssrc[half], (uint32_t)(npairs * ng * 4), &bar);
+  const ExpertPtrs X = expert_ptrs(L, d.n_experts, e);
+  uint4 w[RW][IT];
+  float s[RW][IT];
+#pragma unroll
+  for (int r = 0; r < RW; ++r) {
+    const int pair = i0 + (r % PPW);
+    const size_t row = (size_t)(r < PPW ? 0 : H) + pair;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int c = lane + 32 * it;
+      const bool ok = pair < H && c < chunks;
+      w[r][it] = ok ? ldg_stream(X.gu + row * prow + (size_t)c * 16) : make_uint4(0, 0, 0, 0);
+      s[r][it] = (ok && (c & (cpg - 1)) == 0) ? __ldcs(X.gu_s + row * ng + (c >> gsh)) : 0.0f;
+    }
   }
-  copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_ffn), d.dim >> 4, true);
-  if (threadIdx.x == 0) xs_s = __ldcg(b.xs_ffn);
-  __syncthreads();
   CHALOT_TRACE(slot, 3);
-  if (!mbar_wait(&bar, 0, b.err)) return;
-  CHALOT_TRACE(layer * 8 + 7, 1);
-  // row r = t/4, quarter q = t%4 over groups [q*ng/4, (q+1)*ng/4)
-  const int r = threadIdx.x >> 2, q = threadIdx.x & 3;
-  const int g0 = q * ng / kSegs, g1 = (q + 1) * ng / kSegs;
-  const bool live = (r % kGuPairs) < npairs;
-  const float xs = xs_s;
-  float p[kMaxSegGroups];
 #pragma unroll
-  for (int i = 0; i < kMaxSegGroups; ++i) {
-    const int g = g0 + i;
-    p[i] = 0.0f;
-    if (live && g < g1)
-      p[i] = __fmul_rn(__fmul_rn((float)group_dot_smem(W + r * wst, xq, g, cpg), S[r * ng + g]), xs);
+  for (int r = 0; r < RW; ++r)
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int c = lane + 32 * it;
+      int dv = dot32_rp(w[r][it], xa[it], xb[it]);
+      for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+      if (c < chunks && (c & (cpg - 1)) == 0)
+        P[(warp * RW + r) * PS + (c >> gsh)] = __fmul_rn(__fmul_rn((float)dv, s[r][it]), xs);
+    }
+  __syncwarp();
+  float tot = 0.0f;
+  if (lane < RW) {  // row `lane` of this warp: t = t + p_g in group order
+    const float* p = P + (warp * RW + lane) * PS;
+    int g = 0;
+    for (; g + 8 <= ng; g += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = p[g + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) tot = __fadd_rn(tot, v[u]);
+    }
+    for (; g < ng; ++g) tot = __fadd_rn(tot, p[g]);
   }
-  float acc = 0.0f;
-  const int lane = threadIdx.x & 31, lead = lane & ~3;
-#pragma unroll
-  for (int st = 0; st < kSegs; ++st) {
-    if (q == st)
-#pragma unroll
-      for (int i = 0; i < kMaxSegGroups; ++i)
-        if (g0 + i < g1) acc = __fadd_rn(acc, p[i]);
-    acc = __shfl_sync(0xffffffffu, acc, lead + st);
-  }
-  if (q == 0) tots[r] = acc;
-  __syncthreads();
   CHALOT_TRACE(slot, 4);
+  const float up = __shfl_sync(0xffffffffu, tot, (lane + PPW) & 31);  // lane p: up row of pair p
   float m = 0.0f;
-  if (threadIdx.x < npairs) {
-    const int rr = base + threadIdx.x;
-    const float hv = swiglu_elem(tots[threadIdx.x], tots[kGuPairs + threadIdx.x], rr, H);
-    b.h[(size_t)j * H + rr] = hv;
+  if (lane < PPW && i0 + lane < H) {
+    const int pair = i0 + lane;
+    const float hv = swiglu_elem(tot, up, pair, H);
+    b.h[(size_t)j * H + pair] = hv;
     m = fabsf(hv);
   }
-  m = warp_max(m);  // npairs <= 32: only warp 0 holds values
-  if (threadIdx.x == 0) atomicMax(&b.amax[j], __float_as_uint(m));
-  const bool tail = last_cta(b.counters + 3);
-  CHALOT_TRACE(slot, 5);
-  if (!tail) return;
-  const int h4 = H >> 2;
-  for (int jj = 0; jj < d.top_k; ++jj) {
-    float scale, inv;
-    quant_scale(__uint_as_float(__ldcg(b.amax + jj)), &scale, &inv);
-    if (threadIdx.x == 0) b.xs_h[jj] = scale;
-    quant_store_words(reinterpret_cast<uint32_t*>(b.xq_h) + (size_t)jj * h4,
-                      reinterpret_cast<const float4*>(b.h) + (size_t)jj * h4, h4, inv, H);
+  m = warp_max(m);
+  if (lane == 0) wmax[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float mm = wmax[0];
+#pragma unroll
+    for (int i = 1; i < kWarps; ++i) mm = fmaxf(mm, wmax[i]);
+    atomicMax(&b.amax[j], __float_as_uint(mm));  // one update per CTA
   }
-  CHALOT_TRACE(slot, 6);
+  CHALOT_TRACE(slot, 5);
 }
 
-// Output rows r0..r0+rpc-1 for every routed expert (one row per warp). The
-// routing is two launches old, so the rows are requested by TMA bulk copies
-// (and the scales and the next norm's weights staged) before waiting for the
-// gate/up kernel; then each warp forms the exact group products against the
-// quantized h and one thread per row adds them in group order; x[r] +=
-// sum_j w_j * y_j[r] in selection order (engine.rs:380-401). The last CTA
+// Output rows r0..r0+rpc-1 for every routed expert, one row per warp
+// (engine.rs:380-401). The routing is two launches old, so before waiting for
+// the gate/up kernel the CTA requests its rows and their scales (one bulk
+// copy per expert: the rpc rows are contiguous), the x values it will update
+// and the next norm's weights. After the wait it quantizes h of every routed
+// expert into shared memory itself (quantize_f32_to_i8 with the absmax the
+// gate/up CTAs left), in one pass over L2; lane l of a warp then dots the
+// chunks l, l+32, ... (IT of them) of its row, lane 0 adds the group products
+// in order, and x[r] += sum_j w_j * y_j[r] in selection order. The last CTA
 // computes the next layer's quantized attention input from the finished x.
-__global__ void __launch_bounds__(kThreads) k_down(Dims d, LayerPtrs L, int layer,
+constexpr int kHq = 10;  // float4 of h per thread and pass
+template <int IT>
+__global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int layer,
                                                    const float* next_norm, DecodeBufs b, int dense,
                                                    int rpc) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int slot = layer * 8 + 5;
   CHALOT_TRACE(slot, 0);
-  const int H = d.hidden, K = d.top_k, ng = H / d.group, ps = ng + 1, cpg = d.group >> 5;
-  const int prow = H >> 1, wst = prow + 16;
+  const int H = d.hidden, K = d.top_k, ng = H / d.group, cpg = d.group >> 5, gsh = __ffs(cpg) - 1;
+  const int prow = H >> 1, chunks = H >> 5;
   const int nrow = K * rpc;  // <= kWarps
-  uint8_t* W = smem;                                          // [nrow][wst]
-  float* S = reinterpret_cast<float*>(W + kWarps * wst);      // [nrow][ng]
+  uint8_t* W = smem;                                          // [nrow][prow]
+  float* S = reinterpret_cast<float*>(W + kWarps * prow);     // [nrow][ng]
   int8_t* xq = reinterpret_cast<int8_t*>(S + kWarps * ng);    // [K][H]
-  float* P = reinterpret_cast<float*>(xq + (size_t)K * H);    // [nrow][ng+1]
-  float* wn = P + kWarps * ps;                                // [dim] next norm weights
-  float* xb = wn + d.dim;                                     // [dim] tail scratch
+  float* P = reinterpret_cast<float*>(xq + (size_t)K * H);    // [nrow][ng] (ng % 4 == 0)
+  float* wn = P + kWarps * ng;                                // [dim] next norm weights
+  float* xbuf = wn + d.dim;                                   // [dim] tail scratch
   __shared__ __align__(8) uint64_t bar;
-  __shared__ const uint8_t* rsrc[kWarps];
-  __shared__ const float* ssrc[kWarps];
-  __shared__ float xs_j[8];
+  __shared__ float xs_j[8], inv_j[8];
   __shared__ float selw_s[8];
   __shared__ float y[kWarps];
   __shared__ float red[40];
+  __shared__ int ok_s;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = blockIdx.x * rpc;
   const int nr = min(rpc, d.dim - r0);
   if (threadIdx.x == 0) {
     mbar_init(&bar);
-    // rows, and per expert one block of rpc scale rows (rpc*ng floats at a
-    // 16-byte aligned offset: dim % rpc == 0, rpc*ng*4 % 16 == 0)
-    mbar_expect_tx(&bar, (uint32_t)(nrow * prow + K * rpc * ng * 4));
+    // per expert rpc rows and rpc scale rows, each block contiguous and at a
+    // 16-byte aligned offset (prow % 16 == 0, ng % 4 == 0, dim % rpc == 0)
+    mbar_expect_tx(&bar, (uint32_t)(K * rpc * (prow + ng * 4)));
   }
-  if (threadIdx.x < nrow) {
-    const int jx = threadIdx.x / rpc, i = threadIdx.x % rpc;
-    const ExpertPtrs E = expert_ptrs(L, d.n_experts, __ldcg(b.sel + jx));
-    const int r = r0 + i;  // dim % rpc == 0: every CTA has rpc whole rows
-    rsrc[threadIdx.x] = E.dn + (size_t)r * prow;
-    ssrc[threadIdx.x] = E.dn_s + (size_t)r * ng;
-  }
-  if (threadIdx.x < K) selw_s[threadIdx.x] = __ldcg(b.selw + threadIdx.x);
   __syncthreads();
-  if (threadIdx.x < nrow) {
-    tma_load(W + threadIdx.x * wst, rsrc[threadIdx.x], prow, &bar);
-    if (threadIdx.x % rpc == 0)  // first row of each expert's block: its rpc scale rows
-      tma_load(S + threadIdx.x * ng, ssrc[threadIdx.x], (uint32_t)(rpc * ng * 4), &bar);
+  if (threadIdx.x < K) {
+    const int jx = threadIdx.x;
+    const ExpertPtrs E = expert_ptrs(L, d.n_experts, __ldcg(b.sel + jx));
+    const uint64_t pol = l2_evict_first();
+    tma_load_hint(W + (size_t)jx * rpc * prow, E.dn + (size_t)r0 * prow, (uint32_t)(rpc * prow), &bar, pol);
+    tma_load_hint(S + (size_t)jx * rpc * ng, E.dn_s + (size_t)r0 * ng, (uint32_t)(rpc * ng * 4), &bar, pol);
+    selw_s[jx] = __ldcg(b.selw + jx);
   }
+  // x[r] was last written by the O-projection, two launches back
+  const float xold = threadIdx.x < nr ? __ldcg(b.x + r0 + threadIdx.x) : 0.0f;
   load_f32(wn, next_norm, d.dim);
   CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  // the quantized h of every routed expert (the gate/up kernel's last CTA)
-  copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_h), (K * H) >> 4, true);
-  if (threadIdx.x < K) xs_j[threadIdx.x] = __ldcg(b.xs_h + threadIdx.x);
+  // quantize_f32_to_i8 of h_j (quantization.rs:56-104). hidden % 8 == 0, so
+  // every element takes the vector rounding (no scalar tail).
+  if (threadIdx.x < K) {
+    float sc, inv;
+    quant_scale(__uint_as_float(__ldcg(b.amax + threadIdx.x)), &sc, &inv);
+    xs_j[threadIdx.x] = sc;
+    inv_j[threadIdx.x] = inv;
+  }
+  const int n4 = (K * H) >> 2, h4 = H >> 2;
+  const float4* hv = reinterpret_cast<const float4*>(b.h);
+  uint32_t* xw = reinterpret_cast<uint32_t*>(xq);
+  for (int base = 0; base < n4; base += kHq * kThreads) {
+    float4 v[kHq];
+#pragma unroll
+    for (int u = 0; u < kHq; ++u) {
+      const int i = base + u * kThreads + threadIdx.x;
+      if (i < n4) v[u] = __ldcg(hv + i);
+    }
+    if (base == 0) __syncthreads();  // the scales
+#pragma unroll
+    for (int u = 0; u < kHq; ++u) {
+      const int i = base + u * kThreads + threadIdx.x;
+      if (i < n4) {
+        int jx = 0;
+        while (jx + 1 < K && i >= (jx + 1) * h4) ++jx;
+        const float inv = inv_j[jx];
+        const uint32_t q0 = (uint8_t)quant_elem(v[u].x, inv), q1 = (uint8_t)quant_elem(v[u].y, inv);
+        const uint32_t q2 = (uint8_t)quant_elem(v[u].z, inv), q3 = (uint8_t)quant_elem(v[u].w, inv);
+        xw[i] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+      }
+    }
+  }
+  if (threadIdx.x == 0) ok_s = mbar_wait(&bar, 0, b.err) ? 1 : 0;
   __syncthreads();
   CHALOT_TRACE(slot, 3);
-  if (!mbar_wait(&bar, 0, b.err)) return;
-#ifdef CHALOT_PHASE_TRACE
-  long long c0_ = clock64();
-#endif
+  if (!ok_s) return;
   if (warp < nrow) {
     const int jx = warp / rpc;
+    const uint8_t* wrow = W + (size_t)warp * prow;
     const int8_t* xj = xq + (size_t)jx * H;
-    const uint8_t* wrow = W + warp * wst;
+    const float* srow = S + (size_t)warp * ng;
     const float xs = xs_j[jx];
-    for (int g = lane; g < ng; g += 32)
-      P[warp * ps + g] = __fmul_rn(__fmul_rn((float)group_dot_smem(wrow, xj, g, cpg), S[warp * ng + g]), xs);
+    uint4 wv[IT];
+    float sc[IT];
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int cc = min(lane + 32 * it, chunks - 1);
+      wv[it] = lds16(wrow + (size_t)cc * 16);
+      sc[it] = srow[cc >> gsh];
+    }
+    float* prow_p = P + (size_t)warp * ng;
+#pragma unroll
+    for (int it = 0; it < IT; ++it) {
+      const int c = lane + 32 * it, cc = min(c, chunks - 1);
+      const uint4 x0 = lds16(xj + (size_t)cc * 32), x1 = lds16(xj + (size_t)cc * 32 + 16);
+      int dv = dot32_rp(wv[it], x0, x1);
+      for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+      if (c < chunks && (c & (cpg - 1)) == 0) prow_p[c >> gsh] = __fmul_rn(__fmul_rn((float)dv, sc[it]), xs);
+    }
+    __syncwarp();
+    if (lane == 0) {  // t = t + p_g in group order, four groups per load
+      float t = 0.0f;
+      int g4 = 0;
+      for (; g4 + 4 <= (ng >> 2); g4 += 4) {
+        float4 a[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) a[u] = lds16f(prow_p + 4 * (g4 + u));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          t = __fadd_rn(t, a[u].x);
+          t = __fadd_rn(t, a[u].y);
+          t = __fadd_rn(t, a[u].z);
+          t = __fadd_rn(t, a[u].w);
+        }
+      }
+      for (; g4 < (ng >> 2); ++g4) {
+        const float4 a = lds16f(prow_p + 4 * g4);
+        t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(t, a.x), a.y), a.z), a.w);
+      }
+      y[warp] = t;
+    }
   }
   __syncthreads();
-  if (threadIdx.x < nrow) y[threadIdx.x] = ordered_sum(P + threadIdx.x * ps, ng);
-  __syncthreads();
   CHALOT_TRACE(slot, 4);
-#ifdef CHALOT_PHASE_TRACE
-  if (threadIdx.x == 0 && blockIdx.x == 0)  // SM cycles of the compute, next to its ns (phases 3..4)
-    g_phase_trace[((size_t)(layer * 8 + 7) * kTraceCtas + 1000) * kTracePhases] = clock64() - c0_;
-#endif
   if (threadIdx.x < nr) {
-    const int r = r0 + threadIdx.x;
     float add;
     if (dense) {
       add = y[threadIdx.x];  // engine.rs:436-440
     } else {
       add = 0.0f;  // expert_out = sum_k w_k * y_k in selection order (engine.rs:390-396)
-      for (int j = 0; j < K; ++j) add = __fadd_rn(add, __fmul_rn(selw_s[j], y[j * rpc + threadIdx.x]));
+      for (int jx = 0; jx < K; ++jx) add = __fadd_rn(add, __fmul_rn(selw_s[jx], y[jx * rpc + threadIdx.x]));
     }
-    b.x[r] = __fadd_rn(__ldcg(b.x + r), add);
+    b.x[r0 + threadIdx.x] = __fadd_rn(xold, add);
   }
   const bool tail = last_cta(b.counters + 2);
   CHALOT_TRACE(slot, 5);
   if (!tail) return;
-  norm_quant_tail(b.x, wn, d.dim, b.xq_attn, b.xs_attn, xb, red);
+  norm_quant_tail(b.x, wn, d.dim, b.xq_attn, b.xs_attn, xbuf, red);
   CHALOT_TRACE(slot, 6);
 }
 
@@ -442,32 +486,48 @@ __global__ void __launch_bounds__(kThreads) k_router_op(int32_t* idx, float* w,
 
 }  // namespace
 
-static size_t gateup_smem(const Dims& d) {
-  const size_t ng = d.dim / d.group, wst = d.dim / 2 + 16;
-  return 2 * kGuPairs * wst + 2 * kGuPairs * ng * 4 + d.dim;
-}
 static size_t down_smem(const Dims& d) {
-  const size_t H = d.hidden, K = d.top_k, ng = H / d.group, wst = H / 2 + 16;
-  return kWarps * wst + kWarps * ng * 4 + K * H + kWarps * (ng + 1) * 4 + (size_t)d.dim * 8;
+  const size_t H = d.hidden, K = d.top_k, ng = H / d.group, prow = H / 2;
+  return kWarps * prow + kWarps * ng * 4 + K * H + kWarps * ng * 4 + (size_t)d.dim * 8;
 }
 
 void launch_gateup(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
                    bool pdl) {
-  const size_t smem = gateup_smem(d);
-  if (smem > 48 * 1024) cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  dim3 grid((d.hidden + kGuPairs - 1) / kGuPairs, d.top_k);
-  launch_k(k_gateup, grid, dim3(kThreads), smem, s, pdl, d, L, layer, b);
+  const int lc = (d.dim / 32 + 31) / 32;  // chunks per lane and row: dim <= 4096 gives 1..4
+  const int it = lc <= 1 ? 1 : lc <= 2 ? 2 : 4;
+  const int ppc = kWarps * (8 / it) / 2;
+  dim3 grid((d.hidden + ppc - 1) / ppc, d.top_k);
+  if (it == 1)
+    launch_k(k_gateup<1>, grid, dim3(kThreads), 0, s, pdl, d, L, layer, b);
+  else if (it == 2)
+    launch_k(k_gateup<2>, grid, dim3(kThreads), 0, s, pdl, d, L, layer, b);
+  else
+    launch_k(k_gateup<4>, grid, dim3(kThreads), 0, s, pdl, d, L, layer, b);
+}
+
+template <int IT>
+static void launch_down_it(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
+                           const DecodeBufs& b, cudaStream_t s, bool pdl, int grid, int dense, int rpc) {
+  const size_t smem = down_smem(d);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(k_down<IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_k(k_down<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc);
 }
 
 void launch_down(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
                  const DecodeBufs& b, cudaStream_t s, bool pdl) {
   const int rpc = std::max(1, kWarps / d.top_k);  // rows per CTA: one row per warp over all experts
-  const size_t smem = down_smem(d);
   const int grid = (d.dim + rpc - 1) / rpc;
   const int dense = d.n_experts < 2 ? 1 : 0;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_k(k_down, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc);
+  switch ((d.hidden / 32 + 31) / 32) {  // hidden <= 8192: 1..8 chunks per lane
+    case 1: launch_down_it<1>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+    case 2: launch_down_it<2>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+    case 3: launch_down_it<3>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+    case 4: launch_down_it<4>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+    case 5: launch_down_it<5>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+    case 6: launch_down_it<6>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+    default: launch_down_it<8>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
+  }
 }
 
 cudaError_t repack_int4(uint8_t* p, size_t bytes, cudaStream_t s) {

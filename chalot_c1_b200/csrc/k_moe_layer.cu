@@ -239,9 +239,9 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
         const int col = g * d.group + q * 4;
         uint4 xv[SPW], wv[4];
 #pragma unroll
-        for (int s = 0; s < SPW; ++s) xv[s] = *reinterpret_cast<const uint4*>(X + (warp * SPW + s) * kKC + col);
+        for (int s = 0; s < SPW; ++s) xv[s] = lds16(X + (warp * SPW + s) * kKC + col);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wv[i] = *reinterpret_cast<const uint4*>(W + (lane + 32 * i) * kWS + col);
+        for (int i = 0; i < 4; ++i) wv[i] = lds16(W + (lane + 32 * i) * kWS + col);
 #pragma unroll
         for (int s = 0; s < SPW; ++s)
 #pragma unroll

@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
 #pragma unroll
       for (int c0 = 0; c0 < HD / 16; ++c0) {
         const int c = (c0 + t) & (HD / 16 - 1);  // rotated so neighbouring rows hit different banks
-        const uint4 w = kr[c], a = q1w[c], b2 = q2w[c];
+        const uint4 w = lds16(kr + c), a = lds16(q1w + c), b2 = lds16(q2w + c);
         i1 = __dp4a((int)w.x, (int)a.x, i1);
         i1 = __dp4a((int)w.y, (int)a.y, i1);
         i1 = __dp4a((int)w.z, (int)a.z, i1);

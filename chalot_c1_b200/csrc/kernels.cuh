@@ -70,8 +70,6 @@ struct DecodeBufs {
   float* selw;       // [top_k] their weights
   float* h;          // [top_k][hidden] SwiGLU output
   unsigned* amax;    // [top_k] absmax bits of h
-  int8_t* xq_h;      // [top_k][hidden] quantized h (down-projection input)
-  float* xs_h;       // [top_k] its scales
   float* logits;     // [vocab]
   StepState* st;
   const uint32_t* prompt;  // [max_seq] prompt of the running generate call

@@ -35,6 +35,24 @@ CHALOT_DEV void tma_load(void* dst, const void* src, uint32_t bytes, uint64_t* b
       : "memory");
 }
 
+// L2 policy for data read once per step (weights, KV pages): evict first, so
+// the streamed bytes do not push the step's small working set (activations,
+// routing, tables) and the kernels' code out of L2.
+CHALOT_DEV uint64_t l2_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// tma_load with an L2 cache policy (l2_evict_first()).
+CHALOT_DEV void tma_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+      "[%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 // Waits for phase `parity` of `bar` to complete. Gives up after a bounded
 // number of polls (each poll suspends the thread for a hardware-defined
 // interval), records the failure in *err and returns false.

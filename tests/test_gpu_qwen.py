@@ -28,3 +28,22 @@ def test_qwen_greedy_identical(chalot, oracle_lib, qwen_model):
     finally:
         e.close()
         o.close()
+
+
+def test_1b_shape_greedy_identical(chalot, oracle_lib, model_dir):
+    """The 1B-class shape (d2048, 16 layers, 16 experts top-2, hidden 5632):
+    two 32-column chunks per lane in the gate/up kernel and six in the down
+    kernel. Greedy tokens identical to the oracle's, logits within 1e-3."""
+    path = chalot.ensure_shape(model_dir, "1b")
+    prompt = np.random.default_rng(3).integers(0, 32000, 12).tolist()
+    e = chalot.Engine.load(path)
+    o = oracle_lib.OracleEngine(path, threads=oracle_lib.hw_threads())
+    try:
+        g = e.generate(prompt, 8)
+        c = o.generate(prompt, 8)
+        assert g == c
+        a, b = e.logits(), o.logits()
+        assert float(np.max(np.abs(a - b)) / np.max(np.abs(b))) <= 1e-3
+    finally:
+        e.close()
+        o.close()
