@@ -127,12 +127,20 @@ __device__ __forceinline__ void norm_quant_tail(const float* x, const float* wsm
   if (threadIdx.x < 8) {  // lane j accumulates x[8c+j]^2 over c in order
     float s = 0.0f;
     int c = 0;
-    for (; c + 8 <= chunks; c += 8) {
-      float v[8];
+    if (chunks >= 8) {  // the next 8 values load while the current 8 are added
+      float cur[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = xb[(c + u) * 8 + threadIdx.x];
+      for (int u = 0; u < 8; ++u) cur[u] = xb[u * 8 + threadIdx.x];
+      for (; c + 8 <= chunks; c += 8) {
+        float nxt[8];
+        const bool more = c + 16 <= chunks;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) s = __fadd_rn(s, __fmul_rn(v[u], v[u]));
+        for (int u = 0; u < 8; ++u) nxt[u] = more ? xb[(c + 8 + u) * 8 + threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s = __fadd_rn(s, __fmul_rn(cur[u], cur[u]));
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+      }
     }
     for (; c < chunks; ++c) {
       const float v = xb[c * 8 + threadIdx.x];

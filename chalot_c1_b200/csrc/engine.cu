@@ -477,8 +477,6 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.rope_sin = rs;
     b.xq_attn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
     b.xs_attn = e->dalloc<float>(1);
-    b.xq_o = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
-    b.xs_o = e->dalloc<float>(1);
     b.xq_ffn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
     b.xs_ffn = e->dalloc<float>(1);
     b.counters = e->dalloc<unsigned>(8);
@@ -487,6 +485,8 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.h = e->dalloc<float>(std::max<size_t>(c.top_k, 1) * H);
     b.amax = e->dalloc<unsigned>(std::max<size_t>(c.top_k, 1));
+    b.xq_h = e->dalloc<int8_t>(std::max<size_t>(c.top_k, 1) * H);
+    b.xs_h = e->dalloc<float>(std::max<size_t>(c.top_k, 1));
     b.logits = e->dalloc<float>(V);
     b.st = e->dalloc<StepState>(1);
     b.prompt = e->dalloc<uint32_t>(c.max_seq_len);
@@ -773,8 +773,7 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
       DecodeBufs bl = b;
       bl.sel = sel + l * K;
       bl.selw = selw + l * K;
-      CK(cudaMemsetAsync(bl.amax, 0, sizeof(unsigned) * K, e->stream));
-      launch_gateup(d, e->layers[l], l, bl, e->stream, false);
+      launch_gateup(d, e->layers[l], l, bl, e->stream, l > 0);
       launch_down(d, e->layers[l], l, e->layers[l].rms_attn, bl, e->stream, true);
     }
     CK(cudaStreamEndCapture(e->stream, &g));

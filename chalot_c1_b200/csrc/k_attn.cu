@@ -12,8 +12,10 @@
 //                  (engine.rs:302-308). The add chain of a column is serial by
 //                  definition, so each CTA owns 8 columns of one head: its 256
 //                  threads stage V[0..pos][8 columns] in shared memory with
-//                  wide loads (spreading the KV read over heads*hd/8 CTAs) and
-//                  8 threads then run the chains out of shared memory.
+//                  wide loads (spreading the KV read over heads*hd/8 CTAs),
+//                  transposed so each column is contiguous, and 8 threads then
+//                  run the chains out of shared memory, loading the next 16
+//                  products while adding the current ones.
 // The cache layout is the reference's: [layer][max_seq][dim], head h at
 // columns h*hd .. h*hd+hd-1.
 #include <cuda_runtime.h>
@@ -86,8 +88,11 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer
 constexpr int kPvThreads = 256;
 constexpr int kPvCols = 8;     // output columns per CTA: V loads spread over heads*hd/8 CTAs
 constexpr int kPvTile = 1024;  // V rows staged in shared memory at a time
+constexpr int kPvLd = kPvTile + 4;  // row stride of the staged columns (16-byte aligned, bank spread)
 
-__device__ __forceinline__ void stage_v(float* vt, const float* vbase, int dim, int t0, int rows,
+// Stages V[t0 .. t0+rows)[8 columns] transposed into vt[col][t - t0 + off]:
+// each column contiguous, so a chain thread reads its column four t at a time.
+__device__ __forceinline__ void stage_v(float* vt, const float* vbase, int dim, int t0, int rows, int off,
                                         bool coherent) {
   constexpr int U = 8;
   const int n = rows * (kPvCols / 4);
@@ -105,7 +110,14 @@ __device__ __forceinline__ void stage_v(float* vt, const float* vbase, int dim, 
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int i = base + u * kPvThreads + (int)threadIdx.x;
-      if (i < n) reinterpret_cast<float4*>(vt)[i] = v[u];
+      if (i < n) {
+        const int r = i / (kPvCols / 4), q = i % (kPvCols / 4);
+        float* d = vt + (q * 4) * kPvLd + off + r;
+        d[0] = v[u].x;
+        d[kPvLd] = v[u].y;
+        d[2 * kPvLd] = v[u].z;
+        d[3 * kPvLd] = v[u].w;
+      }
     }
   }
 }
@@ -115,19 +127,19 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   const int slot = layer * 8 + 2;
   CHALOT_TRACE(slot, 0);
   float* p = sm;                            // [max_seq] probabilities
-  float* vt = sm + ((d.max_seq + 3) & ~3);  // [kPvTile][kPvCols] staged V (16-B aligned)
+  float* vt = sm + ((d.max_seq + 3) & ~3);  // [kPvCols][kPvLd] staged V columns (16-B aligned)
   __shared__ float red[40];
   __shared__ float inv_s;
   const int h = blockIdx.x, hd = d.head_dim, c0 = blockIdx.y * kPvCols;
   const int n = (int)b.st->pos + 1;
   const float* vbase = b.vc + (size_t)layer * d.max_seq * d.dim + (size_t)h * hd + c0;
   // V rows 0..n-2 of the first tile were written by earlier forwards
-  stage_v(vt, vbase, d.dim, 0, min(n - 1, kPvTile), false);
+  stage_v(vt, vbase, d.dim, 0, min(n - 1, kPvTile), 0, false);
   CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  if (n - 1 < kPvTile) stage_v(vt + (n - 1) * kPvCols, vbase, d.dim, n - 1, 1, true);
+  if (n - 1 < kPvTile) stage_v(vt, vbase, d.dim, n - 1, 1, n - 1, true);
   const float* s = b.scores + (size_t)h * d.max_seq;
   // softmax_avx2 over the n scores of this head (normalization.rs:106-160)
   float mx = -INFINITY;
@@ -177,42 +189,54 @@ __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, Decod
   for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
   __syncthreads();
   CHALOT_TRACE(slot, 3);
-  // out[c] = sum_t p_t * V[t][c], added in t order (engine.rs:302-308)
+  // out[c] = sum_t p_t * V[t][c], added in t order (engine.rs:302-308): the
+  // products of the next 16 t are loaded while this block's adds run
   float acc = 0.0f;
   for (int t0 = 0; t0 < n; t0 += kPvTile) {
     const int rows = min(kPvTile, n - t0);
     if (t0 > 0) {  // later tiles: stage now
       __syncthreads();
-      stage_v(vt, vbase, d.dim, t0, rows, true);
+      stage_v(vt, vbase, d.dim, t0, rows, 0, true);
       __syncthreads();
     }
     if (threadIdx.x < kPvCols) {
-      const float* pv = p + t0;
+      const float* pv = p + t0;  // t0 % 4 == 0: 16-byte aligned
+      const float* vc = vt + threadIdx.x * kPvLd;
       int t = 0;
-      for (; t + 16 <= rows; t += 16) {  // 16 products first, then 16 dependent adds
-        float pr[16];
+      if (rows >= 16) {
+        float4 pa[4], va[4];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) pr[u] = __fmul_rn(pv[t + u], vt[(t + u) * kPvCols + threadIdx.x]);
+        for (int u = 0; u < 4; ++u) {
+          pa[u] = lds16f(pv + 4 * u);
+          va[u] = lds16f(vc + 4 * u);
+        }
+        for (; t + 16 <= rows; t += 16) {
+          float4 pb[4], vb[4];
+          const bool more = t + 32 <= rows;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, pr[u]);
+          for (int u = 0; u < 4; ++u) {
+            pb[u] = more ? lds16f(pv + t + 16 + 4 * u) : pa[u];
+            vb[u] = more ? lds16f(vc + t + 16 + 4 * u) : va[u];
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            acc = __fadd_rn(acc, __fmul_rn(pa[u].x, va[u].x));
+            acc = __fadd_rn(acc, __fmul_rn(pa[u].y, va[u].y));
+            acc = __fadd_rn(acc, __fmul_rn(pa[u].z, va[u].z));
+            acc = __fadd_rn(acc, __fmul_rn(pa[u].w, va[u].w));
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            pa[u] = pb[u];
+            va[u] = vb[u];
+          }
+        }
       }
-      for (; t < rows; ++t) acc = __fadd_rn(acc, __fmul_rn(pv[t], vt[t * kPvCols + threadIdx.x]));
+      for (; t < rows; ++t) acc = __fadd_rn(acc, __fmul_rn(pv[t], vc[t]));
     }
   }
   if (threadIdx.x < kPvCols) b.att_out[h * hd + c0 + threadIdx.x] = acc;
   CHALOT_TRACE(slot, 4);
-  // the last CTA quantizes the finished att_out for the O projection
-  const bool tail = last_cta(b.counters + 0);
-  CHALOT_TRACE(slot, 5);
-  if (!tail) return;
-  float* a = sm;  // reuse
-  load_f32_cg(a, b.att_out, d.dim);
-  __syncthreads();
-  float scale, qinv;
-  quant_scale(absmax_smem(a, d.dim, red), &scale, &qinv);
-  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) b.xq_o[i] = quant_any(a[i], qinv, i, d.dim);
-  if (threadIdx.x == 0) *b.xs_o = scale;
-  CHALOT_TRACE(slot, 6);
 }
 
 }  // namespace
@@ -241,7 +265,7 @@ void launch_scores(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s
 
 void launch_pv(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl) {
   dim3 g2(d.n_heads, d.head_dim / kPvCols);
-  const size_t smem = ((((size_t)d.max_seq + 3) & ~size_t(3)) + (size_t)kPvTile * kPvCols) * 4;
+  const size_t smem = ((((size_t)d.max_seq + 3) & ~size_t(3)) + (size_t)kPvLd * kPvCols) * 4;
   if (smem > 48 * 1024) cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   launch_k(k_attn_pv, g2, dim3(kPvThreads), smem, s, pdl, d, layer, b);
 }

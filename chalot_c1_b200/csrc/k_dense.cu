@@ -6,7 +6,7 @@
 // The decode kernels fuse the producer and consumer of that GEMV:
 //   k_qkv    rmsnorm(x) -> quantize -> Q/K/V rows -> RoPE -> KV-cache write
 //            (engine.rs:235-280)
-//   k_oproj  quantize(att_out) -> O rows -> x += out (engine.rs:312-322)
+//   k_oproj  quantize(att_out) (every CTA) -> O rows -> x += out (engine.rs:312-322)
 //   k_lmhead rmsnorm(x) -> quantize -> vocab rows -> logits + argmax
 //            (engine.rs:470-493, sampling.rs:34-41)
 // Rows are streamed with 16-byte non-allocating loads; each warp owns a few
@@ -87,9 +87,13 @@ __device__ __forceinline__ void rows_dot_i8_loop(const int8_t* __restrict__ W, i
   for (int i = 0; i < R; ++i) acc[i] = warp_sum_i(acc[i]);
 }
 
-// Copies a quantized vector (n bytes, n % 16 == 0) produced by another grid
-// into shared memory through L2.
-__device__ __forceinline__ void load_q(int8_t* dst, const int8_t* src, int n) {
+// Copies a quantized vector (n bytes, n % 16 == 0) and its scale, produced by
+// another grid, into shared memory through L2: one request per line and CTA
+// (every warp reading the same lines would queue thousands of requests on a
+// few L2 slices).
+__device__ __forceinline__ void load_q(int8_t* dst, const int8_t* src, int n, float* xs_dst,
+                                       const float* xs_src) {
+  if (threadIdx.x == blockDim.x - 1) *xs_dst = __ldcg(xs_src);
   copy16(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n >> 4, true);
 }
 
@@ -141,11 +145,12 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  load_q(xq, b.xq_attn, d.dim);
+  __shared__ float xs_s;
+  load_q(xq, b.xq_attn, d.dim, &xs_s, b.xs_attn);
   __syncthreads();
   CHALOT_TRACE(slot, 3);
   if (r0 >= n_rows) return;
-  const float xs = __ldcg(b.xs_attn);
+  const float xs = xs_s;
   int acc[kQkvRows];
   rows_dot_i8<kQkvRows, IT>(w, d.dim, xq, acc);
   if ((threadIdx.x & 31) != 0) return;
@@ -173,8 +178,7 @@ constexpr int kORows = 2;
 
 // O rows + residual; the last CTA then runs the FFN prologue of the layer
 // once for every later kernel: xb = rmsnorm(x, rms_ffn), xq_ffn/xs_ffn =
-// quantize(xb), router logits and softmax_top_k -> sel/selw (engine.rs:325-344),
-// and clears the absmax slots of h.
+// quantize(xb), router logits and softmax_top_k -> sel/selw (engine.rs:325-344).
 template <int IT>
 __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
   extern __shared__ __align__(16) float osm[];  // tail scratch: xb, wbuf [dim] each, lanes [16E], logit [E]
@@ -204,11 +208,21 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  load_q(xq, b.xq_o, d.dim);
+  // quantize_f32_to_i8 of the attention output (engine.rs:312-314), by every
+  // CTA from the f32 values the attention kernel left in L2
+  __shared__ float xs_s;
+  load_f32_cg(xb, b.att_out, d.dim);
+  __syncthreads();
+  {
+    float scale, qinv;
+    quant_scale(absmax_smem(xb, d.dim, red), &scale, &qinv);
+    for (int i = threadIdx.x; i < d.dim; i += blockDim.x) xq[i] = quant_any(xb[i], qinv, i, d.dim);
+    if (threadIdx.x == 0) xs_s = scale;
+  }
   __syncthreads();
   CHALOT_TRACE(slot, 3);
   if (r0 < d.dim) {
-    const float xs = __ldcg(b.xs_o);
+    const float xs = xs_s;
     int acc[kORows];
     rows_dot_i8<kORows, IT>(w, d.dim, xq, acc);
     if (lane < kORows && r0 + lane < d.dim) {
@@ -228,7 +242,6 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   CHALOT_TRACE(tslot, 0);
   norm_quant_tail(b.x, wbuf, d.dim, b.xq_ffn, b.xs_ffn, xb, red);
   CHALOT_TRACE(tslot, 2);
-  if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;
   if (E >= 2) {
     router_logits(rw, rbias, xb, d.dim, E, lanes, logit);
     CHALOT_TRACE(tslot, 3);
@@ -257,9 +270,10 @@ __global__ void __launch_bounds__(kThreads) k_lmhead(Dims d, const int8_t* __res
   rows_load_i8<kLmRows, IT>(W, d.dim, r0, d.vocab, w);
   pdl_wait();
   pdl_trigger();
-  load_q(xq, b.xq_attn, d.dim);  // rmsnorm(x, final_norm) quantized by the last down kernel
+  __shared__ float xs_s;
+  load_q(xq, b.xq_attn, d.dim, &xs_s, b.xs_attn);  // rmsnorm(x, final_norm) quantized by the last down kernel
   __syncthreads();
-  const float xs = __ldcg(b.xs_attn);
+  const float xs = xs_s;
   unsigned long long best = 0ull;
   for (; r0 < d.vocab; r0 += step) {
     int acc[kLmRows];

@@ -138,6 +138,45 @@ __device__ __forceinline__ void chunk_sums(const int8_t* xp, int n, int* csum) {
 
 constexpr int kMaxGroups = 64;  // dim / group (checked at load)
 
+// quantize_f32_to_i8 of h_j for every routed expert j (quantization.rs:56-104)
+// by one CTA, with the absmax the gate/up CTAs left: the scales and up to
+// kHq float4 of h per thread are requested together, so one pass costs one
+// L2 round trip. hidden % 8 == 0, so every element takes the vector rounding.
+constexpr int kHq = 10;
+__device__ __forceinline__ void quantize_h(const DecodeBufs& b, int K, int H, int8_t* xq, float* xs) {
+  __shared__ float inv_j[8];
+  if (threadIdx.x < K) {
+    float sc, inv;
+    quant_scale(__uint_as_float(__ldcg(b.amax + threadIdx.x)), &sc, &inv);
+    xs[threadIdx.x] = sc;
+    inv_j[threadIdx.x] = inv;
+  }
+  const int n4 = (K * H) >> 2, h4 = H >> 2;
+  const float4* hv = reinterpret_cast<const float4*>(b.h);
+  uint32_t* xw = reinterpret_cast<uint32_t*>(xq);
+  for (int base = 0; base < n4; base += kHq * (int)blockDim.x) {
+    float4 v[kHq];
+#pragma unroll
+    for (int u = 0; u < kHq; ++u) {
+      const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+      if (i < n4) v[u] = __ldcg(hv + i);
+    }
+    if (base == 0) __syncthreads();  // the scales
+#pragma unroll
+    for (int u = 0; u < kHq; ++u) {
+      const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
+      if (i < n4) {
+        int jx = 0;
+        while (jx + 1 < K && i >= (jx + 1) * h4) ++jx;
+        const float inv = inv_j[jx];
+        const uint32_t q0 = (uint8_t)quant_elem(v[u].x, inv), q1 = (uint8_t)quant_elem(v[u].y, inv);
+        const uint32_t q2 = (uint8_t)quant_elem(v[u].z, inv), q3 = (uint8_t)quant_elem(v[u].w, inv);
+        xw[i] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
+      }
+    }
+  }
+}
+
 // Gate and up rows of routed expert sel[blockIdx.y] (engine.rs:366-374), then
 // SwiGLU (activations.rs:59-87) into h and |h| into the expert's absmax slot.
 // Warp w owns PPW = 4/IT row pairs (gate rows i and up rows H+i); lane l holds
@@ -146,12 +185,15 @@ constexpr int kMaxGroups = 64;  // dim / group (checked at load)
 // chunks of the quantized input. A chunk is one group when group == 32 (else
 // the group's chunks, on consecutive lanes, are reduced exactly by shuffles).
 // The group products go to shared memory and one lane per row adds them in
-// group order.
+// group order. The last CTA quantizes h of every routed expert.
 template <int IT>
 __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
   constexpr int RW = 8 / IT, PPW = RW / 2, PPC = kWarps * PPW, PS = kMaxGroups + 1;
   __shared__ float P[kWarps * RW * PS];
   __shared__ float wmax[kWarps];
+  __shared__ __align__(16) int8_t xsm[32 * 32 * IT];  // the quantized FFN input (dim <= 1024 * IT)
+  __shared__ int e_s;
+  __shared__ float xs_s;
   const int slot = layer * 8 + 4;
   CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -161,15 +203,19 @@ __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int
   pdl_wait();  // the routing and the quantized FFN input come from the O-projection's last CTA
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  const int e = __ldcg(b.sel + j);
-  const float xs = __ldcg(b.xs_ffn);
+  // the routing and the input once per CTA (one request per line and CTA)
+  if (threadIdx.x == 0) e_s = __ldcg(b.sel + j);
+  if (threadIdx.x == 1) xs_s = __ldcg(b.xs_ffn);
+  copy16(reinterpret_cast<uint4*>(xsm), reinterpret_cast<const uint4*>(b.xq_ffn), d.dim >> 4, true);
+  __syncthreads();
+  const int e = e_s;
+  const float xs = xs_s;
   uint4 xa[IT], xb[IT];
 #pragma unroll
   for (int it = 0; it < IT; ++it) {
-    const int c = lane + 32 * it;
-    const uint4* xv = reinterpret_cast<const uint4*>(b.xq_ffn) + 2 * c;
-    xa[it] = c < chunks ? __ldcg(xv) : make_uint4(0, 0, 0, 0);
-    xb[it] = c < chunks ? __ldcg(xv + 1) : make_uint4(0, 0, 0, 0);
+    const int c = min(lane + 32 * it, chunks - 1);
+    xa[it] = lds16(xsm + c * 32);
+    xb[it] = lds16(xsm + c * 32 + 16);
   }
   const ExpertPtrs X = expert_ptrs(L, d.n_experts, e);
   uint4 w[RW][IT];
@@ -229,21 +275,24 @@ __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int
     for (int i = 1; i < kWarps; ++i) mm = fmaxf(mm, wmax[i]);
     atomicMax(&b.amax[j], __float_as_uint(mm));  // one update per CTA
   }
+  const bool tail = last_cta(b.counters + 3);
   CHALOT_TRACE(slot, 5);
+  if (!tail) return;
+  quantize_h(b, d.top_k, H, b.xq_h, b.xs_h);  // once, for every down CTA
+  if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;  // read by this thread only: clear for the next layer
+  CHALOT_TRACE(slot, 6);
 }
 
 // Output rows r0..r0+rpc-1 for every routed expert, one row per warp
 // (engine.rs:380-401). The routing is two launches old, so before waiting for
 // the gate/up kernel the CTA requests its rows and their scales (one bulk
 // copy per expert: the rpc rows are contiguous), the x values it will update
-// and the next norm's weights. After the wait it quantizes h of every routed
-// expert into shared memory itself (quantize_f32_to_i8 with the absmax the
-// gate/up CTAs left), in one pass over L2; lane l of a warp then dots the
-// chunks l, l+32, ... (IT of them) of its row, lane 0 adds the group products
-// in order, and x[r] += sum_j w_j * y_j[r] in selection order. The last CTA
+// and the next norm's weights. After the wait it copies the quantized h of
+// every routed expert into shared memory. The warps of an expert split its
+// 32-column chunks, each x chunk serving all rpc rows; lane 0 of warp r adds
+// row r's group products in order, and x[r] += sum_j w_j * y_j[r] in
+// selection order. The last CTA
 // computes the next layer's quantized attention input from the finished x.
-constexpr int kHq = 10;  // float4 of h per thread and pass
-template <int IT>
 __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int layer,
                                                    const float* next_norm, DecodeBufs b, int dense,
                                                    int rpc) {
@@ -260,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int l
   float* wn = P + kWarps * ng;                                // [dim] next norm weights
   float* xbuf = wn + d.dim;                                   // [dim] tail scratch
   __shared__ __align__(8) uint64_t bar;
-  __shared__ float xs_j[8], inv_j[8];
+  __shared__ float xs_j[8];
   __shared__ float selw_s[8];
   __shared__ float y[kWarps];
   __shared__ float red[40];
@@ -291,87 +340,57 @@ __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int l
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  // quantize_f32_to_i8 of h_j (quantization.rs:56-104). hidden % 8 == 0, so
-  // every element takes the vector rounding (no scalar tail).
-  if (threadIdx.x < K) {
-    float sc, inv;
-    quant_scale(__uint_as_float(__ldcg(b.amax + threadIdx.x)), &sc, &inv);
-    xs_j[threadIdx.x] = sc;
-    inv_j[threadIdx.x] = inv;
-  }
-  const int n4 = (K * H) >> 2, h4 = H >> 2;
-  const float4* hv = reinterpret_cast<const float4*>(b.h);
-  uint32_t* xw = reinterpret_cast<uint32_t*>(xq);
-  for (int base = 0; base < n4; base += kHq * kThreads) {
-    float4 v[kHq];
-#pragma unroll
-    for (int u = 0; u < kHq; ++u) {
-      const int i = base + u * kThreads + threadIdx.x;
-      if (i < n4) v[u] = __ldcg(hv + i);
-    }
-    if (base == 0) __syncthreads();  // the scales
-#pragma unroll
-    for (int u = 0; u < kHq; ++u) {
-      const int i = base + u * kThreads + threadIdx.x;
-      if (i < n4) {
-        int jx = 0;
-        while (jx + 1 < K && i >= (jx + 1) * h4) ++jx;
-        const float inv = inv_j[jx];
-        const uint32_t q0 = (uint8_t)quant_elem(v[u].x, inv), q1 = (uint8_t)quant_elem(v[u].y, inv);
-        const uint32_t q2 = (uint8_t)quant_elem(v[u].z, inv), q3 = (uint8_t)quant_elem(v[u].w, inv);
-        xw[i] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
-      }
-    }
-  }
+  // the quantized h of every routed expert (the gate/up kernel's last CTA)
+  if (threadIdx.x < K) xs_j[threadIdx.x] = __ldcg(b.xs_h + threadIdx.x);
+  copy16(reinterpret_cast<uint4*>(xq), reinterpret_cast<const uint4*>(b.xq_h), (K * H) >> 4, true);
   if (threadIdx.x == 0) ok_s = mbar_wait(&bar, 0, b.err) ? 1 : 0;
   __syncthreads();
   CHALOT_TRACE(slot, 3);
   if (!ok_s) return;
-  if (warp < nrow) {
-    const int jx = warp / rpc;
-    const uint8_t* wrow = W + (size_t)warp * prow;
+  // group products: the warps of expert j split its chunks, and each x chunk
+  // (read from shared memory once per CTA) serves the expert's rpc rows
+  const int wpe = kWarps / K;  // warps per expert (K <= 8)
+  if (warp < K * wpe) {
+    const int jx = warp / wpe, wq = warp % wpe;
     const int8_t* xj = xq + (size_t)jx * H;
-    const float* srow = S + (size_t)warp * ng;
     const float xs = xs_j[jx];
-    uint4 wv[IT];
-    float sc[IT];
-#pragma unroll
-    for (int it = 0; it < IT; ++it) {
-      const int cc = min(lane + 32 * it, chunks - 1);
-      wv[it] = lds16(wrow + (size_t)cc * 16);
-      sc[it] = srow[cc >> gsh];
-    }
-    float* prow_p = P + (size_t)warp * ng;
-#pragma unroll
-    for (int it = 0; it < IT; ++it) {
-      const int c = lane + 32 * it, cc = min(c, chunks - 1);
+    for (int c0 = wq * 32; c0 < chunks; c0 += 32 * wpe) {  // warp-uniform
+      const int c = c0 + lane, cc = min(c, chunks - 1), g = cc >> gsh;
+      const bool lead = c < chunks && (c & (cpg - 1)) == 0;
       const uint4 x0 = lds16(xj + (size_t)cc * 32), x1 = lds16(xj + (size_t)cc * 32 + 16);
-      int dv = dot32_rp(wv[it], x0, x1);
-      for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
-      if (c < chunks && (c & (cpg - 1)) == 0) prow_p[c >> gsh] = __fmul_rn(__fmul_rn((float)dv, sc[it]), xs);
-    }
-    __syncwarp();
-    if (lane == 0) {  // t = t + p_g in group order, four groups per load
-      float t = 0.0f;
-      int g4 = 0;
-      for (; g4 + 4 <= (ng >> 2); g4 += 4) {
-        float4 a[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) a[u] = lds16f(prow_p + 4 * (g4 + u));
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          t = __fadd_rn(t, a[u].x);
-          t = __fadd_rn(t, a[u].y);
-          t = __fadd_rn(t, a[u].z);
-          t = __fadd_rn(t, a[u].w);
+      for (int i = 0; i < 8; ++i) {
+        if (i < rpc) {  // CTA-uniform
+          const int row = jx * rpc + i;
+          int dv = dot32_rp(lds16(W + (size_t)row * prow + (size_t)cc * 16), x0, x1);
+          for (int o = 1; o < cpg; o <<= 1) dv += __shfl_xor_sync(0xffffffffu, dv, o);
+          if (lead) P[row * ng + g] = __fmul_rn(__fmul_rn((float)dv, S[row * ng + g]), xs);
         }
       }
-      for (; g4 < (ng >> 2); ++g4) {
-        const float4 a = lds16f(prow_p + 4 * g4);
-        t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(t, a.x), a.y), a.z), a.w);
-      }
-      y[warp] = t;
     }
+  }
+  __syncthreads();
+  if (warp < nrow && lane == 0) {  // row `warp`: t = t + p_g in group order, four groups per load
+    const float* prow_p = P + (size_t)warp * ng;
+    float t = 0.0f;
+    int g4 = 0;
+    for (; g4 + 4 <= (ng >> 2); g4 += 4) {
+      float4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = lds16f(prow_p + 4 * (g4 + u));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        t = __fadd_rn(t, a[u].x);
+        t = __fadd_rn(t, a[u].y);
+        t = __fadd_rn(t, a[u].z);
+        t = __fadd_rn(t, a[u].w);
+      }
+    }
+    for (; g4 < (ng >> 2); ++g4) {
+      const float4 a = lds16f(prow_p + 4 * g4);
+      t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(t, a.x), a.y), a.z), a.w);
+    }
+    y[warp] = t;
   }
   __syncthreads();
   CHALOT_TRACE(slot, 4);
@@ -505,29 +524,15 @@ void launch_gateup(const Dims& d, const LayerPtrs& L, int layer, const DecodeBuf
     launch_k(k_gateup<4>, grid, dim3(kThreads), 0, s, pdl, d, L, layer, b);
 }
 
-template <int IT>
-static void launch_down_it(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
-                           const DecodeBufs& b, cudaStream_t s, bool pdl, int grid, int dense, int rpc) {
-  const size_t smem = down_smem(d);
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(k_down<IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_k(k_down<IT>, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc);
-}
-
 void launch_down(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
                  const DecodeBufs& b, cudaStream_t s, bool pdl) {
-  const int rpc = std::max(1, kWarps / d.top_k);  // rows per CTA: one row per warp over all experts
+  const int rpc = std::max(1, kWarps / d.top_k);  // rows per CTA: the CTA's warps over all experts
   const int grid = (d.dim + rpc - 1) / rpc;
   const int dense = d.n_experts < 2 ? 1 : 0;
-  switch ((d.hidden / 32 + 31) / 32) {  // hidden <= 8192: 1..8 chunks per lane
-    case 1: launch_down_it<1>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-    case 2: launch_down_it<2>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-    case 3: launch_down_it<3>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-    case 4: launch_down_it<4>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-    case 5: launch_down_it<5>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-    case 6: launch_down_it<6>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-    default: launch_down_it<8>(d, L, layer, next_norm, b, s, pdl, grid, dense, rpc); break;
-  }
+  const size_t smem = down_smem(d);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_k(k_down, dim3(grid), dim3(kThreads), smem, s, pdl, d, L, layer, next_norm, b, dense, rpc);
 }
 
 cudaError_t repack_int4(uint8_t* p, size_t bytes, cudaStream_t s) {

@@ -60,8 +60,6 @@ struct DecodeBufs {
   const float* rope_sin;
   int8_t* xq_attn;   // [dim] quantized attention input (rmsnorm(x) of this layer)
   float* xs_attn;    // [1] its scale
-  int8_t* xq_o;      // [dim] quantized attention output (O-projection input)
-  float* xs_o;       // [1]
   int8_t* xq_ffn;    // [dim] quantized FFN input
   float* xs_ffn;     // [1] its scale
   unsigned* counters;  // [8] last-CTA tickets, one per kernel kind
@@ -70,6 +68,8 @@ struct DecodeBufs {
   float* selw;       // [top_k] their weights
   float* h;          // [top_k][hidden] SwiGLU output
   unsigned* amax;    // [top_k] absmax bits of h
+  int8_t* xq_h;      // [top_k][hidden] quantized h (down-projection input)
+  float* xs_h;       // [top_k] its scales
   float* logits;     // [vocab]
   StepState* st;
   const uint32_t* prompt;  // [max_seq] prompt of the running generate call
@@ -86,11 +86,11 @@ void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const fl
 // Q/K/V rows from xq_attn, RoPE, KV-cache write.
 void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
                 bool pdl);
-// Scores and softmax.P.V; the last CTA quantizes att_out into xq_o.
+// Scores and softmax.P.V into att_out.
 void launch_attention(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl);
 void launch_scores(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl);
 void launch_pv(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bool pdl);
-// O rows from xq_o, x += ; the last CTA computes the FFN norm, xq_ffn and the routing.
+// O rows from quantize(att_out), x += ; the last CTA computes the FFN norm, xq_ffn and the routing.
 void launch_oproj(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b,
                   cudaStream_t s, bool pdl);
 // Gate/up rows of the routed experts + SwiGLU -> h, absmax(h).
