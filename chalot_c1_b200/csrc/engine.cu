@@ -180,11 +180,12 @@ struct chalot_engine {
       if (marks) cudaEventRecordWithFlags(marks[m++], s, cudaEventRecordExternal);
     };
     mark();
-    launch_embed(d, emb, emb_s, layers[0].rms_attn, b, s);
+    launch_embed(d, emb, emb_s, b, s);
     mark();
     for (int l = 0; l < d.n_layers; ++l) {
       const LayerPtrs& L = layers[l];
-      const float* next_norm = (l + 1 < d.n_layers) ? layers[l + 1].rms_attn : final_norm;
+      // the last layer's down kernel also computes rmsnorm(x, final_norm) for the lm_head
+      const float* next_norm = (l + 1 < d.n_layers) ? nullptr : final_norm;
       launch_qkv(d, L, l, b, s, pdl);
       mark();
       launch_scores(d, l, b, s, pdl);
@@ -774,7 +775,7 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
       bl.sel = sel + l * K;
       bl.selw = selw + l * K;
       launch_gateup(d, e->layers[l], l, bl, e->stream, l > 0);
-      launch_down(d, e->layers[l], l, e->layers[l].rms_attn, bl, e->stream, true);
+      launch_down(d, e->layers[l], l, nullptr, bl, e->stream, true);
     }
     CK(cudaStreamEndCapture(e->stream, &g));
     CK(cudaGraphInstantiate(&ex, g, 0));

@@ -4,7 +4,7 @@
 // quantized per call (quantize_f32_to_i8, quantization.rs:56-104), every row
 // dot is an exact int32, and the row result is ((float)dot * w_scale) * x_scale.
 // The decode kernels fuse the producer and consumer of that GEMV:
-//   k_qkv    rmsnorm(x) -> quantize -> Q/K/V rows -> RoPE -> KV-cache write
+//   k_qkv    rmsnorm(x) -> quantize (every CTA) -> Q/K/V rows -> RoPE -> KV-cache write
 //            (engine.rs:235-280)
 //   k_oproj  quantize(att_out) (every CTA) -> O rows -> x += out (engine.rs:312-322)
 //   k_lmhead rmsnorm(x) -> quantize -> vocab rows -> logits + argmax
@@ -99,28 +99,24 @@ __device__ __forceinline__ void load_q(int8_t* dst, const int8_t* src, int n, fl
 
 // ---------------------------------------------------------------------------
 
-// x = embedding row (engine.rs:201-210); then rmsnorm with the first layer's
-// attention norm and quantize_f32_to_i8 into xq_attn (one CTA).
+// x = embedding row (engine.rs:201-210), one CTA.
 __global__ void __launch_bounds__(kThreads) k_embed(Dims d, const int8_t* __restrict__ emb,
-                                                    const float* __restrict__ emb_s,
-                                                    const float* __restrict__ rms0, DecodeBufs b) {
-  extern __shared__ __align__(16) float esm[];
-  __shared__ float red[40];
-  load_f32(esm + d.dim, rms0, d.dim);
+                                                    const float* __restrict__ emb_s, DecodeBufs b) {
   const uint32_t tok = b.st->token;
   const float s = emb_s[tok];
   const int8_t* row = emb + (size_t)tok * d.dim;
   for (int i = threadIdx.x; i < d.dim; i += blockDim.x) b.x[i] = __fmul_rn((float)row[i], s);
   if (threadIdx.x == 0) b.st->argmax_key = 0ull;
-  __syncthreads();
-  norm_quant_tail(b.x, esm + d.dim, d.dim, b.xq_attn, b.xs_attn, esm, red);
 }
 
 constexpr int kQkvRows = 2;  // rows per warp: one RoPE pair
 
 template <int IT>
 __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
+  extern __shared__ __align__(16) float qsm[];  // [dim] attention norm weights, [dim] scratch
   __shared__ __align__(16) int8_t xq[512 * IT];
+  __shared__ float red[40];
+  __shared__ float xs_s;
   const int slot = layer * 8 + 0;
   CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5;
@@ -141,12 +137,14 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer
       sn = b.rope_sin[pos * half + i];
     }
   }
+  load_f32(qsm, L.rms_attn, d.dim);
   CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
   CHALOT_TRACE(slot, 2);
-  __shared__ float xs_s;
-  load_q(xq, b.xq_attn, d.dim, &xs_s, b.xs_attn);
+  // rmsnorm(x, rms_attn) then quantize_f32_to_i8 (engine.rs:230-236), by every
+  // CTA from the x the previous layer's down kernel left in L2
+  norm_quant_tail(b.x, qsm, d.dim, xq, &xs_s, qsm + d.dim, red);
   __syncthreads();
   CHALOT_TRACE(slot, 3);
   if (r0 >= n_rows) return;
@@ -416,9 +414,9 @@ __global__ void __launch_bounds__(kThreads) k_quantize_op(int8_t* __restrict__ q
 // in_dim of the dense projections is at most 4096: 16-byte chunks per lane
 static int dense_it(int dim) { return (dim + 511) / 512; }
 
-void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const float* rms0,
-                  const DecodeBufs& b, cudaStream_t s) {
-  launch_k(k_embed, dim3(1), dim3(kThreads), (size_t)d.dim * 8, s, false, d, emb, emb_s, rms0, b);
+void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const DecodeBufs& b,
+                  cudaStream_t s) {
+  launch_k(k_embed, dim3(1), dim3(kThreads), 0, s, false, d, emb, emb_s, b);
 }
 
 #define CHALOT_IT_SWITCH(it, CALL) \
@@ -437,7 +435,8 @@ void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& 
                 bool pdl) {
   const int rows_per_block = kWarps * kQkvRows;
   const int grid = (3 * d.dim + rows_per_block - 1) / rows_per_block;
-#define QKV_CALL(IT) launch_k(k_qkv<IT>, dim3(grid), dim3(kThreads), 0, s, pdl, d, L, layer, b)
+#define QKV_CALL(IT) \
+  launch_k(k_qkv<IT>, dim3(grid), dim3(kThreads), (size_t)d.dim * 8, s, pdl, d, L, layer, b)
   CHALOT_IT_SWITCH(dense_it(d.dim), QKV_CALL)
 #undef QKV_CALL
 }

@@ -287,12 +287,12 @@ __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int
 // (engine.rs:380-401). The routing is two launches old, so before waiting for
 // the gate/up kernel the CTA requests its rows and their scales (one bulk
 // copy per expert: the rpc rows are contiguous), the x values it will update
-// and the next norm's weights. After the wait it copies the quantized h of
-// every routed expert into shared memory. The warps of an expert split its
-// 32-column chunks, each x chunk serving all rpc rows; lane 0 of warp r adds
-// row r's group products in order, and x[r] += sum_j w_j * y_j[r] in
-// selection order. The last CTA
-// computes the next layer's quantized attention input from the finished x.
+// and the final norm's weights after the last layer. After the wait it copies
+// the quantized h of every routed expert into shared memory. The warps of an
+// expert split its 32-column chunks, each x chunk serving all rpc rows; lane 0
+// of warp r adds row r's group products in order, and x[r] += sum_j w_j *
+// y_j[r] in selection order. After the last layer (next_norm = the final
+// norm, else null) the last CTA computes the lm_head's quantized input.
 __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int layer,
                                                    const float* next_norm, DecodeBufs b, int dense,
                                                    int rpc) {
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int l
   }
   // x[r] was last written by the O-projection, two launches back
   const float xold = threadIdx.x < nr ? __ldcg(b.x + r0 + threadIdx.x) : 0.0f;
-  load_f32(wn, next_norm, d.dim);
+  if (next_norm) load_f32(wn, next_norm, d.dim);
   CHALOT_TRACE(slot, 1);
   pdl_wait();
   pdl_trigger();
@@ -404,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int l
     }
     b.x[r0 + threadIdx.x] = __fadd_rn(xold, add);
   }
+  if (!next_norm) return;
   const bool tail = last_cta(b.counters + 2);
   CHALOT_TRACE(slot, 5);
   if (!tail) return;

@@ -80,10 +80,10 @@ struct DecodeBufs {
 // ---- decode step (batch 1) ---------------------------------------------------
 // Kernels after the first of a forward are launched with programmatic
 // dependent launch (`pdl`); see pdl.cuh for the rules they follow.
-// x = embedding(token); xq_attn = quantize(rmsnorm(x, rms_attn of layer 0)).
-void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const float* rms0,
-                  const DecodeBufs& b, cudaStream_t s);
-// Q/K/V rows from xq_attn, RoPE, KV-cache write.
+// x = embedding(token).
+void launch_embed(const Dims& d, const int8_t* emb, const float* emb_s, const DecodeBufs& b,
+                  cudaStream_t s);
+// quantize(rmsnorm(x, rms_attn)) in every CTA, Q/K/V rows, RoPE, KV-cache write.
 void launch_qkv(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
                 bool pdl);
 // Scores and softmax.P.V into att_out.
@@ -93,12 +93,13 @@ void launch_pv(const Dims& d, int layer, const DecodeBufs& b, cudaStream_t s, bo
 // O rows from quantize(att_out), x += ; the last CTA computes the FFN norm, xq_ffn and the routing.
 void launch_oproj(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b,
                   cudaStream_t s, bool pdl);
-// Gate/up rows of the routed experts + SwiGLU -> h, absmax(h).
+// Gate/up rows of the routed experts + SwiGLU -> h, absmax(h); the last CTA
+// quantizes h into xq_h/xs_h.
 void launch_gateup(const Dims& d, const LayerPtrs& L, int layer, const DecodeBufs& b, cudaStream_t s,
                    bool pdl);
-// Down rows of every routed expert, gated combine, x += ; the last CTA computes
-// xq_attn for the next layer (rmsnorm with `next_norm`: the next layer's
-// attention norm, or the final norm after the last layer).
+// Down rows of every routed expert, gated combine, x += ; with `next_norm`
+// (the final norm, after the last layer) the last CTA computes xq_attn for
+// the lm_head; null for the other layers.
 void launch_down(const Dims& d, const LayerPtrs& L, int layer, const float* next_norm,
                  const DecodeBufs& b, cudaStream_t s, bool pdl);
 // Logits from xq_attn (the final-norm input) + argmax.
