@@ -237,7 +237,7 @@ struct chalot_engine {
     CK(cudaMemcpy(&h, b.err, sizeof h, cudaMemcpyDeviceToHost));
     if (h) {
       CK(cudaMemset(b.err, 0, 4 * sizeof(unsigned)));
-      CK(cudaMemset(b.counters, 0, 8 * sizeof(unsigned)));
+      CK(cudaMemset(b.counters, 0, kTickets * sizeof(unsigned)));
       throw CudaFail{CHALOT_ERR_TIMEOUT, "a device wait for a bulk copy timed out"};
     }
   }
@@ -480,7 +480,7 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     b.xs_attn = e->dalloc<float>(1);
     b.xq_ffn = e->dalloc<int8_t>((dim + 15) & ~size_t(15));
     b.xs_ffn = e->dalloc<float>(1);
-    b.counters = e->dalloc<unsigned>(8);
+    b.counters = e->dalloc<unsigned>(kTickets);
     b.err = e->dalloc<unsigned>(4);
     b.sel = e->dalloc<int32_t>(std::max<size_t>(c.top_k, 1));
     b.selw = e->dalloc<float>(std::max<size_t>(c.top_k, 1));

@@ -138,22 +138,22 @@ __device__ __forceinline__ void chunk_sums(const int8_t* xp, int n, int* csum) {
 
 constexpr int kMaxGroups = 64;  // dim / group (checked at load)
 
-// quantize_f32_to_i8 of h_j for every routed expert j (quantization.rs:56-104)
-// by one CTA, with the absmax the gate/up CTAs left: the scales and up to
-// kHq float4 of h per thread are requested together, so one pass costs one
-// L2 round trip. hidden % 8 == 0, so every element takes the vector rounding.
-constexpr int kHq = 10;
-__device__ __forceinline__ void quantize_h(const DecodeBufs& b, int K, int H, int8_t* xq, float* xs) {
-  __shared__ float inv_j[8];
-  if (threadIdx.x < K) {
+// quantize_f32_to_i8 of h_j (quantization.rs:56-104) by one CTA, with the
+// absmax the expert's gate/up CTAs left: the scale and up to kHq float4 of h
+// per thread are requested together, so one pass costs one L2 round trip.
+// hidden % 8 == 0, so every element takes the vector rounding.
+constexpr int kHq = 8;
+__device__ __forceinline__ void quantize_h(const DecodeBufs& b, int j, int H) {
+  __shared__ float inv_s;
+  if (threadIdx.x == 0) {
     float sc, inv;
-    quant_scale(__uint_as_float(__ldcg(b.amax + threadIdx.x)), &sc, &inv);
-    xs[threadIdx.x] = sc;
-    inv_j[threadIdx.x] = inv;
+    quant_scale(__uint_as_float(__ldcg(b.amax + j)), &sc, &inv);
+    b.xs_h[j] = sc;
+    inv_s = inv;
   }
-  const int n4 = (K * H) >> 2, h4 = H >> 2;
-  const float4* hv = reinterpret_cast<const float4*>(b.h);
-  uint32_t* xw = reinterpret_cast<uint32_t*>(xq);
+  const int n4 = H >> 2;
+  const float4* hv = reinterpret_cast<const float4*>(b.h + (size_t)j * H);
+  uint32_t* xw = reinterpret_cast<uint32_t*>(b.xq_h + (size_t)j * H);
   for (int base = 0; base < n4; base += kHq * (int)blockDim.x) {
     float4 v[kHq];
 #pragma unroll
@@ -161,14 +161,12 @@ __device__ __forceinline__ void quantize_h(const DecodeBufs& b, int K, int H, in
       const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
       if (i < n4) v[u] = __ldcg(hv + i);
     }
-    if (base == 0) __syncthreads();  // the scales
+    if (base == 0) __syncthreads();  // the scale
+    const float inv = inv_s;
 #pragma unroll
     for (int u = 0; u < kHq; ++u) {
       const int i = base + u * (int)blockDim.x + (int)threadIdx.x;
       if (i < n4) {
-        int jx = 0;
-        while (jx + 1 < K && i >= (jx + 1) * h4) ++jx;
-        const float inv = inv_j[jx];
         const uint32_t q0 = (uint8_t)quant_elem(v[u].x, inv), q1 = (uint8_t)quant_elem(v[u].y, inv);
         const uint32_t q2 = (uint8_t)quant_elem(v[u].z, inv), q3 = (uint8_t)quant_elem(v[u].w, inv);
         xw[i] = q0 | (q1 << 8) | (q2 << 16) | (q3 << 24);
@@ -185,7 +183,7 @@ __device__ __forceinline__ void quantize_h(const DecodeBufs& b, int K, int H, in
 // chunks of the quantized input. A chunk is one group when group == 32 (else
 // the group's chunks, on consecutive lanes, are reduced exactly by shuffles).
 // The group products go to shared memory and one lane per row adds them in
-// group order. The last CTA quantizes h of every routed expert.
+// group order. The last CTA of each expert quantizes that expert's h.
 template <int IT>
 __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int layer, DecodeBufs b) {
   constexpr int RW = 8 / IT, PPW = RW / 2, PPC = kWarps * PPW, PS = kMaxGroups + 1;
@@ -275,11 +273,11 @@ __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int
     for (int i = 1; i < kWarps; ++i) mm = fmaxf(mm, wmax[i]);
     atomicMax(&b.amax[j], __float_as_uint(mm));  // one update per CTA
   }
-  const bool tail = last_cta(b.counters + 3);
+  const bool tail = last_cta(b.counters + 8 + j, gridDim.x);  // the last CTA of expert j
   CHALOT_TRACE(slot, 5);
   if (!tail) return;
-  quantize_h(b, d.top_k, H, b.xq_h, b.xs_h);  // once, for every down CTA
-  if (threadIdx.x < d.top_k) b.amax[threadIdx.x] = 0u;  // read by this thread only: clear for the next layer
+  quantize_h(b, j, H);  // once, for every down CTA
+  if (threadIdx.x == 0) b.amax[j] = 0u;  // read by this thread only: clear for the next layer
   CHALOT_TRACE(slot, 6);
 }
 

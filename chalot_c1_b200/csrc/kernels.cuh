@@ -48,6 +48,8 @@ __device__ __forceinline__ ExpertPtrs expert_ptrs(const LayerPtrs& L, int E, int
   return L.experts[e];
 }
 
+constexpr int kTickets = 16;
+
 // Per-engine device buffers of the batch-1 decode path.
 struct DecodeBufs {
   float* x;          // [dim] residual stream
@@ -62,7 +64,7 @@ struct DecodeBufs {
   float* xs_attn;    // [1] its scale
   int8_t* xq_ffn;    // [dim] quantized FFN input
   float* xs_ffn;     // [1] its scale
-  unsigned* counters;  // [8] last-CTA tickets, one per kernel kind
+  unsigned* counters;  // [kTickets] last-CTA tickets: [1] O-projection, [2] down, [8 + j] gate/up of expert j
   unsigned* err;       // [1] set when a bounded wait gave up
   int32_t* sel;      // [top_k] selected experts
   float* selw;       // [top_k] their weights

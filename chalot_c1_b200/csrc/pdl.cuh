@@ -21,17 +21,18 @@ namespace chalot {
 CHALOT_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 CHALOT_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// True in exactly one CTA of the grid: the last one to get here. The other
-// CTAs' global writes made before their call are visible to it (read them
-// with __ldcg). Resets the counter for the next launch.
+// True in exactly one CTA of the grid (or of the n CTAs sharing `counter`):
+// the last one to get here. The other CTAs' global writes made before their
+// call are visible to it (read them with __ldcg). Resets the counter for the
+// next launch.
 // The CTA barrier orders the CTA's writes before thread 0's device-scope
 // fence and ticket (the pattern of a cooperative grid barrier).
-__device__ __forceinline__ bool last_cta(unsigned* counter) {
+__device__ __forceinline__ bool last_cta(unsigned* counter, unsigned n = 0) {
   __shared__ bool is_last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const unsigned n = gridDim.x * gridDim.y * gridDim.z;
+    if (n == 0) n = gridDim.x * gridDim.y * gridDim.z;
     const unsigned t = atomicAdd(counter, 1u);
     is_last = (t == n - 1);
     if (is_last) {
