@@ -127,20 +127,12 @@ __device__ __forceinline__ void norm_quant_tail(const float* x, const float* wsm
   if (threadIdx.x < 8) {  // lane j accumulates x[8c+j]^2 over c in order
     float s = 0.0f;
     int c = 0;
-    if (chunks >= 8) {  // the next 8 values load while the current 8 are added
-      float cur[8];
+    for (; c + 16 <= chunks; c += 16) {  // 16 loads issued together, then the chain
+      float v[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) cur[u] = xb[u * 8 + threadIdx.x];
-      for (; c + 8 <= chunks; c += 8) {
-        float nxt[8];
-        const bool more = c + 16 <= chunks;
+      for (int u = 0; u < 16; ++u) v[u] = xb[(c + u) * 8 + threadIdx.x];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) nxt[u] = more ? xb[(c + 8 + u) * 8 + threadIdx.x] : 0.0f;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) s = __fadd_rn(s, __fmul_rn(cur[u], cur[u]));
-#pragma unroll
-        for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
-      }
+      for (int u = 0; u < 16; ++u) s = __fadd_rn(s, __fmul_rn(v[u], v[u]));
     }
     for (; c < chunks; ++c) {
       const float v = xb[c * 8 + threadIdx.x];
@@ -213,32 +205,23 @@ __device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t*
   float sum = hsum8(l8);
   for (int i = full; i < n; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, i));
   const float p = __fmul_rn(e, __fdiv_rn(1.0f, sum));
-  // k rounds of (max probability, lowest index); lane j keeps round j's pick
-  bool taken = lane >= n;
-  float tot = -0.0f, my_w = 0.0f;
-  int my_i = 0;
-  for (int j = 0; j < k; ++j) {
-    float bv = taken ? -INFINITY : p;
-    int bi = taken ? 0x7fffffff : lane;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == bi) taken = true;
-    tot = __fadd_rn(tot, bv);
-    if (lane == j) {
-      my_i = bi;
-      my_w = bv;
-    }
+  // the k rounds of (max probability, lowest index) as ranks: rank r is the
+  // pick of round r
+  int rank = 0;
+  for (int o = 0; o < n; ++o) {
+    const float q = __shfl_sync(0xffffffffu, p, o);
+    rank += (q > p || (q == p && o < lane)) ? 1 : 0;
   }
-  if (lane < k) {
-    idx[lane] = my_i;
-    w[lane] = (tot > 1e-12f) ? __fdiv_rn(my_w, tot) : my_w;
+  const bool live = lane < n;
+  float tot = -0.0f;  // the picks' sum in round order
+  for (int r = 0; r < k; ++r) {
+    const unsigned m = __ballot_sync(0xffffffffu, live && rank == r);
+    const float pr = __shfl_sync(0xffffffffu, p, m ? __ffs(m) - 1 : 0);
+    tot = __fadd_rn(tot, pr);
+  }
+  if (live && rank < k) {
+    idx[rank] = lane;
+    w[rank] = (tot > 1e-12f) ? __fdiv_rn(p, tot) : p;
   }
 }
 
