@@ -382,8 +382,9 @@ def bench_moe_ep(ws: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
 
 def run_profile(args):
     """A short decode for profilers: 32 prompt tokens + 8 new tokens on the
-    Qwen-shaped model (40 forwards, 171 kernel launches each), run twice; the
-    second run is the one to capture (skip the first 6840 launches)."""
+    Qwen-shaped model (40 forwards, 147 kernel launches each: embed, 6 per
+    layer, lm_head, advance), run twice; the second run is the one to capture
+    (skip the first 5880 launches)."""
     import numpy as np
 
     import chalot_c1_b200 as cb
