@@ -31,6 +31,7 @@
 
 #include "batch.h"
 #include "capi_internal.h"
+#include "ep_link.h"
 #include "kernels.cuh"
 #include "moe_layer.h"
 #include "myai.h"
@@ -144,6 +145,23 @@ struct chalot_engine {
     uint32_t* h_io = nullptr;  // pinned staging: slots, tokens, positions, results
     std::vector<MlExperts> experts;  // per layer, the engine's repacked experts
   } bt;
+  // expert parallelism of the batched forward: this engine computes the
+  // experts e with e % world == rank and exchanges token rows with its peers
+  std::unique_ptr<EpLink> ep;
+  struct EpBufs {
+    int cap = 0, world = 0;  // sized for cap tokens per rank and world ranks
+    int8_t* rows = nullptr;     // [cap*K][dim] rows to send, in plan order
+    float* rscale = nullptr;    // [cap*K]
+    int8_t* rrows = nullptr;    // [world*cap*K][dim] rows received
+    float* rrscale = nullptr;   // [world*cap*K]
+    int32_t* rexp = nullptr;    // [world*cap*K] local expert of each received row
+    float* y = nullptr;         // [world*cap*K][dim] outputs of the received rows
+    float* yback = nullptr;     // [cap*K][dim] outputs of my rows, in plan order
+    int32_t* offs = nullptr;    // [E+1] plan offsets (rank-major, then local expert)
+    int32_t* cnt = nullptr;     // [2][world*El] counts sent / received
+    void* ws = nullptr;         // expert workspace for world*cap*K rows
+    int32_t* h = nullptr;       // pinned: offsets, counts, row experts
+  } epb;
 
   ~chalot_engine() {
     if (g_fwd) cudaGraphExecDestroy(g_fwd);
@@ -156,6 +174,7 @@ struct chalot_engine {
     if (h_stage) cudaFreeHost(h_stage);
     if (h_tokens) cudaFreeHost(h_tokens);
     if (bt.h_io) cudaFreeHost(bt.h_io);
+    if (epb.h) cudaFreeHost(epb.h);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -914,6 +933,124 @@ __attribute__((visibility("default"))) int chalot_batch_reserve(chalot_engine* e
   return CHALOT_OK;
 }
 
+// ---- expert parallelism of the batched forward --------------------------------
+
+// Exchange buffers for `cap` tokens per rank (every rank of the group reserves
+// the same max_seqs): a rank receives at most world*cap*top_k rows.
+static void ep_reserve(chalot_engine* e) {
+  auto& p = e->epb;
+  const ModelConfig& c = e->cfg;
+  const int G = e->ep->world();
+  if (p.cap == e->bt.cap && p.world == G) return;
+  const size_t S = e->bt.cap, K = c.top_k, D = c.dim, E = c.n_experts, El = E / G;
+  const size_t R = (size_t)G * S * K;
+  p.rows = e->dalloc<int8_t>(S * K * D);
+  p.rscale = e->dalloc<float>(S * K);
+  p.rrows = e->dalloc<int8_t>(R * D);
+  p.rrscale = e->dalloc<float>(R);
+  p.rexp = e->dalloc<int32_t>(R);
+  p.y = e->dalloc<float>(R * D);
+  p.yback = e->dalloc<float>(S * K * D);
+  p.offs = e->dalloc<int32_t>(E + 1);
+  p.cnt = e->dalloc<int32_t>(2 * G * El);
+  const MlDims xd{(int)R, (int)D, (int)c.hidden_dim, (int)El, 1, (int)c.int4_group_size};
+  const size_t simt = ml_layout(xd, nullptr, nullptr);
+  p.ws = e->dalloc<unsigned char>(ml_tc_eligible(xd) ? ml_tc_layout(xd, simt, nullptr, nullptr) : simt);
+  if (p.h) cudaFreeHost(p.h);
+  p.h = nullptr;
+  CK(cudaMallocHost(&p.h, (E + 1 + 2 * G * El + R) * sizeof(int32_t)));
+  p.cap = (int)S;
+  p.world = G;
+}
+
+// The expert block of layer l for this rank's B tokens (rows b.xb) with the
+// experts spread over the group (expert e on rank e % world), into b.eout:
+// route, order the (token, choice) slots by destination rank and local expert,
+// exchange counts, int8 rows and scales, run the local experts on the rows
+// received, send the f32 outputs back and combine them per token in selection
+// order (engine.rs:334-401). Every rank takes the same exchanges in the same
+// order, B == 0 included. Returns a CHALOT_ status.
+static int ep_moe(chalot_engine* e, int l, int B, const MlDims& md, MlWork w, cudaStream_t s, std::string* msg) {
+  auto& p = e->epb;
+  auto& b = e->bt;
+  const ModelConfig& c = e->cfg;
+  EpLink& link = *e->ep;
+  const int G = link.world(), rank = link.rank(), E = (int)c.n_experts, El = E / G, K = (int)c.top_k;
+  const size_t D = c.dim, R = (size_t)G * p.cap * K;
+  const LayerPtrs& L = e->layers[l];
+  int32_t* h_offs = p.h;
+  int32_t* h_cnt = p.h + E + 1;  // [0, G*El): sent, [G*El, 2*G*El): received
+  int32_t* h_rexp = h_cnt + 2 * G * El;
+  int rc;
+  if (B > 0) {
+    ml_launch_route(md, b.xb, L.router_w, L.router_b, w, s);
+    ml_launch_plan(MlDims{B * K, 0, 0, E, 1, 32}, w, G, p.offs, s);
+    MlTcWork t{};
+    t.xp = p.rows;
+    t.xsp = p.rscale;
+    CK(ml_tc_gather_rows(MlDims{B, (int)D, 0, 1, K, 32}, w, t, s));
+    CK(cudaMemcpyAsync(h_offs, p.offs, (E + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    if ((rc = link.sync(s, msg)) != CHALOT_OK) return rc;
+  } else {
+    std::memset(h_offs, 0, (E + 1) * sizeof(int32_t));
+  }
+  for (int i = 0; i < G * El; ++i) h_cnt[i] = h_offs[i + 1] - h_offs[i];  // rank-major plan offsets
+  CK(cudaMemcpyAsync(p.cnt, h_cnt, G * El * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  std::vector<size_t> sb(G, El * sizeof(int32_t)), rb(G, El * sizeof(int32_t));
+  if ((rc = link.all_to_all(p.cnt, sb.data(), p.cnt + G * El, rb.data(), s, msg)) != CHALOT_OK) return rc;
+  CK(cudaMemcpyAsync(h_cnt + G * El, p.cnt + G * El, G * El * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  if ((rc = link.sync(s, msg)) != CHALOT_OK) return rc;
+  std::vector<size_t> ns(G, 0), nr(G, 0);
+  size_t n_in = 0;
+  for (int g = 0; g < G; ++g) {
+    for (int i = 0; i < El; ++i) {
+      ns[g] += (size_t)h_cnt[g * El + i];
+      nr[g] += (size_t)h_cnt[G * El + g * El + i];
+    }
+    n_in += nr[g];
+  }
+  if (n_in > R) {
+    *msg = "EP: more rows received than reserved (every rank must reserve the same max_seqs)";
+    return CHALOT_ERR_STATE;
+  }
+  size_t k = 0;  // received rows: source-major, then local expert
+  for (int g = 0; g < G; ++g)
+    for (int i = 0; i < El; ++i)
+      for (int r = 0; r < h_cnt[G * El + g * El + i]; ++r) h_rexp[k++] = i;
+  if (n_in) CK(cudaMemcpyAsync(p.rexp, h_rexp, n_in * sizeof(int32_t), cudaMemcpyHostToDevice, s));
+  auto scaled = [&](const std::vector<size_t>& n, size_t unit) {
+    std::vector<size_t> v(G);
+    for (int g = 0; g < G; ++g) v[g] = n[g] * unit;
+    return v;
+  };
+  if ((rc = link.all_to_all(p.rows, scaled(ns, D).data(), p.rrows, scaled(nr, D).data(), s, msg)) != CHALOT_OK)
+    return rc;
+  if ((rc = link.all_to_all(p.rscale, scaled(ns, 4).data(), p.rrscale, scaled(nr, 4).data(), s, msg)) != CHALOT_OK)
+    return rc;
+  if (n_in) {
+    const MlDims xd{(int)n_in, (int)D, (int)c.hidden_dim, El, 1, (int)c.int4_group_size};
+    MlWork xw;
+    const size_t simt = ml_layout(xd, p.ws, &xw);
+    const bool tc = ml_use_tc(xd);
+    MlTcWork xt{};
+    if (tc) ml_tc_layout(xd, simt, p.ws, &xt);
+    xw.sel = p.rexp;
+    xw.xq = p.rrows;
+    xw.xs = p.rrscale;
+    MlExperts X{};
+    for (int i = 0; i < El; ++i) X.ex[i] = b.experts[l].ex[rank + G * i];
+    X.repacked = b.experts[l].repacked;
+    CK(ml_run_rows(xd, X, xw, tc ? &xt : nullptr, p.y, s));
+  }
+  if ((rc = link.all_to_all(p.y, scaled(nr, D * 4).data(), p.yback, scaled(ns, D * 4).data(), s, msg)) != CHALOT_OK)
+    return rc;
+  if (B > 0) {
+    w.y = p.yback;  // w.inv: slot -> position in plan order, w.selw: the gate weights
+    ml_launch_combine(MlDims{B, (int)D, 0, 1, K, 32}, w, b.eout, s);
+  }
+  return CHALOT_OK;
+}
+
 __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e, const uint32_t* slots,
                                                                 const uint32_t* toks, const uint32_t* pos,
                                                                 uint32_t n, uint32_t* out_toks) {
@@ -929,11 +1066,21 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
     for (uint32_t j = 0; j < i; ++j)
       if (slots[j] == slots[i]) return set_error(CHALOT_ERR_ARG, "forward_batch: a slot appears twice");
   }
-  if (n == 0) return CHALOT_OK;
+  if (n == 0 && !e->ep) return CHALOT_OK;
   try {
     CK(cudaSetDevice(e->device));
     cudaStream_t s = e->stream;
     CK(cudaStreamSynchronize(s));  // the pinned staging may still feed a previous call
+    std::string msg;
+    if (e->ep) ep_reserve(e);
+    if (n == 0) {  // no tokens here: still take every exchange of the group
+      const MlDims md0 = batch_moe_dims(e, 0);
+      MlWork w0;
+      ml_layout(md0, b.moe_ws, &w0);
+      for (int l = 0; l < (int)c.n_layers; ++l)
+        if (int rc = ep_moe(e, l, 0, md0, w0, s, &msg)) return set_error(rc, "forward_batch: " + msg);
+      return CHALOT_OK;
+    }
     uint32_t* io = b.h_io;
     std::memcpy(io, slots, n * 4);
     std::memcpy(io + b.cap, toks, n * 4);
@@ -958,8 +1105,12 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
       CK(op_quantize_i8(b.xq, b.xs, b.att, B, D, s));
       b_gemm_i8(B, D, D, L.o, L.o_s, b.xq, b.xs, b.x, D, true, s);  // residual (engine.rs:312-322)
       b_rmsnorm(bd, B, b.x, L.rms_ffn, b.xb, s);
-      CK(tc ? ml_run_tc(md, b.xb, L.router_w, L.router_b, b.experts[l], w, t, b.eout, s)
-            : ml_run(md, b.xb, L.router_w, L.router_b, b.experts[l], w, b.eout, s));
+      if (e->ep) {
+        if (int rc = ep_moe(e, l, B, md, w, s, &msg)) return set_error(rc, "forward_batch: " + msg);
+      } else {
+        CK(tc ? ml_run_tc(md, b.xb, L.router_w, L.router_b, b.experts[l], w, t, b.eout, s)
+              : ml_run(md, b.xb, L.router_w, L.router_b, b.experts[l], w, b.eout, s));
+      }
       b_add((long)B * D, b.x, b.eout, s);  // x += expert_out (engine.rs:401)
       b_norm_quant(bd, B, b.x, l + 1 < (int)c.n_layers ? e->layers[l + 1].rms_attn : e->final_norm, b.xq, b.xs, s);
     }
@@ -987,6 +1138,61 @@ __attribute__((visibility("default"))) int chalot_get_batch_logits(chalot_engine
   } catch (const CudaFail& f) {
     return fail(f);
   }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_ep_nccl_id(uint8_t* id) {
+  if (!id) return set_error(CHALOT_ERR_ARG, "ep_nccl_id: null argument");
+  std::string msg;
+  const int rc = ep_nccl_unique_id(id, &msg);
+  return rc == CHALOT_OK ? CHALOT_OK : set_error(rc, "ep_nccl_id: " + msg);
+}
+
+static int ep_check_attach(chalot_engine* e, uint32_t rank, uint32_t world) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "ep_attach: null engine");
+  if (e->ep) return set_error(CHALOT_ERR_STATE, "ep_attach: already attached");
+  const uint32_t E = (uint32_t)e->cfg.n_experts;
+  if (E < 2) return set_error(CHALOT_ERR_ARG, "ep_attach: expert parallelism needs a MoE model");
+  if (world < 1 || world > E || E % world || rank >= world)
+    return set_error(CHALOT_ERR_ARG, "ep_attach: need world dividing n_experts and rank < world");
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_ep_attach_nccl(chalot_engine* e, uint32_t rank, uint32_t world,
+                                                                const uint8_t* id) {
+  if (int rc = ep_check_attach(e, rank, world)) return rc;
+  if (!id) return set_error(CHALOT_ERR_ARG, "ep_attach: null id");
+  std::string msg;
+  const int rc = ep_nccl_link((int)rank, (int)world, id, e->device, &e->ep, &msg);
+  return rc == CHALOT_OK ? CHALOT_OK : set_error(rc, "ep_attach: " + msg);
+}
+
+__attribute__((visibility("default"))) chalot_ep_hub* chalot_ep_hub_create(uint32_t world) {
+  if (world < 1 || world > 32) {
+    set_error(CHALOT_ERR_ARG, "ep_hub_create: world in [1, 32]");
+    return nullptr;
+  }
+  return reinterpret_cast<chalot_ep_hub*>(ep_hub_create((int)world));
+}
+
+__attribute__((visibility("default"))) void chalot_ep_hub_free(chalot_ep_hub* hub) {
+  ep_hub_release(reinterpret_cast<EpHub*>(hub));
+}
+
+__attribute__((visibility("default"))) int chalot_ep_attach_hub(chalot_engine* e, chalot_ep_hub* hub,
+                                                               uint32_t rank) {
+  if (!hub) return set_error(CHALOT_ERR_ARG, "ep_attach: null hub");
+  EpHub* h = reinterpret_cast<EpHub*>(hub);
+  if (int rc = ep_check_attach(e, rank, (uint32_t)ep_hub_world(h))) return rc;
+  std::string msg;
+  const int rc = ep_hub_link(h, (int)rank, &e->ep, &msg);
+  return rc == CHALOT_OK ? CHALOT_OK : set_error(rc, "ep_attach: " + msg);
+}
+
+__attribute__((visibility("default"))) int chalot_ep_detach(chalot_engine* e) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "ep_detach: null engine");
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  e->ep.reset();
   return CHALOT_OK;
 }
 

@@ -42,6 +42,27 @@ class SamplingConfig:
         return s, stops
 
 
+class EpHub:
+    """An in-process expert-parallel group of `world` engines (chalot_ep_hub)."""
+
+    def __init__(self, world: int):
+        self.world = world
+        self._h = lib().chalot_ep_hub_create(world)
+        if not self._h:
+            check(-1)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().chalot_ep_hub_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def _u32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
 
@@ -49,6 +70,7 @@ def _u32(a) -> np.ndarray:
 class Engine:
     def __init__(self, handle: C.c_void_p):
         self._h = handle
+        self._ep = None
         cfg = ModelConfig()
         check(lib().chalot_get_config(self._h, C.byref(cfg)))
         self.config = cfg.as_dict()
@@ -107,6 +129,34 @@ class Engine:
     def reserve_batch(self, max_seqs: int) -> None:
         check(lib().chalot_batch_reserve(self._h, max_seqs))
 
+    # ---- expert parallelism of the batched forward ----
+
+    def attach_ep_nccl(self, rank: int, world: int, group=None) -> None:
+        """Joins an expert-parallel group of `world` engines over NCCL (one
+        process per GPU). The NCCL id travels over torch.distributed (the
+        default process group, or `group`), from rank 0 to the others."""
+        import torch
+        import torch.distributed as dist
+        idb = (C.c_uint8 * 128)()
+        if rank == 0:
+            check(lib().chalot_ep_nccl_id(idb))
+        t = torch.tensor(list(bytes(idb)), dtype=torch.uint8)
+        if dist.get_backend(group) == "nccl":
+            t = t.cuda()
+        dist.broadcast(t, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        idb = (C.c_uint8 * 128)(*t.cpu().tolist())
+        check(lib().chalot_ep_attach_nccl(self._h, rank, world, idb))
+        self._ep = (rank, world)
+
+    def attach_ep_hub(self, hub: "EpHub", rank: int) -> None:
+        """Joins an in-process group (engines on threads of this process)."""
+        check(lib().chalot_ep_attach_hub(self._h, hub._h, rank))
+        self._ep = (rank, hub.world)
+
+    def detach_ep(self) -> None:
+        check(lib().chalot_ep_detach(self._h))
+        self._ep = None
+
     def forward_batch(self, slots: Sequence[int], tokens: Sequence[int], positions: Sequence[int]) -> list[int]:
         """Engine::forward for several sequences at once (one token each)."""
         s, t, p = _u32(slots), _u32(tokens), _u32(positions)
@@ -120,17 +170,31 @@ class Engine:
         check(lib().chalot_get_batch_logits(self._h, row, v.ctypes.data_as(C.c_void_p), v.size))
         return v
 
-    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new: int) -> list[list[int]]:
+    @staticmethod
+    def batch_steps(prompts: Sequence[Sequence[int]], max_new: int) -> int:
+        """forward_batch calls generate_batch makes for these prompts."""
+        if not prompts:
+            return 0
+        return max(len(list(p) or [0]) for p in prompts) + max_new
+
+    def generate_batch(self, prompts: Sequence[Sequence[int]], max_new: int, reserve: int | None = None,
+                       steps: int | None = None) -> list[list[int]]:
         """Greedy Engine::generate (engine.rs:497-548) of every prompt at once:
         sequence i uses slot i; each call advances every sequence that still
-        has a prompt token or a token to decode. Returns the new tokens."""
+        has a prompt token or a token to decode. Returns the new tokens.
+        In an expert-parallel group every rank must make the same number of
+        forward_batch calls: pass `steps` = the group's maximum of
+        batch_steps(), and `reserve` = the group's common max_seqs."""
         n = len(prompts)
-        self.reserve_batch(n)
+        self.reserve_batch(reserve or max(n, 1))
         prompts = [list(p) or [0] for p in prompts]
         nxt = [0] * n
         out = [[] for _ in range(n)]
-        steps = max(len(p) for p in prompts) + max_new - 1
-        for step in range(steps + 1):
+        own = self.batch_steps(prompts, max_new)
+        total = own if steps is None else steps
+        if total < own:
+            raise ValueError("steps is below this rank's own step count")
+        for step in range(total):
             slots, toks, pos, who = [], [], [], []
             for i, p in enumerate(prompts):
                 if step < len(p):
@@ -143,7 +207,7 @@ class Engine:
                 toks.append(tok)
                 pos.append(step)
                 who.append(i)
-            if not slots:
+            if not slots and not self._ep:
                 break
             res = self.forward_batch(slots, toks, pos)
             for i, r in zip(who, res):

@@ -161,6 +161,36 @@ int chalot_forward_batch(chalot_engine* e, const uint32_t* slots, const uint32_t
 /* Logits of row `row` (the i-th token) of the last chalot_forward_batch. */
 int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst, size_t n);
 
+/* ---- expert parallelism of the batched forward ---------------------------- */
+/* The reference runs one process; these spread the expert block of
+ * Engine::forward (engine.rs:353-401) over a group of engines, one per GPU:
+ * expert e is computed by rank e % world, attention and the other dense parts
+ * by every rank for its own sequences. Per MoE layer chalot_forward_batch then
+ * routes its tokens, sends each (token, choice) row (int8, exact) to the
+ * expert's rank, runs its local experts on the rows it received, sends the
+ * f32 outputs back and combines them in selection order, so every sequence
+ * decodes exactly as on one GPU. All ranks must reserve the same max_seqs and
+ * call chalot_forward_batch the same number of times (n = 0 allowed: the rank
+ * still takes part in the exchanges). Waits on peers are bounded
+ * (CHALOT_ERR_TIMEOUT). */
+
+/* A 128-byte NCCL unique id, made on rank 0 and passed to the others out of
+ * band (e.g. torch.distributed). */
+int chalot_ep_nccl_id(uint8_t* id);
+/* Joins the group `id` as `rank` of `world` over NCCL on the engine's device
+ * (world divides n_experts). */
+int chalot_ep_attach_nccl(chalot_engine* e, uint32_t rank, uint32_t world, const uint8_t* id);
+
+/* In-process group: engines of one process (one per thread) exchange through
+ * a hub; several may share a GPU. For tests of the distributed path. */
+typedef struct chalot_ep_hub chalot_ep_hub;
+chalot_ep_hub* chalot_ep_hub_create(uint32_t world);
+void chalot_ep_hub_free(chalot_ep_hub* hub);
+int chalot_ep_attach_hub(chalot_engine* e, chalot_ep_hub* hub, uint32_t rank);
+
+/* Leaves the group (the engine computes every expert again). */
+int chalot_ep_detach(chalot_engine* e);
+
 /* Device time of the prefill and decode phases of the last chalot_generate,
  * measured with CUDA events on the engine's stream, and the forward counts. */
 int chalot_last_timing(chalot_engine* e, double* prefill_ms, double* decode_ms,
