@@ -231,6 +231,8 @@ def run_ours(args, ws, rank, local):
     barrier(ws)
     clocks = clk.summary()
     ep_res = bench_moe_ep(ws, rank) if ws > 1 else None
+    bep = bench_batch_ep(ws, rank, local) if ws > 1 else None
+    bep_dt = allmax(ws, bep["dt"]) if ws > 1 else None
     # every reduction runs on every rank, before rank 0 alone builds the line
     decode_s = allmax(ws, dev_decode_ms / 1000.0)
     prefill_s = allmax(ws, dev_prefill_ms / 1000.0)
@@ -273,6 +275,12 @@ def run_ours(args, ws, rank, local):
     if ep_res is not None:
         line["moe_layer_prefill_ep"] = dict(ep_res, workload="expert-parallel MoE layer prefill over NCCL, "
                                             "4096 tokens per rank, experts e on rank e % n_gpus", scaling="weak")
+    if bep is not None:
+        line["batch_decode_ep"] = {
+            "workload": "1B-class MoE (d2048 L16 E16 top-2) batched decode, 64 sequences after 256-token "
+                        "prompts split over the ranks, experts e on rank e % n_gpus, token rows over NCCL",
+            "tok_s": BT_SEQS * bep["decode_steps"] / bep_dt, "ms_per_step": bep_dt / bep["decode_steps"] * 1000,
+            "scaling": "strong", "parallelism": f"ep{ws}"}
     eng.close()
     if ws == 1:
         td = bench_tiny()
@@ -587,8 +595,66 @@ def bench_batch(decode_steps: int = 64, warmup: int = 3, cpu: bool = True) -> di
     return res
 
 
+def bench_batch_ep(ws: int, rank: int, local: int, decode_steps: int = 16, warmup: int = 2) -> dict:
+    """The batched decode of bench_batch, expert-parallel over the ws ranks:
+    each rank decodes BT_SEQS/ws of the 64 sequences (the 64-sequence job split
+    over the group: strong scaling) on its GPU, its engine computing the
+    experts e with e % ws == rank and exchanging token rows over NCCL at every
+    MoE layer. Returns this rank's decode wall time; the caller takes the max
+    over ranks."""
+    import numpy as np
+    import torch
+
+    import chalot_c1_b200 as cb
+    torch.cuda.set_device(local)
+    if rank == 0:
+        cb.ensure_shape(model_dir(), "1b")  # written once, by rank 0
+    barrier(ws)
+    path = cb.ensure_shape(model_dir(), "1b")
+    eng = cb.Engine.load(path, device=local)
+    try:
+        eng.attach_ep_nccl(rank, ws)
+        V = eng.config["vocab_size"]
+        prompts = np.random.default_rng(2).integers(0, V, (BT_SEQS, BT_PROMPT))
+        mine = list(range(rank, BT_SEQS, ws))  # the sequences of this rank
+        eng.reserve_batch(-(-BT_SEQS // ws))
+        slots = list(range(len(mine)))
+        nxt = None
+        for p in range(BT_PROMPT):
+            nxt = eng.forward_batch(slots, prompts[mine, p].tolist(), [p] * len(mine))
+        pos = BT_PROMPT
+        for _ in range(warmup):
+            nxt = eng.forward_batch(slots, nxt, [pos] * len(mine))
+            pos += 1
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(decode_steps):
+            nxt = eng.forward_batch(slots, nxt, [pos] * len(mine))
+            pos += 1
+        dt = time.perf_counter() - t0
+        eng.detach_ep()
+    finally:
+        eng.close()
+    return {"dt": dt, "decode_steps": decode_steps}
+
+
 def run_batch(args):
-    print(json.dumps(bench_batch(decode_steps=max(args.steps, 8), warmup=args.warmup)), flush=True)
+    ws, rank, local = dist_setup()
+    try:
+        if ws == 1:
+            print(json.dumps(bench_batch(decode_steps=max(args.steps, 8), warmup=args.warmup)), flush=True)
+            return
+        r = bench_batch_ep(ws, rank, local, decode_steps=max(args.steps, 8), warmup=args.warmup)
+        dt = allmax(ws, r["dt"])
+        if rank == 0:
+            print(json.dumps({"seqs": BT_SEQS, "prompt": BT_PROMPT, "n_gpus": ws, "decode_steps": r["decode_steps"],
+                              "ms_per_step": dt / r["decode_steps"] * 1000,
+                              "tok_s": BT_SEQS * r["decode_steps"] / dt, "parallelism": f"ep{ws}",
+                              "scaling": "strong"}), flush=True)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
 
 
 def run_moe(args):
