@@ -1064,7 +1064,8 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
     if (pos[i] >= c.max_seq_len) return set_error(CHALOT_ERR_ARG, "forward_batch: position beyond max_seq_len");
     if (toks[i] >= c.vocab_size) return set_error(CHALOT_ERR_ARG, "forward_batch: token out of range");
     for (uint32_t j = 0; j < i; ++j)
-      if (slots[j] == slots[i]) return set_error(CHALOT_ERR_ARG, "forward_batch: a slot appears twice");
+      if (slots[j] == slots[i] && pos[j] == pos[i])
+        return set_error(CHALOT_ERR_ARG, "forward_batch: a (slot, position) pair appears twice");
   }
   if (n == 0 && !e->ep) return CHALOT_OK;
   try {

@@ -71,6 +71,7 @@ class Engine:
     def __init__(self, handle: C.c_void_p):
         self._h = handle
         self._ep = None
+        self._cap = 0
         cfg = ModelConfig()
         check(lib().chalot_get_config(self._h, C.byref(cfg)))
         self.config = cfg.as_dict()
@@ -128,6 +129,7 @@ class Engine:
 
     def reserve_batch(self, max_seqs: int) -> None:
         check(lib().chalot_batch_reserve(self._h, max_seqs))
+        self._cap = max(self._cap, max_seqs)
 
     # ---- expert parallelism of the batched forward ----
 
@@ -215,6 +217,58 @@ class Engine:
                 if step >= len(prompts[i]) - 1 and len(out[i]) < max_new:
                     out[i].append(r)
         return out
+
+    def prefill_rows(self, slot: int, tokens: Sequence[int], pos0: int) -> int:
+        """Runs tokens at positions pos0, pos0+1, ... of the sequence in `slot`
+        as rows of chalot_forward_batch (as many per call as the batch holds);
+        returns the argmax after the last token (Engine::forward over each in
+        turn, engine.rs:173)."""
+        if not tokens:
+            raise ValueError("prefill_rows: no tokens")
+        cap = self._cap
+        out = None
+        for i in range(0, len(tokens), cap):
+            chunk = list(tokens[i:i + cap])
+            out = self.forward_batch([slot] * len(chunk), chunk, range(pos0 + i, pos0 + i + len(chunk)))[-1]
+        return out
+
+    def generate_speculative(self, tokens: Sequence[int], max_new: int, draft: "Engine", k: int = 4) -> tuple:
+        """Greedy generate with speculative decoding (src/model/speculative.rs:
+        100-249): `draft` (a cheaper engine with the same vocabulary) proposes
+        k tokens, this engine verifies all of them in one chalot_forward_batch
+        over k+1 positions of the sequence, and the longest agreeing prefix
+        plus this engine's own next token are kept. The reference verifies one
+        candidate per forward; the tokens are this engine's greedy tokens
+        either way. Uses KV slot 0 of both engines. Returns (tokens, accepted,
+        proposed)."""
+        if k < 1:
+            raise ValueError("k must be >= 1")
+        for e in (self, draft):
+            e.reserve_batch(max(k + 1, e._cap or 1))
+        prompt = list(tokens) or [0]
+        room = self.config["max_seq_len"]
+        out = [self.prefill_rows(0, prompt, 0)]
+        draft.prefill_rows(0, prompt, 0)
+        d_have = len(prompt)  # the draft's cache holds positions < d_have
+        accepted = proposed = 0
+        while len(out) < max_new:
+            pos = len(prompt) + len(out) - 1  # position of out[-1]
+            kk = min(k, room - 1 - pos, max_new - len(out))
+            if kk < 1:
+                break
+            seq = prompt + out
+            drafts = [draft.prefill_rows(0, seq[d_have:pos + 1], d_have)]
+            for i in range(1, kk):
+                drafts.append(draft.forward_batch([0], [drafts[-1]], [pos + i])[0])
+            verdict = self.forward_batch([0] * (kk + 1), [out[-1]] + drafts, range(pos, pos + kk + 1))
+            j = 0
+            while j < kk and drafts[j] == verdict[j]:
+                j += 1
+            out.extend(drafts[:j] + [verdict[j]])
+            accepted += j
+            proposed += kk
+            d_have = pos + 1 + min(j, kk - 1)
+        return out[:max_new], accepted, proposed
 
     def sample_from_logits(self, sampling: SamplingConfig | None, history: Sequence[int]) -> int:
         h = _u32(list(history) or [0])

@@ -153,8 +153,12 @@ int chalot_get_logits(chalot_engine* e, float* dst, size_t n);
  * and the batch buffers; once per engine. */
 int chalot_batch_reserve(chalot_engine* e, uint32_t max_seqs);
 
-/* Engine::forward for n sequences: token toks[i] at position pos[i] of the
- * sequence in slot slots[i] (distinct slots); writes each argmax token. */
+/* Engine::forward for n rows: token toks[i] at position pos[i] of the
+ * sequence in slot slots[i]; writes each row's argmax token. A slot may appear
+ * in several rows at distinct positions: every row's K/V is written before
+ * any row attends, so rows p, p+1, ... of one sequence run as consecutive
+ * forwards would (a prompt in one pass, or the k draft tokens of speculative
+ * decoding verified at once; Engine::forward has no batch, engine.rs:173). */
 int chalot_forward_batch(chalot_engine* e, const uint32_t* slots, const uint32_t* toks,
                          const uint32_t* pos, uint32_t n, uint32_t* out_toks);
 
