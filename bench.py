@@ -231,7 +231,12 @@ def run_ours(args, ws, rank, local):
     barrier(ws)
     clocks = clk.summary()
     ep_res = bench_moe_ep(ws, rank) if ws > 1 else None
-    bep = bench_batch_ep(ws, rank, local) if ws > 1 else None
+    bep = None
+    if ws > 1:
+        try:
+            bep = bench_batch_ep(ws, rank, local)
+        except Exception as ex:  # reported in the line; every rank still takes the reductions below
+            bep = {"dt": float("nan"), "decode_steps": 0, "error": str(ex)[:300]}
     bep_dt = allmax(ws, bep["dt"]) if ws > 1 else None
     # every reduction runs on every rank, before rank 0 alone builds the line
     decode_s = allmax(ws, dev_decode_ms / 1000.0)
@@ -275,7 +280,9 @@ def run_ours(args, ws, rank, local):
     if ep_res is not None:
         line["moe_layer_prefill_ep"] = dict(ep_res, workload="expert-parallel MoE layer prefill over NCCL, "
                                             "4096 tokens per rank, experts e on rank e % n_gpus", scaling="weak")
-    if bep is not None:
+    if bep is not None and "error" in bep:
+        line["batch_decode_ep"] = {"error": bep["error"]}
+    elif bep is not None:
         line["batch_decode_ep"] = {
             "workload": "1B-class MoE (d2048 L16 E16 top-2) batched decode, 64 sequences after 256-token "
                         "prompts split over the ranks, experts e on rank e % n_gpus, token rows over NCCL",
