@@ -64,3 +64,12 @@ def router_top_k(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, top_k: int):
     check(lib().chalot_router_topk(_ptr(idx), _ptr(wt), _ptr(x), _ptr(w), _ptr(b), T, dim, E,
                                    top_k, _stream()))
     return idx, wt
+
+
+def probe_int8_mma(iters: int = 20000) -> dict:
+    """Measured int8 tensor-core peak of the current device (chalot_probe_int8_mma):
+    one CTA per SM streams tcgen05.mma.kind::i8 out of shared memory."""
+    import ctypes as C
+    tops, ms = C.c_double(), C.c_double()
+    check(lib().chalot_probe_int8_mma(iters, C.byref(tops), C.byref(ms)))
+    return {"tops": tops.value, "ms": ms.value, "iters": iters}

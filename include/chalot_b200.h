@@ -165,6 +165,13 @@ int chalot_forward_batch(chalot_engine* e, const uint32_t* slots, const uint32_t
 /* Logits of row `row` (the i-th token) of the last chalot_forward_batch. */
 int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst, size_t n);
 
+/* Measured peak of the int8 tensor cores on the current device: one CTA per
+ * SM streams `iters` x 4 tcgen05.mma.kind::i8 M128 x N256 x K32 out of shared
+ * memory; *tops = int8 TOP/s (2 ops per multiply-add), *ms = kernel time.
+ * The denominator of the MoE prefill's tensor roofline; no counterpart in the
+ * reference. */
+int chalot_probe_int8_mma(int iters, double* tops, double* ms);
+
 /* ---- expert parallelism of the batched forward ---------------------------- */
 /* The reference runs one process; these spread the expert block of
  * Engine::forward (engine.rs:353-401) over a group of engines, one per GPU:
