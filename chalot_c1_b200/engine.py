@@ -177,7 +177,7 @@ class Engine:
         """forward_batch calls generate_batch makes for these prompts."""
         if not prompts:
             return 0
-        return max(len(list(p) or [0]) for p in prompts) + max_new
+        return max(len(list(p) or [0]) for p in prompts) + max(max_new - 1, 0)
 
     def generate_batch(self, prompts: Sequence[Sequence[int]], max_new: int, reserve: int | None = None,
                        steps: int | None = None) -> list[list[int]]:
