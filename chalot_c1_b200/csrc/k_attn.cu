@@ -39,7 +39,7 @@ __device__ __forceinline__ void load_k_row(const float* k, float4 (&kr)[C16 * 4]
 template <int C16>  // head_dim / 16
 __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(Dims d, int layer, DecodeBufs b) {
   __shared__ __align__(16) float qh[256];
-  const int slot = layer * 8 + 1;
+  [[maybe_unused]] const int slot = layer * 8 + 1;
   CHALOT_TRACE(slot, 0);
   const int h = blockIdx.y, hd = d.head_dim;
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
@@ -124,7 +124,7 @@ __device__ __forceinline__ void stage_v(float* vt, const float* vbase, int dim, 
 
 __global__ void __launch_bounds__(kPvThreads) k_attn_pv(Dims d, int layer, DecodeBufs b) {
   extern __shared__ __align__(16) float sm[];
-  const int slot = layer * 8 + 2;
+  [[maybe_unused]] const int slot = layer * 8 + 2;
   CHALOT_TRACE(slot, 0);
   float* p = sm;                            // [max_seq] probabilities
   float* vt = sm + ((d.max_seq + 3) & ~3);  // [kPvCols][kPvLd] staged V columns (16-B aligned)

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) k_qkv(Dims d, LayerPtrs L, int layer
   __shared__ __align__(16) int8_t xq[512 * IT];
   __shared__ float red[40];
   __shared__ float xs_s;
-  const int slot = layer * 8 + 0;
+  [[maybe_unused]] const int slot = layer * 8 + 0;
   CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5;
   const int r0 = (blockIdx.x * kWarps + warp) * kQkvRows;
@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   extern __shared__ __align__(16) float osm[];  // tail scratch: xb, wbuf [dim] each, lanes [16E], logit [E]
   __shared__ __align__(16) int8_t xq[512 * IT];
   __shared__ float red[40];
-  const int slot = layer * 8 + 3;
+  [[maybe_unused]] const int slot = layer * 8 + 3;
   CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = (blockIdx.x * kWarps + warp) * kORows;
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(kThreads) k_oproj(Dims d, LayerPtrs L, int lay
   const bool tail = last_cta(b.counters + 1);
   CHALOT_TRACE(slot, 5);
   if (!tail) return;
-  const int tslot = layer * 8 + 6;
+  [[maybe_unused]] const int tslot = layer * 8 + 6;
   CHALOT_TRACE(tslot, 0);
   norm_quant_tail(b.x, wbuf, d.dim, b.xq_ffn, b.xs_ffn, xb, red);
   CHALOT_TRACE(tslot, 2);

@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_gateup(Dims d, LayerPtrs L, int
   __shared__ __align__(16) int8_t xsm[32 * 32 * IT];  // the quantized FFN input (dim <= 1024 * IT)
   __shared__ int e_s;
   __shared__ float xs_s;
-  const int slot = layer * 8 + 4;
+  [[maybe_unused]] const int slot = layer * 8 + 4;
   CHALOT_TRACE(slot, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = d.hidden, chunks = d.dim >> 5, cpg = d.group >> 5, gsh = __ffs(cpg) - 1;
@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 4) k_down(Dims d, LayerPtrs L, int l
                                                    const float* next_norm, DecodeBufs b, int dense,
                                                    int rpc) {
   extern __shared__ __align__(16) unsigned char smem[];
-  const int slot = layer * 8 + 5;
+  [[maybe_unused]] const int slot = layer * 8 + 5;
   CHALOT_TRACE(slot, 0);
   const int H = d.hidden, K = d.top_k, ng = H / d.group, cpg = d.group >> 5, gsh = __ffs(cpg) - 1;
   const int prow = H >> 1, chunks = H >> 5;
