@@ -6,6 +6,7 @@ seconds; the full 512 + 512 run is the benchmark's workload.
 """
 import numpy as np
 import pytest
+from parity import near_tie_report
 
 pytestmark = pytest.mark.gpu
 
@@ -22,7 +23,7 @@ def test_qwen_greedy_identical(chalot, oracle_lib, qwen_model):
     try:
         g = e.generate(prompt, 32)
         c = o.generate(prompt, 32)
-        assert g == c
+        assert g == c, near_tie_report(oracle_lib, qwen_model, prompt, g, c)
         a, b = e.logits(), o.logits()
         assert float(np.max(np.abs(a - b)) / np.max(np.abs(b))) <= 1e-3
     finally:
@@ -41,7 +42,7 @@ def test_1b_shape_greedy_identical(chalot, oracle_lib, model_dir):
     try:
         g = e.generate(prompt, 8)
         c = o.generate(prompt, 8)
-        assert g == c
+        assert g == c, near_tie_report(oracle_lib, path, prompt, g, c)
         a, b = e.logits(), o.logits()
         assert float(np.max(np.abs(a - b)) / np.max(np.abs(b))) <= 1e-3
     finally:
