@@ -150,17 +150,18 @@ struct chalot_engine {
   std::unique_ptr<EpLink> ep;
   struct EpBufs {
     int cap = 0, world = 0;  // sized for cap tokens per rank and world ranks
-    int8_t* rows = nullptr;     // [cap*K][dim] rows to send, in plan order
-    float* rscale = nullptr;    // [cap*K]
-    int8_t* rrows = nullptr;    // [world*cap*K][dim] rows received
-    float* rrscale = nullptr;   // [world*cap*K]
-    int32_t* rexp = nullptr;    // [world*cap*K] local expert of each received row
-    float* y = nullptr;         // [world*cap*K][dim] outputs of the received rows
-    float* yback = nullptr;     // [cap*K][dim] outputs of my rows, in plan order
+    // blocks of R1 = cap*K rows, one per peer
+    int8_t* rows = nullptr;     // [world][R1][dim] rows to send
+    float* rscale = nullptr;    // [world][R1]
+    int8_t* rrows = nullptr;    // [world][R1][dim] rows received
+    float* rrscale = nullptr;   // [world][R1]
+    int32_t* rexp = nullptr;    // [world][R1] local expert of each received row (-1: padding)
+    float* y = nullptr;         // [world][R1][dim] outputs of the received rows
+    float* yback = nullptr;     // [world][R1][dim] outputs of my rows
+    int32_t* ppos = nullptr;    // [cap*K] row of each of my slots in those blocks
     int32_t* offs = nullptr;    // [E+1] plan offsets (rank-major, then local expert)
     int32_t* cnt = nullptr;     // [2][world*El] counts sent / received
-    void* ws = nullptr;         // expert workspace for world*cap*K rows
-    int32_t* h = nullptr;       // pinned: offsets, counts, row experts
+    void* ws = nullptr;         // expert workspace for world*R1 rows
   } epb;
 
   ~chalot_engine() {
@@ -174,7 +175,6 @@ struct chalot_engine {
     if (h_stage) cudaFreeHost(h_stage);
     if (h_tokens) cudaFreeHost(h_tokens);
     if (bt.h_io) cudaFreeHost(bt.h_io);
-    if (epb.h) cudaFreeHost(epb.h);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -934,31 +934,77 @@ __attribute__((visibility("default"))) int chalot_batch_reserve(chalot_engine* e
 }
 
 // ---- expert parallelism of the batched forward --------------------------------
+//
+// Every exchange has a fixed size, so the host never waits for the device in
+// the middle of a forward: rank r sends each peer a block of R1 = cap*top_k
+// rows (the most one rank can route to another; all ranks reserve the same
+// max_seqs), of which the first n are real, n coming from the counts exchange
+// that precedes the rows. The receiving side marks the padding rows invalid
+// (expert -1), which the dispatch of the expert kernels skips.
 
-// Exchange buffers for `cap` tokens per rank (every rank of the group reserves
-// the same max_seqs): a rank receives at most world*cap*top_k rows.
+// Counts per (destination rank, local expert) from the rank-major plan offsets.
+__global__ void k_ep_counts(const int32_t* offs, int n, int32_t* cnt) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) cnt[i] = offs[i + 1] - offs[i];
+}
+
+// One warp per plan position q: copies the int8 row and the scale of slot
+// order[q] into block g (its destination rank) of the send buffer, at row
+// q - (first position of rank g), and records that padded row for the slot.
+__global__ void k_ep_pack(int n_slots, int K, int D, int G, int El, int R1, const int32_t* offs,
+                          const int32_t* order, const int8_t* xq, const float* xs, int8_t* rows, float* rscale,
+                          int32_t* ppos) {
+  const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (q >= n_slots) return;
+  int g = 0;
+  while (g + 1 < G && q >= offs[(g + 1) * El]) ++g;
+  const int dst = g * R1 + (q - offs[g * El]);
+  const int slot = order[q], tok = slot / K;
+  const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)tok * D);
+  uint4* o = reinterpret_cast<uint4*>(rows + (size_t)dst * D);
+  for (int j = lane; j < D / 16; j += 32) o[j] = src[j];
+  if (lane == 0) {
+    rscale[dst] = xs[tok];
+    ppos[slot] = dst;
+  }
+}
+
+// Local expert of every received row: block g holds rcnt[g][0..El) rows in
+// local-expert order, then padding (-1, skipped by the dispatch).
+__global__ void k_ep_row_experts(int G, int El, int R1, const int32_t* rcnt, int32_t* rexp) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= G * R1) return;
+  const int g = i / R1, r = i - g * R1;
+  int acc = 0, ex = -1;
+  for (int k = 0; k < El; ++k) {
+    const int c = rcnt[g * El + k];
+    if (r >= acc && r < acc + c) ex = k;
+    acc += c;
+  }
+  rexp[i] = ex;
+}
+
+// Exchange buffers for `cap` tokens per rank: R1 = cap*top_k rows per peer.
 static void ep_reserve(chalot_engine* e) {
   auto& p = e->epb;
   const ModelConfig& c = e->cfg;
   const int G = e->ep->world();
   if (p.cap == e->bt.cap && p.world == G) return;
   const size_t S = e->bt.cap, K = c.top_k, D = c.dim, E = c.n_experts, El = E / G;
-  const size_t R = (size_t)G * S * K;
-  p.rows = e->dalloc<int8_t>(S * K * D);
-  p.rscale = e->dalloc<float>(S * K);
+  const size_t R = (size_t)G * S * K;  // rows of all blocks, sent or received
+  p.rows = e->dalloc<int8_t>(R * D);
+  p.rscale = e->dalloc<float>(R);
   p.rrows = e->dalloc<int8_t>(R * D);
   p.rrscale = e->dalloc<float>(R);
   p.rexp = e->dalloc<int32_t>(R);
   p.y = e->dalloc<float>(R * D);
-  p.yback = e->dalloc<float>(S * K * D);
+  p.yback = e->dalloc<float>(R * D);
+  p.ppos = e->dalloc<int32_t>(S * K);
   p.offs = e->dalloc<int32_t>(E + 1);
   p.cnt = e->dalloc<int32_t>(2 * G * El);
   const MlDims xd{(int)R, (int)D, (int)c.hidden_dim, (int)El, 1, (int)c.int4_group_size};
   const size_t simt = ml_layout(xd, nullptr, nullptr);
   p.ws = e->dalloc<unsigned char>(ml_tc_eligible(xd) ? ml_tc_layout(xd, simt, nullptr, nullptr) : simt);
-  if (p.h) cudaFreeHost(p.h);
-  p.h = nullptr;
-  CK(cudaMallocHost(&p.h, (E + 1 + 2 * G * El + R) * sizeof(int32_t)));
   p.cap = (int)S;
   p.world = G;
 }
@@ -969,83 +1015,52 @@ static void ep_reserve(chalot_engine* e) {
 // exchange counts, int8 rows and scales, run the local experts on the rows
 // received, send the f32 outputs back and combine them per token in selection
 // order (engine.rs:334-401). Every rank takes the same exchanges in the same
-// order, B == 0 included. Returns a CHALOT_ status.
+// order, B == 0 included; nothing waits for the device. Returns a CHALOT_
+// status.
 static int ep_moe(chalot_engine* e, int l, int B, const MlDims& md, MlWork w, cudaStream_t s, std::string* msg) {
   auto& p = e->epb;
   auto& b = e->bt;
   const ModelConfig& c = e->cfg;
   EpLink& link = *e->ep;
   const int G = link.world(), rank = link.rank(), E = (int)c.n_experts, El = E / G, K = (int)c.top_k;
-  const size_t D = c.dim, R = (size_t)G * p.cap * K;
+  const int R1 = p.cap * K;
+  const size_t D = c.dim, R = (size_t)G * R1;
   const LayerPtrs& L = e->layers[l];
-  int32_t* h_offs = p.h;
-  int32_t* h_cnt = p.h + E + 1;  // [0, G*El): sent, [G*El, 2*G*El): received
-  int32_t* h_rexp = h_cnt + 2 * G * El;
   int rc;
   if (B > 0) {
     ml_launch_route(md, b.xb, L.router_w, L.router_b, w, s);
     ml_launch_plan(MlDims{B * K, 0, 0, E, 1, 32}, w, G, p.offs, s);
-    MlTcWork t{};
-    t.xp = p.rows;
-    t.xsp = p.rscale;
-    CK(ml_tc_gather_rows(MlDims{B, (int)D, 0, 1, K, 32}, w, t, s));
-    CK(cudaMemcpyAsync(h_offs, p.offs, (E + 1) * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-    if ((rc = link.sync(s, msg)) != CHALOT_OK) return rc;
+    k_ep_pack<<<(B * K + 7) / 8, 256, 0, s>>>(B * K, K, (int)D, G, El, R1, p.offs, w.perm, w.xq, w.xs, p.rows,
+                                              p.rscale, p.ppos);
   } else {
-    std::memset(h_offs, 0, (E + 1) * sizeof(int32_t));
+    CK(cudaMemsetAsync(p.offs, 0, (E + 1) * sizeof(int32_t), s));
   }
-  for (int i = 0; i < G * El; ++i) h_cnt[i] = h_offs[i + 1] - h_offs[i];  // rank-major plan offsets
-  CK(cudaMemcpyAsync(p.cnt, h_cnt, G * El * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-  std::vector<size_t> sb(G, El * sizeof(int32_t)), rb(G, El * sizeof(int32_t));
-  if ((rc = link.all_to_all(p.cnt, sb.data(), p.cnt + G * El, rb.data(), s, msg)) != CHALOT_OK) return rc;
-  CK(cudaMemcpyAsync(h_cnt + G * El, p.cnt + G * El, G * El * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
-  if ((rc = link.sync(s, msg)) != CHALOT_OK) return rc;
-  std::vector<size_t> ns(G, 0), nr(G, 0);
-  size_t n_in = 0;
-  for (int g = 0; g < G; ++g) {
-    for (int i = 0; i < El; ++i) {
-      ns[g] += (size_t)h_cnt[g * El + i];
-      nr[g] += (size_t)h_cnt[G * El + g * El + i];
-    }
-    n_in += nr[g];
-  }
-  if (n_in > R) {
-    *msg = "EP: more rows received than reserved (every rank must reserve the same max_seqs)";
-    return CHALOT_ERR_STATE;
-  }
-  size_t k = 0;  // received rows: source-major, then local expert
-  for (int g = 0; g < G; ++g)
-    for (int i = 0; i < El; ++i)
-      for (int r = 0; r < h_cnt[G * El + g * El + i]; ++r) h_rexp[k++] = i;
-  if (n_in) CK(cudaMemcpyAsync(p.rexp, h_rexp, n_in * sizeof(int32_t), cudaMemcpyHostToDevice, s));
-  auto scaled = [&](const std::vector<size_t>& n, size_t unit) {
-    std::vector<size_t> v(G);
-    for (int g = 0; g < G; ++g) v[g] = n[g] * unit;
-    return v;
-  };
-  if ((rc = link.all_to_all(p.rows, scaled(ns, D).data(), p.rrows, scaled(nr, D).data(), s, msg)) != CHALOT_OK)
-    return rc;
-  if ((rc = link.all_to_all(p.rscale, scaled(ns, 4).data(), p.rrscale, scaled(nr, 4).data(), s, msg)) != CHALOT_OK)
-    return rc;
-  if (n_in) {
-    const MlDims xd{(int)n_in, (int)D, (int)c.hidden_dim, El, 1, (int)c.int4_group_size};
-    MlWork xw;
-    const size_t simt = ml_layout(xd, p.ws, &xw);
-    const bool tc = ml_use_tc(xd);
-    MlTcWork xt{};
-    if (tc) ml_tc_layout(xd, simt, p.ws, &xt);
-    xw.sel = p.rexp;
-    xw.xq = p.rrows;
-    xw.xs = p.rrscale;
-    MlExperts X{};
-    for (int i = 0; i < El; ++i) X.ex[i] = b.experts[l].ex[rank + G * i];
-    X.repacked = b.experts[l].repacked;
-    CK(ml_run_rows(xd, X, xw, tc ? &xt : nullptr, p.y, s));
-  }
-  if ((rc = link.all_to_all(p.y, scaled(nr, D * 4).data(), p.yback, scaled(ns, D * 4).data(), s, msg)) != CHALOT_OK)
-    return rc;
+  k_ep_counts<<<1, 1024, 0, s>>>(p.offs, G * El, p.cnt);
+  CK(cudaGetLastError());
+  const std::vector<size_t> cb(G, El * sizeof(int32_t)), rb(G, (size_t)R1 * D), sb(G, (size_t)R1 * 4),
+      yb(G, (size_t)R1 * D * 4);
+  if ((rc = link.all_to_all(p.cnt, cb.data(), p.cnt + G * El, cb.data(), s, msg)) != CHALOT_OK) return rc;
+  if ((rc = link.all_to_all(p.rows, rb.data(), p.rrows, rb.data(), s, msg)) != CHALOT_OK) return rc;
+  if ((rc = link.all_to_all(p.rscale, sb.data(), p.rrscale, sb.data(), s, msg)) != CHALOT_OK) return rc;
+  k_ep_row_experts<<<(unsigned)((R + 255) / 256), 256, 0, s>>>(G, El, R1, p.cnt + G * El, p.rexp);
+  CK(cudaGetLastError());
+  const MlDims xd{(int)R, (int)D, (int)c.hidden_dim, El, 1, (int)c.int4_group_size};
+  MlWork xw;
+  const size_t simt = ml_layout(xd, p.ws, &xw);
+  const bool tc = ml_use_tc(xd);
+  MlTcWork xt{};
+  if (tc) ml_tc_layout(xd, simt, p.ws, &xt);
+  xw.sel = p.rexp;  // -1 on padding rows: not dispatched, their outputs are 0
+  xw.xq = p.rrows;
+  xw.xs = p.rrscale;
+  MlExperts X{};
+  for (int i = 0; i < El; ++i) X.ex[i] = b.experts[l].ex[rank + G * i];
+  X.repacked = b.experts[l].repacked;
+  CK(ml_run_rows(xd, X, xw, tc ? &xt : nullptr, p.y, s));
+  if ((rc = link.all_to_all(p.y, yb.data(), p.yback, yb.data(), s, msg)) != CHALOT_OK) return rc;
   if (B > 0) {
-    w.y = p.yback;  // w.inv: slot -> position in plan order, w.selw: the gate weights
+    w.y = p.yback;   // padded blocks of the outputs of my rows
+    w.inv = p.ppos;  // slot -> its row there
     ml_launch_combine(MlDims{B, (int)D, 0, 1, K, 32}, w, b.eout, s);
   }
   return CHALOT_OK;
