@@ -86,6 +86,7 @@ SIGNATURES = {
     "chalot_forward_batch": (C.c_int, [P, P, P, P, C.c_uint32, P]),
     "chalot_get_batch_logits": (C.c_int, [P, C.c_uint32, P, C.c_size_t]),
     "chalot_probe_int8_mma": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "chalot_myai_validate": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t]),
     "chalot_ep_nccl_id": (C.c_int, [P]),
     "chalot_ep_attach_nccl": (C.c_int, [P, C.c_uint32, C.c_uint32, P]),
     "chalot_ep_hub_create": (P, [C.c_uint32]),

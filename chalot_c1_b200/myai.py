@@ -62,6 +62,15 @@ def inspect(path: str) -> dict:
     return cfg.as_dict()
 
 
+def validate(path: str) -> tuple:
+    """chalot_myai_validate: (ok, report lines)."""
+    buf = C.create_string_buffer(4096)
+    rc = lib().chalot_myai_validate(path.encode(), buf, len(buf))
+    if rc not in (0, -3):
+        check(rc)
+    return rc == 0, [line for line in buf.value.decode().splitlines() if line]
+
+
 def inspect_expected(name: str, **over) -> int:
     """File size of a named shape, from the offset arithmetic alone."""
     kw = dict(SHAPES[name])

@@ -75,6 +75,14 @@ typedef struct chalot_model_config {
 /* Parses the header of a file and computes its size (host only). */
 int chalot_myai_inspect(const char* path, chalot_model_config* out);
 
+/* Checks a whole .myai file (host only): magic, version, flag bits, that the
+ * reserved bytes 32-127 of a v2 header are zero (train_distill.py:898-915
+ * writes the v2 fields there, packed after the v1 ones), the shape, and the
+ * exact size implied by the header (validate_myai.py:99-129 only estimates it
+ * within a factor of two). Returns CHALOT_OK or CHALOT_ERR_FORMAT; `report`
+ * (may be NULL) receives one "error: ..." or "note: ..." line per finding. */
+int chalot_myai_validate(const char* path, char* report, size_t cap);
+
 /* ---- engine ----------------------------------------------------------- */
 
 typedef struct chalot_engine chalot_engine;
