@@ -56,10 +56,9 @@ CHALOT_DEV float hsum8(const float s[8]) {
   return __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
 }
 
-// libm expf as the reference gets it from glibc: evaluated in double and
-// rounded once, i.e. the correctly rounded value, which glibc's expf returns
-// for all but ~0.07% of arguments (where it is 1 ulp away).
-CHALOT_DEV float expf_cr(float x) { return (float)exp((double)x); }
+// libm expf as the reference gets it from glibc (libm::exp_f32, the same
+// method and rounding; libm_f32.h).
+CHALOT_DEV float expf_cr(float x) { return libm::exp_f32(x); }
 
 // SwiGLU of one element at index i of a vector of length n: the first
 // floor(n/8)*8 elements use fast_exp, the tail uses libm exp

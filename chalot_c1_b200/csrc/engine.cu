@@ -24,6 +24,7 @@
 #include <array>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -31,11 +32,13 @@
 
 #include "batch.h"
 #include "capi_internal.h"
+#include "devstat.h"
 #include "ep_link.h"
 #include "kernels.cuh"
 #include "moe_layer.h"
 #include "myai.h"
 #include "pdl.cuh"
+#include "persist.h"
 
 namespace chalot {
 
@@ -127,6 +130,9 @@ struct chalot_engine {
   uint32_t* h_tokens = nullptr;  // pinned, [max_seq]
   uint32_t* d_hist = nullptr;    // [2*max_seq] token history for the penalty
   bool use_graph = true;
+  // the persistent one-kernel decode step (k_persist.cu), when the shape fits
+  bool use_persist = false;
+  PersistArgs pargs{};
   cudaGraphExec_t g_fwd = nullptr;   // embed .. lm_head
   cudaGraphExec_t g_step = nullptr;  // embed .. lm_head + advance
   cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -198,6 +204,12 @@ struct chalot_engine {
     auto mark = [&]() {
       if (marks) cudaEventRecordWithFlags(marks[m++], s, cudaEventRecordExternal);
     };
+    if (use_persist && !marks) {  // the whole step in one cooperative launch
+      CK(launch_persist(pargs, num_sms, s));
+      CK(launch_persist_reset(pargs.bar, pargs.amax, s));
+      if (with_advance) launch_advance(d, b, s, false);
+      return;
+    }
     mark();
     launch_embed(d, emb, emb_s, b, s);
     mark();
@@ -518,6 +530,30 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
     CK(cudaMallocHost(&e->h_stage, e->n_stage * sizeof(StepState)));
     CK(cudaMallocHost(&e->h_tokens, (c.max_seq_len + 1) * sizeof(uint32_t)));
     for (auto& ev : e->ev) CK(cudaEventCreate(&ev));
+    {
+      // the persistent decode kernel when CHALOT_DECODE=persist asks for it
+      // (shapes it does not fit keep the multi-kernel chain)
+      const char* mode = std::getenv("CHALOT_DECODE");
+      PersistArgs& pa = e->pargs;
+      std::string why;
+      if (mode && std::strcmp(mode, "persist") == 0 && persist_plan(e->dims, e->num_sms, &pa.plan, &why)) {
+        pa.d = e->dims;
+        LayerPtrs* dl = e->dalloc<LayerPtrs>(e->layers.size());
+        CK(cudaMemcpy(dl, e->layers.data(), e->layers.size() * sizeof(LayerPtrs), cudaMemcpyHostToDevice));
+        pa.layers = dl;
+        pa.emb = e->emb;
+        pa.emb_s = e->emb_s;
+        pa.final_norm = e->final_norm;
+        pa.out_w = e->out_w;
+        pa.out_s = e->out_s;
+        pa.b = e->b;
+        pa.bar = e->dalloc<unsigned>(kPersistBarWords);
+        pa.amax = e->dalloc<unsigned>(16);
+        pa.err = e->b.err;
+        pa.trace = e->dalloc<unsigned long long>((size_t)(c.n_layers + 1) * 16);
+        e->use_persist = true;
+      }
+    }
     if (e->use_graph) {
       e->g_fwd = e->capture(false);
       e->g_step = e->capture(true);
@@ -812,6 +848,23 @@ __attribute__((visibility("default"))) int chalot_bench_moe_layers(chalot_engine
     cudaFree(x);
     if (ms_per_layer) *ms_per_layer = double(ms) / (double(reps) * L);
     if (bytes_per_layer) *bytes_per_layer = double(K) * double(e->idx.layers[0].experts[0].bytes());
+  } catch (const CudaFail& f) {
+    return fail(f);
+  }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_decode_trace(chalot_engine* e, unsigned long long* dst,
+                                                               size_t n, size_t* n_out) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
+  if (!e->use_persist) return set_error(CHALOT_ERR_STATE, "decode_trace: the engine runs the multi-kernel chain");
+  const size_t total = (size_t)(e->cfg.n_layers + 1) * 16;
+  if (n_out) *n_out = total;
+  if (!dst || n == 0) return CHALOT_OK;
+  try {
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->stream));
+    CK(cudaMemcpy(dst, e->pargs.trace, std::min(n, total) * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
   } catch (const CudaFail& f) {
     return fail(f);
   }
@@ -1135,6 +1188,8 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(io + 3 * b.cap, b.out, n * 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
+    // a tensor-core wait of this forward (or of earlier operator work) that gave up
+    if (int rc = devstat_take("forward_batch")) return rc;
     std::memcpy(out_toks, io + 3 * b.cap, n * 4);
   } catch (const CudaFail& f) {
     return fail(f);

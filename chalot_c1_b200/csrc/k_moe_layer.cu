@@ -32,6 +32,7 @@
 #include "blockops.cuh"
 #include "capi_internal.h"
 #include "common.cuh"
+#include "devstat.h"
 #include "moe_layer.h"
 #include "unpack.cuh"
 
@@ -434,8 +435,7 @@ cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const fl
                       cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
-  cudaError_t r = cudaMemsetAsync(t.err, 0, 16, s);
-  if (r == cudaSuccess) r = cudaMemsetAsync(t.amax, 0, N * 4, s);
+  cudaError_t r = t.err ? cudaMemsetAsync(t.amax, 0, N * 4, s) : cudaErrorInvalidValue;
   if (r != cudaSuccess) return r;
   route_and_dispatch(d, x, rw, rb, w, 128, s);
   if ((r = ml_tc_prepare(d, X, w, t, s)) != cudaSuccess) return r;
@@ -477,8 +477,7 @@ cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, co
   const size_t N = (size_t)d.T;
   k_fill_f32<<<(unsigned)std::min<size_t>((N + 255) / 256, 1024), 256, 0, s>>>(w.selw, N, 1.0f);
   if (t) {
-    cudaError_t r = cudaMemsetAsync(t->err, 0, 16, s);
-    if (r == cudaSuccess) r = cudaMemsetAsync(t->amax, 0, N * 4, s);
+    cudaError_t r = t->err ? cudaMemsetAsync(t->amax, 0, N * 4, s) : cudaErrorInvalidValue;
     if (r != cudaSuccess) return r;
     k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, 128, 1, nullptr);
     if ((r = ml_tc_prepare(d, X, w, *t, s)) != cudaSuccess) return r;
@@ -544,6 +543,8 @@ __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_des
   if (int rc = ml_prepare(desc, n_tok, &d)) return rc;
   if (n_tok == 0) return CHALOT_OK;
   if (!x || !out) return set_error(CHALOT_ERR_ARG, "moe_layer: null x or out");
+  // a tensor-core wait of earlier work that gave up (devstat.h)
+  if (int rc = devstat_poll("moe_layer", static_cast<cudaStream_t>(stream))) return rc;
   const bool tc = use_tc(d);
   const size_t simt = ml_layout(d, nullptr, nullptr);
   const size_t need = tc ? ml_tc_layout(d, simt, nullptr, nullptr) : simt;
@@ -564,13 +565,8 @@ __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_des
   if (r == cudaSuccess && sel_out) r = cudaMemcpyAsync(sel_out, w.sel, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess && selw_out) r = cudaMemcpyAsync(selw_out, w.selw, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
-  if (tc && std::getenv("CHALOT_MOE_SYNC_CHECK")) {  // tests: surface a bounded-wait timeout
-    unsigned err = 0;
-    r = cudaMemcpyAsync(&err, t.err, 4, cudaMemcpyDeviceToHost, s);
-    if (r == cudaSuccess) r = cudaStreamSynchronize(s);
-    if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
-    if (err) return set_error(CHALOT_ERR_TIMEOUT, "moe_layer: a tensor-core pipeline wait timed out");
-  }
+  if (tc && (r = devstat_post(s)) != cudaSuccess)
+    return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
   return CHALOT_OK;
 }
 

@@ -30,6 +30,7 @@
 
 #include "blockops.cuh"
 #include "common.cuh"
+#include "devstat.h"
 #include "moe_layer.h"
 #include "tc.cuh"
 #include "unpack.cuh"
@@ -416,7 +417,8 @@ size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t) {
   w.w8dn = reinterpret_cast<int8_t*>(take((size_t)d.E * d.dim * d.H));
   w.sdn = reinterpret_cast<float*>(take((size_t)d.E * ngh * d.dim * 4));
   w.amax = reinterpret_cast<unsigned*>(take(N * 4));
-  w.err = reinterpret_cast<unsigned*>(take(16));
+  (void)take(16);  // former per-call error word (layout kept)
+  w.err = base ? devstat_word() : nullptr;  // the device's sticky check word (devstat.h)
   if (t) *t = w;
   return off;
 }

@@ -33,6 +33,7 @@
 #include "blockops.cuh"
 #include "capi_internal.h"
 #include "common.cuh"
+#include "devstat.h"
 #include "tc.cuh"
 
 namespace chalot {
@@ -41,9 +42,6 @@ namespace {
 constexpr int kMaxStages = 8;
 constexpr int kMaxCtaPages = 64;  // pages one CTA streams; sets the split count
 constexpr size_t kMaxSmem = 227 * 1024;
-
-// Set by k_paged_store when a page id is out of range (that page is skipped).
-__device__ unsigned g_store_err;
 
 struct PagedDims {
   int P, H, hd, n_pages, n_seq, max_pages, n_split, stages;
@@ -61,7 +59,7 @@ __global__ void __launch_bounds__(256) k_paged_store(PagedDims d, int8_t* data, 
   const int n = d.P * d.hd;
   int page = page_ids[i];
   if (page < 0 || page >= d.n_pages) {  // a bad id is reported, never written through
-    if (threadIdx.x == 0) atomicExch(err, 1u);
+    if (threadIdx.x == 0) atomicOr(err, kDevErrBadPage);
     return;
   }
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
@@ -86,7 +84,7 @@ struct PagedBars {
 
 __device__ __forceinline__ int checked_page(const PagedDims& d, int page, unsigned* err) {
   if (page < 0 || page >= d.n_pages) {
-    atomicExch(err, 1u);
+    atomicOr(err, kDevErrBadPage);
     return 0;  // read an in-bounds page; the call reports the error
   }
   return page;
@@ -363,21 +361,21 @@ __attribute__((visibility("default"))) int chalot_paged_kv_store(const chalot_pa
   if (!page_ids || !k || !v) return set_error(CHALOT_ERR_ARG, "paged_kv_store: null pointer");
   PagedDims d = paged_dims(kv, 0, 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  unsigned* err = nullptr;
-  cudaError_t r = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_store_err);
+  // asynchronous: a page id outside the pool is skipped on the device and
+  // reported by the next operator call or chalot_device_status (devstat.h)
+  if (int rc = devstat_poll("paged_kv_store", s)) return rc;
+  unsigned* err = devstat_word();
+  if (!err) return set_error(CHALOT_ERR_CUDA, "paged_kv_store: device status word unavailable");
   const size_t smem = (size_t)d.P * d.hd * 4;
-  if (r == cudaSuccess && smem > 48 * 1024)
+  cudaError_t r = cudaSuccess;
+  if (smem > 48 * 1024)
     r = cudaFuncSetAttribute(k_paged_store, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (r == cudaSuccess) r = cudaMemsetAsync(err, 0, 4, s);
   if (r == cudaSuccess) {
     k_paged_store<<<dim3((unsigned)n, 2 * d.H), 256, smem, s>>>(d, kv->data, kv->scales, page_ids, k, v, err);
     r = cudaGetLastError();
   }
-  unsigned herr = 0;  // the store is synchronous, as KVPage::write_token is
-  if (r == cudaSuccess) r = cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, s);
-  if (r == cudaSuccess) r = cudaStreamSynchronize(s);
+  if (r == cudaSuccess) r = devstat_post(s);
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("paged_kv_store: ") + cudaGetErrorString(r));
-  if (herr) return set_error(CHALOT_ERR_ARG, "paged_kv_store: a page id is outside [0, n_pages); those pages were skipped");
   return CHALOT_OK;
 }
 
@@ -407,10 +405,12 @@ __attribute__((visibility("default"))) int chalot_paged_attention(const chalot_p
     return set_error(CHALOT_ERR_ARG, "paged_attention: workspace too small (need " + std::to_string(need) + " bytes)");
   PagedDims d = paged_dims(kv, n_seq, max_pages);
   float* part = static_cast<float*>(workspace);
-  unsigned* err = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(workspace) + ((part_bytes(d) + 255) & ~size_t(255)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t r = cudaMemsetAsync(err, 0, 4, s);
-  if (r == cudaSuccess) {
+  if (int rc = devstat_poll("paged_attention", s)) return rc;
+  unsigned* err = devstat_word();  // bad page ids and timed-out waits (devstat.h)
+  if (!err) return set_error(CHALOT_ERR_CUDA, "paged_attention: device status word unavailable");
+  cudaError_t r = cudaSuccess;
+  {
     if (d.hd == 64 && d.P == 16) r = launch_attn<64, 16>(d, kv, page_table, seq_lens, q, part, err, s);
     else if (d.hd == 64 && d.P == 8) r = launch_attn<64, 8>(d, kv, page_table, seq_lens, q, part, err, s);
     else if (d.hd == 64 && d.P == 32) r = launch_attn<64, 32>(d, kv, page_table, seq_lens, q, part, err, s);
@@ -423,13 +423,8 @@ __attribute__((visibility("default"))) int chalot_paged_attention(const chalot_p
     r = cudaGetLastError();
   }
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("paged_attention: ") + cudaGetErrorString(r));
-  if (std::getenv("CHALOT_PAGED_SYNC_CHECK")) {  // tests: surface a bad page id or a wait that ran out
-    unsigned herr = 0;
-    r = cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, s);
-    if (r == cudaSuccess) r = cudaStreamSynchronize(s);
-    if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("paged_attention: ") + cudaGetErrorString(r));
-    if (herr) return set_error(CHALOT_ERR_ARG, "paged_attention: a page id was outside [0, n_pages) or a copy timed out");
-  }
+  if ((r = devstat_post(s)) != cudaSuccess)
+    return set_error(CHALOT_ERR_CUDA, std::string("paged_attention: ") + cudaGetErrorString(r));
   return CHALOT_OK;
 }
 

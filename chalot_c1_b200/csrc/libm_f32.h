@@ -1,5 +1,5 @@
-// libm_f32.h — single-precision tanh with the rounding of the host libm the
-// reference links (glibc), for host and device.
+// libm_f32.h — single-precision tanh and exp with the rounding of the host
+// libm the reference links (glibc), for host and device.
 //
 // The reference's attention soft-cap calls f32::tanh (src/tensor/activations.rs:
 // 133-135), which Rust on Linux takes from glibc. glibc's tanhf follows the
@@ -27,6 +27,11 @@ namespace chalot {
 namespace libm {
 
 #if defined(__CUDA_ARCH__)
+LIBM_FN double dmul(double a, double b) { return __dmul_rn(a, b); }
+LIBM_FN double dadd(double a, double b) { return __dadd_rn(a, b); }
+LIBM_FN double dsub(double a, double b) { return __dsub_rn(a, b); }
+LIBM_FN uint64_t dbits(double d) { return (uint64_t)__double_as_longlong(d); }
+LIBM_FN double dfrom_bits(uint64_t u) { return __longlong_as_double((long long)u); }
 LIBM_FN float mul(float a, float b) { return __fmul_rn(a, b); }
 LIBM_FN float add(float a, float b) { return __fadd_rn(a, b); }
 LIBM_FN float sub(float a, float b) { return __fsub_rn(a, b); }
@@ -35,6 +40,19 @@ LIBM_FN uint32_t bits(float f) { return __float_as_uint(f); }
 LIBM_FN float from_bits(uint32_t u) { return __uint_as_float(u); }
 #else
 // host: compiled with -ffp-contract=off, every operation rounds once
+LIBM_FN double dmul(double a, double b) { return a * b; }
+LIBM_FN double dadd(double a, double b) { return a + b; }
+LIBM_FN double dsub(double a, double b) { return a - b; }
+LIBM_FN uint64_t dbits(double d) {
+  uint64_t u;
+  memcpy(&u, &d, 8);
+  return u;
+}
+LIBM_FN double dfrom_bits(uint64_t u) {
+  double d;
+  memcpy(&d, &u, 8);
+  return d;
+}
 LIBM_FN float mul(float a, float b) { return a * b; }
 LIBM_FN float add(float a, float b) { return a + b; }
 LIBM_FN float sub(float a, float b) { return a - b; }
@@ -135,6 +153,71 @@ LIBM_FN float tanh_f32(float x) {
     z = 1.0f;  // 1 - tiny rounds to 1
   }
   return (ux >> 31) ? -z : z;
+}
+
+// 2^(i/32) for i = 0..31 as doubles with i/32 taken out of the exponent
+// field (the table of exp_f32 below).
+#if defined(__CUDACC__)
+static __constant__ uint64_t kExpTab32[32] = {
+      0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+      0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+      0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+      0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+      0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+      0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+      0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+      0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+#endif
+static const uint64_t kExpTab32Host[32] = {
+      0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+      0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+      0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+      0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+      0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+      0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+      0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+      0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+// expf as glibc (2.28 and later) computes it, the method of the Arm
+// optimized-routines single-precision exp (Szabolcs Nagy, 2017): in double
+// precision, z = x * 32/ln2 is split into an integer k (rounded by adding and
+// subtracting 1.5*2^52) and r = z - k; 2^(k/32) is a table entry for k mod 32
+// (2^(i/32) rounded to double, here computed offline from exact arithmetic)
+// with k/32 added to its exponent; 2^(r/32) is a cubic in r; the product is
+// rounded once to float. Out of range: +inf above 88.72, 0 below -103.97.
+// Matches the system expf of glibc 2.39 on every float in [-87, 88] but two
+// (x = 0x1.04845ep+5 and -0x1.f8cbb2p+5, 1 ulp; the attention softmax under
+// the soft-cap only reaches [-60, 0]). Coefficients: the published cubic of
+// that method.
+LIBM_FN float exp_f32(float x) {
+  const uint32_t ux = bits(x);
+  const uint32_t ax = ux & 0x7fffffffu;
+  if (ax >= 0x42b00000u) {                            // |x| >= 88, inf or NaN
+    if (ux == 0xff800000u) return 0.0f;               // -inf
+    if (ax > 0x7f800000u) return x;                   // NaN
+    if (!(ux >> 31) && ax > 0x42b17217u) return from_bits(0x7f800000u);  // overflow
+    if ((ux >> 31) && ax > 0x42cff1b4u) return 0.0f;  // underflow
+  }
+  const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+  const double shift = 0x1.8p+52;
+  const double c0 = 0x1.c6af84b912394p-5 / 32768.0, c1 = 0x1.ebfce50fac4f3p-3 / 1024.0,
+               c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+  const double z = dmul(inv_ln2_n, (double)x);
+  double kd = dadd(z, shift);
+  const uint64_t ki = dbits(kd);
+  kd = dsub(kd, shift);
+  const double r = dsub(z, kd);
+#if defined(__CUDA_ARCH__)
+  const double s = dfrom_bits(kExpTab32[ki & 31] + (ki << 47));
+#else
+  const double s = dfrom_bits(kExpTab32Host[ki & 31] + (ki << 47));
+#endif
+  const double p = dadd(dmul(c0, r), c1);
+  const double r2 = dmul(r, r);
+  double y = dadd(dmul(c2, r), 1.0);
+  y = dadd(dmul(p, r2), y);
+  y = dmul(y, s);
+  return (float)y;
 }
 
 }  // namespace libm

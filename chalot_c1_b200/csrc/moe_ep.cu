@@ -15,6 +15,7 @@
 #include <string>
 
 #include "capi_internal.h"
+#include "devstat.h"
 #include "moe_layer.h"
 
 using namespace chalot;
@@ -151,6 +152,7 @@ __attribute__((visibility("default"))) int chalot_moe_experts(const chalot_moe_d
   if (!experts_dims(local, n_rows, &m, &why)) return set_error(CHALOT_ERR_ARG, "moe_experts: " + why);
   if (n_rows == 0) return CHALOT_OK;
   if (!rows || !row_scales || !row_expert || !y) return set_error(CHALOT_ERR_ARG, "moe_experts: null pointer");
+  if (int rc = devstat_poll("moe_experts", static_cast<cudaStream_t>(stream))) return rc;
   bool tc;
   const size_t need = experts_need(m, &tc);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
@@ -165,6 +167,7 @@ __attribute__((visibility("default"))) int chalot_moe_experts(const chalot_moe_d
   if (r == cudaSuccess) r = cudaMemcpyAsync(w.xq, rows, n_rows * m.dim, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess) r = cudaMemcpyAsync(w.xs, row_scales, n_rows * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess) r = ml_run_rows(m, ml_experts_from_blob(m, local->experts), w, tc ? &t : nullptr, y, s);
+  if (r == cudaSuccess && tc) r = devstat_post(s);
   return r == cudaSuccess ? CHALOT_OK : cuda_fail("moe_experts", r);
 }
 

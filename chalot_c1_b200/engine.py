@@ -300,6 +300,18 @@ class Engine:
             out[k] = out.get(k, 0.0) + float(v)
         return out
 
+    def decode_trace(self):
+        """Phase timestamps (ns) of the last decode step of the persistent
+        kernel as an array [n_layers + 1][16] (see chalot_decode_trace), or
+        None when the engine runs the multi-kernel chain."""
+        n = C.c_size_t()
+        rc = lib().chalot_decode_trace(self._h, None, 0, C.byref(n))
+        if rc != 0:
+            return None
+        buf = np.zeros(n.value, np.uint64)
+        check(lib().chalot_decode_trace(self._h, buf.ctypes.data_as(C.c_void_p), n.value, C.byref(n)))
+        return buf.reshape(-1, 16)
+
     def bench_moe_layers(self, reps: int = 20) -> tuple[float, float]:
         ms, by = C.c_double(), C.c_double()
         check(lib().chalot_bench_moe_layers(self._h, reps, C.byref(ms), C.byref(by)))

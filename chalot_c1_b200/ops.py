@@ -73,3 +73,13 @@ def probe_int8_mma(iters: int = 20000) -> dict:
     tops, ms = C.c_double(), C.c_double()
     check(lib().chalot_probe_int8_mma(iters, C.byref(tops), C.byref(ms)))
     return {"tops": tops.value, "ms": ms.value, "iters": iters}
+
+
+def device_status(stream=None) -> None:
+    """chalot_device_status: synchronises `stream` (default: the current
+    stream) and raises ChalotError if a device-side check of earlier operator
+    work failed (a bounded wait that gave up, a page id outside a pool). The
+    next operator call on the device raises the same error once that work has
+    finished, without this call."""
+    s = _stream() if stream is None else stream
+    check(lib().chalot_device_status(s))

@@ -44,6 +44,16 @@ extern "C" {
 const char* chalot_last_error(void);
 /* ABI version: major*10000 + minor*100 + patch. */
 int chalot_abi_version(void);
+/* Device-side checks of the asynchronous operators (a bounded wait of the
+ * tensor-core MoE path or of the paged attention that gave up, a page id
+ * outside a paged pool) are recorded on the device and returned by the next
+ * operator call on that device once the failing work has finished
+ * (CHALOT_ERR_TIMEOUT or CHALOT_ERR_ARG), with no synchronisation inside the
+ * calls. This call synchronises `stream` and returns such a status at once
+ * (CHALOT_OK if none); the record is cleared when reported. No reference
+ * counterpart: the reference's ops are synchronous and panic
+ * (src/tensor/matmul.rs:47-54 asserts; src/model/memory.rs:76-84 writes). */
+int chalot_device_status(void* stream);
 
 /* ---- .myai writer (host only) ----------------------------------------- */
 
@@ -222,6 +232,18 @@ int chalot_last_timing(chalot_engine* e, double* prefill_ms, double* decode_ms,
 int chalot_bench_moe_layers(chalot_engine* e, int reps, double* ms_per_layer,
                             double* bytes_per_layer);
 
+/* Phase timestamps of the last decode step when the engine runs the
+ * persistent one-kernel step (the shapes it fits; CHALOT_DECODE=kernels at
+ * load selects the multi-kernel chain, for which this returns
+ * CHALOT_ERR_STATE): %globaltimer ns seen by CTA 0, [n_layers + 1][16]; per
+ * layer 0 start, 1 attention input (after the grid barrier), 2 QKV done,
+ * 3 scores start, 4 scores done, 5 softmax/PV start, 6 PV done, 7 O start,
+ * 8 O done, 9 routing start, 10 expert copies issued, 11 gate/up done,
+ * 12 down start, 13 down done; then the kernel's start, lm_head start and
+ * lm_head end. *n_out receives the element count. No reference counterpart
+ * (measurement of the engine.rs:213-401 layer loop on the device). */
+int chalot_decode_trace(chalot_engine* e, unsigned long long* dst, size_t n, size_t* n_out);
+
 /* Device time of every kernel of one forward (token, pos), in launch order:
  * embed, then per layer qkv, attention scores, attention softmax.PV, O
  * projection (+ routing), gate/up, down; then lm_head. Runs the forward twice
@@ -282,7 +304,9 @@ size_t chalot_moe_workspace_size(const chalot_moe_desc* desc, size_t n_tok);
  * reference's per-token arithmetic. sel_out/selw_out ([n_tok][top_k], may be
  * NULL) receive the router's choices. `workspace` (256-byte aligned, at least
  * chalot_moe_workspace_size bytes) is scratch owned by the caller; calls that
- * share it must not overlap. Asynchronous on `stream`. */
+ * share it must not overlap. Asynchronous on `stream`; a tensor-core wait
+ * that gave up is reported by the next operator call or chalot_device_status
+ * (CHALOT_ERR_TIMEOUT). */
 int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, float* out,
                      int32_t* sel_out, float* selw_out, void* workspace,
                      size_t workspace_bytes, void* stream);
@@ -396,8 +420,10 @@ typedef struct chalot_paged_kv {
 
 /* Quantizes n whole pages into the pool: k and v are f32
  * [n][page_tokens][n_heads][head_dim] (device), the tokens of page page_ids[i]
- * (device int32) in order. Synchronous, as KVPage::write_token
- * (memory.rs:76-84) is. Out-of-range page ids are skipped and reported. */
+ * (device int32) in order. Asynchronous on `stream` (KVPage::write_token,
+ * memory.rs:76-84, is synchronous on the host). Out-of-range page ids are
+ * skipped on the device and reported by the next operator call or by
+ * chalot_device_status (CHALOT_ERR_ARG). */
 int chalot_paged_kv_store(const chalot_paged_kv* kv, const int32_t* page_ids, size_t n,
                           const float* k, const float* v, void* stream);
 
@@ -411,7 +437,9 @@ size_t chalot_paged_attention_workspace_size(const chalot_paged_kv* kv, size_t n
  * page_table[s][0..] ([n_seq][max_pages] int32, device):
  * s_t = 30*tanh((q.k_t / sqrt(head_dim)) / 30), softmax, out = sum_t p_t v_t.
  * q, out: [n_seq][n_heads][head_dim] f32 (device). Float sums are reordered
- * (split pages, online softmax): agreement is to float tolerance, not bits. */
+ * (split pages, online softmax): agreement is to float tolerance, not bits.
+ * Asynchronous; a page id outside the pool is read as page 0 and reported by
+ * the next operator call or chalot_device_status (CHALOT_ERR_ARG). */
 int chalot_paged_attention(const chalot_paged_kv* kv, const float* q, size_t n_seq,
                            const int32_t* page_table, size_t max_pages, const int32_t* seq_lens,
                            float* out, void* workspace, size_t workspace_bytes, void* stream);

@@ -27,14 +27,14 @@ def test_ep_emulated_matches_single_gpu(chalot, monkeypatch, world, path):
     import torch
     from chalot_c1_b200 import ep, moe
     monkeypatch.setenv("CHALOT_MOE_PATH", path)
-    monkeypatch.setenv("CHALOT_MOE_SYNC_CHECK", "1")
     layer = moe.synthetic_moe_layer(896, 4864, 8, 2, 32, seed=3)
     x = torch.from_numpy(np.random.default_rng(3).standard_normal((600, 896), dtype=np.float32)).cuda()
     ref, ref_sel = _single(layer, x)
     cuts = [int(600 * k / world) for k in range(world + 1)]
     backends = [ep.GpuBackend(layer, world, r) for r in range(world)]
     res = ep.emulated_forward(backends, [x[cuts[r]:cuts[r + 1]].contiguous() for r in range(world)])
-    torch.cuda.synchronize()
+    from chalot_c1_b200 import ops
+    ops.device_status()  # no tensor-core wait gave up
     out = torch.cat([o for o, _ in res])
     sel = torch.cat([s for _, s in res])
     assert torch.equal(sel, ref_sel)

@@ -112,8 +112,10 @@ TC_CASES = [
 
 @pytest.fixture
 def tc_path(monkeypatch):
+    from chalot_c1_b200 import ops
     monkeypatch.setenv("CHALOT_MOE_PATH", "tc")
-    monkeypatch.setenv("CHALOT_MOE_SYNC_CHECK", "1")
+    yield
+    ops.device_status()  # no tensor-core wait gave up
 
 
 @pytest.mark.parametrize("dim,hidden,E,K,T", TC_CASES)
@@ -147,8 +149,8 @@ def test_moe_layer_paths_agree_at_prefill_size(moe, monkeypatch):
     monkeypatch.setenv("CHALOT_MOE_PATH", "simt")
     a, sa, _ = moe.MoeLayer(layer, 4096)(x)
     monkeypatch.setenv("CHALOT_MOE_PATH", "tc")
-    monkeypatch.setenv("CHALOT_MOE_SYNC_CHECK", "1")
     b, sb, _ = moe.MoeLayer(layer, 4096)(x)
-    torch.cuda.synchronize()
+    from chalot_c1_b200 import ops
+    ops.device_status()
     assert torch.equal(sa, sb)
     assert torch.equal(a.view(torch.int32), b.view(torch.int32))

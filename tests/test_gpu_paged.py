@@ -58,21 +58,39 @@ def test_attention_matches_oracle(paged, oracle_lib, P, H, hd, lens):
     assert (np.abs(got - ref) <= tol).all(), np.abs(got - ref).max()
 
 
-def test_attention_reports_bad_page(paged, monkeypatch):
+def test_attention_reports_bad_page(paged):
+    """No environment switch: the bad id is reported by chalot_device_status,
+    or by the next operator call once the work finished, and then cleared."""
     import torch
+
+    from chalot_c1_b200 import ops
     from chalot_c1_b200._capi import ChalotError
-    monkeypatch.setenv("CHALOT_PAGED_SYNC_CHECK", "1")
     pool, _, _, _ = _pool(paged, 4, 16, 2, 64, seed=1)
     table = torch.tensor([[0, 1, 99]], dtype=torch.int32, device="cuda")  # 99 is outside the pool
+    good = torch.tensor([[0, 1, 2]], dtype=torch.int32, device="cuda")
     q = torch.zeros((1, 2, 64), device="cuda")
+    lens = torch.tensor([40], dtype=torch.int32, device="cuda")
+    pool.attention(q, table, lens)  # asynchronous: returns before the check
     with pytest.raises(ChalotError, match="outside"):
-        pool.attention(q, table, torch.tensor([40], dtype=torch.int32, device="cuda"))
+        ops.device_status()
+    ops.device_status()  # reported once
+    pool.attention(q, table, lens)
+    torch.cuda.synchronize()
+    with pytest.raises(ChalotError, match="outside"):
+        pool.attention(q, good, lens)  # the next call reports the earlier failure
+    pool.attention(q, good, lens)
+    ops.device_status()
 
 
 def test_store_reports_bad_page(paged):
     import torch
+
+    from chalot_c1_b200 import ops
     from chalot_c1_b200._capi import ChalotError
     pool = paged.PagedKVPool(2, 16, 2, 64)
     k = torch.zeros((1, 16, 2, 64), device="cuda")
+    pool.store(torch.tensor([5], dtype=torch.int32, device="cuda"), k, k)
     with pytest.raises(ChalotError, match="outside"):
-        pool.store(torch.tensor([5], dtype=torch.int32, device="cuda"), k, k)
+        ops.device_status()
+    pool.store(torch.tensor([1], dtype=torch.int32, device="cuda"), k, k)
+    ops.device_status()
