@@ -307,6 +307,18 @@ def run_ours(args, ws, rank, local):
                          "achieved": mo["tops"], "unit": "TOP/s", "peak": i8_peak,
                          "peak_source": i8_src, "frac": mo["tops"] / i8_peak, "nominal_peak": 4500.0},
             "cpu_baseline": mo.get("cpu")}
+        bt = bench_batch(decode_steps=32, warmup=3)
+        line["batch_decode"] = {
+            "workload": "1B-class MoE (d2048 L16 H16 V32000 E16 top-2 g32) batched decode, 64 sequences after "
+                        "256-token prompts, one KV slot each, 32 decode steps of 64 tokens",
+            "tok_s": bt["tok_s"], "ms_per_step": bt["ms_per_step"],
+            "e2e": {"value": bt["e2e_tok_s"], "unit": "tok/s", "h2d_bytes_per_step": BT_SEQS * 12,
+                    "d2h_bytes_per_step": BT_SEQS * 4},
+            "roofline": {"bound": "hbm", "achieved": bt["gbs"], "unit": "GB/s", "peak": pk["hbm_gbs"],
+                         "frac": bt["gbs"] / pk["hbm_gbs"], "peak_source": pk["source"],
+                         "bytes_per_step": bt["bytes_per_step"],
+                         "bytes": "all 16 experts x 16 layers + dense weights + f32 K/V of 64 sequences"},
+            "cpu_baseline": bt["cpu_baseline"]}
         pg = bench_paged(reps=5, warmup=3)
         cpu_tok_s, cpu_sample_s = paged_cpu_sample()
         line["paged_kv_attention"] = {
@@ -568,17 +580,21 @@ BT_SEQS, BT_PROMPT, BT_NEW = 64, 256, 256
 def bench_batch(decode_steps: int = 64, warmup: int = 3, cpu: bool = True) -> dict:
     """Batched decode of the 1B-class MoE (d2048 L16 H16 V32000 E16 top-2
     g32, seed 2): 64 sequences with 256-token prompts (numpy seed 2) prefilled
-    together, position by position, then decoded together. Device time of
-    `decode_steps` batched decode forwards (64 tokens each) after the prompt;
-    the end-to-end figure is the wall time of chalot_forward_batch calls with
-    host tokens in and out."""
+    together, position by position, then decoded together. `decode_steps`
+    batched decode forwards (64 tokens each) after the prompt: device time
+    from CUDA events on the engine's stream (chalot_last_timing), and the
+    end-to-end wall time of the chalot_forward_batch calls with host tokens in
+    and out. Roofline: algorithmic HBM bytes of a step (every expert of every
+    layer, which 64 tokens x top-2 over 16 experts touch; the dense weights;
+    the f32 K/V rows the 64 sequences attend over) per device second."""
     import numpy as np
     import torch
 
     import chalot_c1_b200 as cb
     path = cb.ensure_shape(model_dir(), "1b")
     eng = cb.Engine.load(path)
-    V = eng.config["vocab_size"]
+    cfg = eng.config
+    V, L, D, E = cfg["vocab_size"], cfg["n_layers"], cfg["dim"], cfg["n_experts"]
     prompts = np.random.default_rng(2).integers(0, V, (BT_SEQS, BT_PROMPT))
     eng.reserve_batch(BT_SEQS)
     slots = list(range(BT_SEQS))
@@ -590,21 +606,30 @@ def bench_batch(decode_steps: int = 64, warmup: int = 3, cpu: bool = True) -> di
         nxt = eng.forward_batch(slots, nxt, [pos] * BT_SEQS)
         pos += 1
     torch.cuda.synchronize()
+    dev_ms, kv_bytes, pos0 = 0.0, 0.0, pos
     t0 = time.perf_counter()
     for _ in range(decode_steps):
         nxt = eng.forward_batch(slots, nxt, [pos] * BT_SEQS)
+        dev_ms += eng.last_timing()["decode_ms"]
+        kv_bytes += BT_SEQS * L * (pos + 1) * D * 4 * 2
         pos += 1
     dt = time.perf_counter() - t0
+    expert_bytes = cfg["expert_bytes"]
+    dense = cfg["total_bytes"] - L * E * expert_bytes - V * (D + 4)  # all but the experts and the embedding table
+    step_bytes = L * E * expert_bytes + dense + kv_bytes / decode_steps
     eng.close()
-    res = {"seqs": BT_SEQS, "prompt": BT_PROMPT, "decode_steps": decode_steps,
-           "ms_per_step": dt / decode_steps * 1000, "tok_s": BT_SEQS * decode_steps / dt}
+    res = {"seqs": BT_SEQS, "prompt": BT_PROMPT, "decode_steps": decode_steps, "positions": [pos0, pos - 1],
+           "ms_per_step": dev_ms / decode_steps, "tok_s": BT_SEQS * decode_steps / (dev_ms / 1000.0),
+           "e2e_tok_s": BT_SEQS * decode_steps / dt, "e2e_ms_per_step": dt / decode_steps * 1000,
+           "bytes_per_step": step_bytes, "gbs": step_bytes / (dev_ms / decode_steps / 1000.0) / 1e9}
     if cpu:
         # the reference runs one Engine per sequence, one after another: its
         # rate is one sequence's decode rate on all host threads
         from oracle import oracle as orc
         v, cdt = cpu_sample(path, orc.hw_threads(), n_tokens=8, start=BT_PROMPT)
         res["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": orc.hw_threads(), "kind": "port",
-                               "sample": f"8 decode forwards of one sequence at positions 257-264 ({cdt:.1f} s)"}
+                               "sample": f"8 decode forwards of one sequence at positions 257-264 ({cdt:.1f} s); "
+                                         "the reference decodes the 64 sequences one after another"}
     return res
 
 

@@ -125,9 +125,11 @@ __attribute__((visibility("default"))) int chalot_myai_validate(const char* path
                       first, u(32), u(36), u(40), u(44), u(48), u(52));
         errs.push_back(buf);
       }
-      if (h.n_experts == 1 || h.n_experts > 4096) {
-        std::snprintf(buf, sizeof buf, "n_experts %u (0 for a dense model, else 2 or more)", h.n_experts);
+      if (h.n_experts > 4096) {
+        std::snprintf(buf, sizeof buf, "n_experts %u above 4096", h.n_experts);
         errs.push_back(buf);
+      } else if (h.n_experts == 1) {  // header.rs:17: is_moe = n_experts >= 2, so 1 loads as dense
+        notes.push_back("n_experts 1: read as a dense model (MoE needs 2 or more)");
       }
       if (h.n_experts >= 2 && (h.top_k == 0 || h.top_k > h.n_experts)) {
         std::snprintf(buf, sizeof buf, "top_k %u outside [1, n_experts = %u]", h.top_k, h.n_experts);

@@ -206,7 +206,7 @@ struct chalot_engine {
     };
     if (use_persist && !marks) {  // the whole step in one cooperative launch
       CK(launch_persist(pargs, num_sms, s));
-      CK(launch_persist_reset(pargs.bar, pargs.amax, s));
+      CK(launch_persist_epoch(const_cast<unsigned*>(pargs.epoch), s));
       if (with_advance) launch_advance(d, b, s, false);
       return;
     }
@@ -547,10 +547,14 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
         pa.out_w = e->out_w;
         pa.out_s = e->out_s;
         pa.b = e->b;
-        pa.bar = e->dalloc<unsigned>(kPersistBarWords);
-        pa.amax = e->dalloc<unsigned>(16);
+        pa.ll.x = e->dalloc<uint64_t>(2 * dim);
+        pa.ll.q = e->dalloc<uint64_t>(3 * dim);
+        pa.ll.score = e->dalloc<uint64_t>((size_t)c.n_heads * c.max_seq_len);
+        pa.ll.att = e->dalloc<uint64_t>(dim);
+        pa.ll.h = e->dalloc<uint64_t>((size_t)c.top_k * H);
+        pa.epoch = e->dalloc<unsigned>(1);
         pa.err = e->b.err;
-        pa.trace = e->dalloc<unsigned long long>((size_t)(c.n_layers + 1) * 16);
+        pa.trace = e->dalloc<unsigned long long>((size_t)(c.n_layers + 1) * 32);
         e->use_persist = true;
       }
     }
@@ -858,7 +862,7 @@ __attribute__((visibility("default"))) int chalot_decode_trace(chalot_engine* e,
                                                                size_t n, size_t* n_out) {
   if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
   if (!e->use_persist) return set_error(CHALOT_ERR_STATE, "decode_trace: the engine runs the multi-kernel chain");
-  const size_t total = (size_t)(e->cfg.n_layers + 1) * 16;
+  const size_t total = (size_t)(e->cfg.n_layers + 1) * 32;
   if (n_out) *n_out = total;
   if (!dst || n == 0) return CHALOT_OK;
   try {
@@ -1159,6 +1163,7 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
     CK(cudaMemcpyAsync(b.pos, io + 2 * b.cap, n * 4, cudaMemcpyHostToDevice, s));
     const int B = (int)n, D = (int)c.dim;
     const BatchDims bd{D, (int)c.n_layers, (int)c.n_heads, (int)c.head_dim, (int)c.max_seq_len};
+    CK(cudaEventRecord(e->ev[0], s));
     b_embed(bd, B, b.toks, e->emb, e->emb_s, e->layers[0].rms_attn, b.x, b.xq, b.xs, s);
     const MlDims md = batch_moe_dims(e, B);
     MlWork w;
@@ -1186,8 +1191,17 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
     b_gemm_i8(B, (int)c.vocab_size, D, e->out_w, e->out_s, b.xq, b.xs, b.logits, (int)c.vocab_size, false, s);
     b_argmax(B, (int)c.vocab_size, b.logits, b.out, s);
     CK(cudaGetLastError());
+    CK(cudaEventRecord(e->ev[1], s));
     CK(cudaMemcpyAsync(io + 3 * b.cap, b.out, n * 4, cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
+    {
+      float ms = 0;
+      CK(cudaEventElapsedTime(&ms, e->ev[0], e->ev[1]));
+      e->last_prefill_ms = 0;
+      e->last_decode_ms = ms;
+      e->last_n_prefill = 0;
+      e->last_n_decode = (uint32_t)n;
+    }
     // a tensor-core wait of this forward (or of earlier operator work) that gave up
     if (int rc = devstat_take("forward_batch")) return rc;
     std::memcpy(out_toks, io + 3 * b.cap, n * 4);

@@ -16,8 +16,11 @@
 // code its name is only a host-side stand-in, so the kernels are given the
 // device address that cudaGetSymbolAddress returns; that lookup runs on the
 // first call on each device (with that device current), so the first call on
-// a device should come before any stream capture on it. Every call on a
-// device shares the one array and it keeps the last call's contents: each call
+// a device should come before any stream capture on it. The address is kept
+// for the life of the process: after cudaDeviceReset the library's device
+// copy may move, so this entry point must not be used across a device reset.
+// Every call on a device shares the one array and it keeps the last call's
+// contents: each call
 // writes every scratch byte it reads, so nothing has to start at zero, and two
 // calls whose executions overlap on the GPU (different streams, or different
 // host threads without ordering) race on the array.
@@ -70,8 +73,13 @@ __attribute__((visibility("default"))) int chalot_moe_layer_noalloc(const chalot
                                                                     float* selw_out, void* stream) {
   if (!desc) return set_error(CHALOT_ERR_ARG, "moe_layer_noalloc: null descriptor");
   if (n_tok == 0) return CHALOT_OK;
-  const size_t need = chalot_moe_workspace_size(desc, n_tok);
-  if (need == 0) return CHALOT_ERR_ARG;  // chalot_last_error holds the reason
+  // validation as chalot_moe_layer does it (0: invalid, chalot_last_error says why)
+  if (chalot_moe_workspace_size(desc, n_tok) == 0) return CHALOT_ERR_ARG;
+  const MlDims d{(int)n_tok, (int)desc->dim, (int)desc->hidden_dim, (int)desc->n_experts,
+                 (int)desc->top_k, (int)(desc->group ? desc->group : 32)};
+  // the scratch of the path this entry point runs (ml_run), whatever path
+  // chalot_moe_layer would pick for the shape
+  const size_t need = ml_layout(d, nullptr, nullptr);
   if (need > kNoAllocScratchBytes)
     return set_error(CHALOT_ERR_ARG, "moe_layer_noalloc: " + std::to_string(n_tok) +
                                          " tokens need " + std::to_string(need) +
@@ -84,8 +92,6 @@ __attribute__((visibility("default"))) int chalot_moe_layer_noalloc(const chalot
   if (r != cudaSuccess)
     return set_error(CHALOT_ERR_CUDA, std::string("moe_layer_noalloc: scratch address: ") +
                                           cudaGetErrorString(r));
-  const MlDims d{(int)n_tok, (int)desc->dim, (int)desc->hidden_dim, (int)desc->n_experts,
-                 (int)desc->top_k, (int)(desc->group ? desc->group : 32)};
   MlWork w;
   ml_layout(d, base, &w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

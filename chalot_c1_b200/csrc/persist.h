@@ -10,14 +10,28 @@
 namespace chalot {
 
 constexpr int kPersistThreads = 512;
-constexpr int kPersistBarWords = 32 * 72;  // grid counter + one 128-byte line per head group
-constexpr int kPvTile = 1024;              // positions of V staged per pass
+constexpr int kPvTile = 1024;              // positions of V products per pass
+constexpr int kLmStages = 4;               // lm_head ring stages
+constexpr int kLmChunk = 2 * (kPersistThreads / 32 - 1);  // lm_head rows per stage: two per compute warp
 
 // Shared-memory plan of one CTA (byte offsets) for a model shape on a GPU.
 struct PersistPlan {
-  int o_xq, o_xf, o_xb, o_own, o_red, o_bars, o_P, o_T, o_xh, o_stage;
+  int o_xq, o_xf, o_xb, o_own, o_red, o_bars, o_xp, o_P, o_T, o_xh, o_stage;
+  int o_vs, o_pp, o_vt;  // offsets inside the staging area (attention phase)
+  int o_hf;              // offset inside the staging area of the f32 h (phase F)
+  int ps_gu, ps_dn;      // row strides of the group products (floats, 4 mod 32)
   size_t smem;
   int max_pairs, max_rows;
+};
+
+// Tagged words (64 bits: the f32 value, then the 32-bit tag) through which
+// the CTAs of one step pass values to each other.
+struct PersistLL {
+  uint64_t* x;      // [2][dim] x after the O projection, after the expert block
+  uint64_t* q;      // [3][dim] this step's q, k, v
+  uint64_t* score;  // [n_heads][max_seq]
+  uint64_t* att;    // [dim] attention output
+  uint64_t* h;      // [top_k][hidden] SwiGLU output of the selected experts
 };
 
 struct PersistArgs {
@@ -30,8 +44,8 @@ struct PersistArgs {
   const int8_t* out_w;
   const float* out_s;
   DecodeBufs b;
-  unsigned* bar;   // [kPersistBarWords] barrier counters, zero at launch
-  unsigned* amax;  // [2][8] absmax(h) per layer parity and choice, zero at launch
+  PersistLL ll;
+  const unsigned* epoch;  // step epoch: advanced after every launch
   unsigned* err;   // set when a bounded wait gave up
   // %globaltimer of CTA 0 at the phase boundaries, [n_layers + 1][16]: per
   // layer 0 start, 1 A (after the barrier), 2 A end, 3 B1, 4 B1 end, 5 B2,
@@ -44,7 +58,7 @@ struct PersistArgs {
 bool persist_plan(const Dims& d, int num_sms, PersistPlan* plan, std::string* why);
 // One decode step: embedding .. argmax into b.st->argmax_key (cooperative launch).
 cudaError_t launch_persist(const PersistArgs& a, int num_sms, cudaStream_t s);
-// Zeroes the barrier counters and absmax slots (after each launch_persist).
-cudaError_t launch_persist_reset(unsigned* bar, unsigned* amax, cudaStream_t s);
+// Advances the step epoch (after each launch_persist, in stream order).
+cudaError_t launch_persist_epoch(unsigned* epoch, cudaStream_t s);
 
 }  // namespace chalot

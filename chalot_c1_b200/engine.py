@@ -310,7 +310,7 @@ class Engine:
             return None
         buf = np.zeros(n.value, np.uint64)
         check(lib().chalot_decode_trace(self._h, buf.ctypes.data_as(C.c_void_p), n.value, C.byref(n)))
-        return buf.reshape(-1, 16)
+        return buf.reshape(-1, 32)
 
     def bench_moe_layers(self, reps: int = 20) -> tuple[float, float]:
         ms, by = C.c_double(), C.c_double()

@@ -221,7 +221,9 @@ int chalot_ep_attach_hub(chalot_engine* e, chalot_ep_hub* hub, uint32_t rank);
 int chalot_ep_detach(chalot_engine* e);
 
 /* Device time of the prefill and decode phases of the last chalot_generate,
- * measured with CUDA events on the engine's stream, and the forward counts. */
+ * measured with CUDA events on the engine's stream, and the forward counts.
+ * After a chalot_forward_batch: its device time as decode_ms, its rows as
+ * n_decode, prefill 0. */
 int chalot_last_timing(chalot_engine* e, double* prefill_ms, double* decode_ms,
                        uint32_t* n_prefill, uint32_t* n_decode);
 
@@ -317,13 +319,14 @@ int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, 
  * owns the device's whole memory budget, or a host binding only plain
  * pointers through an FFI. Its scratch is a fixed 4 MiB array inside the
  * library on each device (held by every GPU that loads the library until the
- * process exits); calls needing more (chalot_moe_workspace_size > 4 MiB,
- * e.g. more than 73 tokens at dim 896, hidden 4864, top-2) fail with
- * CHALOT_ERR_ARG. It allocates nothing. The first call on a device looks up
- * the array's device address, so make that call before any stream capture on
- * the device. All calls on a device share the array: calls that overlap on
- * the GPU (other streams or threads without ordering) race. Output matches
- * chalot_moe_layer's bit for bit. */
+ * process exits); calls needing more scratch than that on the path it runs
+ * (the tile-GEMM path; e.g. more than 73 tokens at dim 896, hidden 4864,
+ * top-2) fail with CHALOT_ERR_ARG. It allocates nothing. The first call on a
+ * device looks up the array's device address, so make that call before any
+ * stream capture on the device; the address is kept, so do not use this
+ * entry point across a cudaDeviceReset. All calls on a device share the
+ * array: calls that overlap on the GPU (other streams or threads without
+ * ordering) race. Output matches chalot_moe_layer's bit for bit. */
 int chalot_moe_layer_noalloc(const chalot_moe_desc* desc, const float* x, size_t n_tok,
                              float* out, int32_t* sel_out, float* selw_out, void* stream);
 

@@ -77,3 +77,16 @@ def test_bad_magic(chalot, small, tmp_path):
         f.write(b"XXXX")
     ok, rep = myai.validate(p)
     assert not ok and any("Bad magic" in r for r in rep)
+
+
+def test_one_expert_reads_as_dense(chalot, tmp_path):
+    """src/model/header.rs:17 treats n_experts < 2 as dense: a dense file whose
+    header says n_experts = 1 is valid (with a note), as the reference loads it."""
+    from chalot_c1_b200 import myai
+    p = chalot.write_shape(str(tmp_path / "dense.myai"), "tiny", n_layers=1, vocab_size=256, n_experts=0)
+    with open(p, "r+b") as f:
+        f.seek(128)
+        f.write(struct.pack("<I", 1))
+    ok, rep = myai.validate(p)
+    assert ok, rep
+    assert any("n_experts 1" in r for r in rep)

@@ -49,6 +49,26 @@ def test_noalloc_matches_workspace_entry_point(chalot):
         assert torch.equal(out.view(torch.int32), ref_out.view(torch.int32)), T
 
 
+def test_noalloc_sized_by_its_own_path_when_tc_is_forced(chalot, monkeypatch):
+    """CHALOT_MOE_PATH=tc makes chalot_moe_layer's workspace include the
+    tensor-core buffers; this entry point runs the tile-GEMM path only, so a
+    1-token call still fits its scratch and matches."""
+    import torch
+    from chalot_c1_b200 import moe
+    layer = moe.synthetic_moe_layer(DIM, HIDDEN, E, K, 32, seed=14)
+    dev = moe.MoeLayer(layer, max_tokens=8)
+    x = torch.from_numpy(np.random.default_rng(15).standard_normal((1, DIM), dtype=np.float32)).cuda()
+    ref_out, ref_sel, ref_w = dev(x)
+    monkeypatch.setenv("CHALOT_MOE_PATH", "tc")
+    out = torch.full_like(ref_out, float("nan"))
+    sel = torch.full_like(ref_sel, -1)
+    selw = torch.full_like(ref_w, float("nan"))
+    _noalloc(dev.desc, x, out, sel, selw)
+    torch.cuda.synchronize()
+    assert torch.equal(sel, ref_sel)
+    assert torch.equal(out.view(torch.int32), ref_out.view(torch.int32))
+
+
 def test_noalloc_rejects_sizes_beyond_its_scratch(chalot):
     import torch
     from chalot_c1_b200 import moe
