@@ -99,7 +99,7 @@ __device__ __forceinline__ void rmsnorm_smem(const float* x, const float* __rest
     for (int j = 0; j < 8; ++j) lanes[j] = red[j];
     float ss = hsum8(lanes);
     for (int i = chunks * 8; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
-    red[8] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), 1e-5f)));
+    red[8] = div_rn(1.0f, __fsqrt_rn(__fadd_rn(div_rn(ss, (float)dim), 1e-5f)));
   }
   __syncthreads();
   const float inv = red[8];
@@ -146,7 +146,7 @@ __device__ __forceinline__ void norm_quant_tail(const float* x, const float* wsm
     for (int j = 0; j < 8; ++j) lanes[j] = red[j];
     float ss = hsum8(lanes);
     for (int i = chunks * 8; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
-    red[8] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), 1e-5f)));
+    red[8] = div_rn(1.0f, __fsqrt_rn(__fadd_rn(div_rn(ss, (float)dim), 1e-5f)));
   }
   __syncthreads();
   const float inv = red[8];
@@ -192,7 +192,10 @@ __device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t*
   const float mx = warp_max(v);
   const int full = n & ~7;
   float e = 0.0f;
-  if (lane < n) e = (lane < full) ? fast_exp(__fsub_rn(v, mx)) : expf_cr(__fsub_rn(v, mx));
+  if (lane < full)
+    e = fast_exp(__fsub_rn(v, mx));
+  else if (lane < n)
+    e = expf_cr(__fsub_rn(v, mx));
   // lane j < 8 accumulates e[8c + j] over c in order
   float acc = 0.0f;
   for (int c = 0; c < (full >> 3); ++c) {
@@ -204,7 +207,7 @@ __device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t*
   for (int j = 0; j < 8; ++j) l8[j] = __shfl_sync(0xffffffffu, acc, j);
   float sum = hsum8(l8);
   for (int i = full; i < n; ++i) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, i));
-  const float p = __fmul_rn(e, __fdiv_rn(1.0f, sum));
+  const float p = __fmul_rn(e, div_rn(1.0f, sum));
   // the k rounds of (max probability, lowest index) as ranks: rank r is the
   // pick of round r
   int rank = 0;
@@ -221,7 +224,7 @@ __device__ __forceinline__ void topk_warp(const float* s, int n, int k, int32_t*
   }
   if (live && rank < k) {
     idx[rank] = lane;
-    w[rank] = (tot > 1e-12f) ? __fdiv_rn(p, tot) : p;
+    w[rank] = (tot > 1e-12f) ? div_rn(p, tot) : p;
   }
 }
 

@@ -1,7 +1,7 @@
 // common.cuh — device helpers shared by the sm_100a kernels.
 //
 // Every float operation on a parity-critical path is written with an explicit
-// round-to-nearest intrinsic (__fmul_rn, __fadd_rn, __fdiv_rn, __fsqrt_rn), so
+// round-to-nearest intrinsic (__fmul_rn, __fadd_rn, div_rn, __fsqrt_rn), so
 // the compiler can neither contract it into an FMA nor reorder it; the library
 // is also compiled with --fmad=false. The orders mirror the reference's AVX2
 // code (citations at each helper).
@@ -13,6 +13,8 @@
 #include "libm_f32.h"
 
 namespace chalot {
+
+using libm::div_rn;  // exact division, fast path (libm_f32.h)
 
 #define CHALOT_DEV __device__ __forceinline__
 
@@ -57,15 +59,21 @@ CHALOT_DEV float hsum8(const float s[8]) {
 }
 
 // libm expf as the reference gets it from glibc (libm::exp_f32, the same
-// method and rounding; libm_f32.h).
-CHALOT_DEV float expf_cr(float x) { return libm::exp_f32(x); }
+// method and rounding; libm_f32.h). Out of line: it runs only for the few tail
+// elements of a softmax or SwiGLU, and inlined next to fast_exp under a
+// select, its double arithmetic and table lookup would run for every element.
+static __device__ __noinline__ float expf_cr(float x) { return libm::exp_f32(x); }
 
 // SwiGLU of one element at index i of a vector of length n: the first
 // floor(n/8)*8 elements use fast_exp, the tail uses libm exp
 // (src/tensor/activations.rs:59-87).
 CHALOT_DEV float swiglu_elem(float g, float u, size_t i, size_t n) {
-  float e = (i < (n & ~size_t(7))) ? fast_exp(__fsub_rn(0.0f, g)) : expf_cr(-g);
-  float silu = __fdiv_rn(g, __fadd_rn(1.0f, e));
+  float e;
+  if (i < (n & ~size_t(7)))
+    e = fast_exp(__fsub_rn(0.0f, g));
+  else
+    e = expf_cr(-g);
+  float silu = div_rn(g, __fadd_rn(1.0f, e));
   return __fmul_rn(silu, u);
 }
 
@@ -73,9 +81,9 @@ CHALOT_DEV float swiglu_elem(float g, float u, size_t i, size_t n) {
 // (src/tensor/quantization.rs:77-80).
 CHALOT_DEV void quant_scale(float amax, float* scale, float* inv) {
   amax = fmaxf(amax, 1e-12f);
-  float s = __fdiv_rn(amax, 127.0f);
+  float s = div_rn(amax, 127.0f);
   *scale = s;
-  *inv = __fdiv_rn(1.0f, s);
+  *inv = div_rn(1.0f, s);
 }
 
 // AVX2 quantization of one element: clamp(x*inv, ±127) then cvtps_epi32

@@ -1,5 +1,7 @@
-// devstat.cu — the sticky device-check word of the operator entry points and
-// its asynchronous readback (devstat.h).
+// devstat.cu — the device-check flags of the operator entry points
+// (devstat.h): two words per device in mapped pinned host memory, written by
+// kernels with plain stores (no atomics across the bus) and read by the host
+// without a copy or an event.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -11,18 +13,15 @@
 namespace chalot {
 namespace {
 
-__device__ unsigned g_dev_status;
-
 constexpr int kMaxDevices = 64;
 
-struct Readback {
-  unsigned* host = nullptr;   // pinned: the last readback of the word
-  cudaEvent_t ev = nullptr;   // recorded after that readback
-  bool posted = false;
+struct Flags {
+  unsigned* host = nullptr;  // [2] mapped pinned: timeout, bad page
+  unsigned* dev = nullptr;   // the same words as the device addresses them
 };
 
 std::mutex g_mu;
-Readback g_rb[kMaxDevices];
+Flags g_flags[kMaxDevices];
 
 int current_device() {
   int dev = 0;
@@ -30,76 +29,53 @@ int current_device() {
   return dev;
 }
 
-int report(unsigned bits, const char* who) {
+// The current device's flags, allocated on first use.
+Flags* flags() {
+  const int dev = current_device();
+  if (dev < 0) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Flags& f = g_flags[dev];
+  if (!f.host) {
+    void* h = nullptr;
+    if (cudaHostAlloc(&h, 2 * sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess) return nullptr;
+    void* d = nullptr;
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+      cudaFreeHost(h);
+      return nullptr;
+    }
+    f.host = static_cast<unsigned*>(h);
+    f.host[0] = f.host[1] = 0u;
+    f.dev = static_cast<unsigned*>(d);
+  }
+  return &f;
+}
+
+}  // namespace
+
+unsigned* devstat_word() {
+  Flags* f = flags();
+  return f ? f->dev : nullptr;
+}
+
+int devstat_poll(const char* who, cudaStream_t) {
+  const int dev = current_device();
+  if (dev < 0) return CHALOT_OK;
+  unsigned* h = g_flags[dev].host;
+  if (!h) return CHALOT_OK;
+  volatile unsigned* v = h;
+  const unsigned timeout = v[0], bad_page = v[1];
+  if (!timeout && !bad_page) return CHALOT_OK;
+  v[0] = 0u;
+  v[1] = 0u;
   const std::string w = who ? who : "device";
-  if (bits & kDevErrTimeout)
+  if (timeout)
     return set_error(CHALOT_ERR_TIMEOUT, w + ": a bounded device wait (bulk copy or tensor-core pipeline) "
                                              "gave up in earlier work; its output is invalid");
   return set_error(CHALOT_ERR_ARG, w + ": a page id outside [0, n_pages) was passed to earlier work; "
                                        "that page was skipped and the output is invalid");
 }
 
-}  // namespace
-
-unsigned* devstat_word() {
-  // Looked up on every call: the address belongs to the current device's
-  // module instance.
-  void* p = nullptr;
-  if (cudaGetSymbolAddress(&p, g_dev_status) != cudaSuccess) return nullptr;
-  return static_cast<unsigned*>(p);
-}
-
-int devstat_poll(const char* who, cudaStream_t s) {
-  const int dev = current_device();
-  if (dev < 0) return CHALOT_OK;
-  std::lock_guard<std::mutex> lk(g_mu);
-  Readback& rb = g_rb[dev];
-  if (!rb.posted || cudaEventQuery(rb.ev) != cudaSuccess) return CHALOT_OK;
-  const unsigned bits = *reinterpret_cast<volatile unsigned*>(rb.host);
-  if (!bits) return CHALOT_OK;
-  *reinterpret_cast<volatile unsigned*>(rb.host) = 0u;
-  rb.posted = false;
-  if (unsigned* w = devstat_word()) cudaMemsetAsync(w, 0, sizeof(unsigned), s);
-  return report(bits, who);
-}
-
-cudaError_t devstat_post(cudaStream_t s) {
-  const int dev = current_device();
-  if (dev < 0) return cudaErrorInvalidDevice;
-  unsigned* w = devstat_word();
-  if (!w) return cudaGetLastError();
-  std::lock_guard<std::mutex> lk(g_mu);
-  Readback& rb = g_rb[dev];
-  cudaError_t r = cudaSuccess;
-  if (!rb.host) {
-    void* h = nullptr;
-    r = cudaHostAlloc(&h, sizeof(unsigned), cudaHostAllocDefault);
-    if (r != cudaSuccess) return r;
-    rb.host = static_cast<unsigned*>(h);
-    *rb.host = 0u;
-    r = cudaEventCreateWithFlags(&rb.ev, cudaEventDisableTiming);
-    if (r != cudaSuccess) return r;
-  }
-  r = cudaMemcpyAsync(rb.host, w, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
-  if (r == cudaSuccess) r = cudaEventRecord(rb.ev, s);
-  if (r == cudaSuccess) rb.posted = true;
-  return r;
-}
-
-int devstat_take(const char* who) {
-  unsigned* w = devstat_word();
-  if (!w) return CHALOT_OK;
-  unsigned bits = 0;
-  if (cudaMemcpy(&bits, w, sizeof bits, cudaMemcpyDeviceToHost) != cudaSuccess || !bits) return CHALOT_OK;
-  cudaMemset(w, 0, sizeof(unsigned));
-  const int dev = current_device();
-  if (dev >= 0) {
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (g_rb[dev].host) *reinterpret_cast<volatile unsigned*>(g_rb[dev].host) = 0u;
-    g_rb[dev].posted = false;
-  }
-  return report(bits, who);
-}
+int devstat_take(const char* who) { return devstat_poll(who, nullptr); }
 
 }  // namespace chalot
 

@@ -206,7 +206,7 @@ struct chalot_engine {
     };
     if (use_persist && !marks) {  // the whole step in one cooperative launch
       CK(launch_persist(pargs, num_sms, s));
-      CK(launch_persist_epoch(const_cast<unsigned*>(pargs.epoch), s));
+      CK(launch_persist_epoch(const_cast<unsigned*>(pargs.epoch), pargs.ll.cnt, s));
       if (with_advance) launch_advance(d, b, s, false);
       return;
     }
@@ -553,8 +553,11 @@ __attribute__((visibility("default"))) int chalot_load(const char* path, const c
         pa.ll.att = e->dalloc<uint64_t>(dim);
         pa.ll.h = e->dalloc<uint64_t>((size_t)c.top_k * H);
         pa.epoch = e->dalloc<unsigned>(1);
+        pa.ll.cnt = e->dalloc<unsigned>(kPersistCntWords);
         pa.err = e->b.err;
         pa.trace = e->dalloc<unsigned long long>((size_t)(c.n_layers + 1) * 32);
+        if (std::getenv("CHALOT_TRACE_MAX"))  // diagnostics: every CTA's marks, latest kept
+          pa.trace_max = e->dalloc<unsigned long long>((size_t)(c.n_layers + 1) * 32);
         e->use_persist = true;
       }
     }
@@ -863,12 +866,16 @@ __attribute__((visibility("default"))) int chalot_decode_trace(chalot_engine* e,
   if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
   if (!e->use_persist) return set_error(CHALOT_ERR_STATE, "decode_trace: the engine runs the multi-kernel chain");
   const size_t total = (size_t)(e->cfg.n_layers + 1) * 32;
-  if (n_out) *n_out = total;
+  if (n_out) *n_out = e->pargs.trace_max ? 2 * total : total;
   if (!dst || n == 0) return CHALOT_OK;
   try {
     CK(cudaSetDevice(e->device));
     CK(cudaStreamSynchronize(e->stream));
     CK(cudaMemcpy(dst, e->pargs.trace, std::min(n, total) * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+    if (e->pargs.trace_max && n >= 2 * total) {  // then the latest-CTA marks, cleared for the next step
+      CK(cudaMemcpy(dst + total, e->pargs.trace_max, total * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+      CK(cudaMemset(e->pargs.trace_max, 0, total * sizeof(unsigned long long)));
+    }
   } catch (const CudaFail& f) {
     return fail(f);
   }

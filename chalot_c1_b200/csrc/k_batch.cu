@@ -190,8 +190,8 @@ __global__ void __launch_bounds__(kScoreT) k_b_scores(BatchDims d, int layer, co
 #pragma unroll
   for (int j = 0; j < 8; ++j) cmb[j] = __fadd_rn(a0[j], a1[j]);
   const float dot = hsum8(cmb);
-  const float x = __fmul_rn(dot, __fdiv_rn(1.0f, __fsqrt_rn((float)hd)));
-  scores[((size_t)b * d.n_heads + h) * d.max_seq + t] = __fmul_rn(30.0f, libm::tanh_f32(__fdiv_rn(x, 30.0f)));
+  const float x = __fmul_rn(dot, div_rn(1.0f, __fsqrt_rn((float)hd)));
+  scores[((size_t)b * d.n_heads + h) * d.max_seq + t] = __fmul_rn(30.0f, libm::tanh_f32(div_rn(x, 30.0f)));
 }
 
 constexpr int kPvCols = 8, kPvTile = 1024;
@@ -225,7 +225,10 @@ __global__ void __launch_bounds__(kT) k_b_pv(BatchDims d, int layer, const int32
   mx = block_max(mx, red);
   const int full = n & ~7;
   for (int i = threadIdx.x; i < n; i += blockDim.x)
-    p[i] = (i < full) ? fast_exp(__fsub_rn(p[i], mx)) : expf_cr(__fsub_rn(p[i], mx));
+    if (i < full)
+      p[i] = fast_exp(__fsub_rn(p[i], mx));
+    else
+      p[i] = expf_cr(__fsub_rn(p[i], mx));
   __syncthreads();
   if (threadIdx.x < 8) {  // lane j sums elements 8c+j in c order
     float acc = 0.0f;
@@ -238,7 +241,7 @@ __global__ void __launch_bounds__(kT) k_b_pv(BatchDims d, int layer, const int32
     for (int j = 0; j < 8; ++j) l8[j] = red[j];
     float sum = hsum8(l8);
     for (int i = full; i < n; ++i) sum = __fadd_rn(sum, p[i]);
-    inv_s = __fdiv_rn(1.0f, sum);
+    inv_s = div_rn(1.0f, sum);
   }
   __syncthreads();
   const float inv = inv_s;

@@ -327,7 +327,7 @@ __global__ void k_penalty(Dims d, DecodeBufs b, const uint32_t* __restrict__ his
       const uint32_t t = hist[i];
       if (t < (uint32_t)d.vocab) {
         const float v = b.logits[t];
-        b.logits[t] = (v > 0.0f) ? __fdiv_rn(v, p) : __fmul_rn(v, p);
+        b.logits[t] = (v > 0.0f) ? div_rn(v, p) : __fmul_rn(v, p);
       }
     }
     b.st->argmax_key = 0ull;

@@ -565,8 +565,6 @@ __attribute__((visibility("default"))) int chalot_moe_layer(const chalot_moe_des
   if (r == cudaSuccess && sel_out) r = cudaMemcpyAsync(sel_out, w.sel, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess && selw_out) r = cudaMemcpyAsync(selw_out, w.selw, N * 4, cudaMemcpyDeviceToDevice, s);
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
-  if (tc && (r = devstat_post(s)) != cudaSuccess)
-    return set_error(CHALOT_ERR_CUDA, std::string("moe_layer: ") + cudaGetErrorString(r));
   return CHALOT_OK;
 }
 

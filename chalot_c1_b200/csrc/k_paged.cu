@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(256) k_paged_store(PagedDims d, int8_t* data, 
   const int n = d.P * d.hd;
   int page = page_ids[i];
   if (page < 0 || page >= d.n_pages) {  // a bad id is reported, never written through
-    if (threadIdx.x == 0) atomicOr(err, kDevErrBadPage);
+    if (threadIdx.x == 0) *(volatile unsigned*)(err + 1) = 1u;  // devstat word 1: a bad page id
     return;
   }
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
@@ -84,7 +84,7 @@ struct PagedBars {
 
 __device__ __forceinline__ int checked_page(const PagedDims& d, int page, unsigned* err) {
   if (page < 0 || page >= d.n_pages) {
-    atomicOr(err, kDevErrBadPage);
+    *(volatile unsigned*)(err + 1) = 1u;  // devstat word 1: a bad page id
     return 0;  // read an in-bounds page; the call reports the error
   }
   return page;
@@ -290,7 +290,7 @@ __global__ void k_paged_combine(PagedDims d, const float* __restrict__ part, flo
       L = __fadd_rn(L, __fmul_rn(pi[1], w));
       O = __fadd_rn(O, __fmul_rn(pi[2 + j], w));
     }
-    out[((size_t)s * d.H + h) * d.hd + j] = L > 0.0f ? __fdiv_rn(O, L) : 0.0f;
+    out[((size_t)s * d.H + h) * d.hd + j] = L > 0.0f ? div_rn(O, L) : 0.0f;
   }
 }
 
@@ -374,7 +374,6 @@ __attribute__((visibility("default"))) int chalot_paged_kv_store(const chalot_pa
     k_paged_store<<<dim3((unsigned)n, 2 * d.H), 256, smem, s>>>(d, kv->data, kv->scales, page_ids, k, v, err);
     r = cudaGetLastError();
   }
-  if (r == cudaSuccess) r = devstat_post(s);
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("paged_kv_store: ") + cudaGetErrorString(r));
   return CHALOT_OK;
 }
@@ -423,8 +422,6 @@ __attribute__((visibility("default"))) int chalot_paged_attention(const chalot_p
     r = cudaGetLastError();
   }
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("paged_attention: ") + cudaGetErrorString(r));
-  if ((r = devstat_post(s)) != cudaSuccess)
-    return set_error(CHALOT_ERR_CUDA, std::string("paged_attention: ") + cudaGetErrorString(r));
   return CHALOT_OK;
 }
 

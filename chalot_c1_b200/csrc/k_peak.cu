@@ -59,10 +59,73 @@ __global__ void __launch_bounds__(128, 1) k_mma_i8_peak(int iters, unsigned* err
   }
 }
 
+// Self-check of libm::div_rn (the fast exact division) against the
+// compiler's division: n pseudo-random pairs (splitmix64 from seed) with
+// exponents in [-40, 40], both signs, plus pairs in the ranges the decode path
+// divides (x / 127, x / 30, 1 / x, x / dim); counts bitwise mismatches.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__global__ void k_div_check(uint64_t n, uint64_t seed, unsigned long long* bad, float* example) {
+  unsigned long long local = 0;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = mix64(seed + 0x9E3779B97F4A7C15ull * (i + 1));
+    const uint32_t ea = 127 - 40 + (uint32_t)((r >> 8) % 81), eb = 127 - 40 + (uint32_t)((r >> 16) % 81);
+    float a = __uint_as_float((uint32_t)(r >> 63) << 31 | ea << 23 | ((uint32_t)(r >> 24) & 0x7fffff));
+    float b = __uint_as_float((uint32_t)((r >> 62) & 1) << 31 | eb << 23 | ((uint32_t)(r >> 40) & 0x7fffff));
+    switch (r & 7) {  // divisors of the decode path
+      case 0: b = 127.0f; break;
+      case 1: b = 30.0f; break;
+      case 2: a = 1.0f; break;
+      case 3: b = 896.0f; break;
+      default: break;
+    }
+    const float q = libm::div_rn(a, b), ref = __fdiv_rn(a, b);
+    if (__float_as_uint(q) != __float_as_uint(ref)) {
+      ++local;
+      example[0] = a;
+      example[1] = b;
+    }
+  }
+  if (local) atomicAdd(bad, local);
+}
+
 }  // namespace
 }  // namespace chalot
 
 extern "C" {
+
+__attribute__((visibility("default"))) int chalot_selftest_division(uint64_t n, uint64_t seed, uint64_t* mismatches,
+                                                                    float* example) {
+  using namespace chalot;
+  if (!mismatches) return set_error(CHALOT_ERR_ARG, "selftest_division: null argument");
+  unsigned long long* bad = nullptr;
+  float* ex = nullptr;
+  cudaError_t r = cudaMalloc(&bad, sizeof(unsigned long long));
+  if (r == cudaSuccess) r = cudaMalloc(&ex, 2 * sizeof(float));
+  if (r == cudaSuccess) r = cudaMemset(bad, 0, sizeof(unsigned long long));
+  if (r == cudaSuccess) r = cudaMemset(ex, 0, 2 * sizeof(float));
+  if (r == cudaSuccess) {
+    k_div_check<<<1184, 256>>>(n, seed, bad, ex);
+    r = cudaDeviceSynchronize();
+  }
+  unsigned long long h = 0;
+  float he[2] = {0, 0};
+  if (r == cudaSuccess) r = cudaMemcpy(&h, bad, sizeof h, cudaMemcpyDeviceToHost);
+  if (r == cudaSuccess) r = cudaMemcpy(he, ex, sizeof he, cudaMemcpyDeviceToHost);
+  if (bad) cudaFree(bad);
+  if (ex) cudaFree(ex);
+  if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("selftest_division: ") + cudaGetErrorString(r));
+  *mismatches = h;
+  if (example) {
+    example[0] = he[0];
+    example[1] = he[1];
+  }
+  return CHALOT_OK;
+}
+
 
 __attribute__((visibility("default"))) int chalot_probe_int8_mma(int iters, double* tops, double* ms) {
   using namespace chalot;

@@ -74,13 +74,50 @@ CHALOT_DEV uint64_t ll_load(const uint64_t* p) {
   return w;
 }
 
+// Announces that this CTA wrote its part of a broadcast: one relaxed add on
+// each of the kCntLines counter lines of `cnt` (the tagged words themselves
+// still validate every value).
+constexpr int kCntLines = 8;
+CHALOT_DEV void ll_announce(unsigned* cnt) {
+  __syncthreads();
+  if (threadIdx.x < kCntLines)
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], 1;" ::"l"(cnt + 32 * threadIdx.x) : "memory");
+}
+
+// Waits (one thread, bounded, with a short back-off) until counter line
+// c % kCntLines of `cnt` reaches `target`: every producer of the broadcast
+// has announced, so the following gather finds its words written. Only a
+// few CTAs poll each line.
+__device__ __noinline__ bool ll_wait_count(const unsigned* cnt, unsigned target, unsigned* err, int* fail_s) {
+  if (threadIdx.x == 0) {
+    const unsigned* p = cnt + 32 * (blockIdx.x % kCntLines);
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    if (v < target) {
+      const unsigned long long t0 = gtimer();
+      for (int k = 1;; ++k) {
+        __nanosleep(32);
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= target) break;
+        if ((k & 63) == 0 && (*(volatile unsigned*)err || gtimer() - t0 > kWaitNs)) {
+          atomicOr(err, 1u);
+          *(volatile int*)fail_s = 1;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return *(volatile int*)fail_s == 0;
+}
+
 // dst[i] = value of p[i] for i < n, each word waited for until it carries
 // `tag`. Every thread of the CTA calls it; the values are in shared memory
 // after the barrier at the end. False (the error word set, or seen set) when
 // a wait ran out.
 __device__ __noinline__ bool ll_gather(const uint64_t* p, int n, uint32_t tag, float* dst, unsigned* err,
                                        int* fail_s) {
-  constexpr int U = 8;
+  constexpr int U = 10;
   bool ok = true;
   for (int base = 0; base < n && ok; base += U * kT) {
     uint64_t w[U];
@@ -222,35 +259,41 @@ CHALOT_DEV void load4(const float* __restrict__ w, int dim, float (&wr)[4]) {
   }
 }
 
-// rmsnorm_avx2 (normalization.rs:35-67) of xs (shared, dim floats) with the
-// weights wr (load4) into xb (shared), then quantize_f32_to_i8
-// (quantization.rs:56-104) into xq (shared); returns the scale.
-CHALOT_DEV float norm_quant_smem(const float* xs, const float (&wr)[4], int dim, float* xb, int8_t* xq,
-                                 float* red) {
-  const int chunks = dim >> 3;
-  if (threadIdx.x < 8) {
-    float s = 0.0f;
-    int c = 0;
-    for (; c + 16 <= chunks; c += 16) {
-      float v[16];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) v[u] = xs[(c + u) * 8 + threadIdx.x];
-#pragma unroll
-      for (int u = 0; u < 16; ++u) s = __fadd_rn(s, __fmul_rn(v[u], v[u]));
-    }
-    for (; c < chunks; ++c) {
-      const float v = xs[c * 8 + threadIdx.x];
-      s = __fadd_rn(s, __fmul_rn(v, v));
-    }
-    red[threadIdx.x] = s;
-  }
+// Block-wide maximum of non-negative values with one barrier; every thread
+// gets it. `part` (kW floats, 16-byte aligned) must not be in use by a
+// concurrent call.
+CHALOT_DEV float block_max1(float v, float* part) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float l8[8];
-    for (int j = 0; j < 8; ++j) l8[j] = red[j];
-    float ss = hsum8(l8);
-    for (int i = chunks * 8; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
-    red[8] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), 1e-5f)));
+  float m = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kW; w += 4) {
+    const float4 q = lds16f(part + w);
+    m = fmaxf(fmaxf(m, q.x), fmaxf(fmaxf(q.y, q.z), q.w));
+  }
+  return m;
+}
+
+// rmsnorm_avx2 (normalization.rs:35-67) of xs (shared, dim floats, dim % 8
+// == 0) with the weights wr (load4) into xb (shared), then
+// quantize_f32_to_i8 (quantization.rs:56-104) into xq (shared); returns the
+// scale. Lane j of 8 adds x[8c+j]^2 over c in order: the squares are first
+// written column by column (sq: 8 rows of `sqs` floats) so each lane's chain
+// reads them with vector loads; the 8 lane sums are combined as hsum8 with
+// shuffles.
+CHALOT_DEV float norm_quant_smem(const float* xs, const float (&wr)[4], int dim, float* xb, int8_t* xq,
+                                 float* red, float* sq, int sqs) {
+  const int nc = dim >> 3;
+  for (int i = threadIdx.x; i < dim; i += kT) sq[(i & 7) * sqs + (i >> 3)] = __fmul_rn(xs[i], xs[i]);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const float sj = lane < 8 ? ordered_sum16(sq + lane * sqs, nc) : 0.0f;
+    const float t = __fadd_rn(sj, __shfl_down_sync(0xffffffffu, sj, 4));  // t_j = s_j + s_{j+4}
+    const float u = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2));    // t0 + t2, t1 + t3
+    const float ss = __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 1));
+    if (lane == 0) red[8] = div_rn(1.0f, __fsqrt_rn(__fadd_rn(div_rn(ss, (float)dim), 1e-5f)));
   }
   __syncthreads();
   const float inv = red[8];
@@ -265,8 +308,12 @@ CHALOT_DEV float norm_quant_smem(const float* xs, const float (&wr)[4], int dim,
     }
   }
   float scale, qinv;
-  quant_scale(block_max(m, red), &scale, &qinv);
-  for (int i = threadIdx.x; i < dim; i += kT) xq[i] = quant_any(xb[i], qinv, i, dim);
+  quant_scale(block_max1(m, red + 32), &scale, &qinv);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int i = threadIdx.x + u * kT;
+    if (i < dim) xq[i] = quant_any(xb[i], qinv, i, dim);
+  }
   __syncthreads();
   return scale;
 }
@@ -315,6 +362,7 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
   float* Tt = reinterpret_cast<float*>(sm + pl.o_T);        // row totals
   int8_t* xh = reinterpret_cast<int8_t*>(sm + pl.o_xh);     // [K][H] quantized h
   ExpertPtrs* xp_s = reinterpret_cast<ExpertPtrs*>(sm + pl.o_xp);  // [E] this layer's experts
+  float* sq = reinterpret_cast<float*>(sm + pl.o_sq);        // [8][sqs] squares of the norm
   unsigned char* stg = sm + pl.o_stage;                     // K/V, router weights, expert rows, lm_head rows
   __shared__ int fail_s;
   __shared__ int sel_s[8];
@@ -344,8 +392,14 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
   // rows of x (O rows, down rows) owned by this CTA
   const int r0 = (int)(((long)c * dim) / NC), r1 = (int)(((long)(c + 1) * dim) / NC), nr = r1 - r0;
   unsigned long long* tr = (a.trace && c == 0 && tid == 0) ? a.trace : nullptr;
+  // with a.trace_max: the latest time any CTA reached each mark
+  unsigned long long* trm = (a.trace_max && tid == 0) ? a.trace_max : nullptr;
   auto mark = [&](int slot) {
     if (tr) tr[slot] = gtimer();
+    if (trm) asm volatile("red.relaxed.gpu.global.max.u64 [%0], %1;" ::"l"(trm + slot), "l"(gtimer()) : "memory");
+  };
+  auto mark_clk = [&](int slot) {  // SM clock cycles (with the ns marks: the clock rate)
+    if (tr) tr[slot] = clock64();
   };
   mark(32 * d.n_layers + 0);
   prefetch_kv<HD>(b, d, 0, h, (int)pos, t0, t1, k0, ncol, ks, vs);
@@ -361,11 +415,12 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
   const int np_h = 3 * HD / 2;  // Q, K, V row pairs of one head
   const int pq0 = (gj * np_h) / gs, pq1 = ((gj + 1) * np_h) / gs;
   const int half = HD >> 1;
-  const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
+  const float inv_sqrt = div_rn(1.0f, __fsqrt_rn((float)HD));
   float wn[4];  // norm weights of the next normalisation, requested before its wait
   for (int l = 0; l < d.n_layers; ++l) {
     const LayerPtrs& L = a.layers[l];
     mark(l * 32 + 0);
+    mark_clk(l * 32 + 30);
     // ---- A: QKV of head h ----
     // before the wait: this warp's first row pair, its scales and rotation,
     // the norm weights
@@ -387,10 +442,12 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
       }
       load4(L.rms_attn, dim, wn);
     }
-    if (l > 0 && !ll_gather(ll.x + dim, dim, tag(l - 1, kTagXf), xf, a.err, &fail_s)) break;
+    if (l > 0 && !(ll_wait_count(ll.cnt + kCntXf, (unsigned)(NC * l), a.err, &fail_s) &&
+                   ll_gather(ll.x + dim, dim, tag(l - 1, kTagXf), xf, a.err, &fail_s)))
+      break;
     mark(l * 32 + 1);
     {
-      const float s = norm_quant_smem(xf, wn, dim, xb, xq, red);
+      const float s = norm_quant_smem(xf, wn, dim, xb, xq, red, sq, pl.sqs);
       mark(l * 32 + 16);
       for (int p = pq0 + warp; p < pq1; p += kW) {
         const int sec = p / half, i = p % half;
@@ -460,7 +517,7 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) cmb[j] = __fadd_rn(a0[j], a1[j]);
         const float x = __fmul_rn(hsum8(cmb), inv_sqrt);
-        ll_store(ll.score + (size_t)h * d.max_seq + t, __fmul_rn(30.0f, libm::tanh_f32(__fdiv_rn(x, 30.0f))),
+        ll_store(ll.score + (size_t)h * d.max_seq + t, __fmul_rn(30.0f, libm::tanh_f32(div_rn(x, 30.0f))),
                  tag(l, kTagScore));
       }
     }
@@ -471,34 +528,41 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
       if (!ll_gather(ll.q + 2 * dim + h * HD + k0, ncol, tag(l, kTagQkv), vs + (size_t)pos * ncol, a.err, &fail_s))
         break;
       mark(l * 32 + 5);
+      // softmax_avx2 (normalization.rs:106-160): max; e = fast_exp(s - max) on
+      // whole 8-chunks, libm exp on the tail; lane j of 8 adds e[8c+j] over c
+      // in order (the e of the chunks also written column by column, eT, for
+      // vector loads), hsum8, then the tail in order; inv = 1/sum.
       float mx = -INFINITY;
       for (int i = tid; i < n; i += kT) mx = fmaxf(mx, pp[i]);
-      mx = block_max(mx, red);
-      const int full = n & ~7;
-      for (int i = tid; i < n; i += kT)
-        pp[i] = (i < full) ? fast_exp(__fsub_rn(pp[i], mx)) : expf_cr(__fsub_rn(pp[i], mx));
-      __syncthreads();
-      if (tid < 8) {
-        float acc = 0.0f;
-        const int nc8 = full >> 3;
-        int cc = 0;
-        for (; cc + 8 <= nc8; cc += 8) {
-          float v[8];
+      {  // block max (scores may be negative)
+        mx = warp_max(mx);
+        if (lane == 0) red[32 + warp] = mx;
+        __syncthreads();
+        mx = red[32];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = pp[(cc + u) * 8 + tid];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, v[u]);
-        }
-        for (; cc < nc8; ++cc) acc = __fadd_rn(acc, pp[cc * 8 + tid]);
-        red[tid] = acc;
+        for (int w = 1; w < kW; ++w) mx = fmaxf(mx, red[32 + w]);
+      }
+      const int full = n & ~7, nc8 = full >> 3, es = pl.ets;
+      float* eT = vt;  // [8][es]: the chunk part of e by lane (the products come later)
+      for (int i = tid; i < n; i += kT) {
+        float e;
+        if (i < full)
+          e = fast_exp(__fsub_rn(pp[i], mx));
+        else
+          e = expf_cr(__fsub_rn(pp[i], mx));
+        pp[i] = e;
+        if (i < full) eT[(i & 7) * es + (i >> 3)] = e;
       }
       __syncthreads();
-      if (tid == 0) {
-        float l8[8];
-        for (int j = 0; j < 8; ++j) l8[j] = red[j];
-        float sum = hsum8(l8);
-        for (int i = full; i < n; ++i) sum = __fadd_rn(sum, pp[i]);
-        red[9] = __fdiv_rn(1.0f, sum);
+      if (warp == 0) {
+        const float sj = lane < 8 ? ordered_sum16(eT + lane * es, nc8) : 0.0f;
+        const float t = __fadd_rn(sj, __shfl_down_sync(0xffffffffu, sj, 4));
+        const float u = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2));
+        float sum = __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 1));
+        if (lane == 0) {
+          for (int i = full; i < n; ++i) sum = __fadd_rn(sum, pp[i]);
+          red[9] = div_rn(1.0f, sum);
+        }
       }
       __syncthreads();
       mark(l * 32 + 17);
@@ -579,6 +643,7 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
           ll_store(ll.x + r0 + w, own[w], tag(l, kTagXc));
         }
       }
+      ll_announce(ll.cnt + kCntXc);
     }
     mark(l * 32 + 8);
     // before the wait: FFN norm weights, router bias, this layer's expert pointers
@@ -587,14 +652,15 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
       rb_s[tid] = __ldg(L.router_b + tid);
       xp_s[tid] = layer_expert(L, E, tid);
     }
-    if (!ll_gather(ll.x, dim, tag(l, kTagXc), xf, a.err, &fail_s)) {
+    if (!(ll_wait_count(ll.cnt + kCntXc, (unsigned)(NC * (l + 1)), a.err, &fail_s) &&
+          ll_gather(ll.x, dim, tag(l, kTagXc), xf, a.err, &fail_s))) {
       if (tid == 0) mbar_wait_t(&bars[2], l & 1, a.err);
       break;
     }
     mark(l * 32 + 9);
     // ---- D: FFN norm, quantize, routing (engine.rs:325-344) ----
     {
-      const float s = norm_quant_smem(xf, wn, dim, xb, xq, red);
+      const float s = norm_quant_smem(xf, wn, dim, xb, xq, red, sq, pl.sqs);
       mark(l * 32 + 19);
       float* lanes = rw_s + (size_t)E * dim;  // [16E]
       float* logit = lanes + 16 * E;
@@ -606,9 +672,11 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
       mark(l * 32 + 21);
       if (warp == 0) topk_warp(logit, E, K, sel_s, selw_s);
       if (tid == 0) xs_s = s;
+      mark(l * 32 + 14);
       if (c == 0 && b.router_trace)
         for (int e = tid; e < E; e += kT) b.router_trace[l * E + e] = logit[e];
       __syncthreads();
+      mark(l * 32 + 15);
     }
     // bulk copies of this CTA's gate/up pairs [q0, q1) over the K*H (choice,
     // unit) pairs and of its down rows of every selected expert
@@ -619,27 +687,42 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
     float* gu_s = reinterpret_cast<float*>(gu_w + (size_t)pl.max_pairs * 2 * prow);  // [2*npair][ngd]
     unsigned char* dn_w = reinterpret_cast<unsigned char*>(gu_s + (size_t)pl.max_pairs * 2 * ngd);  // [K*nr][hrow]
     float* dn_s = reinterpret_cast<float*>(dn_w + (size_t)K * pl.max_rows * hrow);             // [K*nr][ngh]
-    if (tid == 0) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_expect_tx(&bars[0], (uint32_t)npair * 2 * (prow + ngd * 4));
+    if (warp == 0) {  // the copies, one per lane of warp 0
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(&bars[0], (uint32_t)npair * 2 * (prow + ngd * 4));
+        mbar_expect_tx(&bars[1], (uint32_t)(K * nr * (hrow + ngh * 4)));
+      }
+      __syncwarp();
       const uint64_t pol = l2_evict_first();
-      int lb = 0;
-      for (int q = q0; q < q1;) {  // segment of choice j, units [u0, u0+m), local rows from lb
+      // segments of the pair range: choice j, units [u0, u0+m), local rows from lb;
+      // copy k of segment sg: 0 gate rows, 1 up rows, 2 gate scales, 3 up scales
+      int lb = 0, sg = 0;
+      for (int q = q0; q < q1; ++sg) {
         const int j = q / H, u0 = q % H, m = min(H, u0 + (q1 - q)) - u0;
         if (m <= 0) break;
-        const ExpertPtrs& X = xp_s[sel_s[j]];
-        tma_load_hint(gu_w + (size_t)lb * prow, X.gu + (size_t)u0 * prow, (uint32_t)(m * prow), &bars[0], pol);
-        tma_load_hint(gu_w + (size_t)(lb + m) * prow, X.gu + (size_t)(H + u0) * prow, (uint32_t)(m * prow), &bars[0], pol);
-        tma_load_hint(gu_s + (size_t)lb * ngd, X.gu_s + (size_t)u0 * ngd, (uint32_t)(m * ngd * 4), &bars[0], pol);
-        tma_load_hint(gu_s + (size_t)(lb + m) * ngd, X.gu_s + (size_t)(H + u0) * ngd, (uint32_t)(m * ngd * 4), &bars[0], pol);
+        if (lane >= 4 * sg && lane < 4 * sg + 4) {
+          const ExpertPtrs& X = xp_s[sel_s[j]];
+          const int k = lane - 4 * sg, up = k & 1;
+          if (k < 2)
+            tma_load_hint(gu_w + (size_t)(lb + up * m) * prow, X.gu + (size_t)(up * H + u0) * prow,
+                          (uint32_t)(m * prow), &bars[0], pol);
+          else
+            tma_load_hint(gu_s + (size_t)(lb + up * m) * ngd, X.gu_s + (size_t)(up * H + u0) * ngd,
+                          (uint32_t)(m * ngd * 4), &bars[0], pol);
+        }
         lb += 2 * m;
         q += m;
       }
-      mbar_expect_tx(&bars[1], (uint32_t)(K * nr * (hrow + ngh * 4)));
-      for (int j = 0; j < K && nr > 0; ++j) {
+      // down rows and scales of choice j: lanes 16 + 2j (rows), 17 + 2j (scales)
+      if (lane >= 16 && lane < 16 + 2 * K && nr > 0) {
+        const int j = (lane - 16) >> 1;
         const ExpertPtrs& X = xp_s[sel_s[j]];
-        tma_load_hint(dn_w + (size_t)j * nr * hrow, X.dn + (size_t)r0 * hrow, (uint32_t)(nr * hrow), &bars[1], pol);
-        tma_load_hint(dn_s + (size_t)j * nr * ngh, X.dn_s + (size_t)r0 * ngh, (uint32_t)(nr * ngh * 4), &bars[1], pol);
+        if (((lane - 16) & 1) == 0)
+          tma_load_hint(dn_w + (size_t)j * nr * hrow, X.dn + (size_t)r0 * hrow, (uint32_t)(nr * hrow), &bars[1], pol);
+        else
+          tma_load_hint(dn_s + (size_t)j * nr * ngh, X.dn_s + (size_t)r0 * ngh, (uint32_t)(nr * ngh * 4), &bars[1],
+                        pol);
       }
     }
     mark(l * 32 + 10);
@@ -654,11 +737,17 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
       }
       mark(l * 32 + 22);
       const int nrow = 2 * npair, PS = pl.ps_gu;
-      for (int it = tid; it < nrow * ngd; it += kT) {
-        const int row = it / ngd, g = it - row * ngd;
-        const uint4 w = lds16(gu_w + (size_t)row * prow + g * 16);
-        const int dv = dot32_rp(w, lds16(xq + g * 32), lds16(xq + g * 32 + 16));
-        P[row * PS + g] = __fmul_rn(__fmul_rn((float)dv, gu_s[(size_t)row * ngd + g]), xs);
+      // warp w: rows w, w + kW, ...; lane g: groups g, g + 32, ... (x chunks in registers)
+      for (int g0 = 0; g0 < ngd; g0 += 32) {
+        const int g = g0 + lane;
+        const bool gl = g < ngd;
+        const uint4 x0 = gl ? lds16(xq + g * 32) : make_uint4(0, 0, 0, 0);
+        const uint4 x1 = gl ? lds16(xq + g * 32 + 16) : make_uint4(0, 0, 0, 0);
+        if (gl)
+          for (int row = warp; row < nrow; row += kW) {
+            const int dv = dot32_rp(lds16(gu_w + (size_t)row * prow + g * 16), x0, x1);
+            P[row * PS + g] = __fmul_rn(__fmul_rn((float)dv, gu_s[(size_t)row * ngd + g]), xs);
+          }
       }
       __syncthreads();
       mark(l * 32 + 23);
@@ -674,51 +763,79 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
         lb += 2 * m;
         q += m;
       }
+      ll_announce(ll.cnt + kCntH);
     }
     mark(l * 32 + 11);
     // ---- F: quantize h, down rows, gated combine, residual (engine.rs:380-401) ----
     {
       float* hf = reinterpret_cast<float*>(stg + pl.o_hf);  // [K][H] f32 h (the gate/up rows are consumed)
-      if (!ll_gather(ll.h, K * H, tag(l, kTagH), hf, a.err, &fail_s)) {
+      if (!(ll_wait_count(ll.cnt + kCntH, (unsigned)(NC * (l + 1)), a.err, &fail_s) &&
+            ll_gather(ll.h, K * H, tag(l, kTagH), hf, a.err, &fail_s))) {
         if (tid == 0) mbar_wait_t(&bars[1], l & 1, a.err);
         break;
       }
       mark(l * 32 + 12);
       float* xsh = red + 16;  // [K] scales of h
-      float* invh = red + 24;
-      for (int j = 0; j < K; ++j) {  // quantize_f32_to_i8 of h_j (quantization.rs:56-104)
-        float m = 0.0f;
-        for (int i = tid; i < H; i += kT) m = fmaxf(m, fabsf(hf[(size_t)j * H + i]));
-        m = block_max(m, red);
-        if (tid == 0) {
+      {  // quantize_f32_to_i8 of each h_j (quantization.rs:56-104): absmax, then RNE
+        const int n4 = (K * H) >> 2, h4 = H >> 2;
+        float mj[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) mj[j] = 0.0f;
+        for (int i = tid; i < n4; i += kT) {
+          const float4 v = lds16f(hf + 4 * i);
+          const float m4 = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+          const int j = i / h4;
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj)
+            if (jj == j) mj[jj] = fmaxf(mj[jj], m4);
+        }
+        float* part = P;  // [K][kW] warp maxima (the products come later)
+        for (int j = 0; j < K; ++j) {
+          const float m = warp_max(mj[j]);
+          if (lane == 0) part[j * kW + warp] = m;
+        }
+        __syncthreads();
+        for (int j = 0; j < K; ++j) {
+          float m = 0.0f;
+#pragma unroll
+          for (int w = 0; w < kW; w += 4) {
+            const float4 q = lds16f(part + j * kW + w);
+            m = fmaxf(fmaxf(m, q.x), fmaxf(fmaxf(q.y, q.z), q.w));
+          }
           float sc, inv;
           quant_scale(m, &sc, &inv);
-          xsh[j] = sc;
-          invh[j] = inv;
+          mj[j] = inv;
+          if (tid == 0) xsh[j] = sc;
         }
-      }
-      __syncthreads();
-      mark(l * 32 + 25);
-      const int n4 = (K * H) >> 2;
-      uint32_t* xw = reinterpret_cast<uint32_t*>(xh);
-      for (int i = tid; i < n4; i += kT) {
-        const float4 v = lds16f(hf + 4 * i);
-        const float inv = invh[(i * 4) / H];
-        const uint32_t b0 = (uint8_t)quant_elem(v.x, inv), b1 = (uint8_t)quant_elem(v.y, inv);
-        const uint32_t b2 = (uint8_t)quant_elem(v.z, inv), b3 = (uint8_t)quant_elem(v.w, inv);
-        xw[i] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        mark(l * 32 + 25);
+        uint32_t* xw = reinterpret_cast<uint32_t*>(xh);
+        for (int i = tid; i < n4; i += kT) {
+          const float4 v = lds16f(hf + 4 * i);
+          const int j = i / h4;
+          float inv = mj[0];
+#pragma unroll
+          for (int jj = 1; jj < 8; ++jj)
+            if (jj == j) inv = mj[jj];
+          const uint32_t b0 = (uint8_t)quant_elem(v.x, inv), b1 = (uint8_t)quant_elem(v.y, inv);
+          const uint32_t b2 = (uint8_t)quant_elem(v.z, inv), b3 = (uint8_t)quant_elem(v.w, inv);
+          xw[i] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
       }
       if (tid == 0 && !mbar_wait_t(&bars[1], l & 1, a.err)) fail_s = 1;
       __syncthreads();
       if (fail_s) break;
       mark(l * 32 + 26);
       const int nrow = K * nr, PS = pl.ps_dn;
-      for (int it = tid; it < nrow * ngh; it += kT) {
-        const int row = it / ngh, g = it - row * ngh, j = row / nr;
-        const uint4 w = lds16(dn_w + (size_t)row * hrow + g * 16);
-        const int8_t* xj = xh + (size_t)j * H + g * 32;
-        const int dv = dot32_rp(w, lds16(xj), lds16(xj + 16));
-        P[row * PS + g] = __fmul_rn(__fmul_rn((float)dv, dn_s[(size_t)row * ngh + g]), xsh[j]);
+      for (int row = warp; row < nrow; row += kW) {  // warp per row, lanes over the groups
+        const int j = row / nr;
+        const int8_t* xj = xh + (size_t)j * H;
+        const unsigned char* wr = dn_w + (size_t)row * hrow;
+        const float* sr = dn_s + (size_t)row * ngh;
+        const float xsj = xsh[j];
+        for (int g = lane; g < ngh; g += 32) {
+          const int dv = dot32_rp(lds16(wr + g * 16), lds16(xj + g * 32), lds16(xj + g * 32 + 16));
+          P[row * PS + g] = __fmul_rn(__fmul_rn((float)dv, sr[g]), xsj);
+        }
       }
       __syncthreads();
       mark(l * 32 + 27);
@@ -731,9 +848,10 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
         own[tid] = __fadd_rn(own[tid], add);
         ll_store(ll.x + dim + r0 + tid, own[tid], tag(l, kTagXf));
       }
-      __syncthreads();  // the staging area is free again
+      ll_announce(ll.cnt + kCntXf);  // (its barrier also frees the staging area)
     }
     mark(l * 32 + 13);
+    mark_clk(l * 32 + 31);
     if (l + 1 < d.n_layers) prefetch_kv<HD>(b, d, l + 1, h, (int)pos, t0, t1, k0, ncol, ks, vs);
   }
   if (fail_s) {
@@ -760,10 +878,11 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
     }
   }
   load4(a.final_norm, dim, wn);
-  const bool ok = ll_gather(ll.x + dim, dim, tag(d.n_layers - 1, kTagXf), xf, a.err, &fail_s);
+  const bool ok = ll_wait_count(ll.cnt + kCntXf, (unsigned)(NC * d.n_layers), a.err, &fail_s) &&
+                  ll_gather(ll.x + dim, dim, tag(d.n_layers - 1, kTagXf), xf, a.err, &fail_s);
   mark(32 * d.n_layers + 1);
   float xs = 0.0f;
-  if (ok) xs = norm_quant_smem(xf, wn, dim, xb, xq, red);
+  if (ok) xs = norm_quant_smem(xf, wn, dim, xb, xq, red, sq, pl.sqs);
   mark(32 * d.n_layers + 3);
   if (warp == kW - 1) {  // producer: refill stage k % S once its rows were consumed
     if (lane == 0)
@@ -813,8 +932,9 @@ __global__ void __launch_bounds__(kT, 1) k_persist(PersistArgs a) {
 
 // Advances the step epoch after a launch of k_persist (stream order), so the
 // tagged words of this step never match the next step's tags.
-__global__ void k_persist_epoch(unsigned* epoch) {
+__global__ void k_persist_epoch(unsigned* epoch, unsigned* cnt) {
   if (threadIdx.x == 0) *epoch += 1u;
+  for (int i = threadIdx.x; i < kPersistCntWords; i += blockDim.x) cnt[i] = 0u;
 }
 
 }  // namespace
@@ -858,12 +978,15 @@ bool persist_plan(const Dims& d, int num_sms, PersistPlan* pl, std::string* why)
   pl->o_P = take(std::max(p_gu, p_dn) * 4);
   pl->o_T = take((size_t)std::max(2 * max_pairs, K * max_rows) * 4);
   pl->o_xh = take((size_t)K * H);
+  pl->sqs = ((dim / 8 + 3) & ~3) + 4;
+  pl->o_sq = take((size_t)8 * pl->sqs * 4);
   // the staging area, by phase: K/V slices, probabilities and products
   // (attention); router weights (routing); expert rows; lm_head ring
   pl->o_vs = (int)r128((size_t)max_trows * d.head_dim * 4);
   pl->o_pp = pl->o_vs + (int)r128((size_t)d.max_seq * max_cols * 4);
   pl->o_vt = pl->o_pp + (int)r128((size_t)d.max_seq * 4);
-  const size_t st_att = (size_t)pl->o_vt + (size_t)max_cols * (kPvTile + 4) * 4;
+  pl->ets = ((d.max_seq / 8 + 3) & ~3) + 4;
+  const size_t st_att = (size_t)pl->o_vt + std::max((size_t)max_cols * (kPvTile + 4), (size_t)8 * pl->ets) * 4;
   const size_t gu_bytes = (size_t)max_pairs * 2 * (dim / 2 + ngd * 4);
   const size_t dn_end = gu_bytes + (size_t)K * max_rows * (H / 2 + ngh * 4);
   const size_t hf_bytes = (size_t)K * H * 4;  // f32 h in F: over the consumed gate/up rows if they fit
@@ -902,8 +1025,8 @@ cudaError_t launch_persist(const PersistArgs& a, int num_sms, cudaStream_t s) {
   return cudaLaunchKernelEx(&cfg, k, a);
 }
 
-cudaError_t launch_persist_epoch(unsigned* epoch, cudaStream_t s) {
-  k_persist_epoch<<<1, 32, 0, s>>>(epoch);
+cudaError_t launch_persist_epoch(unsigned* epoch, unsigned* cnt, cudaStream_t s) {
+  k_persist_epoch<<<1, 256, 0, s>>>(epoch, cnt);
   return cudaGetLastError();
 }
 

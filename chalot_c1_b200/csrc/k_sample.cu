@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ logits
   c.kmin = 0;
   c.kidx = -1;
   const bool scale_t = strategy == 1 ? temperature > 0.0f : (temperature > 0.0f && temperature != 1.0f);
-  c.scale = scale_t ? __fdiv_rn(1.0f, temperature) : 1.0f;
+  c.scale = scale_t ? div_rn(1.0f, temperature) : 1.0f;
   float mx = -INFINITY;
   for (int i = c.c0; i < c.c1; ++i) mx = fmaxf(mx, scaled(c, i));
   c.mx = block_max_f(mx, &sm);
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kST) k_sample(const float* __restrict__ logits
     c.mode = 1;
     float s = 0.0f;
     for (int i = c.c0; i < c.c1; ++i) s += fast_exp(__fsub_rn(scaled(c, i), c.mx));
-    c.inv_sum = __fdiv_rn(1.0f, block_sum_f(s, &sm));
+    c.inv_sum = div_rn(1.0f, block_sum_f(s, &sm));
     if (strategy == 2) {
       unsigned kc;
       float before;

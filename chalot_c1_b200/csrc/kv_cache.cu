@@ -59,14 +59,14 @@ __global__ void k_kv_write(int8_t* data, float* scales, const RowJob* jobs, cons
   if (threadIdx.x == 0) {
     float m = 0.0f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
-    red[32] = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+    red[32] = m > 0.0f ? div_rn(m, 127.0f) : 1.0f;
   }
   __syncthreads();
   const float s = red[32];
   const size_t base = (size_t)j.slot * 2 * kRefPageTokens + (size_t)kv * kRefPageTokens + j.off;
   int8_t* out = data + base * dim;
   for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-    const float q = __fdiv_rn(row[i], s);
+    const float q = div_rn(row[i], s);
     out[i] = (q != q) ? 0 : (int8_t)__float2int_rz(fminf(fmaxf(q, -128.0f), 127.0f));
   }
   if (threadIdx.x == 0) scales[base] = s;

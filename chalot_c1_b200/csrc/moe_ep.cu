@@ -167,7 +167,6 @@ __attribute__((visibility("default"))) int chalot_moe_experts(const chalot_moe_d
   if (r == cudaSuccess) r = cudaMemcpyAsync(w.xq, rows, n_rows * m.dim, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess) r = cudaMemcpyAsync(w.xs, row_scales, n_rows * 4, cudaMemcpyDeviceToDevice, s);
   if (r == cudaSuccess) r = ml_run_rows(m, ml_experts_from_blob(m, local->experts), w, tc ? &t : nullptr, y, s);
-  if (r == cudaSuccess && tc) r = devstat_post(s);
   return r == cudaSuccess ? CHALOT_OK : cuda_fail("moe_experts", r);
 }
 

@@ -10,6 +10,9 @@
 namespace chalot {
 
 constexpr int kPersistThreads = 512;
+// broadcast counters (ll.cnt): three groups of 8 lines (32 words apart)
+constexpr int kCntXc = 0, kCntH = 32 * 8, kCntXf = 2 * 32 * 8;
+constexpr int kPersistCntWords = 3 * 32 * 8;
 constexpr int kPvTile = 1024;              // positions of V products per pass
 constexpr int kLmStages = 4;               // lm_head ring stages
 constexpr int kLmChunk = 2 * (kPersistThreads / 32 - 1);  // lm_head rows per stage: two per compute warp
@@ -19,6 +22,8 @@ struct PersistPlan {
   int o_xq, o_xf, o_xb, o_own, o_red, o_bars, o_xp, o_P, o_T, o_xh, o_stage;
   int o_vs, o_pp, o_vt;  // offsets inside the staging area (attention phase)
   int o_hf;              // offset inside the staging area of the f32 h (phase F)
+  int o_sq, sqs;         // squares of the norm, [8][sqs] floats
+  int ets;               // row stride of the exps by lane, [8][ets] floats (over the products)
   int ps_gu, ps_dn;      // row strides of the group products (floats, 4 mod 32)
   size_t smem;
   int max_pairs, max_rows;
@@ -32,6 +37,7 @@ struct PersistLL {
   uint64_t* score;  // [n_heads][max_seq]
   uint64_t* att;    // [dim] attention output
   uint64_t* h;      // [top_k][hidden] SwiGLU output of the selected experts
+  unsigned* cnt;    // [kPersistCntWords] producer counts of the x and h broadcasts (zero at launch)
 };
 
 struct PersistArgs {
@@ -52,13 +58,15 @@ struct PersistArgs {
   // 6 B2 end, 7 C, 8 C end, 9 D, 10 expert copies issued, 11 E end, 12 F,
   // 13 F end; then kernel start, lm_head start, lm_head end. May be null.
   unsigned long long* trace;
+  unsigned long long* trace_max;  // diagnostics: per mark the latest CTA's time (atomicMax), may be null
 };
 
 // False (with the reason) when the shape does not fit the kernel.
 bool persist_plan(const Dims& d, int num_sms, PersistPlan* plan, std::string* why);
 // One decode step: embedding .. argmax into b.st->argmax_key (cooperative launch).
 cudaError_t launch_persist(const PersistArgs& a, int num_sms, cudaStream_t s);
-// Advances the step epoch (after each launch_persist, in stream order).
-cudaError_t launch_persist_epoch(unsigned* epoch, cudaStream_t s);
+// Advances the step epoch and zeroes the broadcast counters (after each
+// launch_persist, in stream order).
+cudaError_t launch_persist_epoch(unsigned* epoch, unsigned* cnt, cudaStream_t s);
 
 }  // namespace chalot

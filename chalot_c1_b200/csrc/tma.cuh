@@ -67,7 +67,7 @@ CHALOT_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
         : "memory");
     if (ok) return true;
   }
-  if (err) atomicOr(err, 1u);  // kDevErrTimeout (devstat.h)
+  if (err) *(volatile unsigned*)err = 1u;  // word 0: a timeout (devstat.h; engine error words)
   return false;
 }
 

@@ -190,6 +190,15 @@ int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst, size_t n
  * reference. */
 int chalot_probe_int8_mma(int iters, double* tops, double* ms);
 
+/* Self-check of the library's exact float division (the kernels divide with a
+ * fused-multiply-add correction of a reciprocal approximation instead of the
+ * compiler's slower sequence, and must round exactly as IEEE division): n
+ * pseudo-random pairs from `seed` plus pairs in the ranges the decode path
+ * divides; *mismatches receives the count of bitwise differences from the
+ * compiler's division, example[0..1] (may be NULL) one mismatching pair. No
+ * reference counterpart (device arithmetic check). */
+int chalot_selftest_division(uint64_t n, uint64_t seed, uint64_t* mismatches, float* example);
+
 /* ---- expert parallelism of the batched forward ---------------------------- */
 /* The reference runs one process; these spread the expert block of
  * Engine::forward (engine.rs:353-401) over a group of engines, one per GPU:

@@ -134,3 +134,16 @@ def test_bad_arguments_raise(chalot, ops):
         ops.matmul_int4(out, w, s, x, 2, 64, 33)  # odd group
     with pytest.raises(ValueError):
         ops.matmul_int8(out, torch.zeros(3, dtype=torch.int8, device="cuda"), s, x, 2, 64)
+
+
+def test_device_division_is_ieee_exact(chalot):
+    """The kernels' fast division (reciprocal approximation + Newton step + two
+    fma remainder corrections) against the compiler's IEEE division, bit for
+    bit, on 2^30 pairs over 80 binades and the decode path's divisors."""
+    import ctypes as C
+
+    from chalot_c1_b200._capi import check, lib
+    bad = C.c_uint64()
+    ex = (C.c_float * 2)()
+    check(lib().chalot_selftest_division(1 << 30, 12345, C.byref(bad), ex))
+    assert bad.value == 0, (bad.value, ex[0], ex[1])
