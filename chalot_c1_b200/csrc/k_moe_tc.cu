@@ -6,7 +6,7 @@
 // t = t + ((float)gdot_g * s_g) * x_scale in group order. Here the group dots
 // come from the tensor cores: one M=128 x N=128 x K=32 MMA per group writes
 // the int32 dots of a 128-slot x 128-row tile into TMEM (overwrite, not
-// accumulate), and eight epilogue warps read them back and run the f32 group
+// accumulate), and sixteen epilogue warps read them back and run the f32 group
 // epilogue in registers, in group order. Four TMEM buffers let the MMAs run
 // up to three groups ahead of the epilogue, which is the bound.
 //
@@ -19,9 +19,9 @@
 //   S: the group scales, transposed to [group][row] so a 4-group x 128-row
 //      box lands as four 512-byte scale rows.
 // Warp roles: warp 0 issues TMA, warp 1 owns TMEM and issues the MMAs,
-// warps 2..9 are the epilogue (warp w reads TMEM lanes 32*(w%4).., columns
-// split in halves by (w-2)/4). Every wait is bounded and records a failure in
-// the error word instead of hanging.
+// warps 2..17 are the epilogue (warp w reads TMEM lanes 32*(w%4).., columns
+// split in quarters by (w-2)/4, 16 warps). Every wait is bounded and records
+// a failure in the error word instead of hanging.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -38,7 +38,8 @@
 namespace chalot {
 namespace {
 
-constexpr int kTcThreads = 320;
+constexpr int kEpiWarps = 16;                 // epilogue warps: 4 per TMEM lane quadrant
+constexpr int kTcThreads = 64 + 32 * kEpiWarps;
 constexpr int kStages = 4;        // A/B ring depth (128 columns each)
 constexpr int kSRing = 4;         // scale ring depth
 constexpr int kTileBytes = 128 * 128;
@@ -63,6 +64,7 @@ __device__ __forceinline__ float i2f_exact(int v) {
 
 // One warp per destination row: int4 -> int8, scales transposed.
 __global__ void __launch_bounds__(256) k_tc_unpack(MlDims d, const MlExperts X, MlTcWork t) {
+  if (reinterpret_cast<volatile int*>(t.key)[8] == 0) return;  // the workspace holds these experts already
   const int lane = threadIdx.x & 31;
   const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const long gu_rows = (long)d.E * 2 * d.H, dn_rows = (long)d.E * d.dim;
@@ -88,6 +90,28 @@ __global__ void __launch_bounds__(256) k_tc_unpack(MlDims d, const MlExperts X, 
     const float* sc = X.ex[e].dns + (size_t)i * ngh;
     for (int g = lane; g < ngh; g += 32) t.sdn[((size_t)e * ngh + g) * d.dim + i] = __ldg(sc + g);
   }
+}
+
+// The int8 copy of the experts in the workspace is kept between calls: a
+// 4-word key (the experts' addresses, the shape and layout) records what it
+// holds. Before an unpack the key is compared and, if it differs, cleared
+// (so an interrupted unpack is never taken for a complete one); after it the
+// new key is written. Changing the expert weights in place at the same
+// address requires a fresh (or cleared) workspace.
+__global__ void k_tc_key_check(MlTcWork t, unsigned long long k0, unsigned long long k1, unsigned long long k2,
+                               unsigned long long k3) {
+  if (threadIdx.x != 0) return;
+  const bool same = t.key[0] == k0 && t.key[1] == k1 && t.key[2] == k2 && t.key[3] == k3;
+  reinterpret_cast<int*>(t.key)[8] = same ? 0 : 1;
+  if (!same) t.key[0] = t.key[1] = t.key[2] = t.key[3] = 0ull;
+}
+__global__ void k_tc_key_write(MlTcWork t, unsigned long long k0, unsigned long long k1, unsigned long long k2,
+                               unsigned long long k3) {
+  if (threadIdx.x != 0 || reinterpret_cast<int*>(t.key)[8] == 0) return;
+  t.key[0] = k0;
+  t.key[1] = k1;
+  t.key[2] = k2;
+  t.key[3] = k3;
 }
 
 // One warp per slot: its token's int8 row and scale, in expert-sorted order.
@@ -148,11 +172,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int i = 0; i < kSRing; ++i) {
       mbar_init_n(&sm->s_full[i], 1);
-      mbar_init_n(&sm->s_empty[i], 8);
+      mbar_init_n(&sm->s_empty[i], kEpiWarps);
     }
     for (int i = 0; i < kTBufs; ++i) {
       mbar_init_n(&sm->t_full[i], 1);
-      mbar_init_n(&sm->t_empty[i], 8);
+      mbar_init_n(&sm->t_empty[i], kEpiWarps);
     }
     mbar_init_n(&sm->done, 1);
     sm->abort = 0;
@@ -229,15 +253,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_commit(&sm->done);  // every MMA issued has completed before TMEM is freed
       mbar_wait(&sm->done, 0, t.err);
     }
-  } else {  // epilogue
-    const int ew = warp - 2, q = warp & 3, half = ew >> 2;
-    const int col_a = GU ? 32 * half : 64 * half;
-    const int col_b = GU ? 64 + 32 * half : 64 * half + 32;
+  } else {  // epilogue: warp w reads TMEM lanes 32*(w%4).., columns by quarter (w-2)/4
+    const int ew = warp - 2, q = warp & 3, quarter = ew >> 2;
+    // gate/up tiles: gate units 16*quarter.. (columns) and their up units 64 + 16*quarter..;
+    // down tiles: columns 32*quarter..
+    const int col_a = GU ? 16 * quarter : 32 * quarter;
+    const int col_b = GU ? 64 + 16 * quarter : 32 * quarter + 16;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
     // every buffer starts at the bias
     for (int b = 0; b < kTBufs; ++b) {
-      tc_st32_fill(lane_addr + b * 128 + col_a, kMagic);
-      tc_st32_fill(lane_addr + b * 128 + col_b, kMagic);
+      tc_st16_fill(lane_addr + b * 128 + col_a, kMagic);
+      tc_st16_fill(lane_addr + b * 128 + col_b, kMagic);
     }
     tc_wait_st();
     tc_fence_before();
@@ -254,9 +280,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool live = row < cnt;
       const float xs1 = live ? (GU ? t.xsp[p0 + row] : w.hs[p0 + row]) : 0.0f;
       const f32x2 xs = f2_pack(xs1, xs1);
-      f32x2 acc0[16], acc1[16];
+      f32x2 acc0[8], acc1[8];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) acc0[j] = acc1[j] = 0ull;
+      for (int j = 0; j < 8; ++j) acc0[j] = acc1[j] = 0ull;
       for (int g = 0; g < ngroups; ++g, ++gall) {
         const int buf = gall % kTBufs, gl = g & 3, ss = it % kSRing;
         if (!wait_or_abort(&sm->t_full[buf], (gall / kTBufs) & 1, t.err, sm)) {
@@ -268,32 +294,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ok = false;
           break;
         }
-        // one 32-column half at a time keeps the live registers under the
-        // 168 a thread gets with 3 warps per SM sub-partition
         const uint32_t ta = lane_addr + buf * 128;
         const f32x2* sa = reinterpret_cast<const f32x2*>(S + (ss * 4 + gl) * 128 + col_a);
         const f32x2* sb = reinterpret_cast<const f32x2*>(S + (ss * 4 + gl) * 128 + col_b);
-        uint32_t r[32];
-        tc_ld32(ta + col_a, r);
+        uint32_t r[16];
+        tc_ld16(ta + col_a, r);
         tc_wait_ld();
+        // acc = acc + ((float)gdot * s) * xs, lane-wise in f32
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {  // acc = acc + ((float)gdot * s) * xs, lane-wise in f32
+        for (int j = 0; j < 8; ++j) {
           const f32x2 ga = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
           acc0[j] = f2_add_nc(acc0[j], f2_mul(f2_mul(ga, sa[j]), xs));
         }
-        tc_ld32(ta + col_b, r);
+        tc_ld16(ta + col_b, r);
         tc_wait_ld();
-        tc_st32_fill(ta + col_a, kMagic);
-        tc_st32_fill(ta + col_b, kMagic);
+        tc_st16_fill(ta + col_a, kMagic);
+        tc_st16_fill(ta + col_b, kMagic);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const f32x2 gb = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
+          acc1[j] = f2_add_nc(acc1[j], f2_mul(f2_mul(gb, sb[j]), xs));
+        }
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->t_empty[buf]);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const f32x2 gb = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
-          acc1[j] = f2_add_nc(acc1[j], f2_mul(f2_mul(gb, sb[j]), xs));
-        }
         if (gl == 3) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm->s_empty[ss]);
@@ -304,11 +329,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (live) {
         const size_t p = (size_t)(p0 + row);
         if (GU) {
-          const int hu0 = nb * 64 + 32 * half;
+          const int hu0 = nb * 64 + 16 * quarter;
           float4* o = reinterpret_cast<float4*>(w.h + p * d.H + hu0);
           float amax = 0.0f;
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) {
+          for (int j = 0; j < 8; j += 2) {
             float g0, g1, g2, g3, u0, u1, u2, u3;
             f2_unpack(acc0[j], g0, g1);
             f2_unpack(acc0[j + 1], g2, g3);
@@ -324,9 +349,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else {
           f32x2* o = reinterpret_cast<f32x2*>(w.y + p * d.dim + nb * 128 + col_a);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[j] = acc0[j];
+          for (int j = 0; j < 8; ++j) o[j] = acc0[j];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) o[16 + j] = acc1[j];
+          for (int j = 0; j < 8; ++j) o[8 + j] = acc1[j];
         }
       }
     }
@@ -412,6 +437,7 @@ size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t) {
   MlTcWork w{};
   w.xp = reinterpret_cast<int8_t*>(take(N * d.dim));
   w.xsp = reinterpret_cast<float*>(take(N * 4));
+  w.key = reinterpret_cast<unsigned long long*>(take(256));
   w.w8gu = reinterpret_cast<int8_t*>(take((size_t)d.E * 2 * d.H * d.dim));
   w.sgu = reinterpret_cast<float*>(take((size_t)d.E * ngd * 2 * d.H * 4));
   w.w8dn = reinterpret_cast<int8_t*>(take((size_t)d.E * d.dim * d.H));
@@ -426,7 +452,14 @@ size_t ml_tc_layout(const MlDims& d, size_t off, void* base, MlTcWork* t) {
 cudaError_t ml_tc_prepare(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork& t,
                           cudaStream_t s) {
   const long rows = (long)d.E * 2 * d.H + (long)d.E * d.dim;
+  const unsigned long long k0 = reinterpret_cast<uintptr_t>(X.ex[0].gu) | 1ull;  // never 0
+  const unsigned long long k1 = reinterpret_cast<uintptr_t>(X.ex[d.E - 1].dn);
+  const unsigned long long k2 = (unsigned long long)d.E | ((unsigned long long)d.dim << 16) |
+                                ((unsigned long long)d.H << 40);
+  const unsigned long long k3 = (unsigned long long)d.group | ((unsigned long long)X.repacked << 32);
+  k_tc_key_check<<<1, 32, 0, s>>>(t, k0, k1, k2, k3);
   k_tc_unpack<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(d, X, t);
+  k_tc_key_write<<<1, 32, 0, s>>>(t, k0, k1, k2, k3);
   const long N = (long)d.T * d.K;
   k_tc_gather<<<(unsigned)((N + 7) / 8), 256, 0, s>>>(d, w, t);
   return cudaGetLastError();

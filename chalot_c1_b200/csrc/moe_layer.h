@@ -52,6 +52,7 @@ struct MlTcWork {
   int8_t* w8dn;   // [E*dim][H] down weights as int8
   float* sdn;     // [E*H/group][dim] their group scales, transposed
   unsigned* amax; // [T*k] absmax of each h row (float bits), reduced by the gate/up epilogue
+  unsigned long long* key;  // [4] which experts w8gu..sdn hold (0: none); [4] as int: unpack needed
   unsigned* err;  // nonzero when a bounded wait ran out
 };
 

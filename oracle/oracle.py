@@ -20,8 +20,11 @@ _lib = None
 
 def build(force: bool = False) -> str:
     """Compiles liboracle.so with the committed Makefile (g++, AVX2, no FMA)."""
-    src = os.path.join(_HERE, "oracle.cpp")
-    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    csrc = os.path.join(os.path.dirname(_HERE), "chalot_c1_b200", "csrc")
+    srcs = [os.path.join(_HERE, f) for f in ("oracle.cpp", "synth_entry.cpp", "Makefile")] + \
+        [os.path.join(csrc, f) for f in ("myai.cpp", "myai_synth.cpp", "myai.h")]
+    newest = max(os.path.getmtime(p) for p in srcs if os.path.exists(p))
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < newest:
         subprocess.run(["make", "-s", "-C", _HERE, "-B" if force else "liboracle.so"], check=True)
     return _LIB_PATH
 
@@ -289,6 +292,42 @@ def paged_attention(data, scales, page_table, lens, P, H, hd, q, threads=1):
     lib().orc_paged_attention(_p(data), _p(scales), _p(pt), pt.shape[1], _p(ln), n_seq, P, H, hd, _p(q),
                               _p(out), threads)
     return out
+
+
+class _SynthSpec(C.Structure):  # chalot_synth_spec (include/chalot_b200.h)
+    _fields_ = [("dim", C.c_uint32), ("hidden_dim", C.c_uint32), ("n_layers", C.c_uint32),
+                ("n_heads", C.c_uint32), ("vocab_size", C.c_uint32), ("n_experts", C.c_uint32),
+                ("top_k", C.c_uint32), ("int4_group_size", C.c_uint32),
+                ("max_seq_len", C.c_uint32), ("rope_theta_x100", C.c_uint32),
+                ("weight_std", C.c_float), ("seed", C.c_uint64), ("n_threads", C.c_int)]
+
+
+def write_synthetic(path: str, *, dim, hidden_dim, n_layers, n_heads, vocab_size, n_experts=8, top_k=2,
+                    int4_group_size=32, max_seq_len=512, rope_theta_x100=0, seed=0, weight_std=0.02,
+                    n_threads=0) -> str:
+    """The synthetic .myai writer, compiled into this library from the CUDA
+    library's own writer sources (same bytes), for callers that must not load
+    the CUDA library (the CPU reference arm of the benchmark)."""
+    spec = _SynthSpec(dim, hidden_dim, n_layers, n_heads, vocab_size, n_experts, top_k, int4_group_size,
+                      max_seq_len, rope_theta_x100, weight_std, seed, n_threads)
+    L = lib()
+    L.orc_write_synthetic.restype = C.c_int
+    L.orc_write_synthetic.argtypes = [C.c_char_p, C.c_void_p]
+    rc = L.orc_write_synthetic(path.encode(), C.byref(spec))
+    if rc != 0:
+        raise RuntimeError(f"orc_write_synthetic failed ({rc}): {path}")
+    return path
+
+
+def ensure_model(directory: str, name: str, shape: dict) -> str:
+    """directory/name.myai, written once (through a temporary file)."""
+    os.makedirs(directory, exist_ok=True)
+    path = os.path.join(directory, f"{name}.myai")
+    if not os.path.exists(path):
+        tmp = path + ".tmp"
+        write_synthetic(tmp, **shape)
+        os.replace(tmp, path)
+    return path
 
 
 def hw_threads() -> int:

@@ -237,3 +237,16 @@ def test_kvcache_truncating_quantizer(oracle_lib):
     s = np.float32(1.0) / np.float32(127.0)
     assert k[1] == np.float32(np.float32(int(np.float32(0.9) / s)) * s)
     assert (v == 0).all()  # an all-zero row keeps scale 1.0 and zeros
+
+
+def test_oracle_writer_matches_library_writer(tmp_path):
+    """The oracle's copy of the synthetic writer (compiled from the library's
+    writer sources, used by the CPU reference arm) writes the same bytes."""
+    import filecmp
+
+    import chalot_c1_b200 as cb
+    from oracle import oracle as orc
+    shape = dict(cb.SHAPES["tiny"], n_layers=1, vocab_size=512)
+    a = cb.write_synthetic(str(tmp_path / "lib.myai"), **shape)
+    b = orc.write_synthetic(str(tmp_path / "orc.myai"), **shape)
+    assert filecmp.cmp(a, b, shallow=False)
