@@ -159,8 +159,10 @@ CHALOT_DEV f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
 }
 // acc + p lane-wise with scalar add.rn.f32. A packed add (or fma(p, 1, acc))
 // fed by a packed multiply was contracted into one fused multiply-add by the
-// assembler despite .rn (measured: results then equal fma(x, y, acc)); a
-// scalar add with an explicit rounding modifier is never contracted.
+// assembler despite .rn (measured: results then equal fma(x, y, acc)), also
+// with the assembler's own contraction switched off (-Xptxas -fmad=false:
+// the 4096-token layer then differs from the oracle); a scalar add with an
+// explicit rounding modifier is never contracted.
 CHALOT_DEV f32x2 f2_add_nc(f32x2 acc, f32x2 p) {
   float a0, a1, p0, p1;
   f2_unpack(acc, a0, a1);
