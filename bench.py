@@ -395,9 +395,10 @@ def paged_cpu_sample():
 
 
 def bench_moe_ep(ws: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
-    """Expert-parallel MoE layer prefill over NCCL: every rank holds 4096
-    tokens (weak scaling) and experts e % ws == rank of the Qwen-shaped
-    layer. Device time per call, max over ranks."""
+    """Expert-parallel MoE layer prefill (chalot_moe_layer_ep: tokens to the
+    experts and back over NVLink peer memory): every rank holds 4096 tokens
+    (weak scaling) and experts e % ws == rank of the Qwen-shaped layer. Device
+    time per call (CUDA events on the calling stream), max over ranks."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -405,21 +406,26 @@ def bench_moe_ep(ws: int, rank: int, reps: int = 10, warmup: int = 3) -> dict:
     layer = moe.synthetic_moe_layer(MOE_DIM, MOE_H, MOE_E, MOE_K, 32, seed=3)
     x = torch.from_numpy(np.random.default_rng(100 + rank).standard_normal((MOE_T, MOE_DIM),
                                                                            dtype=np.float32)).cuda()
-    be = ep.GpuBackend(layer, ws, rank)
-    a2a = ep.dist_all_to_all()
-    for _ in range(warmup):
-        ep.ep_forward(be, x, a2a, ws)
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        ep.ep_forward(be, x, a2a, ws)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = allmax(ws, e0.elapsed_time(e1) / reps)
+    pl = ep.PeerExpertLayer(layer, rank, ws, max_tokens=MOE_T)
+    try:
+        for _ in range(warmup):
+            pl(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            pl(x)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+    finally:
+        pl.close()
+    ms = allmax(ws, ms)
     return {"tokens_per_rank": MOE_T, "ms": ms, "tok_s": MOE_T * ws / (ms * 1e-3),
-            "tops": MOE_OPS * ws / (ms * 1e-3) / 1e12}
+            "tops": MOE_OPS * ws / (ms * 1e-3) / 1e12,
+            "exchange": "int8 rows to the experts and f32 outputs back by NVLink peer stores in "
+                        "chalot_moe_layer_ep (counts on the device, no host round trip)"}
 
 
 def run_profile(args):

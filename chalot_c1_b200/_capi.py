@@ -71,6 +71,11 @@ SIGNATURES = {
     "chalot_last_error": (C.c_char_p, []),
     "chalot_abi_version": (C.c_int, []),
     "chalot_device_status": (C.c_int, [C.c_void_p]),
+    "chalot_ep_comm_create": (C.c_int, [C.c_uint32, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+    "chalot_ep_comm_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "chalot_ep_comm_free": (None, [C.c_void_p]),
+    "chalot_moe_layer_ep": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_void_p]),
     "chalot_selftest_division": (C.c_int, [C.c_uint64, C.c_uint64, C.c_void_p, C.c_void_p]),
     "chalot_decode_trace": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "chalot_myai_write_synthetic": (C.c_int, [C.c_char_p, C.POINTER(SynthSpec)]),

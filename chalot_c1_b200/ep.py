@@ -118,6 +118,57 @@ class GpuBackend:
         return out
 
 
+class PeerExpertLayer:
+    """chalot_moe_layer_ep: the expert-parallel layer as one library call,
+    tokens moved to the experts and back with NVLink peer stores (no host
+    round trip, no padding). One instance per rank (one process per GPU);
+    construction all-gathers the ranks' exchange-arena handles over
+    torch.distributed, and every rank must then call it in lockstep."""
+
+    def __init__(self, layer: SyntheticMoeLayer, rank: int, world: int, max_tokens: int, group=None,
+                 device="cuda"):
+        import torch.distributed as dist
+
+        from ._capi import MoeDesc, check, lib
+        self.layer, self.rank, self.world, self.device = layer, rank, world, device
+        self.router_w = torch.from_numpy(layer.router_w).to(device)
+        self.router_b = torch.from_numpy(layer.router_b).to(device)
+        self.local = torch.from_numpy(local_blob(layer, world, rank)).to(device)
+        self.desc = MoeDesc(layer.dim, layer.hidden, layer.n_experts, layer.top_k, layer.group,
+                            self.router_w.data_ptr(), self.router_b.data_ptr(), self.local.data_ptr())
+        self._comm = C.c_void_p()
+        handle = (C.c_uint8 * 64)()
+        check(lib().chalot_ep_comm_create(rank, world, C.byref(self.desc), max_tokens, C.byref(self._comm), handle))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        buf = (C.c_uint8 * (64 * world)).from_buffer_copy(b"".join(handles))
+        check(lib().chalot_ep_comm_connect(self._comm, buf))
+
+    def __call__(self, x):
+        from ._capi import check, lib
+        T, K = x.shape[0], self.layer.top_k
+        out = torch.empty((T, self.layer.dim), dtype=torch.float32, device=self.device)
+        sel = torch.empty((T, K), dtype=torch.int32, device=self.device)
+        selw = torch.empty((T, K), dtype=torch.float32, device=self.device)
+        check(lib().chalot_moe_layer_ep(self._comm, C.byref(self.desc), x.data_ptr() if T else None, T,
+                                        out.data_ptr() if T else None, sel.data_ptr() if T else None,
+                                        selw.data_ptr() if T else None, torch.cuda.current_stream().cuda_stream))
+        return out, sel
+
+    def close(self) -> None:
+        from ._capi import lib
+        if self._comm:
+            torch.cuda.synchronize()
+            lib().chalot_ep_comm_free(self._comm)
+            self._comm = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def _counts(offs, world: int, n_local: int):
     c = offs[1:] - offs[:-1]
     return c.reshape(world, n_local)

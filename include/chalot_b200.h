@@ -339,6 +339,40 @@ int chalot_moe_layer(const chalot_moe_desc* desc, const float* x, size_t n_tok, 
 int chalot_moe_layer_noalloc(const chalot_moe_desc* desc, const float* x, size_t n_tok,
                              float* out, int32_t* sel_out, float* selw_out, void* stream);
 
+/* ---- expert-parallel MoE layer in one call ------------------------------ */
+/* Expert e lives on rank e % world, one rank per GPU of one node with NVLink
+ * peer access. Each rank exports an exchange arena in its GPU memory; the
+ * ranks move int8 token rows to the experts and f32 outputs back with plain
+ * peer stores (counts and offsets stay on the device: no host round trip, no
+ * padding on the wire) and the layer is bit-identical to chalot_moe_layer on
+ * one GPU. It replaces the parallel region of the reference's expert block,
+ * the rayon par_iter over the selected experts (src/model/engine.rs:353-387),
+ * with expert parallelism across GPUs. */
+#define CHALOT_EP_HANDLE_BYTES 64
+typedef struct chalot_ep_comm chalot_ep_comm;
+
+/* This rank's side of a group of `world` ranks (<= 8) for layers shaped like
+ * `desc` (its experts pointer is ignored here) and calls of up to max_tokens
+ * tokens, on the current device. `handle` receives CHALOT_EP_HANDLE_BYTES
+ * bytes that the other ranks need to reach this rank's arena; all-gather the
+ * handles over any host transport (rank order) and pass them to
+ * chalot_ep_comm_connect. */
+int chalot_ep_comm_create(uint32_t rank, uint32_t world, const chalot_moe_desc* desc, size_t max_tokens,
+                          chalot_ep_comm** out, uint8_t* handle);
+/* Maps every other rank's arena (all_handles: world x CHALOT_EP_HANDLE_BYTES). */
+int chalot_ep_comm_connect(chalot_ep_comm* comm, const uint8_t* all_handles);
+void chalot_ep_comm_free(chalot_ep_comm* comm);
+
+/* The expert block (as chalot_moe_layer) for this rank's n_tok rows, with the
+ * experts spread over the group: desc holds the full router (n_experts = all
+ * experts) and in `experts` only this rank's experts e (e % world == rank),
+ * in increasing e, each in the file layout. Every rank of the group must call
+ * it, the same number of times and in the same order (n_tok may be 0); a rank
+ * that does not arrive makes the others report CHALOT_ERR_TIMEOUT (bounded
+ * device waits). Asynchronous on `stream`. */
+int chalot_moe_layer_ep(chalot_ep_comm* comm, const chalot_moe_desc* desc, const float* x, size_t n_tok,
+                        float* out, int32_t* sel_out, float* selw_out, void* stream);
+
 /* ---- expert-parallel MoE layer: building blocks ------------------------- */
 /* Expert e lives on rank e % n_ranks. Per layer each rank routes its tokens,
  * plans and gathers its (token, choice) slots by destination, exchanges

@@ -51,3 +51,17 @@ def test_ep_nccl_two_gpus(chalot):
                        env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "EP_NCCL_OK" in r.stdout
+
+
+def test_ep_peer_memory_two_gpus(chalot):
+    """chalot_moe_layer_ep over NVLink peer memory on two GPUs, bit-identical
+    to the single-GPU layer (tests/ep_p2p_check.py)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29537", os.path.join(ROOT, "tests", "ep_p2p_check.py")]
+    r = subprocess.run(["timeout", "-k", "30", "600"] + cmd, capture_output=True, text=True, cwd=ROOT,
+                       env=dict(os.environ, NCCL_NVLS_ENABLE="0"))
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "EP_P2P_OK" in r.stdout
