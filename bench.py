@@ -282,7 +282,7 @@ def run_ours(args, ws, rank, local):
         "clocks": clocks,
     }
     if ep_res is not None:
-        line["moe_layer_prefill_ep"] = dict(ep_res, workload="expert-parallel MoE layer prefill over NCCL, "
+        line["moe_layer_prefill_ep"] = dict(ep_res, workload="expert-parallel MoE layer prefill over NVLink peer memory, "
                                             "4096 tokens per rank, experts e on rank e % n_gpus", scaling="weak")
     if bep is not None and "error" in bep:
         line["batch_decode_ep"] = {"error": bep["error"]}
