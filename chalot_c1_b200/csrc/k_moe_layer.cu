@@ -285,6 +285,187 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
   }
 }
 
+// Few-slot expert products (batched decode: a handful of slots per expert).
+// The tile GEMM above stages unpacked weights in shared memory and feeds one
+// slot per 16-byte load, which is instruction-bound at 8 slots; here the
+// weights stream once per expert through a cp.async ring in their packed
+// form, coalesced, and each thread keeps whole weight rows: thread t owns
+// rows (gate/up: the gate and the up row of hidden unit r0+t; down: output
+// row r0+t), unpacks each 16-byte group chunk once and dots it with every
+// slot of the expert (up to kFewSlots, staged per chunk and read by
+// broadcast). Each group dot is one dp4a chain started at the bits of
+// 1.5*2^23, so its result is already (float)dot in biased form (i2f_exact
+// without the add); the f32 group epilogue t = t + ((float)dot * s_g) * xs
+// runs in registers in group order, as in matmul_int4 (src/tensor/matmul.rs:
+// 452-654). Group 32 only; dims multiples of kFewKc.
+constexpr int kFewSlots = 16;                    // slots per block (the dispatch's tile size)
+constexpr int kFewKc = 128;                      // columns per stage: 4 groups of 32
+constexpr int kFewStages = 4;
+constexpr int kFewWStride = kFewKc / 2 + 16;     // packed row stride in shared memory (80 B: conflict-free)
+constexpr int kFewGuThreads = 64;                // gate/up: 64 hidden units (128 rows) per block
+constexpr int kFewDnThreads = 128;               // down: 128 output rows per block
+
+template <bool GU, int NT>
+__host__ __device__ constexpr size_t few_stage_bytes() {
+  return (size_t)(GU ? 2 : 1) * NT * (kFewWStride + 16) + (size_t)kFewSlots * kFewKc;
+}
+template <bool GU, int NT>
+__host__ __device__ constexpr size_t few_smem() {
+  return few_stage_bytes<GU, NT>() * kFewStages;
+}
+
+CHALOT_DEV void few_cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+CHALOT_DEV void few_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+CHALOT_DEV void few_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// 16 packed bytes (32 int4) -> 8 words of signed int8 in column order.
+// Repacked layout: word j byte b = column 8j+b (low nibble) and 8j+4+b
+// (high), two's complement; file layout: byte k = columns 2k (low) and 2k+1
+// (high), value + 8.
+template <bool RP>
+CHALOT_DEV void few_unpack(uint4 p, int (&o)[8]) {
+  const uint32_t in[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t v = RP ? in[i] ^ 0x88888888u : in[i];  // every nibble as value + 8
+    uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
+    if (!RP) {
+      const uint32_t a = __byte_perm(lo, hi, 0x5140), b = __byte_perm(lo, hi, 0x7362);
+      lo = a;
+      hi = b;
+    }
+    o[2 * i] = (int)nib_minus8(lo);
+    o[2 * i + 1] = (int)nib_minus8(hi);
+  }
+}
+
+template <bool GU, bool RP, int NT>
+__global__ void __launch_bounds__(NT) k_ml_few(MlDims d, const MlExperts XP, MlWork w) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int R = GU ? 2 : 1;  // weight rows per thread
+  constexpr int ROWS = R * NT;
+  const int mb = blockIdx.y;
+  if (mb >= *w.n_mb) return;
+  const int e = w.mb_e[mb], p0 = w.mb_p0[mb], cnt = w.mb_n[mb];
+  const int in_dim = GU ? d.dim : d.H;
+  const int out_rows = GU ? d.H : d.dim;
+  const int ng = in_dim >> 5;
+  const int r0 = blockIdx.x * NT;
+  const int tid = threadIdx.x;
+  const uint8_t* wmat = GU ? XP.ex[e].gu : XP.ex[e].dn;
+  const float* smat = GU ? XP.ex[e].gus : XP.ex[e].dns;
+
+  // stage layout: packed rows [ROWS][kFewWStride], scales [ROWS][4] f32, x [kFewSlots][kFewKc]
+  auto wst = [&](int st) { return smem + (size_t)st * few_stage_bytes<GU, NT>(); };
+  auto sst = [&](int st) { return reinterpret_cast<float*>(wst(st) + ROWS * kFewWStride); };
+  auto xst = [&](int st) { return reinterpret_cast<int8_t*>(wst(st) + ROWS * (kFewWStride + 16)); };
+
+  float xs[kFewSlots];
+#pragma unroll
+  for (int s = 0; s < kFewSlots; ++s)
+    xs[s] = s < cnt ? (GU ? w.xs[w.perm[p0 + s] / d.K] : w.hs[p0 + s]) : 0.0f;
+
+  const int nk = in_dim / kFewKc;
+  auto load = [&](int k) {
+    unsigned char* W = wst(k % kFewStages);
+    float* S = sst(k % kFewStages);
+    int8_t* X = xst(k % kFewStages);
+    const int k0 = k * kFewKc;
+    for (int c = tid; c < ROWS * 4; c += NT) {  // 4 x 16 B of packed weights per row
+      const int lr = c >> 2, j = c & 3;
+      const int unit = r0 + (GU ? lr % NT : lr);
+      if (unit < out_rows) {
+        const int mrow = GU ? (lr < NT ? unit : d.H + unit) : unit;
+        few_cp16(W + lr * kFewWStride + j * 16, wmat + (size_t)mrow * (in_dim >> 1) + (k0 >> 1) + j * 16);
+      }
+    }
+    for (int lr = tid; lr < ROWS; lr += NT) {  // the row's 4 group scales
+      const int unit = r0 + (GU ? lr % NT : lr);
+      if (unit < out_rows) {
+        const int mrow = GU ? (lr < NT ? unit : d.H + unit) : unit;
+        few_cp16(S + lr * 4, smat + (size_t)mrow * ng + (k0 >> 5));
+      }
+    }
+    for (int c = tid; c < cnt * (kFewKc / 16); c += NT) {  // the slots' activation chunks
+      const int s = c / (kFewKc / 16), j = c % (kFewKc / 16);
+      const int8_t* a = GU ? w.xq + (size_t)(w.perm[p0 + s] / d.K) * in_dim : w.hq + (size_t)(p0 + s) * in_dim;
+      few_cp16(X + s * kFewKc + j * 16, a + k0 + j * 16);
+    }
+  };
+
+  float acc[R][kFewSlots];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int s = 0; s < kFewSlots; ++s) acc[r][s] = 0.0f;
+
+#pragma unroll
+  for (int k = 0; k < kFewStages - 1; ++k) {
+    if (k < nk) load(k);
+    few_commit();
+  }
+  for (int k = 0; k < nk; ++k) {
+    few_wait<kFewStages - 2>();
+    __syncthreads();  // stage k landed for every thread; stage k-1 is free
+    if (k + kFewStages - 1 < nk) load(k + kFewStages - 1);
+    few_commit();
+    const unsigned char* W = wst(k % kFewStages);
+    const float* S = sst(k % kFewStages);
+    const int8_t* X = xst(k % kFewStages);
+    float4 sc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) sc[r] = lds16f(S + (tid + r * NT) * 4);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      int wv[R][8];
+#pragma unroll
+      for (int r = 0; r < R; ++r) few_unpack<RP>(lds16(W + (tid + r * NT) * kFewWStride + g * 16), wv[r]);
+      float ws[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) ws[r] = g == 0 ? sc[r].x : g == 1 ? sc[r].y : g == 2 ? sc[r].z : sc[r].w;
+#pragma unroll
+      for (int s = 0; s < kFewSlots; ++s) {
+        if (s < cnt) {
+          const uint4 xa = lds16(X + s * kFewKc + g * 32), xb = lds16(X + s * kFewKc + g * 32 + 16);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            int t = 0x4B400000;  // 1.5*2^23: the chain ends at the float bits of 1.5*2^23 + dot
+            t = __dp4a(wv[r][0], (int)xa.x, t);
+            t = __dp4a(wv[r][1], (int)xa.y, t);
+            t = __dp4a(wv[r][2], (int)xa.z, t);
+            t = __dp4a(wv[r][3], (int)xa.w, t);
+            t = __dp4a(wv[r][4], (int)xb.x, t);
+            t = __dp4a(wv[r][5], (int)xb.y, t);
+            t = __dp4a(wv[r][6], (int)xb.z, t);
+            t = __dp4a(wv[r][7], (int)xb.w, t);
+            const float f = __fsub_rn(__int_as_float(t), 12582912.0f);
+            acc[r][s] = __fadd_rn(acc[r][s], __fmul_rn(__fmul_rn(f, ws[r]), xs[s]));
+          }
+        }
+      }
+    }
+  }
+  const int unit = r0 + tid;
+  if (unit >= out_rows) return;
+#pragma unroll
+  for (int s = 0; s < kFewSlots; ++s) {
+    if (s < cnt) {
+      const size_t p = (size_t)(p0 + s);
+      if (GU)
+        w.h[p * d.H + unit] = swiglu_elem(acc[0][s], acc[R - 1][s], unit, d.H);
+      else
+        w.y[p * d.dim + unit] = acc[0][s];
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kThreads) k_ml_quant(MlDims d, MlWork w) {
   extern __shared__ __align__(16) unsigned char smem[];
   float* v = reinterpret_cast<float*>(smem);
@@ -392,9 +573,25 @@ static void quantize_h(const MlDims& d, const MlWork& w, cudaStream_t s) {
   k_ml_quant<<<(unsigned)((size_t)d.T * d.K), kThreads, qsm, s>>>(d, w);
 }
 
-// Slots per tile of the tile GEMMs: 8 when the experts get few slots each
-// (batched decode), else 32.
-static int tile_slots(const MlDims& d) { return (size_t)d.T * d.K / d.E < 24 ? 8 : kBM; }
+// The few-slot kernels need group 32, dims that are multiples of kFewKc and
+// 16-byte aligned expert tensors (their cp.async copies are 16 bytes).
+static bool few_eligible(const MlDims& d, const MlExperts& X) {
+  if (d.group != 32 || d.dim % kFewKc || d.H % kFewKc) return false;
+  for (int e = 0; e < d.E && e < 32; ++e) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(X.ex[e].gu) | reinterpret_cast<uintptr_t>(X.ex[e].gus) |
+                        reinterpret_cast<uintptr_t>(X.ex[e].dn) | reinterpret_cast<uintptr_t>(X.ex[e].dns);
+    if (a & 15) return false;
+  }
+  return true;
+}
+
+// Slots per tile: when the experts get few slots each (batched decode), the
+// few-slot kernels (kFewSlots) or, for shapes they do not take, 8-slot tile
+// GEMMs; else 32-slot tile GEMMs.
+static int tile_slots(const MlDims& d, const MlExperts& X) {
+  if ((size_t)d.T * d.K / d.E >= 24) return kBM;
+  return few_eligible(d, X) ? kFewSlots : 8;
+}
 
 // gate/up tile GEMM, quantize h, down tile GEMM, with tiles of bm slots.
 static void tile_gemms(const MlDims& d, const MlExperts& X, const MlWork& w, int bm, cudaStream_t s) {
@@ -402,7 +599,23 @@ static void tile_gemms(const MlDims& d, const MlExperts& X, const MlWork& w, int
   const size_t gsm = gemm_smem();
   const unsigned nmb = (unsigned)std::min(N, N / bm + d.E);
   const dim3 ggu((d.H + kBN / 2 - 1) / (kBN / 2), nmb), gdn((d.dim + kBN - 1) / kBN, nmb);
-  if (bm == 8) {
+  if (bm == kFewSlots) {
+    const dim3 fgu((d.H + kFewGuThreads - 1) / kFewGuThreads, nmb), fdn((d.dim + kFewDnThreads - 1) / kFewDnThreads, nmb);
+    constexpr size_t sgu = few_smem<true, kFewGuThreads>(), sdn = few_smem<false, kFewDnThreads>();
+    if (X.repacked) {
+      cudaFuncSetAttribute(k_ml_few<true, true, kFewGuThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sgu);
+      cudaFuncSetAttribute(k_ml_few<false, true, kFewDnThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sdn);
+      k_ml_few<true, true, kFewGuThreads><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
+      quantize_h(d, w, s);
+      k_ml_few<false, true, kFewDnThreads><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
+    } else {
+      cudaFuncSetAttribute(k_ml_few<true, false, kFewGuThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sgu);
+      cudaFuncSetAttribute(k_ml_few<false, false, kFewDnThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sdn);
+      k_ml_few<true, false, kFewGuThreads><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
+      quantize_h(d, w, s);
+      k_ml_few<false, false, kFewDnThreads><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
+    }
+  } else if (bm == 8) {
     cudaFuncSetAttribute(k_ml_gemm<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
     cudaFuncSetAttribute(k_ml_gemm<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
     k_ml_gemm<true, 1><<<ggu, kThreads, gsm, s>>>(d, X, w);
@@ -421,7 +634,7 @@ cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float
                    const MlExperts& X, const MlWork& w, float* out, cudaStream_t s) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T * d.K;
-  const int bm = tile_slots(d);
+  const int bm = tile_slots(d, X);
   route_and_dispatch(d, x, rw, rb, w, bm, s);
   tile_gemms(d, X, w, bm, s);
   (void)N;
@@ -486,7 +699,7 @@ cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, co
     if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
     if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
   } else {
-    const int bm = tile_slots(d);
+    const int bm = tile_slots(d, X);
     k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
     tile_gemms(d, X, w, bm, s);
   }
