@@ -18,6 +18,11 @@ void b_norm_quant(const BatchDims& d, int B, const float* x, const float* w, int
                   cudaStream_t s);
 void b_gemm_i8(int B, int R, int C, const int8_t* W, const float* ws, const int8_t* xq, const float* xs,
                float* out, int ldo, bool add, cudaStream_t s);
+// The same GEMM on the tensor cores (k_dense_tc.cu) when eligible: B <= 256,
+// C % 128 == 0, W and xq 16-byte aligned.
+bool b_gemm_tc_eligible(int B, int C, const int8_t* W, const int8_t* xq);
+cudaError_t b_gemm_tc(int B, int R, int C, const int8_t* W, const float* ws, const int8_t* xq, const float* xs,
+                      float* out, int ldo, bool add, cudaStream_t s);
 void b_rope_kv(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* qkv,
                float* q, float* kc, float* vc, const float* rcos, const float* rsin, cudaStream_t s);
 void b_attention(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* q,

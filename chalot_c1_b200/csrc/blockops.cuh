@@ -242,8 +242,16 @@ __device__ __forceinline__ void router_logits(const float* __restrict__ W,
     const int e = t >> 4, l = t & 15, half = l >> 3, j = l & 7;
     const float* w = W + (size_t)e * dim;
     float s = 0.0f;
+    int c = 0;
+    for (; c + 32 <= c16; c += 32) {  // 32 weight loads in flight, then the ordered sum
+      float wv[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) wv[u] = w[(c + u) * 16 + half * 8 + j];  // W may be in shared memory
+#pragma unroll
+      for (int u = 0; u < 32; ++u) s = __fadd_rn(s, __fmul_rn(wv[u], xb[(c + u) * 16 + half * 8 + j]));
+    }
 #pragma unroll 8
-    for (int c = 0; c < c16; ++c) {
+    for (; c < c16; ++c) {
       const int k = c * 16 + half * 8 + j;
       s = __fadd_rn(s, __fmul_rn(w[k], xb[k]));
     }

@@ -258,6 +258,101 @@ __global__ void __launch_bounds__(kT) k_b_pv(BatchDims d, int layer, const int32
   if (threadIdx.x < kPvCols) att[(size_t)b * d.dim + h * hd + c0 + threadIdx.x] = acc;
 }
 
+constexpr int kAttT = 128;  // threads of the fused attention CTA (head_dim <= 128)
+constexpr int kAttU = 16;   // V rows in flight per thread
+
+// CTA (head h, token b): the scores of positions 0..pos (one thread per
+// position: dot_f32_avx2 order, then 30*tanh(x/30)), softmax_avx2 over them
+// in shared memory, then o[c] = sum_t p_t v_t[c] in t order (thread c), with
+// kAttU V rows loaded ahead. One pass over this head's K and V, and the
+// softmax once per head instead of once per 8 output columns.
+template <int C16>
+__global__ void __launch_bounds__(kAttT, 6) k_b_attn(BatchDims d, int layer, const int32_t* pos, const int32_t* slot,
+                                                  const float* q, const float* kc, const float* vc, float* att) {
+  extern __shared__ __align__(16) float p[];  // [max_seq] scores, then probabilities
+  __shared__ __align__(16) float qh[256];
+  __shared__ float red[40];
+  __shared__ float inv_s;
+  const int h = blockIdx.x, b = blockIdx.y, hd = d.head_dim;
+  const int n = pos[b] + 1;
+  const size_t base = ((size_t)slot[b] * d.n_layers + layer) * d.max_seq * d.dim + (size_t)h * hd;
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = q[(size_t)b * d.dim + h * hd + i];
+  __syncthreads();
+  const float rs = div_rn(1.0f, __fsqrt_rn((float)hd));
+  float mx = -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float* k = kc + base + (size_t)t * d.dim;
+    float a0[8], a1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a0[j] = a1[j] = 0.0f;
+#pragma unroll 2
+    for (int c = 0; c < C16; ++c) {
+      const float4* kk = reinterpret_cast<const float4*>(k + c * 16);
+      const float4 k0 = kk[0], k1 = kk[1], k2 = kk[2], k3 = kk[3];
+      const float kv[16] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w,
+                            k2.x, k2.y, k2.z, k2.w, k3.x, k3.y, k3.z, k3.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[c * 16 + j], kv[j]));
+        a1[j] = __fadd_rn(a1[j], __fmul_rn(qh[c * 16 + 8 + j], kv[8 + j]));
+      }
+    }
+    const int rem = C16 * 16;
+    if (rem + 8 <= hd)  // head_dim % 16 == 8: one more 8-chunk into acc0
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[rem + j], k[rem + j]));
+    float cmb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cmb[j] = __fadd_rn(a0[j], a1[j]);
+    const float x = __fmul_rn(hsum8(cmb), rs);
+    const float s = __fmul_rn(30.0f, libm::tanh_f32(div_rn(x, 30.0f)));
+    p[t] = s;
+    mx = fmaxf(mx, s);
+  }
+  mx = block_max(mx, red);  // its barriers also publish p[]
+  const int full = n & ~7;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    p[i] = i < full ? fast_exp(__fsub_rn(p[i], mx)) : expf_cr(__fsub_rn(p[i], mx));
+  __syncthreads();
+  if (threadIdx.x < 8) {  // lane j sums elements 8c+j in c order
+    float acc = 0.0f;
+    for (int c = 0; c < (full >> 3); ++c) acc = __fadd_rn(acc, p[c * 8 + threadIdx.x]);
+    red[threadIdx.x] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float l8[8];
+    for (int j = 0; j < 8; ++j) l8[j] = red[j];
+    float sum = hsum8(l8);
+    for (int i = full; i < n; ++i) sum = __fadd_rn(sum, p[i]);
+    inv_s = div_rn(1.0f, sum);
+  }
+  __syncthreads();
+  const float inv = inv_s;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
+  __syncthreads();
+  if (threadIdx.x >= hd) return;
+  const float* v = vc + base + threadIdx.x;
+  const size_t ld = d.dim;
+  float acc = 0.0f, cur[kAttU], nxt[kAttU];
+  const int nb = n / kAttU;
+  if (nb > 0)
+#pragma unroll
+    for (int u = 0; u < kAttU; ++u) cur[u] = v[(size_t)u * ld];
+  for (int i = 0; i < nb; ++i) {
+    const int t = i * kAttU;
+    if (i + 1 < nb)
+#pragma unroll
+      for (int u = 0; u < kAttU; ++u) nxt[u] = v[(size_t)(t + kAttU + u) * ld];
+#pragma unroll
+    for (int u = 0; u < kAttU; ++u) acc = __fadd_rn(acc, __fmul_rn(p[t + u], cur[u]));
+#pragma unroll
+    for (int u = 0; u < kAttU; ++u) cur[u] = nxt[u];
+  }
+  for (int t = nb * kAttU; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[(size_t)t * ld]));
+  att[(size_t)b * d.dim + h * hd + threadIdx.x] = acc;
+}
+
 __global__ void __launch_bounds__(kT) k_b_rmsnorm(int dim, const float* x, const float* __restrict__ w, float* xb) {
   extern __shared__ __align__(16) float esm[];  // xb [dim], wbuf [dim]
   __shared__ float red[40];
@@ -308,6 +403,8 @@ void b_norm_quant(const BatchDims& d, int B, const float* x, const float* w, int
 
 void b_gemm_i8(int B, int R, int C, const int8_t* W, const float* ws, const int8_t* xq, const float* xs,
                float* out, int ldo, bool add, cudaStream_t s) {
+  if (b_gemm_tc_eligible(B, C, W, xq) && b_gemm_tc(B, R, C, W, ws, xq, xs, out, ldo, add, s) == cudaSuccess)
+    return;
   const int tt = (B + kGT - 1) / kGT;
   // 128-row tiles while they give two waves of CTAs, else 32-row tiles
   const bool wide = (long)((R + 127) / 128) * tt >= 296;
@@ -329,6 +426,21 @@ void b_rope_kv(const BatchDims& d, int layer, int B, const int32_t* pos, const i
 
 void b_attention(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* q,
                  const float* kc, const float* vc, float* scores, float* att, cudaStream_t s) {
+  if (d.head_dim <= kAttT) {  // one fused CTA per (head, token)
+    const size_t psm = (size_t)d.max_seq * 4;
+    const dim3 g(d.n_heads, B);
+    switch (d.head_dim / 16) {  // 16 <= head_dim <= 128, head_dim % 8 == 0
+#define CHALOT_B_ATTN(C)                                                                             \
+  case C:                                                                                            \
+    cudaFuncSetAttribute(k_b_attn<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm);        \
+    k_b_attn<C><<<g, kAttT, psm, s>>>(d, layer, pos, slot, q, kc, vc, att);                          \
+    break;
+      CHALOT_B_ATTN(1) CHALOT_B_ATTN(2) CHALOT_B_ATTN(3) CHALOT_B_ATTN(4)
+      CHALOT_B_ATTN(5) CHALOT_B_ATTN(6) CHALOT_B_ATTN(7) default: CHALOT_B_ATTN(8)
+#undef CHALOT_B_ATTN
+    }
+    return;
+  }
   dim3 g1((d.max_seq + kScoreT - 1) / kScoreT, d.n_heads, B);
   switch (d.head_dim / 16) {  // 16 <= head_dim <= 256, head_dim % 8 == 0
 #define CHALOT_B_SCORES(C) \

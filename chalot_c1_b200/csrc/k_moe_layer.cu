@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(1024) k_ml_dispatch(MlDims d, MlWork w, int bm
   const int chunk = ((N + 1023) / 1024) * 32;
   const int beg = warp * chunk, end = min(N, beg + chunk);
   for (int i = threadIdx.x; i < 32 * 33; i += blockDim.x) (&cnt[0][0])[i] = 0;
+  if (w.amax)  // the h absmax the few-slot gate/up kernel raises
+    for (int i = threadIdx.x; i < N; i += blockDim.x) w.amax[i] = 0u;
   __syncthreads();
   for (int i0 = beg; i0 < end; i0 += 32) {
     const int i = i0 + lane;
@@ -289,33 +291,35 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
 // The tile GEMM above stages unpacked weights in shared memory and feeds one
 // slot per 16-byte load, which is instruction-bound at 8 slots; here the
 // weights stream once per expert through a cp.async ring in their packed
-// form, coalesced, and each thread keeps whole weight rows: thread t owns
-// rows (gate/up: the gate and the up row of hidden unit r0+t; down: output
-// row r0+t), unpacks each 16-byte group chunk once and dots it with every
-// slot of the expert (up to kFewSlots, staged per chunk and read by
-// broadcast). Each group dot is one dp4a chain started at the bits of
-// 1.5*2^23, so its result is already (float)dot in biased form (i2f_exact
-// without the add); the f32 group epilogue t = t + ((float)dot * s_g) * xs
-// runs in registers in group order, as in matmul_int4 (src/tensor/matmul.rs:
-// 452-654). Group 32 only; dims multiples of kFewKc.
-constexpr int kFewSlots = 16;                    // slots per block (the dispatch's tile size)
-constexpr int kFewKc = 128;                      // columns per stage: 4 groups of 32
-constexpr int kFewStages = 4;
-constexpr int kFewWStride = kFewKc / 2 + 16;     // packed row stride in shared memory (80 B: conflict-free)
-constexpr int kFewGuThreads = 64;                // gate/up: 64 hidden units (128 rows) per block
-constexpr int kFewDnThreads = 128;               // down: 128 output rows per block
+// form, coalesced, and each thread keeps whole weight rows: a thread owns R
+// rows (gate/up: the gate and the up row of one hidden unit; down: one output
+// row), unpacks each 16-byte group chunk once and dots it with its share of
+// the expert's slots (up to kFewSlots, staged per chunk and read by
+// broadcast). With SPLIT = 2 two threads share each row, one taking slots
+// 0-3, 8-11 and the other 4-7, 12-15, which doubles the threads of a
+// few-row pass. Each group dot is one dp4a chain started at the bits of
+// 1.5*2^23, so its result is already (float)dot in biased form; the f32 group
+// epilogue t = t + ((float)dot * s_g) * xs runs in registers in group order,
+// as in matmul_int4 (src/tensor/matmul.rs:452-654). Group 32 only; dims
+// multiples of kFewKc.
+constexpr int kFewSlots = 16;  // slots per block (the dispatch's tile size)
+constexpr int kFewKc = 64;     // columns per stage: 2 groups of 32
+constexpr int kFewStages = 3;
+constexpr int kFewGuThreads = 128;  // gate/up: 128 hidden units (256 rows) per block
+constexpr int kFewDnThreads = 128;  // down: 64 output rows per block, two threads per row
 
-template <bool GU, int NT>
-__host__ __device__ constexpr size_t few_stage_bytes() {
-  return (size_t)(GU ? 2 : 1) * NT * (kFewWStride + 16) + (size_t)kFewSlots * kFewKc;
-}
-template <bool GU, int NT>
-__host__ __device__ constexpr size_t few_smem() {
-  return few_stage_bytes<GU, NT>() * kFewStages;
-}
+// Stage: packed rows [rows][32 B] (16-byte chunks swizzled by row bit 2, so
+// eight consecutive rows read by eight lanes hit eight bank groups), scales
+// [rows][2] f32, activations [kFewSlots][kFewKc].
+__host__ __device__ constexpr size_t few_stage_bytes(int rows) { return (size_t)rows * 40 + kFewSlots * kFewKc; }
 
 CHALOT_DEV void few_cp16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+CHALOT_DEV void few_cp8(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
                "l"(src)
                : "memory");
 }
@@ -346,51 +350,49 @@ CHALOT_DEV void few_unpack(uint4 p, int (&o)[8]) {
   }
 }
 
-template <bool GU, bool RP, int NT>
+template <bool GU, bool RP, int NT, int SPLIT>
 __global__ void __launch_bounds__(NT) k_ml_few(MlDims d, const MlExperts XP, MlWork w) {
   extern __shared__ __align__(16) unsigned char smem[];
-  constexpr int R = GU ? 2 : 1;  // weight rows per thread
-  constexpr int ROWS = R * NT;
+  constexpr int R = GU ? 2 : 1;     // weight rows per thread
+  constexpr int RT = NT / SPLIT;    // row threads per block
+  constexpr int ROWS = R * RT;
+  constexpr size_t SB = few_stage_bytes(ROWS);
   const int mb = blockIdx.y;
   if (mb >= *w.n_mb) return;
   const int e = w.mb_e[mb], p0 = w.mb_p0[mb], cnt = w.mb_n[mb];
   const int in_dim = GU ? d.dim : d.H;
   const int out_rows = GU ? d.H : d.dim;
   const int ng = in_dim >> 5;
-  const int r0 = blockIdx.x * NT;
+  const int r0 = blockIdx.x * RT;
   const int tid = threadIdx.x;
+  const int rt = tid % RT, half = tid / RT;  // row thread, slot share (warp-uniform)
   const uint8_t* wmat = GU ? XP.ex[e].gu : XP.ex[e].dn;
   const float* smat = GU ? XP.ex[e].gus : XP.ex[e].dns;
 
-  // stage layout: packed rows [ROWS][kFewWStride], scales [ROWS][4] f32, x [kFewSlots][kFewKc]
-  auto wst = [&](int st) { return smem + (size_t)st * few_stage_bytes<GU, NT>(); };
-  auto sst = [&](int st) { return reinterpret_cast<float*>(wst(st) + ROWS * kFewWStride); };
-  auto xst = [&](int st) { return reinterpret_cast<int8_t*>(wst(st) + ROWS * (kFewWStride + 16)); };
-
-  float xs[kFewSlots];
+  constexpr int NA = kFewSlots / SPLIT;  // this thread's slots: accumulator ai holds slot
+  float xs[NA];                          // ((ai / 4) * SPLIT + half) * 4 + ai % 4
 #pragma unroll
-  for (int s = 0; s < kFewSlots; ++s)
-    xs[s] = s < cnt ? (GU ? w.xs[w.perm[p0 + s] / d.K] : w.hs[p0 + s]) : 0.0f;
+  for (int ai = 0; ai < NA; ++ai) {
+    const int s = ((ai >> 2) * SPLIT + half) * 4 + (ai & 3);
+    xs[ai] = s < cnt ? (GU ? w.xs[w.perm[p0 + s] / d.K] : w.hs[p0 + s]) : 0.0f;
+  }
 
   const int nk = in_dim / kFewKc;
   auto load = [&](int k) {
-    unsigned char* W = wst(k % kFewStages);
-    float* S = sst(k % kFewStages);
-    int8_t* X = xst(k % kFewStages);
+    unsigned char* W = smem + (size_t)(k % kFewStages) * SB;
+    float* S = reinterpret_cast<float*>(W + ROWS * 32);
+    int8_t* X = reinterpret_cast<int8_t*>(W + ROWS * 40);
     const int k0 = k * kFewKc;
-    for (int c = tid; c < ROWS * 4; c += NT) {  // 4 x 16 B of packed weights per row
-      const int lr = c >> 2, j = c & 3;
-      const int unit = r0 + (GU ? lr % NT : lr);
+    for (int c = tid; c < ROWS * 3; c += NT) {  // per row: 2 x 16 B of packed weights, 8 B of scales
+      const int lr = c / 3, j = c - lr * 3;
+      const int unit = r0 + (GU ? lr % RT : lr);
       if (unit < out_rows) {
-        const int mrow = GU ? (lr < NT ? unit : d.H + unit) : unit;
-        few_cp16(W + lr * kFewWStride + j * 16, wmat + (size_t)mrow * (in_dim >> 1) + (k0 >> 1) + j * 16);
-      }
-    }
-    for (int lr = tid; lr < ROWS; lr += NT) {  // the row's 4 group scales
-      const int unit = r0 + (GU ? lr % NT : lr);
-      if (unit < out_rows) {
-        const int mrow = GU ? (lr < NT ? unit : d.H + unit) : unit;
-        few_cp16(S + lr * 4, smat + (size_t)mrow * ng + (k0 >> 5));
+        const int mrow = GU ? (lr < RT ? unit : d.H + unit) : unit;
+        if (j < 2)
+          few_cp16(W + lr * 32 + 16 * (j ^ ((lr >> 2) & 1)),
+                   wmat + (size_t)mrow * (in_dim >> 1) + (k0 >> 1) + j * 16);
+        else
+          few_cp8(S + lr * 2, smat + (size_t)mrow * ng + (k0 >> 5));
       }
     }
     for (int c = tid; c < cnt * (kFewKc / 16); c += NT) {  // the slots' activation chunks
@@ -400,11 +402,11 @@ __global__ void __launch_bounds__(NT) k_ml_few(MlDims d, const MlExperts XP, MlW
     }
   };
 
-  float acc[R][kFewSlots];
+  float acc[R][NA];
 #pragma unroll
   for (int r = 0; r < R; ++r)
 #pragma unroll
-    for (int s = 0; s < kFewSlots; ++s) acc[r][s] = 0.0f;
+    for (int ai = 0; ai < NA; ++ai) acc[r][ai] = 0.0f;
 
 #pragma unroll
   for (int k = 0; k < kFewStages - 1; ++k) {
@@ -416,23 +418,32 @@ __global__ void __launch_bounds__(NT) k_ml_few(MlDims d, const MlExperts XP, MlW
     __syncthreads();  // stage k landed for every thread; stage k-1 is free
     if (k + kFewStages - 1 < nk) load(k + kFewStages - 1);
     few_commit();
-    const unsigned char* W = wst(k % kFewStages);
-    const float* S = sst(k % kFewStages);
-    const int8_t* X = xst(k % kFewStages);
-    float4 sc[R];
+    const unsigned char* W = smem + (size_t)(k % kFewStages) * SB;
+    const float* S = reinterpret_cast<const float*>(W + ROWS * 32);
+    const int8_t* X = reinterpret_cast<const int8_t*>(W + ROWS * 40);
+    float2 sc[R];
 #pragma unroll
-    for (int r = 0; r < R; ++r) sc[r] = lds16f(S + (tid + r * NT) * 4);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
+    for (int r = 0; r < R; ++r) sc[r] = *reinterpret_cast<const float2*>(S + (rt + r * RT) * 2);
+#pragma unroll 1
+    for (int g = 0; g < 2; ++g) {
       int wv[R][8];
-#pragma unroll
-      for (int r = 0; r < R; ++r) few_unpack<RP>(lds16(W + (tid + r * NT) * kFewWStride + g * 16), wv[r]);
       float ws[R];
 #pragma unroll
-      for (int r = 0; r < R; ++r) ws[r] = g == 0 ? sc[r].x : g == 1 ? sc[r].y : g == 2 ? sc[r].z : sc[r].w;
+      for (int r = 0; r < R; ++r) {
+        const int lr = rt + r * RT;
+        few_unpack<RP>(lds16(W + lr * 32 + 16 * (g ^ ((lr >> 2) & 1))), wv[r]);
+        ws[r] = g ? sc[r].y : sc[r].x;
+      }
+      // this thread's slots in fours, with a real branch past the last four
+      // that holds a slot (slots past cnt within it read stale chunks; never
+      // stored)
 #pragma unroll
-      for (int s = 0; s < kFewSlots; ++s) {
-        if (s < cnt) {
+      for (int q = 0; q < kFewSlots / (4 * SPLIT); ++q) {
+        const int sg = q * SPLIT + half;
+        if (sg * 4 >= cnt) break;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int s = sg * 4 + u;
           const uint4 xa = lds16(X + s * kFewKc + g * 32), xb = lds16(X + s * kFewKc + g * 32 + 16);
 #pragma unroll
           for (int r = 0; r < R; ++r) {
@@ -446,24 +457,59 @@ __global__ void __launch_bounds__(NT) k_ml_few(MlDims d, const MlExperts XP, MlW
             t = __dp4a(wv[r][6], (int)xb.z, t);
             t = __dp4a(wv[r][7], (int)xb.w, t);
             const float f = __fsub_rn(__int_as_float(t), 12582912.0f);
-            acc[r][s] = __fadd_rn(acc[r][s], __fmul_rn(__fmul_rn(f, ws[r]), xs[s]));
+            const int ai = q * 4 + u;  // this thread's accumulator of slot s
+            acc[r][ai] = __fadd_rn(acc[r][ai], __fmul_rn(__fmul_rn(f, ws[r]), xs[ai]));
           }
         }
       }
     }
   }
-  const int unit = r0 + tid;
-  if (unit >= out_rows) return;
+  const int unit = r0 + rt;
+  const bool live = unit < out_rows;
 #pragma unroll
-  for (int s = 0; s < kFewSlots; ++s) {
-    if (s < cnt) {
-      const size_t p = (size_t)(p0 + s);
-      if (GU)
-        w.h[p * d.H + unit] = swiglu_elem(acc[0][s], acc[R - 1][s], unit, d.H);
-      else
-        w.y[p * d.dim + unit] = acc[0][s];
+  for (int q = 0; q < kFewSlots / (4 * SPLIT); ++q) {
+    const int sg = q * SPLIT + half;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int s = sg * 4 + u, ai = q * 4 + u;
+      if (s < cnt) {
+        const size_t p = (size_t)(p0 + s);
+        if (GU) {
+          // h, and its absmax over the row for the quantization (non-negative
+          // floats order as their bits)
+          const float h = live ? swiglu_elem(acc[0][ai], acc[R - 1][ai], unit, d.H) : 0.0f;
+          if (live) w.h[p * d.H + unit] = h;
+          const float m = warp_max(fabsf(h));
+          if ((tid & 31) == 0) atomicMax(w.amax + p, __float_as_uint(m));
+        } else if (live) {
+          w.y[p * d.dim + unit] = acc[0][ai];
+        }
+      }
     }
   }
+}
+
+// quantize_f32_to_i8 of each h row with its absmax reduced by the few-slot
+// gate/up kernel: 16 elements per thread, one 16-byte store (H % 16 == 0, so
+// every element takes the vector path of the quantizer).
+__global__ void __launch_bounds__(256) k_ml_quant_amax(MlDims d, MlWork w) {
+  const int per_row = d.H >> 4;
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)d.T * d.K * per_row) return;
+  const long p = i / per_row;
+  const int c = (int)(i - p * per_row);
+  float scale, inv;
+  quant_scale(__uint_as_float(w.amax[p]), &scale, &inv);
+  const float4* src = reinterpret_cast<const float4*>(w.h + p * d.H + c * 16);
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 v = src[k];
+    o[k] = (uint32_t)(uint8_t)quant_elem(v.x, inv) | ((uint32_t)(uint8_t)quant_elem(v.y, inv) << 8) |
+           ((uint32_t)(uint8_t)quant_elem(v.z, inv) << 16) | ((uint32_t)(uint8_t)quant_elem(v.w, inv) << 24);
+  }
+  *reinterpret_cast<uint4*>(w.hq + p * d.H + c * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+  if (c == 0) w.hs[p] = scale;
 }
 
 __global__ void __launch_bounds__(kThreads) k_ml_quant(MlDims d, MlWork w) {
@@ -543,6 +589,7 @@ size_t ml_layout(const MlDims& d, void* base, MlWork* w) {
   t.hq = reinterpret_cast<int8_t*>(take(N * d.H));
   t.hs = reinterpret_cast<float*>(take(N * 4));
   t.y = reinterpret_cast<float*>(take(N * d.dim * 4));
+  t.amax = reinterpret_cast<unsigned*>(take(N * 4));
   if (w) *w = t;
   return off;
 }
@@ -573,6 +620,11 @@ static void quantize_h(const MlDims& d, const MlWork& w, cudaStream_t s) {
   k_ml_quant<<<(unsigned)((size_t)d.T * d.K), kThreads, qsm, s>>>(d, w);
 }
 
+static void quantize_h_amax(const MlDims& d, const MlWork& w, cudaStream_t s) {
+  const long n = (long)d.T * d.K * (d.H / 16);
+  k_ml_quant_amax<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(d, w);
+}
+
 // The few-slot kernels need group 32, dims that are multiples of kFewKc and
 // 16-byte aligned expert tensors (their cp.async copies are 16 bytes).
 static bool few_eligible(const MlDims& d, const MlExperts& X) {
@@ -600,20 +652,17 @@ static void tile_gemms(const MlDims& d, const MlExperts& X, const MlWork& w, int
   const unsigned nmb = (unsigned)std::min(N, N / bm + d.E);
   const dim3 ggu((d.H + kBN / 2 - 1) / (kBN / 2), nmb), gdn((d.dim + kBN - 1) / kBN, nmb);
   if (bm == kFewSlots) {
-    const dim3 fgu((d.H + kFewGuThreads - 1) / kFewGuThreads, nmb), fdn((d.dim + kFewDnThreads - 1) / kFewDnThreads, nmb);
-    constexpr size_t sgu = few_smem<true, kFewGuThreads>(), sdn = few_smem<false, kFewDnThreads>();
+    constexpr int RG = kFewGuThreads, RD = kFewDnThreads / 2;  // row threads per block
+    const dim3 fgu((d.H + RG - 1) / RG, nmb), fdn((d.dim + RD - 1) / RD, nmb);
+    const size_t sgu = few_stage_bytes(2 * RG) * kFewStages, sdn = few_stage_bytes(RD) * kFewStages;
     if (X.repacked) {
-      cudaFuncSetAttribute(k_ml_few<true, true, kFewGuThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sgu);
-      cudaFuncSetAttribute(k_ml_few<false, true, kFewDnThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sdn);
-      k_ml_few<true, true, kFewGuThreads><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
-      quantize_h(d, w, s);
-      k_ml_few<false, true, kFewDnThreads><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
+      k_ml_few<true, true, kFewGuThreads, 1><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
+      quantize_h_amax(d, w, s);
+      k_ml_few<false, true, kFewDnThreads, 2><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
     } else {
-      cudaFuncSetAttribute(k_ml_few<true, false, kFewGuThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sgu);
-      cudaFuncSetAttribute(k_ml_few<false, false, kFewDnThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sdn);
-      k_ml_few<true, false, kFewGuThreads><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
-      quantize_h(d, w, s);
-      k_ml_few<false, false, kFewDnThreads><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
+      k_ml_few<true, false, kFewGuThreads, 1><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
+      quantize_h_amax(d, w, s);
+      k_ml_few<false, false, kFewDnThreads, 2><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
     }
   } else if (bm == 8) {
     cudaFuncSetAttribute(k_ml_gemm<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);

@@ -33,6 +33,7 @@
 #include "devstat.h"
 #include "moe_layer.h"
 #include "tc.cuh"
+#include "tmap.h"
 #include "unpack.cuh"
 
 namespace chalot {
@@ -386,6 +387,8 @@ __global__ void __launch_bounds__(256) k_tc_quant(MlDims d, MlWork w, MlTcWork t
   if (c == 0) w.hs[p] = scale;
 }
 
+}  // namespace
+
 // ---- host: tensor maps -------------------------------------------------------
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -393,7 +396,7 @@ using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, 
                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
                                  CUtensorMapFloatOOBfill);
 
-EncodeTiled encoder() {
+static EncodeTiled encoder() {
   static EncodeTiled fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -420,7 +423,6 @@ bool make_map(CUtensorMap* m, CUtensorMapDataType dt, size_t esize, const void* 
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-}  // namespace
 
 bool ml_tc_eligible(const MlDims& d) {
   return d.group == 32 && d.dim % 128 == 0 && d.H % 128 == 0 && d.dim <= 16384 && d.H <= 16384;

@@ -41,6 +41,7 @@ struct MlWork {
   int8_t* hq;     // [T*k][H] quantized h
   float* hs;      // [T*k]
   float* y;       // [T*k][dim] expert outputs, by position
+  unsigned* amax; // [T*k] absmax of each h row (float bits): zeroed by the dispatch, raised by the few-slot gate/up
 };
 
 // Extra workspace of the tensor-core path (k_moe_tc.cu).
