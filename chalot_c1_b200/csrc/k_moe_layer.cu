@@ -288,38 +288,39 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
 }
 
 // Few-slot expert products (batched decode: a handful of slots per expert).
-// The tile GEMM above stages unpacked weights in shared memory and feeds one
-// slot per 16-byte load, which is instruction-bound at 8 slots; here the
-// weights stream once per expert through a cp.async ring in their packed
-// form, coalesced, and each thread keeps whole weight rows: a thread owns R
-// rows (gate/up: the gate and the up row of one hidden unit; down: one output
-// row), unpacks each 16-byte group chunk once and dots it with its share of
-// the expert's slots (up to kFewSlots, staged per chunk and read by
-// broadcast). With SPLIT = 2 two threads share each row, one taking slots
-// 0-3, 8-11 and the other 4-7, 12-15, which doubles the threads of a
-// few-row pass. Each group dot is one dp4a chain started at the bits of
-// 1.5*2^23, so its result is already (float)dot in biased form; the f32 group
-// epilogue t = t + ((float)dot * s_g) * xs runs in registers in group order,
-// as in matmul_int4 (src/tensor/matmul.rs:452-654). Group 32 only; dims
-// multiples of kFewKc.
-constexpr int kFewSlots = 16;  // slots per block (the dispatch's tile size)
-constexpr int kFewKc = 64;     // columns per stage: 2 groups of 32
-constexpr int kFewStages = 3;
-constexpr int kFewGuThreads = 128;  // gate/up: 128 hidden units (256 rows) per block
-constexpr int kFewDnThreads = 128;  // down: 64 output rows per block, two threads per row
-
-// Stage: packed rows [rows][32 B] (16-byte chunks swizzled by row bit 2, so
-// eight consecutive rows read by eight lanes hit eight bank groups), scales
-// [rows][2] f32, activations [kFewSlots][kFewKc].
-__host__ __device__ constexpr size_t few_stage_bytes(int rows) { return (size_t)rows * 40 + kFewSlots * kFewKc; }
+// Expert weights stream once per expert through a cp.async ring in their
+// packed form, coalesced; the group dots run on the tensor cores as
+// mma.sync m16n8k32 (s8 x s8 -> s32) straight from registers: a warp owns 16
+// weight rows and takes, per group of 32 columns, one MMA per 8 slots. Its A
+// fragment is unpacked from the staged int4 bytes (lane (g, t) holds packed
+// word t of rows g and g+8: low nibbles as k 4t..4t+3, high nibbles as
+// 16+4t..; the activations' B fragment pairs the same columns), its
+// accumulator input is the bits of 1.5*2^23, so every D element reads back as
+// 12582912 + gdot, exact, and one subtraction gives (float)gdot. The f32
+// group epilogue t = t + ((float)gdot * s_g) * xs then runs on the D fragment
+// in registers, in group order, as in matmul_int4 (src/tensor/matmul.rs:
+// 452-654). Gate/up warps hold 8 gate rows (units u..u+7) and the 8 up rows
+// of the same units, so lane (g, t) ends with gate and up of unit u+g for its
+// slots and applies SwiGLU itself. Only as many MMAs (and epilogues) as 8-slot
+// tiles hold slots run. Group 32 only; dims multiples of kFewKc.
+//
+// A dp4a formulation of the same products spends 8 dp4a per (row, slot,
+// group) on top of the 4-operation epilogue; here the MMA covers 16 rows x 8
+// slots x 32 columns in one instruction and the epilogue is what remains.
+constexpr int kFewSlots = 16;     // slots per block (the dispatch's tile size): two 8-slot MMA tiles
+constexpr int kFewKc = 128;       // columns per stage: 4 groups of 32
+constexpr int kFewStages = 4;
+constexpr int kFewWarps = 8;      // 16 weight rows per warp: 128 rows per block
+constexpr int kFewThreads = 32 * kFewWarps;
+constexpr int kFewRows = 16 * kFewWarps;
+constexpr int kFewWStride = kFewKc / 2 + 16;  // packed row stride (80 B: A-fragment loads conflict-free)
+constexpr int kFewXStride = kFewKc + 32;      // activation row stride (160 B: B-fragment loads conflict-free)
+// stage: packed rows [kFewRows][kFewWStride], scales [kFewRows][4] f32, activations [kFewSlots][kFewXStride]
+constexpr size_t kFewStageBytes = (size_t)kFewRows * (kFewWStride + 16) + (size_t)kFewSlots * kFewXStride;
+constexpr size_t kFewSmem = kFewStageBytes * kFewStages;
 
 CHALOT_DEV void few_cp16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
-               "l"(src)
-               : "memory");
-}
-CHALOT_DEV void few_cp8(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
                "l"(src)
                : "memory");
 }
@@ -329,161 +330,151 @@ CHALOT_DEV void few_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// 16 packed bytes (32 int4) -> 8 words of signed int8 in column order.
-// Repacked layout: word j byte b = column 8j+b (low nibble) and 8j+4+b
-// (high), two's complement; file layout: byte k = columns 2k (low) and 2k+1
-// (high), value + 8.
+// One packed int4 word (8 columns) -> the signed int8 words of its low and
+// high nibbles. Repacked layout: low nibbles are columns 8j..8j+3, high ones
+// 8j+4..8j+7, two's complement. File layout: byte k holds columns 2k (low)
+// and 2k+1 (high) as value + 8, so low nibbles are the even columns.
 template <bool RP>
-CHALOT_DEV void few_unpack(uint4 p, int (&o)[8]) {
-  const uint32_t in[4] = {p.x, p.y, p.z, p.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t v = RP ? in[i] ^ 0x88888888u : in[i];  // every nibble as value + 8
-    uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
-    if (!RP) {
-      const uint32_t a = __byte_perm(lo, hi, 0x5140), b = __byte_perm(lo, hi, 0x7362);
-      lo = a;
-      hi = b;
-    }
-    o[2 * i] = (int)nib_minus8(lo);
-    o[2 * i + 1] = (int)nib_minus8(hi);
-  }
+CHALOT_DEV void few_nibbles(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t v = RP ? w ^ 0x88888888u : w;  // every nibble as value + 8
+  lo = nib_minus8(v & 0x0F0F0F0Fu);
+  hi = nib_minus8((v >> 4) & 0x0F0F0F0Fu);
 }
 
-template <bool GU, bool RP, int NT, int SPLIT>
-__global__ void __launch_bounds__(NT) k_ml_few(MlDims d, const MlExperts XP, MlWork w) {
+// D = A * B + C, m16n8k32, A row-major s8, B column-major s8, s32 accumulators.
+CHALOT_DEV void mma_s8_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                             uint32_t b1, int c) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c));
+}
+
+template <bool GU, bool RP>
+__global__ void __launch_bounds__(kFewThreads) k_ml_few(MlDims d, const MlExperts XP, MlWork w) {
   extern __shared__ __align__(16) unsigned char smem[];
-  constexpr int R = GU ? 2 : 1;     // weight rows per thread
-  constexpr int RT = NT / SPLIT;    // row threads per block
-  constexpr int ROWS = R * RT;
-  constexpr size_t SB = few_stage_bytes(ROWS);
   const int mb = blockIdx.y;
   if (mb >= *w.n_mb) return;
   const int e = w.mb_e[mb], p0 = w.mb_p0[mb], cnt = w.mb_n[mb];
   const int in_dim = GU ? d.dim : d.H;
   const int out_rows = GU ? d.H : d.dim;
   const int ng = in_dim >> 5;
-  const int r0 = blockIdx.x * RT;
-  const int tid = threadIdx.x;
-  const int rt = tid % RT, half = tid / RT;  // row thread, slot share (warp-uniform)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  // block rows: gate/up: units u0 + 8*warp + i (i < 8: gate row, i >= 8: up row of unit i-8); down: r0 + row
+  const int r0 = blockIdx.x * (GU ? kFewRows / 2 : kFewRows);
   const uint8_t* wmat = GU ? XP.ex[e].gu : XP.ex[e].dn;
   const float* smat = GU ? XP.ex[e].gus : XP.ex[e].dns;
+  const int ntiles = cnt > 8 ? 2 : 1;
 
-  constexpr int NA = kFewSlots / SPLIT;  // this thread's slots: accumulator ai holds slot
-  float xs[NA];                          // ((ai / 4) * SPLIT + half) * 4 + ai % 4
+  // this lane's slots: nt*8 + 2t and nt*8 + 2t + 1 of each 8-slot tile
+  float xs[2][2];
 #pragma unroll
-  for (int ai = 0; ai < NA; ++ai) {
-    const int s = ((ai >> 2) * SPLIT + half) * 4 + (ai & 3);
-    xs[ai] = s < cnt ? (GU ? w.xs[w.perm[p0 + s] / d.K] : w.hs[p0 + s]) : 0.0f;
-  }
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int s = nt * 8 + 2 * t + j;
+      xs[nt][j] = s < cnt ? (GU ? w.xs[w.perm[p0 + s] / d.K] : w.hs[p0 + s]) : 0.0f;
+    }
+
+  auto unit_of = [&](int lr) { return GU ? r0 + (lr >> 4) * 8 + (lr & 7) : r0 + lr; };
+  auto mrow_of = [&](int lr, int unit) { return GU ? ((lr & 8) ? d.H + unit : unit) : unit; };
 
   const int nk = in_dim / kFewKc;
   auto load = [&](int k) {
-    unsigned char* W = smem + (size_t)(k % kFewStages) * SB;
-    float* S = reinterpret_cast<float*>(W + ROWS * 32);
-    int8_t* X = reinterpret_cast<int8_t*>(W + ROWS * 40);
+    unsigned char* W = smem + (size_t)(k % kFewStages) * kFewStageBytes;
+    unsigned char* S = W + kFewRows * kFewWStride;
+    int8_t* X = reinterpret_cast<int8_t*>(S + kFewRows * 16);
     const int k0 = k * kFewKc;
-    for (int c = tid; c < ROWS * 3; c += NT) {  // per row: 2 x 16 B of packed weights, 8 B of scales
-      const int lr = c / 3, j = c - lr * 3;
-      const int unit = r0 + (GU ? lr % RT : lr);
+    for (int c = tid; c < kFewRows * 5; c += kFewThreads) {  // per row: 4 x 16 B of packed weights, 16 B of scales
+      const int lr = c / 5, j = c - lr * 5;
+      const int unit = unit_of(lr);
       if (unit < out_rows) {
-        const int mrow = GU ? (lr < RT ? unit : d.H + unit) : unit;
-        if (j < 2)
-          few_cp16(W + lr * 32 + 16 * (j ^ ((lr >> 2) & 1)),
-                   wmat + (size_t)mrow * (in_dim >> 1) + (k0 >> 1) + j * 16);
+        const int mrow = mrow_of(lr, unit);
+        if (j < 4)
+          few_cp16(W + lr * kFewWStride + j * 16, wmat + (size_t)mrow * (in_dim >> 1) + (k0 >> 1) + j * 16);
         else
-          few_cp8(S + lr * 2, smat + (size_t)mrow * ng + (k0 >> 5));
+          few_cp16(S + lr * 16, smat + (size_t)mrow * ng + (k0 >> 5));
       }
     }
-    for (int c = tid; c < cnt * (kFewKc / 16); c += NT) {  // the slots' activation chunks
+    for (int c = tid; c < cnt * (kFewKc / 16); c += kFewThreads) {  // the slots' activation chunks
       const int s = c / (kFewKc / 16), j = c % (kFewKc / 16);
       const int8_t* a = GU ? w.xq + (size_t)(w.perm[p0 + s] / d.K) * in_dim : w.hq + (size_t)(p0 + s) * in_dim;
-      few_cp16(X + s * kFewKc + j * 16, a + k0 + j * 16);
+      few_cp16(X + s * kFewXStride + j * 16, a + k0 + j * 16);
     }
   };
 
-  float acc[R][NA];
+  float acc[2][4];
 #pragma unroll
-  for (int r = 0; r < R; ++r)
+  for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-    for (int ai = 0; ai < NA; ++ai) acc[r][ai] = 0.0f;
+    for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
 
 #pragma unroll
   for (int k = 0; k < kFewStages - 1; ++k) {
     if (k < nk) load(k);
     few_commit();
   }
+  const int la = warp * 16 + g, lb = la + 8;  // this lane's two rows in the block
   for (int k = 0; k < nk; ++k) {
     few_wait<kFewStages - 2>();
     __syncthreads();  // stage k landed for every thread; stage k-1 is free
     if (k + kFewStages - 1 < nk) load(k + kFewStages - 1);
     few_commit();
-    const unsigned char* W = smem + (size_t)(k % kFewStages) * SB;
-    const float* S = reinterpret_cast<const float*>(W + ROWS * 32);
-    const int8_t* X = reinterpret_cast<const int8_t*>(W + ROWS * 40);
-    float2 sc[R];
+    const unsigned char* W = smem + (size_t)(k % kFewStages) * kFewStageBytes;
+    const float* S = reinterpret_cast<const float*>(W + kFewRows * kFewWStride);
+    const int8_t* X = reinterpret_cast<const int8_t*>(S + kFewRows * 4);
+    const float4 sa = *reinterpret_cast<const float4*>(S + la * 4), sb = *reinterpret_cast<const float4*>(S + lb * 4);
 #pragma unroll
-    for (int r = 0; r < R; ++r) sc[r] = *reinterpret_cast<const float2*>(S + (rt + r * RT) * 2);
-#pragma unroll 1
-    for (int g = 0; g < 2; ++g) {
-      int wv[R][8];
-      float ws[R];
+    for (int q = 0; q < 4; ++q) {  // the stage's groups, in order
+      uint32_t a0, a1, a2, a3;
+      few_nibbles<RP>(*reinterpret_cast<const uint32_t*>(W + la * kFewWStride + q * 16 + 4 * t), a0, a2);
+      few_nibbles<RP>(*reinterpret_cast<const uint32_t*>(W + lb * kFewWStride + q * 16 + 4 * t), a1, a3);
+      const float wa = q == 0 ? sa.x : q == 1 ? sa.y : q == 2 ? sa.z : sa.w;
+      const float wb = q == 0 ? sb.x : q == 1 ? sb.y : q == 2 ? sb.z : sb.w;
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const int lr = rt + r * RT;
-        few_unpack<RP>(lds16(W + lr * 32 + 16 * (g ^ ((lr >> 2) & 1))), wv[r]);
-        ws[r] = g ? sc[r].y : sc[r].x;
-      }
-      // this thread's slots in fours, with a real branch past the last four
-      // that holds a slot (slots past cnt within it read stale chunks; never
-      // stored)
+      for (int nt = 0; nt < 2; ++nt) {
+        if (nt < ntiles) {
+          // B fragment: columns 8t..8t+7 of the group for slot nt*8 + g (even/odd split in the file layout)
+          const uint2 xv = *reinterpret_cast<const uint2*>(X + (nt * 8 + g) * kFewXStride + q * 32 + 8 * t);
+          const uint32_t b0 = RP ? xv.x : __byte_perm(xv.x, xv.y, 0x6420);
+          const uint32_t b1 = RP ? xv.y : __byte_perm(xv.x, xv.y, 0x7531);
+          int dd[4];
+          mma_s8_16832(dd, a0, a1, a2, a3, b0, b1, 0x4B400000);
 #pragma unroll
-      for (int q = 0; q < kFewSlots / (4 * SPLIT); ++q) {
-        const int sg = q * SPLIT + half;
-        if (sg * 4 >= cnt) break;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int s = sg * 4 + u;
-          const uint4 xa = lds16(X + s * kFewKc + g * 32), xb = lds16(X + s * kFewKc + g * 32 + 16);
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            int t = 0x4B400000;  // 1.5*2^23: the chain ends at the float bits of 1.5*2^23 + dot
-            t = __dp4a(wv[r][0], (int)xa.x, t);
-            t = __dp4a(wv[r][1], (int)xa.y, t);
-            t = __dp4a(wv[r][2], (int)xa.z, t);
-            t = __dp4a(wv[r][3], (int)xa.w, t);
-            t = __dp4a(wv[r][4], (int)xb.x, t);
-            t = __dp4a(wv[r][5], (int)xb.y, t);
-            t = __dp4a(wv[r][6], (int)xb.z, t);
-            t = __dp4a(wv[r][7], (int)xb.w, t);
-            const float f = __fsub_rn(__int_as_float(t), 12582912.0f);
-            const int ai = q * 4 + u;  // this thread's accumulator of slot s
-            acc[r][ai] = __fadd_rn(acc[r][ai], __fmul_rn(__fmul_rn(f, ws[r]), xs[ai]));
+          for (int i = 0; i < 4; ++i) {
+            const float f = __fsub_rn(__int_as_float(dd[i]), 12582912.0f);
+            acc[nt][i] = __fadd_rn(acc[nt][i], __fmul_rn(__fmul_rn(f, i < 2 ? wa : wb), xs[nt][i & 1]));
           }
         }
       }
     }
   }
-  const int unit = r0 + rt;
-  const bool live = unit < out_rows;
+  // D fragment: acc[nt][0..1] = row la, slots nt*8+2t+{0,1}; acc[nt][2..3] = row lb, same slots
 #pragma unroll
-  for (int q = 0; q < kFewSlots / (4 * SPLIT); ++q) {
-    const int sg = q * SPLIT + half;
+  for (int nt = 0; nt < 2; ++nt) {
+    if (nt >= ntiles) break;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int s = sg * 4 + u, ai = q * 4 + u;
-      if (s < cnt) {
-        const size_t p = (size_t)(p0 + s);
-        if (GU) {
-          // h, and its absmax over the row for the quantization (non-negative
-          // floats order as their bits)
-          const float h = live ? swiglu_elem(acc[0][ai], acc[R - 1][ai], unit, d.H) : 0.0f;
-          if (live) w.h[p * d.H + unit] = h;
-          const float m = warp_max(fabsf(h));
-          if ((tid & 31) == 0) atomicMax(w.amax + p, __float_as_uint(m));
-        } else if (live) {
-          w.y[p * d.dim + unit] = acc[0][ai];
-        }
+    for (int j = 0; j < 2; ++j) {
+      const int s = nt * 8 + 2 * t + j;
+      const bool ok = s < cnt;
+      const size_t p = (size_t)(p0 + s);
+      if (GU) {
+        // gate (row la) and up (row lb) of unit u: h, and its absmax over the
+        // row for the quantization (non-negative floats order as their bits)
+        const int u = unit_of(la);
+        const bool live = ok && u < out_rows;
+        const float h = live ? swiglu_elem(acc[nt][j], acc[nt][2 + j], u, d.H) : 0.0f;
+        if (live) w.h[p * d.H + u] = h;
+        float m = fabsf(h);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+        if (g == 0 && ok) atomicMax(w.amax + p, __float_as_uint(m));
+      } else if (ok) {
+        const int ua = unit_of(la), ub = unit_of(lb);
+        if (ua < out_rows) w.y[p * d.dim + ua] = acc[nt][j];
+        if (ub < out_rows) w.y[p * d.dim + ub] = acc[nt][2 + j];
       }
     }
   }
@@ -652,18 +643,14 @@ static void tile_gemms(const MlDims& d, const MlExperts& X, const MlWork& w, int
   const unsigned nmb = (unsigned)std::min(N, N / bm + d.E);
   const dim3 ggu((d.H + kBN / 2 - 1) / (kBN / 2), nmb), gdn((d.dim + kBN - 1) / kBN, nmb);
   if (bm == kFewSlots) {
-    constexpr int RG = kFewGuThreads, RD = kFewDnThreads / 2;  // row threads per block
-    const dim3 fgu((d.H + RG - 1) / RG, nmb), fdn((d.dim + RD - 1) / RD, nmb);
-    const size_t sgu = few_stage_bytes(2 * RG) * kFewStages, sdn = few_stage_bytes(RD) * kFewStages;
-    if (X.repacked) {
-      k_ml_few<true, true, kFewGuThreads, 1><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
-      quantize_h_amax(d, w, s);
-      k_ml_few<false, true, kFewDnThreads, 2><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
-    } else {
-      k_ml_few<true, false, kFewGuThreads, 1><<<fgu, kFewGuThreads, sgu, s>>>(d, X, w);
-      quantize_h_amax(d, w, s);
-      k_ml_few<false, false, kFewDnThreads, 2><<<fdn, kFewDnThreads, sdn, s>>>(d, X, w);
-    }
+    const dim3 fgu((d.H + kFewRows / 2 - 1) / (kFewRows / 2), nmb), fdn((d.dim + kFewRows - 1) / kFewRows, nmb);
+    auto gu = X.repacked ? k_ml_few<true, true> : k_ml_few<true, false>;
+    auto dn = X.repacked ? k_ml_few<false, true> : k_ml_few<false, false>;
+    cudaFuncSetAttribute(gu, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFewSmem);
+    cudaFuncSetAttribute(dn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFewSmem);
+    gu<<<fgu, kFewThreads, kFewSmem, s>>>(d, X, w);
+    quantize_h_amax(d, w, s);
+    dn<<<fdn, kFewThreads, kFewSmem, s>>>(d, X, w);
   } else if (bm == 8) {
     cudaFuncSetAttribute(k_ml_gemm<true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
     cudaFuncSetAttribute(k_ml_gemm<false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm);
