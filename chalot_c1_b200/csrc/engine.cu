@@ -1185,15 +1185,16 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
       b_attention(bd, l, B, b.pos, b.slot, b.q, b.kc, b.vc, b.scores, b.att, s);
       CK(op_quantize_i8(b.xq, b.xs, b.att, B, D, s));
       b_gemm_i8(B, D, D, L.o, L.o_s, b.xq, b.xs, b.x, D, true, s);  // residual (engine.rs:312-322)
-      b_rmsnorm(bd, B, b.x, L.rms_ffn, b.xb, s);
+      const float* next_norm = l + 1 < (int)c.n_layers ? e->layers[l + 1].rms_attn : e->final_norm;
       if (e->ep) {
+        b_rmsnorm(bd, B, b.x, L.rms_ffn, b.xb, s);
         if (int rc = ep_moe(e, l, B, md, w, s, &msg)) return set_error(rc, "forward_batch: " + msg);
-      } else {
-        CK(tc ? ml_run_tc(md, b.xb, L.router_w, L.router_b, b.experts[l], w, t, b.eout, s)
-              : ml_run(md, b.xb, L.router_w, L.router_b, b.experts[l], w, b.eout, s));
+        b_add((long)B * D, b.x, b.eout, s);  // x += expert_out (engine.rs:401)
+        b_norm_quant(bd, B, b.x, next_norm, b.xq, b.xs, s);
+      } else {  // rmsnorm, MoE block, x += expert_out (engine.rs:325-401) and the next norm + quantize
+        CK(ml_run_decode(md, b.x, L.rms_ffn, L.router_w, L.router_b, b.experts[l], w, tc ? &t : nullptr,
+                         next_norm, b.xq, b.xs, s));
       }
-      b_add((long)B * D, b.x, b.eout, s);  // x += expert_out (engine.rs:401)
-      b_norm_quant(bd, B, b.x, l + 1 < (int)c.n_layers ? e->layers[l + 1].rms_attn : e->final_norm, b.xq, b.xs, s);
     }
     b_gemm_i8(B, (int)c.vocab_size, D, e->out_w, e->out_s, b.xq, b.xs, b.logits, (int)c.vocab_size, false, s);
     b_argmax(B, (int)c.vocab_size, b.logits, b.out, s);

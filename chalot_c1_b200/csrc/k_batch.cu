@@ -261,13 +261,13 @@ __global__ void __launch_bounds__(kT) k_b_pv(BatchDims d, int layer, const int32
 constexpr int kAttT = 128;  // threads of the fused attention CTA (head_dim <= 128)
 constexpr int kAttU = 16;   // V rows in flight per thread
 
-// CTA (head h, token b): the scores of positions 0..pos (one thread per
+// CTA (head h, token b): the scores of positions 0..pos (four lanes per
 // position: dot_f32_avx2 order, then 30*tanh(x/30)), softmax_avx2 over them
 // in shared memory, then o[c] = sum_t p_t v_t[c] in t order (thread c), with
 // kAttU V rows loaded ahead. One pass over this head's K and V, and the
 // softmax once per head instead of once per 8 output columns.
 template <int C16>
-__global__ void __launch_bounds__(kAttT, 6) k_b_attn(BatchDims d, int layer, const int32_t* pos, const int32_t* slot,
+__global__ void __launch_bounds__(kAttT, 4) k_b_attn(BatchDims d, int layer, const int32_t* pos, const int32_t* slot,
                                                   const float* q, const float* kc, const float* vc, float* att) {
   extern __shared__ __align__(16) float p[];  // [max_seq] scores, then probabilities
   __shared__ __align__(16) float qh[256];
@@ -279,35 +279,48 @@ __global__ void __launch_bounds__(kAttT, 6) k_b_attn(BatchDims d, int layer, con
   for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = q[(size_t)b * d.dim + h * hd + i];
   __syncthreads();
   const float rs = div_rn(1.0f, __fsqrt_rn((float)hd));
+  // scores: four lanes per position, lane l4 owning elements 4*l4..4*l4+3 of
+  // every 16-element chunk, i.e. the dot_f32_avx2 accumulators a0[0..3]
+  // (l4 = 0), a0[4..7] (1), a1[0..3] (2), a1[4..7] (3), each summed in chunk
+  // order; the lanes then combine them as the reference does (a0 + a1, then
+  // hsum8). A quad reads 64 contiguous bytes of its K row per chunk.
+  const int lane = threadIdx.x & 31, quad = lane >> 2, l4 = lane & 3;
+  const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  float qv[C16][4];
+#pragma unroll
+  for (int c = 0; c < C16; ++c)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) qv[c][u] = qh[16 * c + 4 * l4 + u];
   float mx = -INFINITY;
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const float* k = kc + base + (size_t)t * d.dim;
-    float a0[8], a1[8];
+  for (int t0 = warp * 8; t0 < n; t0 += nwarps * 8) {
+    const int t = t0 + quad;
+    float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (t < n) {
+      const float* k = kc + base + (size_t)t * d.dim + 4 * l4;
+      float4 kv[C16];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) a0[j] = a1[j] = 0.0f;
-#pragma unroll 2
-    for (int c = 0; c < C16; ++c) {
-      const float4* kk = reinterpret_cast<const float4*>(k + c * 16);
-      const float4 k0 = kk[0], k1 = kk[1], k2 = kk[2], k3 = kk[3];
-      const float kv[16] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w,
-                            k2.x, k2.y, k2.z, k2.w, k3.x, k3.y, k3.z, k3.w};
+      for (int c = 0; c < C16; ++c) kv[c] = *reinterpret_cast<const float4*>(k + 16 * c);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[c * 16 + j], kv[j]));
-        a1[j] = __fadd_rn(a1[j], __fmul_rn(qh[c * 16 + 8 + j], kv[8 + j]));
+      for (int c = 0; c < C16; ++c) {
+        a[0] = __fadd_rn(a[0], __fmul_rn(qv[c][0], kv[c].x));
+        a[1] = __fadd_rn(a[1], __fmul_rn(qv[c][1], kv[c].y));
+        a[2] = __fadd_rn(a[2], __fmul_rn(qv[c][2], kv[c].z));
+        a[3] = __fadd_rn(a[3], __fmul_rn(qv[c][3], kv[c].w));
       }
     }
-    const int rem = C16 * 16;
-    if (rem + 8 <= hd)  // head_dim % 16 == 8: one more 8-chunk into acc0
+    float cmb[4], hi[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) a0[j] = __fadd_rn(a0[j], __fmul_rn(qh[rem + j], k[rem + j]));
-    float cmb[8];
+    for (int u = 0; u < 4; ++u) cmb[u] = __fadd_rn(a[u], __shfl_xor_sync(0xffffffffu, a[u], 2));  // a0 + a1
 #pragma unroll
-    for (int j = 0; j < 8; ++j) cmb[j] = __fadd_rn(a0[j], a1[j]);
-    const float x = __fmul_rn(hsum8(cmb), rs);
-    const float s = __fmul_rn(30.0f, libm::tanh_f32(div_rn(x, 30.0f)));
-    p[t] = s;
-    mx = fmaxf(mx, s);
+    for (int u = 0; u < 4; ++u) hi[u] = __shfl_xor_sync(0xffffffffu, cmb[u], 1);  // cmb[4..7] to l4 = 0
+    if (l4 == 0 && t < n) {
+      const float t0s = __fadd_rn(cmb[0], hi[0]), t1s = __fadd_rn(cmb[1], hi[1]);
+      const float t2s = __fadd_rn(cmb[2], hi[2]), t3s = __fadd_rn(cmb[3], hi[3]);
+      const float x = __fmul_rn(__fadd_rn(__fadd_rn(t0s, t2s), __fadd_rn(t1s, t3s)), rs);
+      const float sc = __fmul_rn(30.0f, libm::tanh_f32(div_rn(x, 30.0f)));
+      p[t] = sc;
+      mx = fmaxf(mx, sc);
+    }
   }
   mx = block_max(mx, red);  // its barriers also publish p[]
   const int full = n & ~7;
@@ -426,10 +439,10 @@ void b_rope_kv(const BatchDims& d, int layer, int B, const int32_t* pos, const i
 
 void b_attention(const BatchDims& d, int layer, int B, const int32_t* pos, const int32_t* slot, const float* q,
                  const float* kc, const float* vc, float* scores, float* att, cudaStream_t s) {
-  if (d.head_dim <= kAttT) {  // one fused CTA per (head, token)
+  if (d.head_dim <= kAttT && d.head_dim % 16 == 0) {  // one fused CTA per (head, token)
     const size_t psm = (size_t)d.max_seq * 4;
     const dim3 g(d.n_heads, B);
-    switch (d.head_dim / 16) {  // 16 <= head_dim <= 128, head_dim % 8 == 0
+    switch (d.head_dim / 16) {  // 16 <= head_dim <= 128, head_dim % 16 == 0
 #define CHALOT_B_ATTN(C)                                                                             \
   case C:                                                                                            \
     cudaFuncSetAttribute(k_b_attn<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psm);        \

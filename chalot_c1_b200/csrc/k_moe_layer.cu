@@ -70,6 +70,27 @@ __global__ void __launch_bounds__(kThreads) k_ml_route(MlDims d, const float* __
   if (threadIdx.x == 0) w.xs[t] = s;
 }
 
+// k_ml_route on the un-normalised residual rows: rmsnorm_avx2 with the FFN
+// norm weights first (the batched decode's k_b_rmsnorm, engine.rs:325-331),
+// then the router, top-k and quantization of the normalised row.
+__global__ void __launch_bounds__(kThreads) k_ml_route_norm(MlDims d, const float* __restrict__ x,
+                                                            const float* __restrict__ norm_w,
+                                                            const float* __restrict__ rw,
+                                                            const float* __restrict__ rb, MlWork w) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* xb = reinterpret_cast<float*>(smem);
+  float* wbuf = xb + d.dim;
+  float* lanes = wbuf + d.dim;
+  float* logit = lanes + 16 * d.E;
+  float* red = logit + 32;
+  const int t = blockIdx.x;
+  rmsnorm_smem(x + (size_t)t * d.dim, norm_w, d.dim, xb, wbuf, red, true);
+  router_logits(rw, rb, xb, d.dim, d.E, lanes, logit);
+  if (threadIdx.x < 32) topk_warp(logit, d.E, d.K, w.sel + (size_t)t * d.K, w.selw + (size_t)t * d.K);
+  const float s = quantize_smem(xb, d.dim, w.xq + (size_t)t * d.dim, red);
+  if (threadIdx.x == 0) w.xs[t] = s;
+}
+
 // Stable counting sort of the N = T*k slots by expert. Warp v walks slots
 // [v*chunk, (v+1)*chunk) in order; lanes holding the same expert are grouped
 // with __match_any_sync, so positions follow slot order within each expert.
@@ -380,28 +401,49 @@ __global__ void __launch_bounds__(kFewThreads) k_ml_few(MlDims d, const MlExpert
   auto unit_of = [&](int lr) { return GU ? r0 + (lr >> 4) * 8 + (lr & 7) : r0 + lr; };
   auto mrow_of = [&](int lr, int unit) { return GU ? ((lr & 8) ? d.H + unit : unit) : unit; };
 
-  const int nk = in_dim / kFewKc;
-  auto load = [&](int k) {
-    unsigned char* W = smem + (size_t)(k % kFewStages) * kFewStageBytes;
-    unsigned char* S = W + kFewRows * kFewWStride;
-    int8_t* X = reinterpret_cast<int8_t*>(S + kFewRows * 16);
-    const int k0 = k * kFewKc;
-    for (int c = tid; c < kFewRows * 5; c += kFewThreads) {  // per row: 4 x 16 B of packed weights, 16 B of scales
+  static_assert(kFewSlots * (kFewKc / 16) <= kFewThreads, "one activation chunk per thread at most");
+  // this thread's copies of every stage (the same rows and chunks each
+  // stage, 128 columns further): up to three 16-byte pieces of packed
+  // weights or scales and one activation chunk
+  constexpr int kPieces = (kFewRows * 5 + kFewThreads - 1) / kFewThreads;
+  const unsigned char* src[kPieces];
+  int dst[kPieces], step[kPieces];
+#pragma unroll
+  for (int i = 0; i < kPieces; ++i) {
+    const int c = tid + i * kFewThreads;
+    src[i] = nullptr;
+    dst[i] = step[i] = 0;
+    if (c < kFewRows * 5) {  // per row: 4 x 16 B of packed weights, 16 B of scales
       const int lr = c / 5, j = c - lr * 5;
       const int unit = unit_of(lr);
       if (unit < out_rows) {
         const int mrow = mrow_of(lr, unit);
-        if (j < 4)
-          few_cp16(W + lr * kFewWStride + j * 16, wmat + (size_t)mrow * (in_dim >> 1) + (k0 >> 1) + j * 16);
-        else
-          few_cp16(S + lr * 16, smat + (size_t)mrow * ng + (k0 >> 5));
+        if (j < 4) {
+          src[i] = wmat + (size_t)mrow * (in_dim >> 1) + j * 16;
+          dst[i] = lr * kFewWStride + j * 16;
+          step[i] = kFewKc / 2;
+        } else {
+          src[i] = reinterpret_cast<const unsigned char*>(smat + (size_t)mrow * ng);
+          dst[i] = kFewRows * kFewWStride + lr * 16;
+          step[i] = kFewKc / 32 * 4;
+        }
       }
     }
-    for (int c = tid; c < cnt * (kFewKc / 16); c += kFewThreads) {  // the slots' activation chunks
-      const int s = c / (kFewKc / 16), j = c % (kFewKc / 16);
-      const int8_t* a = GU ? w.xq + (size_t)(w.perm[p0 + s] / d.K) * in_dim : w.hq + (size_t)(p0 + s) * in_dim;
-      few_cp16(X + s * kFewXStride + j * 16, a + k0 + j * 16);
-    }
+  }
+  const int8_t* xsrc = nullptr;
+  int xdst = 0;
+  if (tid < cnt * (kFewKc / 16)) {  // cnt <= kFewSlots: at most one activation chunk per thread
+    const int s = tid / (kFewKc / 16), j = tid % (kFewKc / 16);
+    xsrc = (GU ? w.xq + (size_t)(w.perm[p0 + s] / d.K) * in_dim : w.hq + (size_t)(p0 + s) * in_dim) + j * 16;
+    xdst = kFewRows * (kFewWStride + 16) + s * kFewXStride + j * 16;
+  }
+  const int nk = in_dim / kFewKc;
+  auto load = [&](int k) {
+    unsigned char* base = smem + (size_t)(k % kFewStages) * kFewStageBytes;
+#pragma unroll
+    for (int i = 0; i < kPieces; ++i)
+      if (src[i]) few_cp16(base + dst[i], src[i] + (size_t)k * step[i]);
+    if (xsrc) few_cp16(base + xdst, xsrc + (size_t)k * kFewKc);
   };
 
   float acc[2][4];
@@ -526,6 +568,30 @@ __global__ void __launch_bounds__(kThreads) k_ml_combine(MlDims d, MlWork w, flo
     }
     out[(size_t)t * d.dim + i] = acc;
   }
+}
+
+// The gated combine of k_ml_combine added to the residual rows (x += expert
+// out, engine.rs:401), then rmsnorm + quantize of the new row with the next
+// norm weights (the batched decode's k_b_add and k_b_norm_quant), per token.
+__global__ void __launch_bounds__(kThreads) k_ml_combine_norm(MlDims d, MlWork w, float* __restrict__ x,
+                                                              const float* __restrict__ norm_w, int8_t* xq,
+                                                              float* xs) {
+  extern __shared__ __align__(16) float cnsm[];  // [dim] norm weights, [dim] scratch
+  __shared__ float red[40];
+  const int t = blockIdx.x;
+  float* xr = x + (size_t)t * d.dim;
+  load_f32(cnsm, norm_w, d.dim);
+  for (int i = threadIdx.x; i < d.dim; i += blockDim.x) {
+    float acc = 0.0f;
+    for (int j = 0; j < d.K; ++j) {
+      const int slot = t * d.K + j;
+      const int p = w.inv[slot];
+      if (p >= 0) acc = __fadd_rn(acc, __fmul_rn(w.selw[slot], w.y[(size_t)p * d.dim + i]));
+    }
+    xr[i] = __fadd_rn(xr[i], acc);
+  }
+  __syncthreads();  // the block's new residual row is visible to all its threads
+  norm_quant_tail(xr, cnsm, d.dim, xq + (size_t)t * d.dim, xs + t, cnsm + d.dim, red);
 }
 
 size_t gemm_smem() {
@@ -675,6 +741,39 @@ cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float
   tile_gemms(d, X, w, bm, s);
   (void)N;
   k_ml_combine<<<d.T, kThreads, 0, s>>>(d, w, out);
+  return cudaGetLastError();
+}
+
+// The batched decode's MoE block with its ends fused: the FFN rmsnorm runs in
+// the router kernel, and the gated combine, the residual add and the next
+// rmsnorm + quantization run in one kernel. x holds the residual rows (read
+// by the router, updated by the combine); xq/xs receive the next layer's
+// quantized input. The expert products between are ml_run's (t: tensor-core path).
+cudaError_t ml_run_decode(const MlDims& d, float* x, const float* norm_ffn, const float* rw, const float* rb,
+                          const MlExperts& X, const MlWork& w, const MlTcWork* t, const float* norm_next,
+                          int8_t* xq, float* xs, cudaStream_t s) {
+  if (d.T == 0) return cudaSuccess;
+  const size_t N = (size_t)d.T * d.K;
+  cudaError_t r = cudaSuccess;
+  if (t && (r = t->err ? cudaMemsetAsync(t->amax, 0, N * 4, s) : cudaErrorInvalidValue) != cudaSuccess) return r;
+  const size_t rsm = ((size_t)2 * d.dim + 16 * d.E + 32 + 40) * 4;
+  cudaFuncSetAttribute(k_ml_route_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm);
+  k_ml_route_norm<<<d.T, kThreads, rsm, s>>>(d, x, norm_ffn, rw, rb, w);
+  if (t) {
+    k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, 128, 1, nullptr);
+    if ((r = ml_tc_prepare(d, X, w, *t, s)) != cudaSuccess) return r;
+    const unsigned nmb = (unsigned)std::min(N, N / 128 + d.E);
+    if ((r = ml_tc_gemm(d, true, w, *t, nmb, s)) != cudaSuccess) return r;
+    if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
+    if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
+  } else {
+    const int bm = tile_slots(d, X);
+    k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
+    tile_gemms(d, X, w, bm, s);
+  }
+  const size_t csm = (size_t)2 * d.dim * 4;
+  cudaFuncSetAttribute(k_ml_combine_norm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csm);
+  k_ml_combine_norm<<<d.T, kThreads, csm, s>>>(d, w, x, norm_next, xq, xs);
   return cudaGetLastError();
 }
 

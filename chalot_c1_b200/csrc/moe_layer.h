@@ -65,6 +65,13 @@ const char* ml_check(const MlDims& d);
 cudaError_t ml_run(const MlDims& d, const float* x, const float* rw, const float* rb,
                    const MlExperts& X, const MlWork& w, float* out, cudaStream_t s);
 
+// The batched decode's MoE block with the FFN rmsnorm fused into the router
+// and the combine + residual add + next rmsnorm/quantize fused after it
+// (t: the tensor-core work, or nullptr for the SIMT/few-slot kernels).
+cudaError_t ml_run_decode(const MlDims& d, float* x, const float* norm_ffn, const float* rw, const float* rb,
+                          const MlExperts& X, const MlWork& w, const MlTcWork* t, const float* norm_next,
+                          int8_t* xq, float* xs, cudaStream_t s);
+
 // Building blocks of the expert-parallel layer (k_moe_layer.cu).
 void ml_launch_route(const MlDims& d, const float* x, const float* rw, const float* rb, const MlWork& w,
                      cudaStream_t s);
