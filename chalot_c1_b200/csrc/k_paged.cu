@@ -14,12 +14,13 @@
 // Attention per (sequence, head) is the attention of Engine::forward
 // (src/model/engine.rs:283-309) over the dequantized rows: s_t =
 // 30*tanh((q.k_t / sqrt(hd)) / 30), softmax, o = sum_t p_t v_t. It runs as
-// split-page flash decoding: CTA (split, seq) streams its share of the
-// sequence's pages through shared memory with 1-D bulk copies (one copy per
-// page, a multi-stage ring), warp h computes head h with an online softmax,
-// and k_paged_combine merges the splits. The dot products run on dp4a: the
-// query is split into two int8 planes (q ~ s1*q1 + s2*q2, s2 = s1/254, error
-// below max|q|*1.6e-5 per element) against the int8 K rows, and the softmax
+// split-page flash decoding in one persistent kernel: each CTA takes
+// (sequence, split) items in turn and streams their pages through shared
+// memory with 1-D bulk copies (one copy per page, a multi-stage ring running
+// across items), warp h computes head h with an online softmax, and
+// k_paged_merge combines the splits of each (sequence, head). The dot products
+// run on dp4a: the query is split into two int8 planes (q ~ s1*q1 + s2*q2,
+// s2 = s1/254, error below max|q|*1.6e-5 per element) against the int8 K rows, and the softmax
 // weights p in [0, 1] into two planes (p ~ (p1 + p2/254)/127) against the
 // dim-major int8 V rows, so the kernel stays bound by HBM reads of the pages.
 // The sums are reordered and the planes round q and p slightly: agreement with
@@ -40,7 +41,6 @@ namespace chalot {
 namespace {
 
 constexpr int kMaxStages = 8;
-constexpr int kMaxCtaPages = 64;  // pages one CTA streams; sets the split count
 constexpr size_t kMaxSmem = 227 * 1024;
 
 struct PagedDims {
@@ -90,8 +90,13 @@ __device__ __forceinline__ int checked_page(const PagedDims& d, int page, unsign
   return page;
 }
 
-// CTA (split, seq): warps 0..H-1 compute heads, warp H issues the page copies.
-// Partial results (running max m, sum l, unnormalised o) go to `part`.
+// Persistent CTA (two per SM): warps 0..H-1 compute heads, warp H issues the
+// page copies. Work items are (sequence, split) pairs, item w -> sequence
+// w / n_split, split w % n_split, taken in the order blockIdx.x, + gridDim.x,
+// ...; the page ring (and the ring of page scales beside it, written by the
+// producer before it arms each stage) runs across items, so the next item's
+// pages stream in while this one finishes. Each item leaves its partial
+// (running max m, sum l, unnormalised o) in `part` for k_paged_merge.
 template <int HD, int P>
 __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_t* __restrict__ data,
                                                         const float* __restrict__ scales,
@@ -105,19 +110,11 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
   const size_t PB = (size_t)2 * d.H * P * HD;
   unsigned char* stage0 = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
   PagedBars* bars = reinterpret_cast<PagedBars*>(stage0 + d.stages * PB);
-
-  const int s = blockIdx.y, split = blockIdx.x;
-  const int L = lens[s];
-  const int npages = min((max(L, 0) + P - 1) / P, d.max_pages);
+  unsigned char* after = reinterpret_cast<unsigned char*>(bars) + sizeof(PagedBars);
+  float* sring = reinterpret_cast<float*>(after + (size_t)d.H * (2 * HD + 64));  // [stages][K|V][head]
+  const int n_items = d.n_seq * d.n_split;
   const int pps = (d.max_pages + d.n_split - 1) / d.n_split;
-  const int pb = split * pps, pe = min(npages, pb + pps);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t* pt = page_table + (size_t)s * d.max_pages;
-
-  // this CTA's page ids and their scales, staged once (at most kMaxCtaPages pages)
-  int* spage = reinterpret_cast<int*>(reinterpret_cast<unsigned char*>(bars) + sizeof(PagedBars) +
-                                      (size_t)d.H * (2 * HD + 64));
-  float* sscale = reinterpret_cast<float*>(spage + kMaxCtaPages);
   if (threadIdx.x == 0) {
     for (int i = 0; i < d.stages; ++i) {
       mbar_init_n(&bars->full[i], 1);
@@ -125,24 +122,58 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
     }
     mbar_fence_init();
   }
-  for (int i = threadIdx.x; i < pe - pb; i += blockDim.x) spage[i] = checked_page(d, pt[pb + i], err);
   __syncthreads();
-  for (int j = threadIdx.x; j < (pe - pb) * 2 * d.H; j += blockDim.x)
-    sscale[j] = __ldg(scales + (size_t)spage[j / (2 * d.H)] * 2 * d.H + j % (2 * d.H));
-  __syncthreads();
+  auto item_pages = [&](int it, int& s, int& split, int& L, int& pb, int& pe) {
+    s = it / d.n_split;
+    split = it - s * d.n_split;
+    L = lens[s];
+    const int npages = min((max(L, 0) + P - 1) / P, d.max_pages);
+    pb = split * pps;
+    pe = min(npages, pb + pps);
+  };
 
-  if (warp == d.H) {
-    if (lane == 0) {  // producer
-      int issued = 0;
+  if (warp == d.H) {  // producer warp: lane 0 arms the stages and issues the copies
+    int* pids = reinterpret_cast<int*>(sring + d.stages * 2 * d.H);  // the item's page ids
+    int issued = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      int s, split, L, pb, pe;
+      item_pages(it, s, split, L, pb, pe);
+      const int32_t* pt = page_table + (size_t)s * d.max_pages;
+      for (int j = lane; j < pe - pb; j += 32) pids[j] = checked_page(d, pt[pb + j], err);
+      __syncwarp();
+      // the scales of the next page, one page ahead: lane j holds entries j and j + 32
+      float n0 = 0.0f, n1 = 0.0f;
+      auto fetch = [&](int i) {
+        const float* sp = scales + (size_t)pids[i - pb] * 2 * d.H;
+        n0 = lane < 2 * d.H ? __ldg(sp + lane) : 0.0f;
+        n1 = lane + 32 < 2 * d.H ? __ldg(sp + lane + 32) : 0.0f;
+      };
+      if (pb < pe) fetch(pb);
       for (int i = pb; i < pe; ++i, ++issued) {
         const int st = issued % d.stages, n = issued / d.stages;
-        if (n > 0 && !mbar_wait(&bars->empty[st], (n - 1) & 1, err)) break;
-        mbar_expect_tx(&bars->full[st], (uint32_t)PB);
-        tma_load(stage0 + st * PB, data + (size_t)spage[i - pb] * PB, (uint32_t)PB, &bars->full[st]);
+        const float c0 = n0, c1 = n1;
+        const int page = pids[i - pb];
+        if (i + 1 < pe) fetch(i + 1);
+        bool free_ok = true;
+        if (lane == 0 && n > 0) free_ok = mbar_wait(&bars->empty[st], (n - 1) & 1, err);
+        if (!__shfl_sync(0xffffffffu, free_ok, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane < 2 * d.H) sring[st * 2 * d.H + lane] = c0;
+        if (lane + 32 < 2 * d.H) sring[st * 2 * d.H + lane + 32] = c1;
+        __syncwarp();  // the scales are written before lane 0's release of the stage
+        if (lane == 0) {
+          mbar_expect_tx(&bars->full[st], (uint32_t)PB);
+          tma_load(stage0 + st * PB, data + (size_t)page * PB, (uint32_t)PB, &bars->full[st]);
+        }
       }
+      __syncwarp();  // pids is rewritten by the next item
+    }
+    if (lane == 0)
       for (int c = max(0, issued - d.stages); c < issued; ++c)  // copies in flight land first
         mbar_wait(&bars->full[c % d.stages], (c / d.stages) & 1, err);
-    }
     return;
   }
 
@@ -150,148 +181,180 @@ __global__ void __launch_bounds__(1024, 1) k_paged_attn(PagedDims d, const int8_
   const int h = warp;
   const int jp = lane / P, t = lane % P;
   // per-warp shared scratch: query planes q1, q2 (HD bytes each), weight planes p1, p2 (32 bytes each)
-  int8_t* wsm = reinterpret_cast<int8_t*>(reinterpret_cast<unsigned char*>(bars) + sizeof(PagedBars)) +
-                h * (2 * HD + 64);
+  int8_t* wsm = reinterpret_cast<int8_t*>(after) + h * (2 * HD + 64);
   int8_t *q1 = wsm, *q2 = wsm + HD, *p1 = wsm + 2 * HD, *p2 = wsm + 2 * HD + 32;
-  float s1, s2;
-  {
-    float qv[DPO], amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < DPO; ++j) {
-      qv[j] = q[((size_t)s * d.H + h) * HD + lane + 32 * j];
-      amax = fmaxf(amax, fabsf(qv[j]));
-    }
-    amax = warp_max(amax);
-    s1 = amax > 0.0f ? amax / 127.0f : 1.0f;
-    s2 = s1 / 254.0f;
-#pragma unroll
-    for (int j = 0; j < DPO; ++j) {
-      const float a = fminf(fmaxf(rintf(qv[j] / s1), -127.0f), 127.0f);
-      const float r = qv[j] - a * s1;
-      q1[lane + 32 * j] = (int8_t)a;
-      q2[lane + 32 * j] = (int8_t)fminf(fmaxf(rintf(r / s2), -127.0f), 127.0f);
-    }
-    __syncwarp();
-  }
-  const float kscale = 1.0f / (sqrtf((float)HD) * 30.0f);  // q.k / sqrt(hd) / 30
-  float m = -INFINITY, l = 0.0f, o[DPO];
-#pragma unroll
-  for (int j = 0; j < DPO; ++j) o[j] = 0.0f;
   const uint4* q1w = reinterpret_cast<const uint4*>(q1);
   const uint4* q2w = reinterpret_cast<const uint4*>(q2);
-  for (int i0 = pb; i0 < pe; i0 += PPI) {
-    const int np = min(PPI, pe - i0);  // pages in this step
-    bool ok = true;
-    for (int j = 0; j < np; ++j) {
-      const int u = i0 + j - pb;
-      ok = ok && mbar_wait(&bars->full[u % d.stages], (u / d.stages) & 1, err);
-    }
-    if (!ok) break;
-    const int i = i0 + jp;
-    const bool have = jp < np;
-    const bool valid = have && i * P + t < L;
-    float sc = -INFINITY;
-    if (valid) {
-      const int u = i - pb;
-      const unsigned char* kb = stage0 + (u % d.stages) * PB + (size_t)h * P * HD;
-      const uint4* kr = reinterpret_cast<const uint4*>(kb + t * HD);
-      int i1 = 0, i2 = 0;  // q.k_t as two exact int32 dot products
+  const float kscale = 1.0f / (sqrtf((float)HD) * 30.0f);  // q.k / sqrt(hd) / 30
+  int u = 0;  // ring uses so far
+  float qn[DPO];  // the query of the next item, loaded one item ahead
+  auto load_q = [&](int it) {
 #pragma unroll
-      for (int c0 = 0; c0 < HD / 16; ++c0) {
-        const int c = (c0 + t) & (HD / 16 - 1);  // rotated so neighbouring rows hit different banks
-        const uint4 w = lds16(kr + c), a = lds16(q1w + c), b2 = lds16(q2w + c);
-        i1 = __dp4a((int)w.x, (int)a.x, i1);
-        i1 = __dp4a((int)w.y, (int)a.y, i1);
-        i1 = __dp4a((int)w.z, (int)a.z, i1);
-        i1 = __dp4a((int)w.w, (int)a.w, i1);
-        i2 = __dp4a((int)w.x, (int)b2.x, i2);
-        i2 = __dp4a((int)w.y, (int)b2.y, i2);
-        i2 = __dp4a((int)w.z, (int)b2.z, i2);
-        i2 = __dp4a((int)w.w, (int)b2.w, i2);
-      }
-      const float dot = fmaf(s1, (float)i1, s2 * (float)i2);
-      sc = 30.0f * tanhf(dot * sscale[u * 2 * d.H + h] * kscale);
-    }
-    const float m_new = fmaxf(m, warp_max(sc));
-    const float c = (m == -INFINITY) ? 0.0f : __expf(m - m_new);
-    const float p = valid ? __expf(sc - m_new) : 0.0f;
-    float ps = p;
-#pragma unroll
-    for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-    l = fmaf(l, c, ps);
-    {  // p in [0, 1] as two int8 planes
-      const float a = rintf(p * 127.0f);
-      p1[lane] = (int8_t)a;
-      p2[lane] = (int8_t)fminf(fmaxf(rintf((p * 127.0f - a) * 254.0f), -127.0f), 127.0f);
-    }
-    __syncwarp();
-    float acc[DPO];
-#pragma unroll
-    for (int j = 0; j < DPO; ++j) acc[j] = 0.0f;
-    for (int jj = 0; jj < np; ++jj) {
-      const int u = i0 + jj - pb;
-      const unsigned char* vb = stage0 + (u % d.stages) * PB + (size_t)(d.H + h) * P * HD;
-      const float sv = sscale[u * 2 * d.H + d.H + h];
+    for (int j = 0; j < DPO; ++j)
+      qn[j] = it < n_items ? q[((size_t)(it / d.n_split) * d.H + h) * HD + lane + 32 * j] : 0.0f;
+  };
+  load_q(blockIdx.x);
+  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    int s, split, L, pb, pe;
+    item_pages(it, s, split, L, pb, pe);
+    float s1, s2;
+    {
+      float qv[DPO], amax = 0.0f;
 #pragma unroll
       for (int j = 0; j < DPO; ++j) {
-        int vw[P / 4];  // the dim's row of P int8 in one shared load
-        const unsigned char* vr = vb + (size_t)(lane + 32 * j) * P;
-        if (P == 8) {
-          const uint2 x = *reinterpret_cast<const uint2*>(vr);
-          vw[0] = (int)x.x;
-          vw[1 % (P / 4)] = (int)x.y;
-        } else {
-#pragma unroll
-          for (int w4 = 0; w4 < P / 16; ++w4) {
-            const uint4 x = reinterpret_cast<const uint4*>(vr)[w4];
-            vw[(4 * w4) % (P / 4)] = (int)x.x;
-            vw[(4 * w4 + 1) % (P / 4)] = (int)x.y;
-            vw[(4 * w4 + 2) % (P / 4)] = (int)x.z;
-            vw[(4 * w4 + 3) % (P / 4)] = (int)x.w;
-          }
-        }
-        int a1 = 0, a2 = 0;
-#pragma unroll
-        for (int w = 0; w < P / 4; ++w) {
-          a1 = __dp4a(vw[w], *reinterpret_cast<const int*>(p1 + jj * P + 4 * w), a1);
-          a2 = __dp4a(vw[w], *reinterpret_cast<const int*>(p2 + jj * P + 4 * w), a2);
-        }
-        acc[j] = fmaf(fmaf((float)a1, 1.0f / 127.0f, (float)a2 * (1.0f / (127.0f * 254.0f))), sv, acc[j]);
+        qv[j] = qn[j];
+        amax = fmaxf(amax, fabsf(qv[j]));
       }
+      load_q(it + gridDim.x);
+      amax = warp_max(amax);
+      s1 = amax > 0.0f ? amax / 127.0f : 1.0f;
+      s2 = s1 / 254.0f;
+      __syncwarp();  // the previous item's reads of the planes are done
+#pragma unroll
+      for (int j = 0; j < DPO; ++j) {
+        const float a = fminf(fmaxf(rintf(qv[j] / s1), -127.0f), 127.0f);
+        const float r = qv[j] - a * s1;
+        q1[lane + 32 * j] = (int8_t)a;
+        q2[lane + 32 * j] = (int8_t)fminf(fmaxf(rintf(r / s2), -127.0f), 127.0f);
+      }
+      __syncwarp();
+    }
+    float m = -INFINITY, l = 0.0f, o[DPO];
+#pragma unroll
+    for (int j = 0; j < DPO; ++j) o[j] = 0.0f;
+    bool ok = true;
+    for (int i0 = pb; i0 < pe; i0 += PPI) {
+      const int np = min(PPI, pe - i0);  // pages in this step
+      for (int j = 0; j < np; ++j) ok = ok && mbar_wait(&bars->full[(u + j) % d.stages], ((u + j) / d.stages) & 1, err);
+      if (!ok) break;
+      const int i = i0 + jp;
+      const bool have = jp < np;
+      const bool valid = have && i * P + t < L;
+      float sc = -INFINITY;
+      if (valid) {
+        const int st = (u + jp) % d.stages;
+        const unsigned char* kb = stage0 + st * PB + (size_t)h * P * HD;
+        const uint4* kr = reinterpret_cast<const uint4*>(kb + t * HD);
+        int i1 = 0, i2 = 0;  // q.k_t as two exact int32 dot products
+#pragma unroll
+        for (int c0 = 0; c0 < HD / 16; ++c0) {
+          const int c = (c0 + t) & (HD / 16 - 1);  // rotated so neighbouring rows hit different banks
+          const uint4 w = lds16(kr + c), a = lds16(q1w + c), b2 = lds16(q2w + c);
+          i1 = __dp4a((int)w.x, (int)a.x, i1);
+          i1 = __dp4a((int)w.y, (int)a.y, i1);
+          i1 = __dp4a((int)w.z, (int)a.z, i1);
+          i1 = __dp4a((int)w.w, (int)a.w, i1);
+          i2 = __dp4a((int)w.x, (int)b2.x, i2);
+          i2 = __dp4a((int)w.y, (int)b2.y, i2);
+          i2 = __dp4a((int)w.z, (int)b2.z, i2);
+          i2 = __dp4a((int)w.w, (int)b2.w, i2);
+        }
+        const float dot = fmaf(s1, (float)i1, s2 * (float)i2);
+        sc = 30.0f * tanhf(dot * sring[st * 2 * d.H + h] * kscale);
+      }
+      const float m_new = fmaxf(m, warp_max(sc));
+      const float c = (m == -INFINITY) ? 0.0f : __expf(m - m_new);
+      const float p = valid ? __expf(sc - m_new) : 0.0f;
+      float ps = p;
+#pragma unroll
+      for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l = fmaf(l, c, ps);
+      {  // p in [0, 1] as two int8 planes
+        const float a = rintf(p * 127.0f);
+        p1[lane] = (int8_t)a;
+        p2[lane] = (int8_t)fminf(fmaxf(rintf((p * 127.0f - a) * 254.0f), -127.0f), 127.0f);
+      }
+      __syncwarp();
+      float acc[DPO];
+#pragma unroll
+      for (int j = 0; j < DPO; ++j) acc[j] = 0.0f;
+      for (int jj = 0; jj < np; ++jj) {
+        const int st = (u + jj) % d.stages;
+        const unsigned char* vb = stage0 + st * PB + (size_t)(d.H + h) * P * HD;
+        const float sv = sring[st * 2 * d.H + d.H + h];
+#pragma unroll
+        for (int j = 0; j < DPO; ++j) {
+          int vw[P / 4];  // the dim's row of P int8 in one shared load
+          const unsigned char* vr = vb + (size_t)(lane + 32 * j) * P;
+          if (P == 8) {
+            const uint2 x = *reinterpret_cast<const uint2*>(vr);
+            vw[0] = (int)x.x;
+            vw[1 % (P / 4)] = (int)x.y;
+          } else {
+#pragma unroll
+            for (int w4 = 0; w4 < P / 16; ++w4) {
+              const uint4 x = reinterpret_cast<const uint4*>(vr)[w4];
+              vw[(4 * w4) % (P / 4)] = (int)x.x;
+              vw[(4 * w4 + 1) % (P / 4)] = (int)x.y;
+              vw[(4 * w4 + 2) % (P / 4)] = (int)x.z;
+              vw[(4 * w4 + 3) % (P / 4)] = (int)x.w;
+            }
+          }
+          int a1 = 0, a2 = 0;
+#pragma unroll
+          for (int w = 0; w < P / 4; ++w) {
+            a1 = __dp4a(vw[w], *reinterpret_cast<const int*>(p1 + jj * P + 4 * w), a1);
+            a2 = __dp4a(vw[w], *reinterpret_cast<const int*>(p2 + jj * P + 4 * w), a2);
+          }
+          acc[j] = fmaf(fmaf((float)a1, 1.0f / 127.0f, (float)a2 * (1.0f / (127.0f * 254.0f))), sv, acc[j]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < DPO; ++j) o[j] = fmaf(o[j], c, acc[j]);
+      m = m_new;
+      __syncwarp();
+      if (lane == 0)
+        for (int j = 0; j < np; ++j) mbar_arrive(&bars->empty[(u + j) % d.stages]);
+      u += np;
+    }
+    if (!ok) return;  // a copy never landed: recorded in err; this warp stops
+    float* pp = part + (((size_t)s * d.H + h) * d.n_split + split) * (HD + 2);
+    if (lane == 0) {
+      pp[0] = m;
+      pp[1] = l;
     }
 #pragma unroll
-    for (int j = 0; j < DPO; ++j) o[j] = fmaf(o[j], c, acc[j]);
-    m = m_new;
-    __syncwarp();
-    if (lane == 0)
-      for (int j = 0; j < np; ++j) mbar_arrive(&bars->empty[(i0 + j - pb) % d.stages]);
+    for (int j = 0; j < DPO; ++j) pp[2 + lane + 32 * j] = o[j];
   }
-  float* pp = part + (((size_t)s * d.H + h) * d.n_split + split) * (HD + 2);
-  if (lane == 0) {
-    pp[0] = m;
-    pp[1] = l;
-  }
-#pragma unroll
-  for (int j = 0; j < DPO; ++j) pp[2 + lane + 32 * j] = o[j];
 }
 
-// Merges the splits of each (sequence, head): o = sum_i o_i e^(m_i - M) / sum_i l_i e^(m_i - M).
-__global__ void k_paged_combine(PagedDims d, const float* __restrict__ part, float* out) {
-  const int s = blockIdx.x / d.H, h = blockIdx.x % d.H;
-  const float* pp = part + ((size_t)s * d.H + h) * d.n_split * (d.hd + 2);
+// Merges the splits of each (sequence, head), one warp per pair: o = sum_i
+// o_i e^(m_i - M) / sum_i l_i e^(m_i - M), eight splits' partials loaded at
+// a time.
+template <int HD>
+__global__ void __launch_bounds__(128) k_paged_merge(PagedDims d, const float* __restrict__ part, float* out) {
+  constexpr int DPO = HD / 32;
+  const int pair = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (pair >= d.n_seq * d.H) return;
+  const float* base = part + (size_t)pair * d.n_split * (HD + 2);
   float M = -INFINITY;
-  for (int i = 0; i < d.n_split; ++i) M = fmaxf(M, pp[i * (d.hd + 2)]);
-  for (int j = threadIdx.x; j < d.hd; j += blockDim.x) {
-    float L = 0.0f, O = 0.0f;
-    for (int i = 0; i < d.n_split; ++i) {
-      const float* pi = pp + i * (d.hd + 2);
-      if (pi[0] == -INFINITY) continue;
-      const float w = __expf(pi[0] - M);
-      L = __fadd_rn(L, __fmul_rn(pi[1], w));
-      O = __fadd_rn(O, __fmul_rn(pi[2 + j], w));
+  for (int i = lane; i < d.n_split; i += 32) M = fmaxf(M, base[(size_t)i * (HD + 2)]);
+  M = warp_max(M);
+  float Ls = 0.0f, O[DPO];
+#pragma unroll
+  for (int j = 0; j < DPO; ++j) O[j] = 0.0f;
+  for (int i0 = 0; i0 < d.n_split; i0 += 8) {  // eight splits' loads in flight, then their sums in order
+    float mi[8], li[8], oi[8][DPO];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const bool in = i0 + k < d.n_split;
+      const float* pi = base + (size_t)(in ? i0 + k : 0) * (HD + 2);
+      mi[k] = in ? pi[0] : -INFINITY;
+      li[k] = pi[1];
+#pragma unroll
+      for (int j = 0; j < DPO; ++j) oi[k][j] = pi[2 + lane + 32 * j];
     }
-    out[((size_t)s * d.H + h) * d.hd + j] = L > 0.0f ? div_rn(O, L) : 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (mi[k] == -INFINITY) continue;  // an empty split
+      const float wgt = __expf(mi[k] - M);
+      Ls = __fadd_rn(Ls, __fmul_rn(li[k], wgt));
+#pragma unroll
+      for (int j = 0; j < DPO; ++j) O[j] = __fadd_rn(O[j], __fmul_rn(oi[k][j], wgt));
+    }
   }
+#pragma unroll
+  for (int j = 0; j < DPO; ++j) out[(size_t)pair * HD + lane + 32 * j] = Ls > 0.0f ? div_rn(O[j], Ls) : 0.0f;
 }
 
 int sm_count() {
@@ -301,6 +364,13 @@ int sm_count() {
   return sms;
 }
 
+constexpr int kMaxItemPages = 64;  // pages of one (sequence, split) item; sets the least split count
+
+size_t attn_smem(int H, int P, int HD, int stages) {
+  return 128 + (size_t)stages * 2 * H * P * HD + sizeof(PagedBars) + (size_t)H * (2 * HD + 64) +
+         (size_t)stages * 2 * H * 4 + kMaxItemPages * 4;
+}
+
 const char* paged_check(const chalot_paged_kv* kv) {
   if (!kv || !kv->data || !kv->scales) return "null cache";
   if (kv->page_tokens != 8 && kv->page_tokens != 16 && kv->page_tokens != 32) return "page_tokens must be 8, 16 or 32";
@@ -308,9 +378,7 @@ const char* paged_check(const chalot_paged_kv* kv) {
   if (kv->n_heads < 1 || kv->n_heads > 31) return "n_heads must be in [1, 31]";
   if (kv->n_pages < 1) return "n_pages must be positive";
   if (reinterpret_cast<uintptr_t>(kv->data) & 15) return "data must be 16-byte aligned";
-  if (2 * ((size_t)2 * kv->n_heads * kv->page_tokens * kv->head_dim) + 128 + 2 * kMaxStages * 8 +
-          (size_t)kv->n_heads * (2 * kv->head_dim + 64) + kMaxCtaPages * 4 +
-          (size_t)kMaxCtaPages * 2 * kv->n_heads * 4 > kMaxSmem)
+  if (attn_smem((int)kv->n_heads, (int)kv->page_tokens, (int)kv->head_dim, 2) > kMaxSmem)
     return "two pages do not fit in shared memory (n_heads * page_tokens * head_dim too large)";
   return nullptr;
 }
@@ -323,10 +391,11 @@ PagedDims paged_dims(const chalot_paged_kv* kv, size_t n_seq, size_t max_pages) 
   d.n_pages = (int)kv->n_pages;
   d.n_seq = (int)n_seq;
   d.max_pages = (int)max_pages;
-  // two CTAs per SM (three page stages each), about four full waves of them
+  // splits: about eight (sequence, split) items per SM for the persistent
+  // CTAs (two per SM, three page stages each) to share out evenly
   const int want = (8 * sm_count() + (int)std::max<size_t>(n_seq, 1) - 1) / (int)std::max<size_t>(n_seq, 1);
   d.n_split = std::max(1, std::min(want, (int)std::max<size_t>(max_pages, 1)));
-  d.n_split = std::max(d.n_split, (int)((max_pages + kMaxCtaPages - 1) / kMaxCtaPages));
+  d.n_split = std::max(d.n_split, (int)((max_pages + kMaxItemPages - 1) / kMaxItemPages));
   const size_t pb = (size_t)2 * d.H * d.P * d.hd;
   d.stages = (int)std::max<size_t>(2, std::min<size_t>(kMaxStages, (size_t)(96 * 1024) / pb));
   return d;
@@ -336,13 +405,14 @@ size_t part_bytes(const PagedDims& d) { return (size_t)d.n_seq * d.H * d.n_split
 
 template <int HD, int P>
 cudaError_t launch_attn(const PagedDims& d, const chalot_paged_kv* kv, const int32_t* pt, const int32_t* lens,
-                        const float* q, float* part, unsigned* err, cudaStream_t s) {
-  const size_t smem = 128 + (size_t)d.stages * 2 * d.H * P * HD + sizeof(PagedBars) + (size_t)d.H * (2 * HD + 64) +
-                      kMaxCtaPages * 4 + (size_t)kMaxCtaPages * 2 * d.H * 4;
+                        const float* q, float* part, float* out, unsigned* err, cudaStream_t s) {
+  const size_t smem = attn_smem(d.H, P, HD, d.stages);
   cudaError_t r = cudaFuncSetAttribute(k_paged_attn<HD, P>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (r != cudaSuccess) return r;
-  k_paged_attn<HD, P><<<dim3(d.n_split, d.n_seq), (d.H + 1) * 32, smem, s>>>(d, kv->data, kv->scales, pt, lens, q,
-                                                                             part, err);
+  const int items = d.n_seq * d.n_split;
+  const int grid = std::max(1, std::min(items, 2 * sm_count()));
+  k_paged_attn<HD, P><<<grid, (d.H + 1) * 32, smem, s>>>(d, kv->data, kv->scales, pt, lens, q, part, err);
+  k_paged_merge<HD><<<(d.n_seq * d.H + 3) / 4, 128, 0, s>>>(d, part, out);
   return cudaGetLastError();
 }
 
@@ -408,19 +478,13 @@ __attribute__((visibility("default"))) int chalot_paged_attention(const chalot_p
   if (int rc = devstat_poll("paged_attention", s)) return rc;
   unsigned* err = devstat_word();  // bad page ids and timed-out waits (devstat.h)
   if (!err) return set_error(CHALOT_ERR_CUDA, "paged_attention: device status word unavailable");
-  cudaError_t r = cudaSuccess;
-  {
-    if (d.hd == 64 && d.P == 16) r = launch_attn<64, 16>(d, kv, page_table, seq_lens, q, part, err, s);
-    else if (d.hd == 64 && d.P == 8) r = launch_attn<64, 8>(d, kv, page_table, seq_lens, q, part, err, s);
-    else if (d.hd == 64 && d.P == 32) r = launch_attn<64, 32>(d, kv, page_table, seq_lens, q, part, err, s);
-    else if (d.hd == 128 && d.P == 16) r = launch_attn<128, 16>(d, kv, page_table, seq_lens, q, part, err, s);
-    else if (d.hd == 128 && d.P == 8) r = launch_attn<128, 8>(d, kv, page_table, seq_lens, q, part, err, s);
-    else r = launch_attn<128, 32>(d, kv, page_table, seq_lens, q, part, err, s);
-  }
-  if (r == cudaSuccess) {
-    k_paged_combine<<<(unsigned)(n_seq * d.H), 128, 0, s>>>(d, part, out);
-    r = cudaGetLastError();
-  }
+  cudaError_t r;
+  if (d.hd == 64 && d.P == 16) r = launch_attn<64, 16>(d, kv, page_table, seq_lens, q, part, out, err, s);
+  else if (d.hd == 64 && d.P == 8) r = launch_attn<64, 8>(d, kv, page_table, seq_lens, q, part, out, err, s);
+  else if (d.hd == 64 && d.P == 32) r = launch_attn<64, 32>(d, kv, page_table, seq_lens, q, part, out, err, s);
+  else if (d.hd == 128 && d.P == 16) r = launch_attn<128, 16>(d, kv, page_table, seq_lens, q, part, out, err, s);
+  else if (d.hd == 128 && d.P == 8) r = launch_attn<128, 8>(d, kv, page_table, seq_lens, q, part, out, err, s);
+  else r = launch_attn<128, 32>(d, kv, page_table, seq_lens, q, part, out, err, s);
   if (r != cudaSuccess) return set_error(CHALOT_ERR_CUDA, std::string("paged_attention: ") + cudaGetErrorString(r));
   return CHALOT_OK;
 }
