@@ -93,6 +93,15 @@ SIGNATURES = {
     "chalot_batch_reserve": (C.c_int, [P, C.c_uint32]),
     "chalot_forward_batch": (C.c_int, [P, P, P, P, C.c_uint32, P]),
     "chalot_get_batch_logits": (C.c_int, [P, C.c_uint32, P, C.c_size_t]),
+    "chalot_batch_reserve_paged": (C.c_int, [P, C.c_uint32, C.c_uint32, C.c_uint32]),
+    "chalot_batch_release": (C.c_int, [P, C.c_uint32]),
+    "chalot_batch_capacity": (C.c_int, [P, C.POINTER(C.c_uint32)]),
+    "chalot_batch_kv_pages": (C.c_int, [P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    "chalot_sched_create": (C.c_int, [P, C.c_uint32, C.POINTER(P)]),
+    "chalot_sched_free": (None, [P]),
+    "chalot_sched_submit": (C.c_int, [P, P, C.c_size_t, C.c_uint32, P, C.c_size_t, C.POINTER(C.c_uint64)]),
+    "chalot_sched_step": (C.c_int, [P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    "chalot_sched_poll": (C.c_int, [P, C.c_uint64, P, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_int)]),
     "chalot_probe_int8_mma": (C.c_int, [C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "chalot_myai_validate": (C.c_int, [C.c_char_p, C.c_char_p, C.c_size_t]),
     "chalot_ep_nccl_id": (C.c_int, [P]),

@@ -8,8 +8,14 @@
 
 namespace chalot {
 
+// Shapes of the batched decode, and where its K/V rows live: either the
+// flat cache [slot][layer][max_seq][dim] (ptab == nullptr) or a pool of pages
+// of 2^pt_shift positions, page p holding [layer][position in page][dim], with
+// the page of position t of a slot at ptab[slot * maxp + (t >> pt_shift)].
 struct BatchDims {
   int dim, n_layers, n_heads, head_dim, max_seq;
+  const int32_t* ptab = nullptr;
+  int pt_shift = 0, maxp = 0;
 };
 
 void b_embed(const BatchDims& d, int B, const uint32_t* toks, const int8_t* emb, const float* emb_s,

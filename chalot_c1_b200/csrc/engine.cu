@@ -150,6 +150,15 @@ struct chalot_engine {
     void* moe_ws = nullptr;
     uint32_t* h_io = nullptr;  // pinned staging: slots, tokens, positions, results
     std::vector<MlExperts> experts;  // per layer, the engine's repacked experts
+    // paged K/V (chalot_batch_reserve_paged): kc/vc are pools of n_pages pages
+    // of 2^pt_shift positions ([layer][position][dim] each); a slot's pages are
+    // taken from the free list as its positions grow and returned by
+    // chalot_batch_release
+    int pt_shift = -1, maxp = 0, n_pages = 0;  // pt_shift < 0: the flat cache
+    int32_t* ptab = nullptr;    // device [cap][maxp]: page of each slot's page index
+    int32_t* h_ptab = nullptr;  // pinned copy, uploaded before a forward that changed it
+    std::vector<std::vector<int>> slot_pages;
+    std::vector<int> free_pages;
   } bt;
   // expert parallelism of the batched forward: this engine computes the
   // experts e with e % world == rank and exchanges token rows with its peers
@@ -181,6 +190,7 @@ struct chalot_engine {
     if (h_stage) cudaFreeHost(h_stage);
     if (h_tokens) cudaFreeHost(h_tokens);
     if (bt.h_io) cudaFreeHost(bt.h_io);
+    if (bt.h_ptab) cudaFreeHost(bt.h_ptab);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -948,21 +958,51 @@ static MlDims batch_moe_dims(const chalot_engine* e, int n) {
   return MlDims{n, (int)c.dim, (int)c.hidden_dim, (int)c.n_experts, (int)c.top_k, (int)c.int4_group_size};
 }
 
-__attribute__((visibility("default"))) int chalot_batch_reserve(chalot_engine* e, uint32_t max_seqs) {
+// Batch state for max_seqs slots; page_tokens == 0: the flat K/V cache
+// [slot][layer][max_seq][dim], else a pool of n_pages pages of page_tokens
+// positions.
+static int batch_reserve(chalot_engine* e, uint32_t max_seqs, uint32_t n_pages, uint32_t page_tokens) {
   if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
   const ModelConfig& c = e->cfg;
   if (c.n_experts < 2) return set_error(CHALOT_ERR_ARG, "batch_reserve: batched decode needs a MoE model");
   if (max_seqs == 0 || max_seqs > 1024) return set_error(CHALOT_ERR_ARG, "batch_reserve: max_seqs in [1, 1024]");
-  if ((int)max_seqs <= e->bt.cap) return CHALOT_OK;
-  if (e->bt.cap) return set_error(CHALOT_ERR_STATE, "batch_reserve: already reserved with fewer slots");
+  const bool paged = page_tokens != 0;
+  if (paged && (page_tokens < 8 || page_tokens > 256 || (page_tokens & (page_tokens - 1))))
+    return set_error(CHALOT_ERR_ARG, "batch_reserve: page_tokens must be a power of two in [8, 256]");
+  if (paged && (n_pages == 0 || n_pages > (1u << 24)))
+    return set_error(CHALOT_ERR_ARG, "batch_reserve: n_pages must be in [1, 2^24]");
+  if (paged && e->cfg.head_dim % 16)
+    return set_error(CHALOT_ERR_ARG, "batch_reserve: paged K/V needs head_dim % 16 == 0");
+  if (e->bt.cap) {
+    const bool same = paged ? e->bt.pt_shift >= 0 && (1u << e->bt.pt_shift) == page_tokens &&
+                                  (uint32_t)e->bt.n_pages >= n_pages
+                            : e->bt.pt_shift < 0;
+    if ((int)max_seqs <= e->bt.cap && (same || !paged)) return CHALOT_OK;  // a flat request takes either layout
+    return set_error(CHALOT_ERR_STATE, "batch_reserve: already reserved (with fewer slots or another K/V layout)");
+  }
   if (const char* m = ml_check(batch_moe_dims(e, (int)max_seqs)))
     return set_error(CHALOT_ERR_ARG, std::string("batch_reserve: ") + m);
   try {
     CK(cudaSetDevice(e->device));
     auto& b = e->bt;
     const size_t S = max_seqs, D = c.dim, L = c.n_layers, M = c.max_seq_len, H = c.n_heads;
-    b.kc = e->dalloc<float>(S * L * M * D);
-    b.vc = e->dalloc<float>(S * L * M * D);
+    if (paged) {
+      b.pt_shift = 0;
+      while ((1u << b.pt_shift) < page_tokens) ++b.pt_shift;
+      b.maxp = (int)((M + page_tokens - 1) / page_tokens);
+      b.n_pages = (int)n_pages;
+      b.kc = e->dalloc<float>((size_t)n_pages * L * page_tokens * D);
+      b.vc = e->dalloc<float>((size_t)n_pages * L * page_tokens * D);
+      b.ptab = e->dalloc<int32_t>(S * b.maxp);
+      CK(cudaMallocHost(&b.h_ptab, S * b.maxp * sizeof(int32_t)));
+      std::memset(b.h_ptab, 0, S * b.maxp * sizeof(int32_t));
+      b.slot_pages.assign(S, {});
+      b.free_pages.resize(n_pages);
+      for (uint32_t i = 0; i < n_pages; ++i) b.free_pages[i] = (int)(n_pages - 1 - i);  // page 0 first
+    } else {
+      b.kc = e->dalloc<float>(S * L * M * D);
+      b.vc = e->dalloc<float>(S * L * M * D);
+    }
     b.x = e->dalloc<float>(S * D);
     b.qkv = e->dalloc<float>(S * 3 * D);
     b.q = e->dalloc<float>(S * D);
@@ -994,6 +1034,43 @@ __attribute__((visibility("default"))) int chalot_batch_reserve(chalot_engine* e
   } catch (const CudaFail& f) {
     return fail(f);
   }
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_batch_reserve(chalot_engine* e, uint32_t max_seqs) {
+  return batch_reserve(e, max_seqs, 0, 0);
+}
+
+__attribute__((visibility("default"))) int chalot_batch_reserve_paged(chalot_engine* e, uint32_t max_seqs,
+                                                                     uint32_t n_pages, uint32_t page_tokens) {
+  if (!page_tokens) return set_error(CHALOT_ERR_ARG, "batch_reserve_paged: page_tokens must be positive");
+  return batch_reserve(e, max_seqs, n_pages, page_tokens);
+}
+
+__attribute__((visibility("default"))) int chalot_batch_release(chalot_engine* e, uint32_t slot) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
+  auto& b = e->bt;
+  if ((int)slot >= b.cap) return set_error(CHALOT_ERR_ARG, "batch_release: slot out of range");
+  if (b.pt_shift < 0) return CHALOT_OK;  // the flat cache keeps every slot's rows
+  for (int p : b.slot_pages[slot]) b.free_pages.push_back(p);
+  b.slot_pages[slot].clear();
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_batch_capacity(chalot_engine* e, uint32_t* max_seqs) {
+  if (!e || !max_seqs) return set_error(CHALOT_ERR_ARG, "null argument");
+  *max_seqs = (uint32_t)e->bt.cap;
+  return CHALOT_OK;
+}
+
+__attribute__((visibility("default"))) int chalot_batch_kv_pages(chalot_engine* e, uint32_t* n_free,
+                                                                uint32_t* n_total, uint32_t* page_tokens) {
+  if (!e) return set_error(CHALOT_ERR_ARG, "null engine");
+  const auto& b = e->bt;
+  const bool paged = b.pt_shift >= 0;
+  if (n_free) *n_free = paged ? (uint32_t)b.free_pages.size() : 0;
+  if (n_total) *n_total = paged ? (uint32_t)b.n_pages : 0;
+  if (page_tokens) *page_tokens = paged ? 1u << b.pt_shift : 0;
   return CHALOT_OK;
 }
 
@@ -1161,6 +1238,21 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
         if (int rc = ep_moe(e, l, 0, md0, w0, s, &msg)) return set_error(rc, "forward_batch: " + msg);
       return CHALOT_OK;
     }
+    if (b.pt_shift >= 0) {  // pages for every position this call writes or attends
+      bool grew = false;
+      for (uint32_t i = 0; i < n; ++i) {
+        auto& pages = b.slot_pages[slots[i]];
+        const size_t need = (size_t)(pos[i] >> b.pt_shift) + 1;
+        while (pages.size() < need) {
+          if (b.free_pages.empty()) return set_error(CHALOT_ERR_OOM, "forward_batch: out of K/V pages");
+          pages.push_back(b.free_pages.back());
+          b.free_pages.pop_back();
+          b.h_ptab[(size_t)slots[i] * b.maxp + pages.size() - 1] = pages.back();
+          grew = true;
+        }
+      }
+      if (grew) CK(cudaMemcpyAsync(b.ptab, b.h_ptab, (size_t)b.cap * b.maxp * 4, cudaMemcpyHostToDevice, s));
+    }
     uint32_t* io = b.h_io;
     std::memcpy(io, slots, n * 4);
     std::memcpy(io + b.cap, toks, n * 4);
@@ -1169,7 +1261,12 @@ __attribute__((visibility("default"))) int chalot_forward_batch(chalot_engine* e
     CK(cudaMemcpyAsync(b.toks, io + b.cap, n * 4, cudaMemcpyHostToDevice, s));
     CK(cudaMemcpyAsync(b.pos, io + 2 * b.cap, n * 4, cudaMemcpyHostToDevice, s));
     const int B = (int)n, D = (int)c.dim;
-    const BatchDims bd{D, (int)c.n_layers, (int)c.n_heads, (int)c.head_dim, (int)c.max_seq_len};
+    BatchDims bd{D, (int)c.n_layers, (int)c.n_heads, (int)c.head_dim, (int)c.max_seq_len};
+    if (b.pt_shift >= 0) {
+      bd.ptab = b.ptab;
+      bd.pt_shift = b.pt_shift;
+      bd.maxp = b.maxp;
+    }
     CK(cudaEventRecord(e->ev[0], s));
     b_embed(bd, B, b.toks, e->emb, e->emb_s, e->layers[0].rms_attn, b.x, b.xq, b.xs, s);
     const MlDims md = batch_moe_dims(e, B);

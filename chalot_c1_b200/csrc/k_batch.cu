@@ -26,6 +26,13 @@ namespace {
 
 constexpr int kT = 256;
 
+// Offset (in floats) of the K or V row of position t of a slot in layer `layer`.
+__device__ __forceinline__ size_t kv_off(const BatchDims& d, int slot, int layer, int t) {
+  if (!d.ptab) return (((size_t)slot * d.n_layers + layer) * d.max_seq + t) * d.dim;
+  const size_t page = (size_t)d.ptab[(size_t)slot * d.maxp + (t >> d.pt_shift)];
+  return (((page * d.n_layers + layer) << d.pt_shift) + (size_t)(t & ((1 << d.pt_shift) - 1))) * d.dim;
+}
+
 __global__ void __launch_bounds__(kT) k_b_embed(int dim, const uint32_t* toks, const int8_t* __restrict__ emb,
                                                 const float* __restrict__ emb_s, const float* __restrict__ rms0,
                                                 float* x, int8_t* xq, float* xs) {
@@ -146,7 +153,7 @@ __global__ void k_b_rope_kv(BatchDims d, int layer, int B, const int32_t* pos, c
     q[(size_t)b * d.dim + rr + 1] = v1;
   } else {
     float* cache = sec == 1 ? kc : vc;
-    const size_t off = (((size_t)slot[b] * d.n_layers + layer) * d.max_seq + p) * d.dim + rr;
+    const size_t off = kv_off(d, slot[b], layer, p) + rr;
     cache[off] = v0;
     cache[off + 1] = v1;
   }
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kScoreT) k_b_scores(BatchDims d, int layer, co
   for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = q[(size_t)b * d.dim + h * hd + i];
   __syncthreads();
   if (t > P) return;
-  const float* k = kc + (((size_t)slot[b] * d.n_layers + layer) * d.max_seq + t) * d.dim + (size_t)h * hd;
+  const float* k = kc + kv_off(d, slot[b], layer, t) + (size_t)h * hd;
   float a0[8], a1[8];  // dot_f32_avx2: two 8-lane accumulators over 16-element strides
 #pragma unroll
   for (int j = 0; j < 8; ++j) a0[j] = a1[j] = 0.0f;
@@ -196,11 +203,13 @@ __global__ void __launch_bounds__(kScoreT) k_b_scores(BatchDims d, int layer, co
 
 constexpr int kPvCols = 8, kPvTile = 1024;
 
-__device__ __forceinline__ void b_stage_v(float* vt, const float* vbase, int dim, int t0, int rows) {
+__device__ __forceinline__ void b_stage_v(float* vt, const float* vc, const BatchDims& d, int slot, int layer,
+                                          int col0, int t0, int rows) {
   const int n = rows * (kPvCols / 4);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int r = i / (kPvCols / 4), qq = i % (kPvCols / 4);
-    reinterpret_cast<float4*>(vt)[i] = *reinterpret_cast<const float4*>(vbase + (size_t)(t0 + r) * dim + qq * 4);
+    reinterpret_cast<float4*>(vt)[i] =
+        *reinterpret_cast<const float4*>(vc + kv_off(d, slot, layer, t0 + r) + col0 + qq * 4);
   }
 }
 
@@ -214,7 +223,6 @@ __global__ void __launch_bounds__(kT) k_b_pv(BatchDims d, int layer, const int32
   __shared__ float inv_s;
   const int h = blockIdx.x, hd = d.head_dim, c0 = blockIdx.y * kPvCols, b = blockIdx.z;
   const int n = pos[b] + 1;
-  const float* vbase = vc + ((size_t)slot[b] * d.n_layers + layer) * d.max_seq * d.dim + (size_t)h * hd + c0;
   const float* s = scores + ((size_t)b * d.n_heads + h) * d.max_seq;
   float mx = -INFINITY;
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -250,7 +258,7 @@ __global__ void __launch_bounds__(kT) k_b_pv(BatchDims d, int layer, const int32
   for (int t0 = 0; t0 < n; t0 += kPvTile) {
     const int rows = min(kPvTile, n - t0);
     __syncthreads();
-    b_stage_v(vt, vbase, d.dim, t0, rows);
+    b_stage_v(vt, vc, d, slot[b], layer, h * hd + c0, t0, rows);
     __syncthreads();
     if (threadIdx.x < kPvCols)
       for (int t = 0; t < rows; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t0 + t], vt[t * kPvCols + threadIdx.x]));
@@ -275,7 +283,7 @@ __global__ void __launch_bounds__(kAttT, 4) k_b_attn(BatchDims d, int layer, con
   __shared__ float inv_s;
   const int h = blockIdx.x, b = blockIdx.y, hd = d.head_dim;
   const int n = pos[b] + 1;
-  const size_t base = ((size_t)slot[b] * d.n_layers + layer) * d.max_seq * d.dim + (size_t)h * hd;
+  const int sl = slot[b];
   for (int i = threadIdx.x; i < hd; i += blockDim.x) qh[i] = q[(size_t)b * d.dim + h * hd + i];
   __syncthreads();
   const float rs = div_rn(1.0f, __fsqrt_rn((float)hd));
@@ -296,7 +304,7 @@ __global__ void __launch_bounds__(kAttT, 4) k_b_attn(BatchDims d, int layer, con
     const int t = t0 + quad;
     float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (t < n) {
-      const float* k = kc + base + (size_t)t * d.dim + 4 * l4;
+      const float* k = kc + kv_off(d, sl, layer, t) + (size_t)h * hd + 4 * l4;
       float4 kv[C16];
 #pragma unroll
       for (int c = 0; c < C16; ++c) kv[c] = *reinterpret_cast<const float4*>(k + 16 * c);
@@ -345,24 +353,24 @@ __global__ void __launch_bounds__(kAttT, 4) k_b_attn(BatchDims d, int layer, con
   for (int i = threadIdx.x; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
   __syncthreads();
   if (threadIdx.x >= hd) return;
-  const float* v = vc + base + threadIdx.x;
-  const size_t ld = d.dim;
+  const float* v = vc + (size_t)h * hd + threadIdx.x;
+  auto vrow = [&](int t) { return v[kv_off(d, sl, layer, t)]; };
   float acc = 0.0f, cur[kAttU], nxt[kAttU];
   const int nb = n / kAttU;
   if (nb > 0)
 #pragma unroll
-    for (int u = 0; u < kAttU; ++u) cur[u] = v[(size_t)u * ld];
+    for (int u = 0; u < kAttU; ++u) cur[u] = vrow(u);
   for (int i = 0; i < nb; ++i) {
     const int t = i * kAttU;
     if (i + 1 < nb)
 #pragma unroll
-      for (int u = 0; u < kAttU; ++u) nxt[u] = v[(size_t)(t + kAttU + u) * ld];
+      for (int u = 0; u < kAttU; ++u) nxt[u] = vrow(t + kAttU + u);
 #pragma unroll
     for (int u = 0; u < kAttU; ++u) acc = __fadd_rn(acc, __fmul_rn(p[t + u], cur[u]));
 #pragma unroll
     for (int u = 0; u < kAttU; ++u) cur[u] = nxt[u];
   }
-  for (int t = nb * kAttU; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[(size_t)t * ld]));
+  for (int t = nb * kAttU; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], vrow(t)));
   att[(size_t)b * d.dim + h * hd + threadIdx.x] = acc;
 }
 

@@ -131,6 +131,27 @@ class Engine:
         check(lib().chalot_batch_reserve(self._h, max_seqs))
         self._cap = max(self._cap, max_seqs)
 
+    def reserve_batch_paged(self, max_seqs: int, n_pages: int, page_tokens: int = 16) -> None:
+        """The batch with a paged f32 K/V cache (chalot_batch_reserve_paged):
+        n_pages pages of page_tokens positions shared by the slots, taken as
+        positions are written and returned by release_slot."""
+        check(lib().chalot_batch_reserve_paged(self._h, max_seqs, n_pages, page_tokens))
+        self._cap = max(self._cap, max_seqs)
+
+    def release_slot(self, slot: int) -> None:
+        """Returns a slot's K/V pages to the pool (chalot_batch_release)."""
+        check(lib().chalot_batch_release(self._h, slot))
+
+    def kv_pages(self) -> dict:
+        """Pool state of a paged reserve: free, total, page_tokens (zeros for the flat cache)."""
+        f, t, p = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        check(lib().chalot_batch_kv_pages(self._h, C.byref(f), C.byref(t), C.byref(p)))
+        return {"free": f.value, "total": t.value, "page_tokens": p.value}
+
+    def scheduler(self, max_rows: int | None = None) -> "Scheduler":
+        """A continuous-batching scheduler over this engine's batch slots."""
+        return Scheduler(self, max_rows or self._cap)
+
     # ---- expert parallelism of the batched forward ----
 
     def attach_ep_nccl(self, rank: int, world: int, group=None) -> None:
@@ -316,3 +337,55 @@ class Engine:
         ms, by = C.c_double(), C.c_double()
         check(lib().chalot_bench_moe_layers(self._h, reps, C.byref(ms), C.byref(by)))
         return ms.value, by.value
+
+
+class Scheduler:
+    """Continuous batching (chalot_sched_*): submit prompts at any time, call
+    step() to run one batched forward (decoding sequences one row each,
+    prefilling ones in prompt chunks, new ones admitted as slots and K/V pages
+    free up), poll() each sequence's greedy tokens. Every sequence's tokens are
+    those of Engine.generate on its prompt alone (engine.rs:497-548)."""
+
+    def __init__(self, engine: Engine, max_rows: int):
+        self.engine = engine
+        h = C.c_void_p()
+        check(lib().chalot_sched_create(engine._h, max_rows, C.byref(h)))
+        self._h = h
+
+    def submit(self, prompt: Sequence[int], max_new: int, stop: Sequence[int] = ()) -> int:
+        p, st = _u32(list(prompt)), _u32(list(stop))
+        i = C.c_uint64()
+        check(lib().chalot_sched_submit(self._h, p.ctypes.data_as(C.c_void_p), p.size, max_new,
+                                        st.ctypes.data_as(C.c_void_p) if st.size else None, st.size, C.byref(i)))
+        return i.value
+
+    def step(self) -> dict:
+        r, w, n = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        check(lib().chalot_sched_step(self._h, C.byref(r), C.byref(w), C.byref(n)))
+        return {"running": r.value, "waiting": w.value, "rows": n.value}
+
+    def poll(self, seq_id: int, cap: int = 1 << 16) -> tuple[list[int], bool]:
+        """(tokens so far, done); a done sequence is forgotten once polled."""
+        buf = np.zeros(max(cap, 1), np.uint32)
+        n, done = C.c_size_t(), C.c_int()
+        check(lib().chalot_sched_poll(self._h, seq_id, buf.ctypes.data_as(C.c_void_p), cap, C.byref(n),
+                                      C.byref(done)))
+        return buf[: min(n.value, cap)].tolist(), bool(done.value)
+
+    def run(self, max_steps: int = 1 << 30) -> None:
+        """Steps until nothing runs or waits."""
+        for _ in range(max_steps):
+            st = self.step()
+            if not st["running"] and not st["waiting"]:
+                return
+
+    def close(self) -> None:
+        if self._h:
+            lib().chalot_sched_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -183,6 +183,62 @@ int chalot_forward_batch(chalot_engine* e, const uint32_t* slots, const uint32_t
 /* Logits of row `row` (the i-th token) of the last chalot_forward_batch. */
 int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst, size_t n);
 
+/* chalot_batch_reserve with a paged K/V cache, the batch counterpart of the
+ * reference's PagedKVCache (src/model/memory.rs:119-185): f32 rows (so every
+ * sequence still decodes exactly as alone) in a pool of n_pages pages of
+ * page_tokens positions (a power of two in [8, 256]), page p holding
+ * [layer][position][dim] for K and for V. A slot takes pages from the pool as
+ * chalot_forward_batch writes its positions (CHALOT_ERR_OOM when none is
+ * left) and returns them with chalot_batch_release, so the cache holds the
+ * positions in use rather than max_seqs x max_seq_len. head_dim % 16 == 0. */
+int chalot_batch_reserve_paged(chalot_engine* e, uint32_t max_seqs, uint32_t n_pages, uint32_t page_tokens);
+
+/* Returns a slot's K/V pages to the pool (paged reserve; a no-op for the flat
+ * cache). The slot's next sequence starts at position 0. */
+int chalot_batch_release(chalot_engine* e, uint32_t slot);
+
+/* The reserve's max_seqs (0 before chalot_batch_reserve). */
+int chalot_batch_capacity(chalot_engine* e, uint32_t* max_seqs);
+
+/* Pool state of a paged reserve: free pages, all pages, positions per page
+ * (all 0 for the flat cache). Any pointer may be NULL. */
+int chalot_batch_kv_pages(chalot_engine* e, uint32_t* n_free, uint32_t* n_total, uint32_t* page_tokens);
+
+/* ---- continuous batching ------------------------------------------------ */
+/* A scheduler over chalot_forward_batch (the reference serves one prompt at a
+ * time, engine.rs:497-548): sequences are submitted at any time; each
+ * chalot_sched_step admits waiting sequences into free slots (with a paged
+ * reserve, only when the pool holds pages for their prompt + max_new
+ * positions beside those the running sequences may still take), gives every
+ * decoding sequence one row and the prefilling ones chunks of their prompt
+ * with the rows left (up to max_rows per forward), runs one forward, and
+ * retires sequences that produced max_new tokens or a stop token (the stop
+ * token is not returned, as in chalot_generate), releasing their slot and
+ * pages. Decoding is greedy; every sequence's tokens are those of
+ * chalot_generate on its prompt alone. One engine, no expert-parallel group. */
+typedef struct chalot_sched chalot_sched;
+
+/* The engine must be reserved (chalot_batch_reserve or _paged); max_rows in
+ * [1, its max_seqs]; slots are the engine's max_seqs slots. */
+int chalot_sched_create(chalot_engine* e, uint32_t max_rows, chalot_sched** out);
+void chalot_sched_free(chalot_sched* s);
+
+/* Queues a prompt (n >= 1 tokens) for max_new >= 1 greedy tokens, ending
+ * early at any of the n_stop stop tokens; n + max_new - 1 <= max_seq_len.
+ * *id identifies it in chalot_sched_poll. */
+int chalot_sched_submit(chalot_sched* s, const uint32_t* prompt, size_t n, uint32_t max_new, const uint32_t* stop,
+                        size_t n_stop, uint64_t* id);
+
+/* One forward over the running sequences (none: nothing runs). Any output
+ * pointer may be NULL: sequences running and waiting after the step, rows in
+ * the forward. */
+int chalot_sched_step(chalot_sched* s, uint32_t* n_running, uint32_t* n_waiting, uint32_t* n_rows);
+
+/* Tokens a sequence has produced so far (up to cap of them into out; *n_out
+ * the total) and whether it is done. A done sequence is forgotten after a poll
+ * that returns all of its tokens. CHALOT_ERR_ARG for an unknown id. */
+int chalot_sched_poll(chalot_sched* s, uint64_t id, uint32_t* out, size_t cap, size_t* n_out, int* done);
+
 /* Measured peak of the int8 tensor cores on the current device: one CTA per
  * SM streams `iters` x 4 tcgen05.mma.kind::i8 M128 x N256 x K32 out of shared
  * memory; *tops = int8 TOP/s (2 ops per multiply-add), *ms = kernel time.
