@@ -967,8 +967,8 @@ static int batch_reserve(chalot_engine* e, uint32_t max_seqs, uint32_t n_pages, 
   if (c.n_experts < 2) return set_error(CHALOT_ERR_ARG, "batch_reserve: batched decode needs a MoE model");
   if (max_seqs == 0 || max_seqs > 1024) return set_error(CHALOT_ERR_ARG, "batch_reserve: max_seqs in [1, 1024]");
   const bool paged = page_tokens != 0;
-  if (paged && (page_tokens < 8 || page_tokens > 256 || (page_tokens & (page_tokens - 1))))
-    return set_error(CHALOT_ERR_ARG, "batch_reserve: page_tokens must be a power of two in [8, 256]");
+  if (paged && (page_tokens < 16 || page_tokens > 256 || (page_tokens & (page_tokens - 1))))
+    return set_error(CHALOT_ERR_ARG, "batch_reserve: page_tokens must be a power of two in [16, 256]");
   if (paged && (n_pages == 0 || n_pages > (1u << 24)))
     return set_error(CHALOT_ERR_ARG, "batch_reserve: n_pages must be in [1, 2^24]");
   if (paged && e->cfg.head_dim % 16)

@@ -354,23 +354,30 @@ __global__ void __launch_bounds__(kAttT, 4) k_b_attn(BatchDims d, int layer, con
   __syncthreads();
   if (threadIdx.x >= hd) return;
   const float* v = vc + (size_t)h * hd + threadIdx.x;
-  auto vrow = [&](int t) { return v[kv_off(d, sl, layer, t)]; };
+  // the rows of positions u..u+kAttU-1 (u a multiple of kAttU) are consecutive:
+  // in the flat cache, and in one page (pages hold a multiple of kAttU positions)
+  auto vblk = [&](int u) { return v + kv_off(d, sl, layer, u); };
+  const size_t ld = d.dim;
   float acc = 0.0f, cur[kAttU], nxt[kAttU];
   const int nb = n / kAttU;
-  if (nb > 0)
+  if (nb > 0) {
+    const float* vb = vblk(0);
 #pragma unroll
-    for (int u = 0; u < kAttU; ++u) cur[u] = vrow(u);
+    for (int u = 0; u < kAttU; ++u) cur[u] = vb[(size_t)u * ld];
+  }
   for (int i = 0; i < nb; ++i) {
     const int t = i * kAttU;
-    if (i + 1 < nb)
+    if (i + 1 < nb) {
+      const float* vb = vblk(t + kAttU);
 #pragma unroll
-      for (int u = 0; u < kAttU; ++u) nxt[u] = vrow(t + kAttU + u);
+      for (int u = 0; u < kAttU; ++u) nxt[u] = vb[(size_t)u * ld];
+    }
 #pragma unroll
     for (int u = 0; u < kAttU; ++u) acc = __fadd_rn(acc, __fmul_rn(p[t + u], cur[u]));
 #pragma unroll
     for (int u = 0; u < kAttU; ++u) cur[u] = nxt[u];
   }
-  for (int t = nb * kAttU; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], vrow(t)));
+  for (int t = nb * kAttU; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[kv_off(d, sl, layer, t)]));
   att[(size_t)b * d.dim + h * hd + threadIdx.x] = acc;
 }
 

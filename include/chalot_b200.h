@@ -186,7 +186,7 @@ int chalot_get_batch_logits(chalot_engine* e, uint32_t row, float* dst, size_t n
 /* chalot_batch_reserve with a paged K/V cache, the batch counterpart of the
  * reference's PagedKVCache (src/model/memory.rs:119-185): f32 rows (so every
  * sequence still decodes exactly as alone) in a pool of n_pages pages of
- * page_tokens positions (a power of two in [8, 256]), page p holding
+ * page_tokens positions (a power of two in [16, 256]), page p holding
  * [layer][position][dim] for K and for V. A slot takes pages from the pool as
  * chalot_forward_batch writes its positions (CHALOT_ERR_OOM when none is
  * left) and returns them with chalot_batch_release, so the cache holds the

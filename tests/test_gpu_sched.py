@@ -41,7 +41,7 @@ def test_scheduler_continuous_batching(chalot, oracle_lib, tiny_model):
     new = [6, 3, 9, 1, 5, 8, 4, 2, 7]
     e = chalot.Engine.load(tiny_model)
     try:
-        e.reserve_batch_paged(3, n_pages=40, page_tokens=8)
+        e.reserve_batch_paged(3, n_pages=20, page_tokens=16)
         sch = e.scheduler(max_rows=3)
         ids = [sch.submit(p, n) for p, n in zip(first, new)]
         for _ in range(4):
@@ -54,7 +54,7 @@ def test_scheduler_continuous_batching(chalot, oracle_lib, tiny_model):
             assert done
             got.append(toks)
         sch.close()
-        assert e.kv_pages()["free"] == 40
+        assert e.kv_pages()["free"] == 20
     finally:
         e.close()
     o = oracle_lib.OracleEngine(tiny_model, threads=oracle_lib.hw_threads())
@@ -72,7 +72,7 @@ def test_scheduler_stop_tokens_and_page_pressure(chalot, tiny_model):
     e = chalot.Engine.load(tiny_model)
     try:
         ref = [e.generate(p, 12) for p in prompts]
-        e.reserve_batch_paged(4, n_pages=8, page_tokens=8)  # 31 positions = 4 pages per generation
+        e.reserve_batch_paged(4, n_pages=4, page_tokens=16)  # 31 positions = 2 pages per generation
         sch = e.scheduler()
         stop = ref[1][5]
         ids = [sch.submit(p, 12, stop=[stop] if i == 1 else []) for i, p in enumerate(prompts)]
@@ -82,7 +82,7 @@ def test_scheduler_stop_tokens_and_page_pressure(chalot, tiny_model):
         outs = [sch.poll(i)[0] for i in ids]
         assert outs[0] == ref[0] and outs[2] == ref[2] and outs[3] == ref[3]
         assert outs[1] == ref[1][: ref[1].index(stop)]
-        assert e.kv_pages()["free"] == 8
+        assert e.kv_pages()["free"] == 4
         sch.close()
     finally:
         e.close()
@@ -94,14 +94,14 @@ def test_scheduler_errors(chalot, tiny_model):
     try:
         with pytest.raises(ChalotError, match="reserve"):
             e.scheduler(max_rows=1)
-        e.reserve_batch_paged(2, n_pages=4, page_tokens=8)
+        e.reserve_batch_paged(2, n_pages=2, page_tokens=16)
         sch = e.scheduler()
         with pytest.raises(ChalotError, match="max_new"):
             sch.submit([1, 2], 0)
         with pytest.raises(ChalotError, match="max_seq_len"):
             sch.submit([1] * 500, 100)
         with pytest.raises(ChalotError, match="pages"):
-            sch.submit([1] * 40, 1)  # 40 positions > 4 pages of 8
+            sch.submit([1] * 40, 1)  # 40 positions > 2 pages of 16
         with pytest.raises(ChalotError, match="unknown"):
             sch.poll(12345)
         sch.close()
