@@ -737,13 +737,51 @@ def run_moe(args):
         print(json.dumps(r), flush=True)
 
 
+def run_kernels(args):
+    """Small cases of the batched-decode kernels, sized for ncu captures:
+    one MoE layer at the 1B shape (dim 2048, hidden 5632, 16 experts, top-2)
+    for 64 tokens through chalot_moe_layer (the few-slot expert kernels), and
+    six chalot_forward_batch steps of 64 sequences of the Qwen-shaped model on
+    a paged K/V pool of 128 pages (the tcgen05 dense GEMMs, the batched
+    attention). Prints the layer time and the step time."""
+    import numpy as np
+    import torch
+
+    import chalot_c1_b200 as cb
+    from chalot_c1_b200 import moe
+    layer = moe.synthetic_moe_layer(2048, 5632, 16, 2, 32, seed=2)
+    x = torch.from_numpy(np.random.default_rng(5).standard_normal((64, 2048), dtype=np.float32)).cuda()
+    dev = moe.MoeLayer(layer, max_tokens=64)
+    for _ in range(max(args.warmup, 1)):
+        out, sel, selw = dev(x)
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(max(args.steps, 1)):
+        dev(x, out=out, sel=sel, selw=selw)
+    en.record()
+    torch.cuda.synchronize()
+    layer_ms = st.elapsed_time(en) / max(args.steps, 1)
+    del dev
+    path = cb.ensure_shape(model_dir(), "qwen")
+    e = cb.Engine.load(path)
+    e.reserve_batch_paged(64, n_pages=128, page_tokens=16)
+    rng = np.random.default_rng(0)
+    step_ms = []
+    for p in range(6):
+        e.forward_batch(list(range(64)), rng.integers(0, 151936, 64).tolist(), [p] * 64)
+        step_ms.append(e.last_timing()["decode_ms"])
+    e.close()
+    print(json.dumps({"moe_layer_1b_64tok_ms": layer_ms, "qwen_batch64_step_ms": step_ms}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe", "paged", "batch"])
+    ap.add_argument("--mode", default="bench", choices=["bench", "profile", "moe", "paged", "batch", "kernels"])
     ap.add_argument("--paged-layers", type=int, default=PG_LAYERS,
                     help="--mode paged: layers (one 470 MB page pool each)")
     a = ap.parse_args()
@@ -758,6 +796,9 @@ def main():
         return
     if a.mode == "batch":
         run_batch(a)
+        return
+    if a.mode == "kernels":
+        run_kernels(a)
         return
     ws, rank, local = dist_setup()
     try:
