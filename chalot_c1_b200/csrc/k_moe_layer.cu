@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "devstat.h"
 #include "moe_layer.h"
+#include "tc.cuh"
 #include "unpack.cuh"
 
 namespace chalot {
@@ -483,11 +484,19 @@ __global__ void __launch_bounds__(kFewThreads) k_ml_few(MlDims d, const MlExpert
           const uint32_t b1 = RP ? xv.y : __byte_perm(xv.x, xv.y, 0x7531);
           int dd[4];
           mma_s8_16832(dd, a0, a1, a2, a3, b0, b1, 0x4B400000);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float f = __fsub_rn(__int_as_float(dd[i]), 12582912.0f);
-            acc[nt][i] = __fadd_rn(acc[nt][i], __fmul_rn(__fmul_rn(f, i < 2 ? wa : wb), xs[nt][i & 1]));
-          }
+          // ((float)gdot * s) * xs for the slot pair of each row as packed f32x2
+          // (each lane rounded as the scalar instruction), then scalar adds,
+          // which the assembler never fuses with the multiplies
+          const f32x2 bias = f2_pack(12582912.0f, 12582912.0f), x01 = f2_pack(xs[nt][0], xs[nt][1]);
+          const f32x2 pa = f2_mul(f2_mul(f2_sub(f2_pack_bits(dd[0], dd[1]), bias), f2_pack(wa, wa)), x01);
+          const f32x2 pb = f2_mul(f2_mul(f2_sub(f2_pack_bits(dd[2], dd[3]), bias), f2_pack(wb, wb)), x01);
+          float v0, v1, v2, v3;
+          f2_unpack(pa, v0, v1);
+          f2_unpack(pb, v2, v3);
+          acc[nt][0] = __fadd_rn(acc[nt][0], v0);
+          acc[nt][1] = __fadd_rn(acc[nt][1], v1);
+          acc[nt][2] = __fadd_rn(acc[nt][2], v2);
+          acc[nt][3] = __fadd_rn(acc[nt][3], v3);
         }
       }
     }
