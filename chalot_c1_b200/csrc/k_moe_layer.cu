@@ -316,9 +316,10 @@ __global__ void __launch_bounds__(kThreads) k_ml_gemm(MlDims d, const MlExperts 
 // weight rows and takes, per group of 32 columns, one MMA per 8 slots. Its A
 // fragment is unpacked from the staged int4 bytes (lane (g, t) holds packed
 // word t of rows g and g+8: low nibbles as k 4t..4t+3, high nibbles as
-// 16+4t..; the activations' B fragment pairs the same columns), its
-// accumulator input is the bits of 1.5*2^23, so every D element reads back as
-// 12582912 + gdot, exact, and one subtraction gives (float)gdot. The f32
+// 16+4t.., each as 16 x its value; the activations' B fragment pairs the same
+// columns), its accumulator input is the bits of 1.5*2^23, so every D element
+// reads back as 12582912 + 16 gdot, exact, and one subtraction gives
+// (float)(16 gdot), which the group scale / 16 turns into gdot * s exactly. The f32
 // group epilogue t = t + ((float)gdot * s_g) * xs then runs on the D fragment
 // in registers, in group order, as in matmul_int4 (src/tensor/matmul.rs:
 // 452-654). Gate/up warps hold 8 gate rows (units u..u+7) and the 8 up rows
@@ -352,15 +353,18 @@ CHALOT_DEV void few_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// One packed int4 word (8 columns) -> the signed int8 words of its low and
-// high nibbles. Repacked layout: low nibbles are columns 8j..8j+3, high ones
-// 8j+4..8j+7, two's complement. File layout: byte k holds columns 2k (low)
-// and 2k+1 (high) as value + 8, so low nibbles are the even columns.
+// One packed int4 word (8 columns) -> int8 words of 16 x its low and high
+// nibbles: a two's complement nibble moved to the top of a byte reads as the
+// signed byte 16 * value (in [-128, 112]), so no sign extension is needed.
+// Repacked layout: low nibbles are columns 8j..8j+3, high ones 8j+4..8j+7,
+// two's complement. File layout: byte k holds columns 2k (low) and 2k+1
+// (high) as value + 8 (flipping a nibble's top bit makes it two's
+// complement), so low nibbles are the even columns.
 template <bool RP>
-CHALOT_DEV void few_nibbles(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  const uint32_t v = RP ? w ^ 0x88888888u : w;  // every nibble as value + 8
-  lo = nib_minus8(v & 0x0F0F0F0Fu);
-  hi = nib_minus8((v >> 4) & 0x0F0F0F0Fu);
+CHALOT_DEV void few_nibbles16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t v = RP ? w : w ^ 0x88888888u;
+  lo = (v << 4) & 0xF0F0F0F0u;
+  hi = v & 0xF0F0F0F0u;
 }
 
 // D = A * B + C, m16n8k32, A row-major s8, B column-major s8, s32 accumulators.
@@ -471,10 +475,13 @@ __global__ void __launch_bounds__(kFewThreads) k_ml_few(MlDims d, const MlExpert
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // the stage's groups, in order
       uint32_t a0, a1, a2, a3;
-      few_nibbles<RP>(*reinterpret_cast<const uint32_t*>(W + la * kFewWStride + q * 16 + 4 * t), a0, a2);
-      few_nibbles<RP>(*reinterpret_cast<const uint32_t*>(W + lb * kFewWStride + q * 16 + 4 * t), a1, a3);
-      const float wa = q == 0 ? sa.x : q == 1 ? sa.y : q == 2 ? sa.z : sa.w;
-      const float wb = q == 0 ? sb.x : q == 1 ? sb.y : q == 2 ? sb.z : sb.w;
+      few_nibbles16<RP>(*reinterpret_cast<const uint32_t*>(W + la * kFewWStride + q * 16 + 4 * t), a0, a2);
+      few_nibbles16<RP>(*reinterpret_cast<const uint32_t*>(W + lb * kFewWStride + q * 16 + 4 * t), a1, a3);
+      // the MMA sums 16 x the group dot (exact, |16 gdot| < 2^22); s / 16 is
+      // exact for every normal scale (s >= 2^-122), and then (16 gdot) * (s / 16)
+      // rounds as gdot * s
+      const float wa = __fmul_rn(q == 0 ? sa.x : q == 1 ? sa.y : q == 2 ? sa.z : sa.w, 0.0625f);
+      const float wb = __fmul_rn(q == 0 ? sb.x : q == 1 ? sb.y : q == 2 ? sb.z : sb.w, 0.0625f);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         if (nt < ntiles) {
