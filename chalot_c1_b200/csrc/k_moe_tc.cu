@@ -141,12 +141,12 @@ constexpr uint32_t kMagic = 0x4B400000u;  // bits of 1.5 * 2^23
 
 // Persistent kernel: CTA b takes tiles b, b + gridDim.x, ... of the
 // (128-slot block, 128-row tile) grid, row tiles fastest. The TMA ring, the
-// scale ring and the two TMEM buffers run continuously across tiles, so the
+// scale ring and the TMEM buffers run continuously across tiles, so the
 // next tile's loads and first MMAs overlap this tile's last groups and its
-// stores. Each TMEM buffer holds 1.5*2^23 in every element before an MMA
-// accumulates a group's int32 dots onto it; the bits then read back as the
-// float 12582912 + gdot (exact, |gdot| < 2^22), so one packed subtraction
-// gives (float)gdot, and the epilogue refills the buffer after reading it.
+// stores. Each group's MMA overwrites its TMEM buffer with the int32 dots;
+// the epilogue adds the bits of 1.5*2^23 to each word as an integer, so the
+// word reads as the float 12582912 + gdot (exact, |gdot| < 2^22) and one
+// packed subtraction gives (float)gdot.
 template <bool GU>
 __global__ void __launch_bounds__(kTcThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               break;
             }
             tc_fence_after();
-            tc_mma_i8(tmem + buf * 128, tc_desc_sw128(a0 + j * 32), tc_desc_sw128(b0 + j * 32), kIdesc, 1);
+            tc_mma_i8(tmem + buf * 128, tc_desc_sw128(a0 + j * 32), tc_desc_sw128(b0 + j * 32), kIdesc, 0);
             tc_commit(&sm->t_full[buf]);
           }
           if (ok) tc_commit(&sm->empty[st]);
@@ -261,12 +261,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int col_a = GU ? 16 * quarter : 32 * quarter;
     const int col_b = GU ? 64 + 16 * quarter : 32 * quarter + 16;
     const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
-    // every buffer starts at the bias
-    for (int b = 0; b < kTBufs; ++b) {
-      tc_st16_fill(lane_addr + b * 128 + col_a, kMagic);
-      tc_st16_fill(lane_addr + b * 128 + col_b, kMagic);
-    }
-    tc_wait_st();
+    // every buffer starts free
     tc_fence_before();
     __syncwarp();
     if (lane == 0)
@@ -304,19 +299,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // acc = acc + ((float)gdot * s) * xs, lane-wise in f32
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const f32x2 ga = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
+          const f32x2 ga = f2_sub(f2_pack_bits(r[2 * j] + kMagic, r[2 * j + 1] + kMagic), bias);
           acc0[j] = f2_add_nc(acc0[j], f2_mul(f2_mul(ga, sa[j]), xs));
         }
         tc_ld16(ta + col_b, r);
         tc_wait_ld();
-        tc_st16_fill(ta + col_a, kMagic);
-        tc_st16_fill(ta + col_b, kMagic);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const f32x2 gb = f2_sub(f2_pack_bits(r[2 * j], r[2 * j + 1]), bias);
+          const f32x2 gb = f2_sub(f2_pack_bits(r[2 * j] + kMagic, r[2 * j + 1] + kMagic), bias);
           acc1[j] = f2_add_nc(acc1[j], f2_mul(f2_mul(gb, sb[j]), xs));
         }
-        tc_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->t_empty[buf]);
