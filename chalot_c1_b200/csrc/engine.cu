@@ -1188,7 +1188,12 @@ static int ep_moe(chalot_engine* e, int l, int B, const MlDims& md, MlWork w, cu
   const MlDims xd{(int)R, (int)D, (int)c.hidden_dim, El, 1, (int)c.int4_group_size};
   MlWork xw;
   const size_t simt = ml_layout(xd, p.ws, &xw);
-  const bool tc = ml_use_tc(xd);
+  // the blocks hold R rows, mostly padding: the kernels are chosen by the rows a
+  // rank receives on average, this rank's B*K (ranks decode similar batches)
+  const int live = std::max(B, 1) * K;
+  MlDims xe = xd;
+  xe.T = std::min(live, (int)R);
+  const bool tc = ml_use_tc(xe);
   MlTcWork xt{};
   if (tc) ml_tc_layout(xd, simt, p.ws, &xt);
   xw.sel = p.rexp;  // -1 on padding rows: not dispatched, their outputs are 0
@@ -1197,7 +1202,7 @@ static int ep_moe(chalot_engine* e, int l, int B, const MlDims& md, MlWork w, cu
   MlExperts X{};
   for (int i = 0; i < El; ++i) X.ex[i] = b.experts[l].ex[rank + G * i];
   X.repacked = b.experts[l].repacked;
-  CK(ml_run_rows(xd, X, xw, tc ? &xt : nullptr, p.y, s));
+  CK(ml_run_rows(xd, X, xw, tc ? &xt : nullptr, p.y, s, live));
   if ((rc = link.all_to_all(p.y, yb.data(), p.yback, yb.data(), s, msg)) != CHALOT_OK) return rc;
   if (B > 0) {
     w.y = p.yback;   // padded blocks of the outputs of my rows

@@ -783,7 +783,9 @@ cudaError_t ml_run_decode(const MlDims& d, float* x, const float* norm_ffn, cons
     if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
     if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
   } else {
-    const int bm = tile_slots(d, X);
+    MlDims de = d;  // the slot tiles from the live rows when the caller knows them
+    if (est_rows >= 0) de.T = std::max(1, std::min(est_rows, d.T));
+    const int bm = tile_slots(de, X);
     k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
     tile_gemms(d, X, w, bm, s);
   }
@@ -836,7 +838,7 @@ void ml_launch_combine(const MlDims& d, const MlWork& w, float* out, cudaStream_
 // output) is written in row order through the combine with weight 1.0, which
 // reproduces y exactly (0 + 1*y).
 cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork* t, float* y,
-                        cudaStream_t s) {
+                        cudaStream_t s, int est_rows) {
   if (d.T == 0) return cudaSuccess;
   const size_t N = (size_t)d.T;
   k_fill_f32<<<(unsigned)std::min<size_t>((N + 255) / 256, 1024), 256, 0, s>>>(w.selw, N, 1.0f);

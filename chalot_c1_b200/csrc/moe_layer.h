@@ -77,8 +77,10 @@ void ml_launch_route(const MlDims& d, const float* x, const float* rw, const flo
                      cudaStream_t s);
 void ml_launch_plan(const MlDims& d, const MlWork& w, int n_ranks, int32_t* offs, cudaStream_t s);
 void ml_launch_combine(const MlDims& d, const MlWork& w, float* out, cudaStream_t s);
+// est_rows >= 0: the expected number of live rows (the rest are padding that the
+// dispatch skips), which picks the expert kernels' slot tiles.
 cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, const MlTcWork* t, float* y,
-                        cudaStream_t s);
+                        cudaStream_t s, int est_rows = -1);
 bool ml_use_tc(const MlDims& d);
 cudaError_t ml_run_tc(const MlDims& d, const float* x, const float* rw, const float* rb, const MlExperts& X,
                       const MlWork& w, const MlTcWork& t, float* out, cudaStream_t s);
