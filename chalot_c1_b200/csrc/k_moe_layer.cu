@@ -783,9 +783,7 @@ cudaError_t ml_run_decode(const MlDims& d, float* x, const float* norm_ffn, cons
     if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
     if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
   } else {
-    MlDims de = d;  // the slot tiles from the live rows when the caller knows them
-    if (est_rows >= 0) de.T = std::max(1, std::min(est_rows, d.T));
-    const int bm = tile_slots(de, X);
+    const int bm = tile_slots(d, X);
     k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
     tile_gemms(d, X, w, bm, s);
   }
@@ -852,7 +850,9 @@ cudaError_t ml_run_rows(const MlDims& d, const MlExperts& X, const MlWork& w, co
     if ((r = ml_tc_quant(d, w, *t, s)) != cudaSuccess) return r;
     if ((r = ml_tc_gemm(d, false, w, *t, nmb, s)) != cudaSuccess) return r;
   } else {
-    const int bm = tile_slots(d, X);
+    MlDims de = d;  // the slot tiles from the live rows when the caller knows them
+    if (est_rows >= 0) de.T = std::max(1, std::min(est_rows, d.T));
+    const int bm = tile_slots(de, X);
     k_ml_dispatch<<<1, 1024, 0, s>>>(d, w, bm, 1, nullptr);
     tile_gemms(d, X, w, bm, s);
   }
