@@ -20,6 +20,8 @@
 #include <cstring>
 #include <deque>
 #include <map>
+#include <memory>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -73,14 +75,20 @@ __attribute__((visibility("default"))) int chalot_sched_create(chalot_engine* e,
   if (!slots) return set_error(CHALOT_ERR_STATE, "sched_create: reserve the batch first (chalot_batch_reserve)");
   if (max_rows < 1 || max_rows > slots) return set_error(CHALOT_ERR_ARG, "sched_create: max_rows must be in [1, max_seqs]");
   if (pt && nfree != ntotal) return set_error(CHALOT_ERR_STATE, "sched_create: the page pool is already in use");
-  auto* s = new chalot_sched;
+  chalot_sched* s = new (std::nothrow) chalot_sched;
+  if (!s) return set_error(CHALOT_ERR_OOM, "sched_create: out of host memory");
   s->e = e;
   s->max_rows = max_rows;
   s->n_slots = slots;
   s->max_seq = c.max_seq_len;
   s->page_tokens = pt;
   s->total_pages = ntotal;
-  s->slot_seq.assign(slots, nullptr);
+  try {
+    s->slot_seq.assign(slots, nullptr);
+  } catch (const std::bad_alloc&) {
+    delete s;
+    return set_error(CHALOT_ERR_OOM, "sched_create: out of host memory");
+  }
   *out = s;
   return CHALOT_OK;
 }
@@ -99,21 +107,28 @@ __attribute__((visibility("default"))) int chalot_sched_submit(chalot_sched* s, 
   if (n < 1 || max_new < 1) return set_error(CHALOT_ERR_ARG, "sched_submit: need a prompt and max_new >= 1");
   if (n + max_new - 1 > s->max_seq)
     return set_error(CHALOT_ERR_ARG, "sched_submit: prompt + max_new - 1 exceeds max_seq_len");
-  auto* q = new Seq;
-  q->id = s->next_id++;
-  q->prompt.assign(prompt, prompt + n);
-  q->max_new = max_new;
-  q->stop.assign(stop, stop + n_stop);
+  uint32_t pages = 0;
   if (s->page_tokens) {
-    q->pages = (uint32_t)((n + max_new - 1 + s->page_tokens - 1) / s->page_tokens);
-    if (q->pages > s->total_pages) {
-      delete q;
+    pages = (uint32_t)((n + max_new - 1 + s->page_tokens - 1) / s->page_tokens);
+    if (pages > s->total_pages)
       return set_error(CHALOT_ERR_ARG, "sched_submit: the generation needs more K/V pages than the pool holds");
-    }
   }
-  s->waiting.push_back(q);
-  s->all[q->id] = q;
-  *id = q->id;
+  try {
+    auto q = std::make_unique<Seq>();
+    q->id = s->next_id;
+    q->prompt.assign(prompt, prompt + n);
+    q->max_new = max_new;
+    q->stop.assign(stop, stop + n_stop);
+    q->pages = pages;
+    s->all[q->id] = q.get();
+    s->waiting.push_back(q.get());
+    *id = q->id;
+    ++s->next_id;
+    q.release();
+  } catch (const std::bad_alloc&) {
+    s->all.erase(s->next_id);
+    return set_error(CHALOT_ERR_OOM, "sched_submit: out of host memory");
+  }
   return CHALOT_OK;
 }
 
@@ -129,9 +144,19 @@ static void take_token(Seq* q, uint32_t tok) {
   if (q->out.size() >= q->max_new) q->done = true;
 }
 
+static int sched_step(chalot_sched* s, uint32_t* n_running, uint32_t* n_waiting, uint32_t* n_rows);
+
 __attribute__((visibility("default"))) int chalot_sched_step(chalot_sched* s, uint32_t* n_running,
                                                             uint32_t* n_waiting, uint32_t* n_rows) {
   if (!s) return set_error(CHALOT_ERR_ARG, "sched_step: null scheduler");
+  try {
+    return sched_step(s, n_running, n_waiting, n_rows);
+  } catch (const std::bad_alloc&) {
+    return set_error(CHALOT_ERR_OOM, "sched_step: out of host memory");
+  }
+}
+
+static int sched_step(chalot_sched* s, uint32_t* n_running, uint32_t* n_waiting, uint32_t* n_rows) {
   // admission: free slots, and pages for the whole generation
   for (uint32_t i = 0; i < s->n_slots && !s->waiting.empty(); ++i) {
     if (s->slot_seq[i]) continue;
